@@ -1,0 +1,202 @@
+/*
+ * sharpinfer_cuda.h -- C ABI of libsharpinfer_cuda, the CUDA (sm_100a)
+ * backend for SharpInference's mat-vec / matrix-multiply instructions.
+ *
+ * Every entry point returns an si_status and never aborts the process; the
+ * message for the last failure on the calling thread is returned by
+ * si_last_error(). Status codes map onto the exception types the reference
+ * raises for the same condition (see si_status).
+ *
+ * Reference interfaces each group replaces are cited as
+ * path:line inside JohnMasen/SharpInference/src.
+ *
+ * Tensor element types use the GGUF type ids of
+ * SharpInference.Gguf/GgufModelFile.cs:24-46 (F32 = 0, F16 = 1, Q8_0 = 8,
+ * Q4_K = 12). Quantized weights are the raw GGUF block bytes, row-major:
+ * row r of a [rows, cols] matrix starts at r * si_row_bytes(type, cols).
+ */
+#ifndef SHARPINFER_CUDA_H
+#define SHARPINFER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SI_ABI_VERSION 1
+
+typedef enum si_status {
+    SI_OK = 0,
+    SI_ERR_INVALID_ARGUMENT = 1, /* ArgumentException / ArgumentOutOfRangeException */
+    SI_ERR_UNSUPPORTED = 2,      /* NotSupportedException (unknown type, no implementation) */
+    SI_ERR_ADAPTATION = 3,       /* InstructionAdaptationException (signature / config mismatch) */
+    SI_ERR_INVALID_DATA = 4,     /* InvalidDataException (bad program, bad block count) */
+    SI_ERR_CUDA = 5,             /* CUDA runtime error (device removed, launch failure) */
+    SI_ERR_OUT_OF_MEMORY = 6,
+    SI_ERR_NCCL = 7,
+    SI_ERR_TIMEOUT = 8,          /* bounded device-side or host-side wait expired */
+    SI_ERR_NO_DEVICE = 9
+} si_status;
+
+typedef enum si_type {
+    SI_TYPE_F32 = 0,
+    SI_TYPE_F16 = 1,
+    SI_TYPE_Q8_0 = 8,
+    SI_TYPE_Q4_K = 12,
+    SI_TYPE_I32 = 26 /* control ports only (GgufModelTensorType.Int32) */
+} si_type;
+
+/* Execution configurations of core.mat-vec
+ * (GpuMatVecExecution.cs:8-10 serial-matvec / cooperative-matvec, plus the
+ * CUDA quantized implementations). SI_MATVEC_DEFAULT picks per type. */
+typedef enum si_matvec_config {
+    SI_MATVEC_DEFAULT = 0,
+    SI_MATVEC_COOPERATIVE = 1, /* "cooperative-matvec": Neumaier per lane + merge (F32/F16 weights) */
+    SI_MATVEC_QUANT_STAGED = 2 /* "cuda-gemv-staged": TMA bulk row staging (Q8_0 / Q4_K) */
+} si_matvec_config;
+
+/* ---------------------------------------------------------------------- */
+/* Library / error state                                                  */
+/* ---------------------------------------------------------------------- */
+int si_abi_version(void);
+/* Copies the calling thread's last error message (NUL-terminated). */
+si_status si_last_error(char *buffer, size_t capacity);
+si_status si_device_count(int *count);
+
+/* ---------------------------------------------------------------------- */
+/* GGUF formats (host only, no GPU needed)                                */
+/* ---------------------------------------------------------------------- */
+/* GgufModelFile.GetByteLength (SharpInference.Gguf/GgufModelFile.cs:301-331),
+ * extended with Q4_K (144 B / 256 elements). A block type whose element
+ * count is not a multiple of its block gives SI_ERR_INVALID_DATA; an unknown
+ * type gives SI_ERR_UNSUPPORTED, as the reference throws. */
+si_status si_tensor_byte_length(uint32_t type, const uint64_t *dims, int rank, uint64_t *bytes);
+/* Byte length of one row of `cols` elements. */
+si_status si_row_bytes(uint32_t type, int64_t cols, uint64_t *bytes);
+/* Host block codecs. Quantizers are deterministic; dequantisation is exact
+ * FP32 arithmetic: Q8_0 w = d*q; Q4_K w = (d*sc)*q - (dmin*m).
+ * No reference counterpart (the reference has no quantized arithmetic). */
+si_status si_quantize(uint32_t type, const float *src, int64_t count, void *dst);
+si_status si_dequantize(uint32_t type, const void *src, int64_t count, float *dst);
+/* Seeded N(0, sigma) generator (SplitMix64 counter + Box-Muller) shared by
+ * tests and benchmarks so CPU and GPU paths see identical bytes. `threads`
+ * <= 0 uses all online cores. */
+si_status si_synth_normal(uint64_t seed, uint64_t offset, int64_t count, float sigma,
+                          float *dst, int threads);
+/* Generate + quantize a [rows, cols] weight matrix in one pass (same values
+ * as si_synth_normal followed by si_quantize). */
+si_status si_synth_weights(uint32_t type, uint64_t seed, int64_t rows, int64_t cols, float sigma,
+                           void *dst, int threads);
+
+/* ---------------------------------------------------------------------- */
+/* Kernel entry points on caller-owned device memory                      */
+/* `stream` is a cudaStream_t (NULL = legacy default stream). Calls are   */
+/* asynchronous; argument errors are reported before anything launches.  */
+/* ---------------------------------------------------------------------- */
+/* core.mat-vec: y[r] = sum_c W[r,c] * x[c]
+ * (TierZeroOperationContracts.cs:113-115,161; GpuTierZeroInstruction.cs:44-90;
+ *  CpuInstructionNumerics.MatVec, CpuInstructionNumerics.cs:16-23).
+ * weight_type: F32, F16 (cooperative Neumaier), Q8_0, Q4_K (staged GEMV).
+ * input_type / output_type: F32 or F16 (F16 only with F32/F16 weights, the
+ * [f16,f16]->f16 signature of the T0 FP16 collection). */
+si_status si_matvec(uint32_t weight_type, const void *weight,
+                    uint32_t input_type, const void *input,
+                    uint32_t output_type, void *output,
+                    int64_t rows, int64_t cols, uint32_t config, void *stream);
+
+/* transformer.batch-shared-matvec
+ * (GpuBatchTransformerInstructions.cs:224-279): for b < control[1],
+ * out[b,o] = sum_i W[o,i] * in[b,i]; rows b >= control[1] are not written.
+ * `control` is a device pointer to int32[2] = (start, validCount), read on
+ * the device. Weight F16, Q8_0 or Q4_K; input/output F32. */
+si_status si_batch_shared_matvec(uint32_t weight_type, const void *weight,
+                                 const float *input, const int32_t *control, float *output,
+                                 int64_t batch, int64_t out_features, int64_t in_features,
+                                 void *stream);
+
+/* core.matrix-multiply with transpose_left=false, transpose_right=true
+ * (TierZeroOperationContracts.cs:172-179; CpuInstructionNumerics.cs:61-82):
+ * Y[m,n] = sum_k X[m,k] * W[n,k]. X, Y F32; W F32, F16, Q8_0 or Q4_K.
+ * `workspace` is caller-owned device scratch of at least
+ * si_matrix_multiply_workspace_bytes(...) bytes (may be NULL when that is 0). */
+si_status si_matrix_multiply_workspace_bytes(uint32_t weight_type, int64_t m, int64_t n, int64_t k,
+                                             uint64_t *bytes);
+si_status si_matrix_multiply(uint32_t weight_type, const float *x, const void *weight, float *y,
+                             int64_t m, int64_t n, int64_t k,
+                             void *workspace, uint64_t workspace_bytes, void *stream);
+
+/* Device error word written by bounded device-side waits (a timed-out
+ * mbarrier wait sets it instead of trapping). Reading clears it. */
+si_status si_device_error_take(int device, uint32_t *code);
+
+/* ---------------------------------------------------------------------- */
+/* Executor: device buffers per slot, uploads/readbacks and stream        */
+/* (D3D12VmExecutor.cs:283-361,452-482 Upload / Readback / Execute /     */
+/*  ExecuteWithTransfers / MeasureGpuMicroseconds; D3D12VmResourcePool).  */
+/* ---------------------------------------------------------------------- */
+typedef struct si_context si_context;
+typedef struct si_buffer si_buffer;
+
+si_status si_context_create(int device, si_context **out);
+si_status si_context_destroy(si_context *ctx);
+/* The context's stream (cudaStream_t) for interop. */
+si_status si_context_stream(si_context *ctx, void **stream);
+si_status si_context_synchronize(si_context *ctx);
+/* Number of kernel launches (submissions) the context has issued. */
+si_status si_context_submission_count(si_context *ctx, uint64_t *count);
+
+si_status si_buffer_create(si_context *ctx, uint64_t bytes, si_buffer **out);
+si_status si_buffer_destroy(si_context *ctx, si_buffer *buffer);
+si_status si_buffer_device_pointer(si_buffer *buffer, void **pointer, uint64_t *bytes);
+/* Synchronous upload / readback at a byte offset (Upload/Readback). */
+si_status si_buffer_upload(si_context *ctx, si_buffer *buffer, uint64_t offset,
+                           const void *src, uint64_t bytes);
+si_status si_buffer_readback(si_context *ctx, si_buffer *buffer, uint64_t offset,
+                             void *dst, uint64_t bytes);
+/* Asynchronous variants on the context stream (src/dst should be pinned). */
+si_status si_buffer_upload_async(si_context *ctx, si_buffer *buffer, uint64_t offset,
+                                 const void *src, uint64_t bytes);
+si_status si_buffer_readback_async(si_context *ctx, si_buffer *buffer, uint64_t offset,
+                                   void *dst, uint64_t bytes);
+si_status si_host_alloc_pinned(uint64_t bytes, void **out);
+si_status si_host_free_pinned(void *ptr);
+
+/* Instruction dispatch on executor buffers. Tensor arguments are
+ * (buffer, byte offset) pairs, mirroring VmArgument.ByteOffset
+ * (SharpInference.Vm/VmProgram.cs:45). */
+si_status si_ctx_matvec(si_context *ctx, uint32_t weight_type, si_buffer *weight, uint64_t weight_offset,
+                        uint32_t input_type, si_buffer *input, uint64_t input_offset,
+                        uint32_t output_type, si_buffer *output, uint64_t output_offset,
+                        int64_t rows, int64_t cols, uint32_t config);
+si_status si_ctx_batch_shared_matvec(si_context *ctx, uint32_t weight_type,
+                                     si_buffer *weight, uint64_t weight_offset,
+                                     si_buffer *input, uint64_t input_offset,
+                                     si_buffer *control, uint64_t control_offset,
+                                     si_buffer *output, uint64_t output_offset,
+                                     int64_t batch, int64_t out_features, int64_t in_features);
+/* Uses a context-owned workspace grown on demand. */
+si_status si_ctx_matrix_multiply(si_context *ctx, uint32_t weight_type,
+                                 si_buffer *x, uint64_t x_offset,
+                                 si_buffer *weight, uint64_t weight_offset,
+                                 si_buffer *y, uint64_t y_offset,
+                                 int64_t m, int64_t n, int64_t k);
+
+/* ---------------------------------------------------------------------- */
+/* Instruction registry (InstructionCollection.cs:146-218)                */
+/* ---------------------------------------------------------------------- */
+/* Resolves (collection GUID, instruction name) for target "cuda". Returns
+ * SI_ERR_UNSUPPORTED when no CUDA implementation exists, as
+ * InstructionRegistry.Resolve throws NotSupportedException. */
+si_status si_instruction_resolve(const char *collection_id, const char *name, int *instruction_id);
+/* Validates a signature: port element types in port order and an execution
+ * configuration name ("" = none). SI_ERR_ADAPTATION mirrors
+ * InstructionAdaptationException. */
+si_status si_instruction_validate(int instruction_id, const uint32_t *port_types, int port_count,
+                                  const char *configuration);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,98 @@
+// Device-side helpers shared by the sm_100a kernels of libsharpinfer_cuda:
+// mbarrier / bulk-copy wrappers with bounded waits, the device error word,
+// binary16 loads and the Neumaier step of the cooperative mat-vec.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace si::dev {
+
+// Device error word, one per translation unit (internal linkage, so no
+// relocatable device code is needed). A bounded wait that runs out sets a
+// bit here instead of trapping; each unit's host code reads and clears its
+// word, and si_device_error_take() ORs them.
+enum : uint32_t {
+    kErrFullBarrierTimeout = 1u,
+    kErrEmptyBarrierTimeout = 2u,
+    kErrMmaBarrierTimeout = 4u,
+    kErrEpilogueTimeout = 8u,
+};
+static __device__ uint32_t g_error_word;
+
+// ~2^26 polls of try_wait (each poll may suspend the thread for a while):
+// seconds, far above any legitimate wait, far below a watchdog.
+constexpr uint32_t kMaxPolls = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records `err`) when
+// the poll budget runs out, so the caller can carry on without hanging.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t err) {
+    for (uint32_t i = 0; i < kMaxPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_error_word, err);
+    return false;
+}
+
+// 1-D bulk copy global -> shared (TMA, no tensor map, no multicast); bytes
+// and both addresses must be multiples of 16. Completion is signalled as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float ldf(const float *p) { return *p; }
+__device__ __forceinline__ float ldf(const __half *p) { return __half2float(*p); }
+__device__ __forceinline__ void stf(float *p, float v) { *p = v; }
+__device__ __forceinline__ void stf(__half *p, float v) { *p = __float2half_rn(v); }
+
+// Neumaier step (add32 of the reference's cooperative mat-vec): rounding
+// error of each addition is collected in `correction`; a non-finite total
+// clears the correction so +/-Inf and NaN survive the final sum.
+__device__ __forceinline__ void add32(float &sum, float &correction, float value) {
+    const float total = __fadd_rn(sum, value);
+    if (isfinite(total)) {
+        const float residual = fabsf(sum) >= fabsf(value) ? __fadd_rn(__fsub_rn(sum, total), value)
+                                                          : __fadd_rn(__fsub_rn(value, total), sum);
+        correction = __fadd_rn(correction, residual);
+    } else {
+        correction = 0.0f;
+    }
+    sum = total;
+}
+
+}  // namespace si::dev

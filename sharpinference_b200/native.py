@@ -1,0 +1,312 @@
+"""ctypes binding of libsharpinfer_cuda (the C ABI in include/sharpinfer_cuda.h).
+
+Status codes become the exception types the reference raises for the same
+condition (SharpInference.Instructions/InstructionCollection.cs:152-156 for
+InstructionAdaptationException; ArgumentException / NotSupportedException /
+InvalidDataException elsewhere). The library is required: importing this
+module without the built shared object raises, there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libsharpinfer_cuda.so"
+
+# GGUF tensor type ids (GgufModelFile.cs:24-46)
+F32, F16, Q8_0, Q4_K, I32 = 0, 1, 8, 12, 26
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", I32: "I32"}
+
+MATVEC_DEFAULT, MATVEC_COOPERATIVE, MATVEC_QUANT_STAGED = 0, 1, 2
+
+(SI_OK, SI_ERR_INVALID_ARGUMENT, SI_ERR_UNSUPPORTED, SI_ERR_ADAPTATION, SI_ERR_INVALID_DATA, SI_ERR_CUDA,
+ SI_ERR_OUT_OF_MEMORY, SI_ERR_NCCL, SI_ERR_TIMEOUT, SI_ERR_NO_DEVICE) = range(10)
+
+
+class SiError(RuntimeError):
+    status = -1
+
+
+class ArgumentError(SiError, ValueError):          # ArgumentException
+    status = SI_ERR_INVALID_ARGUMENT
+
+
+class NotSupportedError(SiError):                  # NotSupportedException
+    status = SI_ERR_UNSUPPORTED
+
+
+class InstructionAdaptationError(SiError):         # InstructionAdaptationException
+    status = SI_ERR_ADAPTATION
+
+
+class InvalidDataError(SiError):                   # InvalidDataException
+    status = SI_ERR_INVALID_DATA
+
+
+class CudaError(SiError):
+    status = SI_ERR_CUDA
+
+
+class OutOfMemoryError(SiError, MemoryError):
+    status = SI_ERR_OUT_OF_MEMORY
+
+
+class NcclError(SiError):
+    status = SI_ERR_NCCL
+
+
+class DeviceTimeoutError(SiError, TimeoutError):
+    status = SI_ERR_TIMEOUT
+
+
+class NoDeviceError(SiError):
+    status = SI_ERR_NO_DEVICE
+
+
+_ERRORS = {c.status: c for c in (ArgumentError, NotSupportedError, InstructionAdaptationError, InvalidDataError,
+                                 CudaError, OutOfMemoryError, NcclError, DeviceTimeoutError, NoDeviceError)}
+
+_vp, _u64, _i64, _u32, _i32 = C.c_void_p, C.c_uint64, C.c_int64, C.c_uint32, C.c_int
+_pu64, _pu32 = C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)
+
+# name -> argtypes (restype is si_status unless listed in _RESTYPE)
+SIGNATURES = {
+    "si_abi_version": [],
+    "si_last_error": [C.c_char_p, C.c_size_t],
+    "si_device_count": [C.POINTER(C.c_int)],
+    "si_tensor_byte_length": [_u32, _pu64, _i32, _pu64],
+    "si_row_bytes": [_u32, _i64, _pu64],
+    "si_quantize": [_u32, _vp, _i64, _vp],
+    "si_dequantize": [_u32, _vp, _i64, _vp],
+    "si_synth_normal": [_u64, _u64, _i64, C.c_float, _vp, _i32],
+    "si_synth_weights": [_u32, _u64, _i64, _i64, C.c_float, _vp, _i32],
+    "si_matvec": [_u32, _vp, _u32, _vp, _u32, _vp, _i64, _i64, _u32, _vp],
+    "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "si_matrix_multiply_workspace_bytes": [_u32, _i64, _i64, _i64, _pu64],
+    "si_matrix_multiply": [_u32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u64, _vp],
+    "si_device_error_take": [_i32, _pu32],
+    "si_context_create": [_i32, C.POINTER(_vp)],
+    "si_context_destroy": [_vp],
+    "si_context_stream": [_vp, C.POINTER(_vp)],
+    "si_context_synchronize": [_vp],
+    "si_context_submission_count": [_vp, _pu64],
+    "si_buffer_create": [_vp, _u64, C.POINTER(_vp)],
+    "si_buffer_destroy": [_vp, _vp],
+    "si_buffer_device_pointer": [_vp, C.POINTER(_vp), _pu64],
+    "si_buffer_upload": [_vp, _vp, _u64, _vp, _u64],
+    "si_buffer_readback": [_vp, _vp, _u64, _vp, _u64],
+    "si_buffer_upload_async": [_vp, _vp, _u64, _vp, _u64],
+    "si_buffer_readback_async": [_vp, _vp, _u64, _vp, _u64],
+    "si_host_alloc_pinned": [_u64, C.POINTER(_vp)],
+    "si_host_free_pinned": [_vp],
+    "si_ctx_matvec": [_vp, _u32, _vp, _u64, _u32, _vp, _u64, _u32, _vp, _u64, _i64, _i64, _u32],
+    "si_ctx_batch_shared_matvec": [_vp, _u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _i64, _i64, _i64],
+    "si_ctx_matrix_multiply": [_vp, _u32, _vp, _u64, _vp, _u64, _vp, _u64, _i64, _i64, _i64],
+    "si_instruction_resolve": [C.c_char_p, C.c_char_p, C.POINTER(C.c_int)],
+    "si_instruction_validate": [_i32, _pu32, _i32, C.c_char_p],
+}
+_RESTYPE = {"si_abi_version": C.c_int}
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m sharpinference_b200.build` "
+                          "(there is no CPU fallback)")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPE.get(name, C.c_int)
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(2048)
+    lib.si_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != SI_OK:
+        raise _ERRORS.get(status, SiError)(last_error() or f"status {status}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib, name)(*args))
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    call("si_device_count", C.byref(n))
+    return n.value
+
+
+def row_bytes(wtype: int, cols: int) -> int:
+    b = C.c_uint64()
+    call("si_row_bytes", wtype, cols, C.byref(b))
+    return b.value
+
+
+def tensor_byte_length(wtype: int, dims) -> int:
+    arr = (C.c_uint64 * len(dims))(*dims)
+    b = C.c_uint64()
+    call("si_tensor_byte_length", wtype, arr, len(dims), C.byref(b))
+    return b.value
+
+
+def device_error_take(device: int = 0) -> int:
+    v = C.c_uint32()
+    call("si_device_error_take", device, C.byref(v))
+    return v.value
+
+
+# ---- numpy helpers (host codecs) -------------------------------------------------
+def _np():
+    import numpy as np
+    return np
+
+
+def synth_normal(seed: int, count: int, sigma: float = 1.0, offset: int = 0, threads: int = 0):
+    np = _np()
+    out = np.empty(count, dtype=np.float32)
+    call("si_synth_normal", seed, offset, count, sigma, out.ctypes.data, threads)
+    return out
+
+
+def synth_weights(wtype: int, seed: int, rows: int, cols: int, sigma: float = 0.02, threads: int = 0):
+    np = _np()
+    out = np.empty(row_bytes(wtype, cols) * rows, dtype=np.uint8)
+    call("si_synth_weights", wtype, seed, rows, cols, sigma, out.ctypes.data, threads)
+    return out
+
+
+def quantize(wtype: int, values):
+    np = _np()
+    values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    out = np.empty(tensor_byte_length(wtype, [values.size]), dtype=np.uint8)
+    call("si_quantize", wtype, values.ctypes.data, values.size, out.ctypes.data)
+    return out
+
+
+def dequantize(wtype: int, blob, count: int):
+    np = _np()
+    blob = np.ascontiguousarray(blob).view(np.uint8)
+    out = np.empty(count, dtype=np.float32)
+    call("si_dequantize", wtype, blob.ctypes.data, count, out.ctypes.data)
+    return out
+
+
+# ---- executor ----------------------------------------------------------------------
+class Buffer:
+    """A device slot owned by a Context (D3D12VmResourcePool-style ownership)."""
+
+    def __init__(self, ctx: "Context", nbytes: int):
+        self.ctx = ctx
+        self.nbytes = nbytes
+        h = C.c_void_p()
+        call("si_buffer_create", ctx.handle, nbytes, C.byref(h))
+        self.handle = h
+        p, n = C.c_void_p(), C.c_uint64()
+        call("si_buffer_device_pointer", h, C.byref(p), C.byref(n))
+        self.device_pointer = p.value
+
+    def upload(self, data, offset: int = 0) -> None:
+        np = _np()
+        arr = np.ascontiguousarray(data)
+        call("si_buffer_upload", self.ctx.handle, self.handle, offset, arr.ctypes.data, arr.nbytes)
+
+    def readback(self, nbytes: int | None = None, offset: int = 0):
+        np = _np()
+        n = self.nbytes - offset if nbytes is None else nbytes
+        out = np.empty(n, dtype=np.uint8)
+        call("si_buffer_readback", self.ctx.handle, self.handle, offset, out.ctypes.data, n)
+        return out
+
+    def free(self) -> None:
+        if self.handle:
+            call("si_buffer_destroy", self.ctx.handle, self.handle)
+            self.handle = None
+
+
+class Context:
+    """Executor context: one device, one stream, serialised calls
+    (the native counterpart of D3D12VmExecutor)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        call("si_context_create", device, C.byref(h))
+        self.handle = h
+        self.device = device
+        s = C.c_void_p()
+        call("si_context_stream", h, C.byref(s))
+        self.stream = s.value
+
+    def buffer(self, nbytes: int) -> Buffer:
+        return Buffer(self, nbytes)
+
+    def synchronize(self) -> None:
+        call("si_context_synchronize", self.handle)
+
+    @property
+    def submission_count(self) -> int:
+        v = C.c_uint64()
+        call("si_context_submission_count", self.handle, C.byref(v))
+        return v.value
+
+    def matvec(self, wtype, weight: Buffer, input: Buffer, output: Buffer, rows, cols, *, weight_offset=0,
+               input_offset=0, output_offset=0, input_type=F32, output_type=F32, config=MATVEC_DEFAULT):
+        call("si_ctx_matvec", self.handle, wtype, weight.handle, weight_offset, input_type, input.handle,
+             input_offset, output_type, output.handle, output_offset, rows, cols, config)
+
+    def batch_shared_matvec(self, wtype, weight: Buffer, input: Buffer, control: Buffer, output: Buffer, batch,
+                            out_features, in_features, *, weight_offset=0, input_offset=0, control_offset=0,
+                            output_offset=0):
+        call("si_ctx_batch_shared_matvec", self.handle, wtype, weight.handle, weight_offset, input.handle,
+             input_offset, control.handle, control_offset, output.handle, output_offset, batch, out_features,
+             in_features)
+
+    def matrix_multiply(self, wtype, x: Buffer, weight: Buffer, y: Buffer, m, n, k, *, x_offset=0,
+                        weight_offset=0, y_offset=0):
+        call("si_ctx_matrix_multiply", self.handle, wtype, x.handle, x_offset, weight.handle, weight_offset,
+             y.handle, y_offset, m, n, k)
+
+    def close(self) -> None:
+        if self.handle:
+            call("si_context_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+# ---- instruction registry ----------------------------------------------------------
+TIER_ZERO_FLOAT32 = "00000000-0000-0000-0000-000000000000"
+TIER_ZERO_FLOAT16 = "00000000-0000-0000-0000-000000000001"
+TRANSFORMER_FLOAT32 = "824d0f9c-16c7-46d8-b49d-0f91d6a4ec83"
+
+
+def resolve(collection_id: str, name: str) -> int:
+    v = C.c_int()
+    call("si_instruction_resolve", collection_id.encode(), name.encode(), C.byref(v))
+    return v.value
+
+
+def validate(instruction_id: int, port_types, configuration: str = "") -> None:
+    arr = (C.c_uint32 * len(port_types))(*port_types)
+    call("si_instruction_validate", instruction_id, arr, len(port_types), configuration.encode())
+
+
+def header_functions(header: Path | None = None) -> list[str]:
+    """Function names declared in include/sharpinfer_cuda.h."""
+    import re
+    header = header or _HERE.parent / "include" / "sharpinfer_cuda.h"
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(si_[a-z0-9_]+)\s*\(", text)))
+
