@@ -266,7 +266,8 @@ si_status si_matrix_multiply(uint32_t weight_type, const float *x, const void *w
 si_status si_device_error_take(int device, uint32_t *code) {
     if (!code) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
     *code = 0;
-    return kernels::take_error_gemv(device, code);
+    if (si_status st = kernels::take_error_gemv(device, code)) return st;
+    return kernels::take_error_gemm(device, code);
 }
 
 // ---- executor ----------------------------------------------------------------

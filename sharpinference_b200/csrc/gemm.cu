@@ -1,20 +1,425 @@
-// core.matrix-multiply (transpose_right) dispatch: Y[m,n] = X[m,k] W[n,k]^T.
+// core.matrix-multiply with transpose_right (Y[m,n] = sum_k X[m,k] W[n,k],
+// CpuInstructionNumerics.cs:61-82) on the sm_100a tensor cores.
+//
+// Precision: the parity gate is relative L2 <= 1e-4 against FP32, which a
+// single BF16 pass cannot meet (2^-9 operand rounding). Both operands are
+// split into BF16 pairs, v = hi + lo with hi = bf16(v), lo = bf16(v - hi),
+// and three products are accumulated in FP32 in tensor memory:
+//   X W ~= Xhi Whi + Xlo Whi + Xhi Wlo       (dropped term ~2^-18 relative)
+//
+// Kernel structure (one CTA = 128 weight rows x 256 input rows, K in 64-wide
+// stages, two-stage ring in shared memory):
+//   warp 0      TMA: X_hi / X_lo tiles (2-D tensor maps, 128-byte swizzle,
+//               no multicast) into the stage, completion as tx bytes
+//   warp 1      allocates 256 TMEM columns; one thread issues
+//               tcgen05.mma (M=128, N=256, K=16, BF16 -> FP32) x 3 products,
+//               then tcgen05.commit frees the stage
+//   warps 2..5  dequantise this stage's 128x64 weight block (GGUF Q8_0 /
+//               Q4_K / F16 / F32) in registers, split hi/lo and store both in
+//               the canonical K-major 128B-swizzled layout; after the last
+//               stage they drain the accumulator (tcgen05.ld) to Y
+// Every mbarrier wait is bounded; a wait that runs out sets the device error
+// word and the kernel still runs to completion (no trap, no hang).
+#include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
+#include "device_common.cuh"
 #include "si_internal.h"
 
+namespace si::dev {
+namespace {
+
+constexpr int kBM = 128;                         // weight rows per CTA (MMA M)
+constexpr int kBN = 256;                         // input rows per CTA (MMA N)
+constexpr int kBK = 64;                          // K per stage (128 B of BF16)
+constexpr int kStages = 2;
+constexpr int kThreads = 192;                    // 6 warps
+constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB (one of hi / lo)
+constexpr uint32_t kBTile = kBN * kBK * 2;       // 32 KB
+constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;  // 96 KB
+constexpr uint32_t kTmemCols = 256;
+
+// Instruction descriptor, kind::f16: D F32, A/B BF16, both K-major,
+// N = 256 (bits 17-22: N>>3), M = 128 (bits 24-28: M>>4).
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
+                            (uint32_t(kBM >> 4) << 24);
+
+// Shared-memory matrix descriptor for a K-major tile in the canonical
+// 128-byte swizzled layout: rows of 128 B, 8-row groups 1024 B apart
+// (stride byte offset), leading byte offset 16 B, version 1, swizzle 128B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float h16(uint32_t bits) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xffffu)));
+}
+
+// 64 consecutive weights of one row, columns k0 .. k0+63 (k0 % 64 == 0).
+template <int FMT>
+__device__ __forceinline__ void load_weights64(const uint8_t *row, int k0, float (&w)[64]) {
+    if constexpr (FMT == SI_TYPE_Q4_K) {
+        const uint8_t *sb = row + (k0 >> 8) * 144;
+        const int j = (k0 >> 6) & 3;
+        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(sb));
+        const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(sb + 16 + 32 * j));
+        const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(sb + 32 + 32 * j));
+        const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+        const uint32_t mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+        const uint32_t scw = j >= 2 ? sc_hi : sc_lo, mnw = j >= 2 ? mn_hi : mn_lo;
+        const int b0 = (2 * j) & 3;
+        const float d = h16(h.x), dmin = h16(h.x >> 16);
+        const float a0 = d * float((scw >> (8 * b0)) & 0xffu), a1 = d * float((scw >> (8 * b0 + 8)) & 0xffu);
+        const float c0 = dmin * float((mnw >> (8 * b0)) & 0xffu), c1 = dmin * float((mnw >> (8 * b0 + 8)) & 0xffu);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint32_t byte = (q[i] >> (8 * b)) & 0xffu;
+                w[4 * i + b] = a0 * float(byte & 15u) - c0;
+                w[32 + 4 * i + b] = a1 * float(byte >> 4) - c1;
+            }
+    } else if constexpr (FMT == SI_TYPE_Q8_0) {
+        const uint8_t *blk = row + (k0 >> 5) * 34;  // two blocks, 68 bytes, 4-byte aligned
+        const uint32_t *u = reinterpret_cast<const uint32_t *>(blk);
+        uint32_t wv[17];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) wv[i] = __ldg(u + i);
+        const float d0 = h16(wv[0]), d1 = h16(wv[8] >> 16);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const int b0 = 2 + e, b1 = 36 + e;
+            w[e] = d0 * float(int8_t((wv[b0 >> 2] >> (8 * (b0 & 3))) & 0xffu));
+            w[32 + e] = d1 * float(int8_t((wv[b1 >> 2] >> (8 * (b1 & 3))) & 0xffu));
+        }
+    } else if constexpr (FMT == SI_TYPE_F16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0) * 2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint4 v = __ldg(p + i);
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                w[8 * i + 2 * t] = h16(vv[t]);
+                w[8 * i + 2 * t + 1] = h16(vv[t] >> 16);
+            }
+        }
+    } else {
+        const float4 *p = reinterpret_cast<const float4 *>(row + size_t(k0) * 4);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float4 v = __ldg(p + i);
+            w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+struct GemmParams {
+    const uint8_t *w;
+    float *y;
+    uint64_t row_bytes;
+    int m, n, k;
+};
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                        const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-byte aligned tiles
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *accum = empty + kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kBM, t0 = blockIdx.y * kBN;
+    const int iters = p.k / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 128 + 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int it = 0; it < iters; ++it) {
+                const int s = it % kStages;
+                if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
+                uint8_t *st = smem + s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], 2 * kBTile);
+                tma_load_2d(st + 2 * kATile, &map_hi, it * kBK, t0, &full[s]);
+                tma_load_2d(st + 2 * kATile + kBTile, &map_lo, it * kBK, t0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int it = 0; it < iters; ++it) {
+                const int s = it % kStages;
+                mbar_wait(&full[s], (it / kStages) & 1, kErrFullBarrierTimeout);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t base = smem_u32(smem + s * kStageBytes);
+                const uint32_t a_hi = base, a_lo = base + kATile, b_hi = base + 2 * kATile,
+                               b_lo = base + 2 * kATile + kBTile;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint32_t off = kk * 32;  // 16 BF16 along K within the 128-byte row
+                    mma_bf16(tmem, smem_desc(a_hi + off), smem_desc(b_hi + off), (it | kk) != 0);
+                    mma_bf16(tmem, smem_desc(a_hi + off), smem_desc(b_lo + off), 1);
+                    mma_bf16(tmem, smem_desc(a_lo + off), smem_desc(b_hi + off), 1);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(accum);
+        }
+        __syncwarp();
+    } else {
+        // warps 2..5: weight producers, then epilogue.
+        const int r = threadIdx.x - 64;  // weight row within the tile, 0..127
+        const bool valid_row = n0 + r < p.n;
+        const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
+        for (int it = 0; it < iters; ++it) {
+            const int s = it % kStages;
+            float w[64];
+            if (valid_row) {
+                load_weights64<FMT>(wrow, it * kBK, w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) w[i] = 0.0f;
+            }
+            if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
+            uint8_t *st = smem + s * kStageBytes;
+            uint8_t *hi_row = st + (r >> 3) * 1024 + (r & 7) * 128;
+            uint8_t *lo_row = hi_row + kATile;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t hv[4], lv[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float v0 = w[8 * c + 2 * t], v1 = w[8 * c + 2 * t + 1];
+                    const uint32_t hb = pack_bf16(v0, v1);
+                    const float h0 = __uint_as_float(hb << 16), h1 = __uint_as_float(hb & 0xffff0000u);
+                    hv[t] = hb;
+                    lv[t] = pack_bf16(v0 - h0, v1 - h1);
+                }
+                const int pc = c ^ (r & 7);
+                *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
+            fence_proxy_async();
+            mbar_arrive(&full[s]);
+        }
+        // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32*(warp%4) ..
+        mbar_wait(accum, 0, kErrMmaBarrierTimeout);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int quarter = warp & 3;
+        const int row = n0 + quarter * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
+            if (row < p.n) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + c0 + j;
+                    if (t < p.m) p.y[size_t(t) * p.n + row] = __uint_as_float(v[j]);
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// X (fp32, [m,k]) -> X_hi, X_lo (bf16, [m,k]) with hi = bf16(x), lo = bf16(x - hi).
+__global__ void split_bf16_kernel(const float4 *__restrict__ x, uint2 *__restrict__ hi, uint2 *__restrict__ lo,
+                                  int64_t n4) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        const float4 v = x[i];
+        const uint32_t h01 = pack_bf16(v.x, v.y), h23 = pack_bf16(v.z, v.w);
+        const uint32_t l01 = pack_bf16(v.x - __uint_as_float(h01 << 16), v.y - __uint_as_float(h01 & 0xffff0000u));
+        const uint32_t l23 = pack_bf16(v.z - __uint_as_float(h23 << 16), v.w - __uint_as_float(h23 & 0xffff0000u));
+        hi[i] = make_uint2(h01, h23);
+        lo[i] = make_uint2(l01, l23);
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+si_status make_x_map(CUtensorMap *map, void *base, int m, int k) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
+    const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+    const cuuint32_t box[2] = {kBK, kBN};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return SI_OK;
+}
+
+constexpr size_t kGemmSmem = size_t(kStages) * kStageBytes + 1024 + 256;
+
+bool tensor_core_shape(uint32_t wtype, int64_t m, int64_t n, int64_t k) {
+    if (m < 64 || k % kBK != 0 || k > (int64_t(1) << 30) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
+        return false;
+    return wtype == SI_TYPE_Q4_K || wtype == SI_TYPE_Q8_0 || wtype == SI_TYPE_F16 || wtype == SI_TYPE_F32;
+}
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+template <int FMT>
+si_status launch_gemm(const void *w, float *y, uint64_t rb, int m, int n, int k, const CUtensorMap &hi,
+                      const CUtensorMap &lo, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(gemm_tcgen05_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem));
+        attr = true;
+    }
+    GemmParams p{static_cast<const uint8_t *>(w), y, rb, m, n, k};
+    const dim3 grid(unsigned((n + kBM - 1) / kBM), unsigned((m + kBN - 1) / kBN));
+    gemm_tcgen05_kernel<FMT><<<grid, kThreads, kGemmSmem, st>>>(hi, lo, p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
+    return SI_OK;
+}
+
+}  // namespace
+}  // namespace si::dev
+
 namespace si::kernels {
+using namespace si::dev;
 
 si_status gemm_workspace_bytes(uint32_t wtype, int64_t m, int64_t n, int64_t k, uint64_t *bytes) {
-    (void)wtype, (void)m, (void)n, (void)k;
-    *bytes = 0;
+    *bytes = tensor_core_shape(wtype, m, n, k) ? 2 * align256(uint64_t(m) * uint64_t(k) * 2) : 0;
     return SI_OK;
 }
 
 si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64_t m, int64_t n, int64_t k,
                   void *workspace, uint64_t workspace_bytes, void *stream) {
-    (void)workspace, (void)workspace_bytes;
-    return shared_weight_matvec(wtype, w, x, nullptr, y, m, n, k, stream);
+    auto st = static_cast<cudaStream_t>(stream);
+    uint64_t need = 0;
+    gemm_workspace_bytes(wtype, m, n, k, &need);
+    const uint64_t rb_check = wtype == SI_TYPE_Q4_K ? 144 * (k / 256) : 0;
+    (void)rb_check;
+    if (!need || reinterpret_cast<uintptr_t>(w) % 16 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0)
+        return shared_weight_matvec(wtype, w, x, nullptr, y, m, n, k, stream);
+    uint64_t rb;
+    if (si_status s = byte_length(wtype, uint64_t(k), &rb)) return s;
+    if (rb % 16 != 0 && wtype != SI_TYPE_Q8_0) return shared_weight_matvec(wtype, w, x, nullptr, y, m, n, k, stream);
+    if (wtype == SI_TYPE_Q8_0 && rb % 4 != 0) return shared_weight_matvec(wtype, w, x, nullptr, y, m, n, k, stream);
+    if (workspace_bytes < need) return fail(SI_ERR_INVALID_ARGUMENT, "workspace too small");
+    auto *hi = static_cast<uint8_t *>(workspace);
+    auto *lo = hi + align256(uint64_t(m) * uint64_t(k) * 2);
+    const int64_t n4 = m * k / 4;
+    const int blocks = int(std::min<int64_t>((n4 + 255) / 256, 148 * 16));
+    split_bf16_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4 *>(x), reinterpret_cast<uint2 *>(hi),
+                                              reinterpret_cast<uint2 *>(lo), n4);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "split launch failed: %s", cudaGetErrorString(e));
+    CUtensorMap map_hi, map_lo;
+    if (si_status s = make_x_map(&map_hi, hi, int(m), int(k))) return s;
+    if (si_status s = make_x_map(&map_lo, lo, int(m), int(k))) return s;
+    switch (wtype) {
+    case SI_TYPE_Q4_K: return launch_gemm<SI_TYPE_Q4_K>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
+    case SI_TYPE_Q8_0: return launch_gemm<SI_TYPE_Q8_0>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
+    case SI_TYPE_F16: return launch_gemm<SI_TYPE_F16>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
+    default: return launch_gemm<SI_TYPE_F32>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
+    }
+}
+
+si_status take_error_gemm(int device, uint32_t *code) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return fail(SI_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    uint32_t v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_error_word, sizeof v);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof zero);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "device error word: %s", cudaGetErrorString(e));
+    *code |= v;
+    return SI_OK;
 }
 
 }  // namespace si::kernels

@@ -158,7 +158,8 @@ struct StagedParams {
     int units;           // G = K / 64
     int slots;           // S row slots; consumer threads = G * S
     int consumer_threads;  // G * S rounded up to whole warps
-    int rows_per_tile;   // RT <= rows held by one stage
+    int rows_per_tile;   // RT = S * (rows per slot), rows held by one stage
+    int segment;         // lanes per shuffle-reduction segment (power of two dividing G, <= 32)
     int stages;
     uint32_t row_bytes;
     uint32_t stage_bytes;  // RT * row_bytes rounded up to 128
@@ -237,44 +238,50 @@ __global__ void __launch_bounds__(kMaxStagedThreads, 1) gemv_staged_kernel(const
     qc.sel_byte0 = 0x7540u | uint32_t((2 * j) & 3);
     qc.sel_byte1 = 0x7540u | uint32_t(((2 * j) & 3) + 1);
 
+    // Lanes are grouped in segments of `seg` consecutive threads (a power of
+    // two dividing G, so a segment never straddles two row slots); each
+    // segment first reduces its units' partials with shuffles, then one lane
+    // per segment stores the segment sum.
+    const int seg = p.segment;
+    const int lane = tid & 31;
+    const int rt = p.rows_per_tile;
+    const int rows_per_slot = rt / p.slots;
+    const int nseg = p.units / seg;  // partials per row
+
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         const int s = it % p.stages;
-        const int r0 = tile * p.rows_per_tile;
-        const int nrows = min(p.rows_per_tile, p.rows - r0);
+        const int r0 = tile * rt;
+        const int nrows = min(rt, p.rows - r0);
         mbar_wait(&full[s], (it / p.stages) & 1, kErrFullBarrierTimeout);
         const uint8_t *tile_smem = stage_base + size_t(s) * p.stage_bytes;
-        float *part = partials + size_t(it & 1) * p.rows_per_tile * p.units;
-        if (active) {
-            for (int r = slot; r < nrows; r += p.slots) {
-                const uint8_t *row = tile_smem + size_t(r) * p.row_bytes;
-                float v;
-                if constexpr (FMT == SI_TYPE_Q4_K)
-                    v = q4k_unit(row + (g >> 2) * 144, j, qc, xv, sx_lo, sx_hi);
-                else
-                    v = q8_0_unit(row + g * 68, xv, c0, c1);
-                part[g * p.rows_per_tile + r] = v;
-            }
+        float *part = partials + size_t(it & 1) * rt * nseg;
+        // Uniform trip count in every consumer thread (shuffles below need
+        // the whole warp); rows past the tile end compute on stale shared
+        // memory inside the stage and are not stored.
+        for (int i = 0; i < rows_per_slot; ++i) {
+            const int r = active ? slot + i * p.slots : 0;
+            const uint8_t *row = tile_smem + size_t(r) * p.row_bytes;
+            float v;
+            if constexpr (FMT == SI_TYPE_Q4_K)
+                v = q4k_unit(row + (g >> 2) * 144, j, qc, xv, sx_lo, sx_hi);
+            else
+                v = q8_0_unit(row + g * 68, xv, c0, c1);
+            for (int off = seg >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (active && r < nrows && (lane & (seg - 1)) == 0) part[(g / seg) * rt + r] = v;
         }
         __syncwarp();
-        if ((tid & 31) == 0) mbar_arrive(&empty[s]);
-        // All partials of this tile are written.
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // All segment partials of this tile are written.
         asm volatile("bar.sync 1, %0;" ::"r"(p.consumer_threads) : "memory");
-        // Row r is summed by lane r / W of warp r % W (W consumer warps), so
-        // the reductions spread over all warps; partials are unit-major, so
-        // the lanes of a warp read consecutive banks.
-        {
-            const int r = (tid & 31) * consumer_warps + (tid >> 5);
-            if (r < nrows) {
-                const float *pr = part + r;
-                const int rt = p.rows_per_tile;
-                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                int u = 0;
-                for (; u + 4 <= p.units; u += 4)
-                    a0 += pr[u * rt], a1 += pr[(u + 1) * rt], a2 += pr[(u + 2) * rt], a3 += pr[(u + 3) * rt];
-                for (; u < p.units; ++u) a0 += pr[u * rt];
-                p.y[r0 + r] = (a0 + a1) + (a2 + a3);
-            }
+        // Warp w sums rows w, w + W, ...: lanes stride the row's segment
+        // partials, then a butterfly finishes the sum (fixed order, so the
+        // result is deterministic).
+        for (int r = tid >> 5; r < nrows; r += consumer_warps) {
+            float a = 0.0f;
+            for (int q = lane; q < nseg; q += 32) a += part[q * rt + r];
+            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (lane == 0) p.y[r0 + r] = a;
         }
     }
 }
@@ -385,7 +392,10 @@ bool plan_staged(uint32_t wtype, int64_t rows, int64_t cols, const void *w, Stag
     p.rows_per_tile = rt;
     p.stage_bytes = uint32_t((uint64_t(rt) * rb + 127) / 128 * 128);
     p.num_tiles = int((rows + rt - 1) / rt);
-    const size_t partial_bytes = size_t(2) * rt * p.units * sizeof(float);
+    int seg = 32;
+    while (p.units % seg) seg >>= 1;
+    p.segment = seg;
+    const size_t partial_bytes = size_t(2) * rt * (p.units / seg) * sizeof(float);
     const size_t budget = 220 * 1024;
     int stages = int((budget - partial_bytes - 256) / p.stage_bytes);
     stages = std::min(stages, 8);

@@ -60,4 +60,5 @@ si_status gemm_workspace_bytes(uint32_t wtype, int64_t m, int64_t n, int64_t k, 
 si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64_t m, int64_t n,
                   int64_t k, void *workspace, uint64_t workspace_bytes, void *stream);
 si_status take_error_gemv(int device, uint32_t *code);
+si_status take_error_gemm(int device, uint32_t *code);
 }  // namespace si::kernels

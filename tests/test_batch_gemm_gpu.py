@@ -69,8 +69,11 @@ def test_batch_shared_quant_parity_and_valid_mask(ctx, wtype, batch, valid):
 
 
 @pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K])
-@pytest.mark.parametrize("m,n,k", [(1, 64, 256), (33, 129, 512), (64, 1000, 768)])
+@pytest.mark.parametrize("m,n,k", [(1, 64, 256), (33, 129, 512), (64, 1000, 768), (300, 200, 256), (257, 128, 1024),
+                                   (64, 7, 256)])
 def test_matrix_multiply_parity(ctx, wtype, m, n, k):
+    """m >= 64 with k % 64 == 0 runs the tcgen05 kernel (tails in m, n and a
+    single K stage included); smaller m runs the SIMT kernel."""
     blob = native.synth_weights(wtype, m + n, n, k, 0.02)
     x = native.synth_normal(77, m * k, 1.0)
     X, W, Y = ctx.buffer(x.nbytes), ctx.buffer(blob.nbytes), ctx.buffer(m * n * 4)
