@@ -61,4 +61,6 @@ si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64
                   int64_t k, void *workspace, uint64_t workspace_bytes, void *stream);
 si_status take_error_gemv(int device, uint32_t *code);
 si_status take_error_gemm(int device, uint32_t *code);
+si_status take_error_gemv_mma(int device, uint32_t *code);
+si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream);
 }  // namespace si::kernels
