@@ -2,12 +2,22 @@
 mat-vec / matrix-multiply instructions.
 
 The product is the native library libsharpinfer_cuda.so (C ABI declared in
-include/sharpinfer_cuda.h); `native` is its ctypes binding. Importing the
-package requires the built library; there is no CPU fallback.
+include/sharpinfer_cuda.h); `native` is its ctypes binding. Using the
+package requires the built library and raises ImportError without it — there
+is no CPU fallback. `sharpinference_b200.build` (the in-tree build step) is
+importable before the library exists.
 """
-from . import native  # noqa: F401
-from .native import (F16, F32, I32, Q4_K, Q8_0, Context, Buffer, SiError, ArgumentError, NotSupportedError,  # noqa: F401
-                     InstructionAdaptationError, InvalidDataError, CudaError)
+from importlib import import_module
 
-__all__ = ["native", "Context", "Buffer", "F32", "F16", "Q8_0", "Q4_K", "I32", "SiError", "ArgumentError",
-           "NotSupportedError", "InstructionAdaptationError", "InvalidDataError", "CudaError"]
+_EXPORTS = ("Context", "Buffer", "F32", "F16", "Q8_0", "Q4_K", "I32", "SiError", "ArgumentError", "NotSupportedError",
+            "InstructionAdaptationError", "InvalidDataError", "CudaError")
+
+__all__ = ["native", *_EXPORTS]
+
+
+def __getattr__(name):
+    if name == "native":
+        return import_module(".native", __name__)
+    if name in _EXPORTS:
+        return getattr(import_module(".native", __name__), name)
+    raise AttributeError(name)
