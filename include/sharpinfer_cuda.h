@@ -127,6 +127,18 @@ si_status si_matrix_multiply(uint32_t weight_type, const float *x, const void *w
                              int64_t m, int64_t n, int64_t k,
                              void *workspace, uint64_t workspace_bytes, void *stream);
 
+/* Same operation, for callers that cannot allocate device memory: hosts
+ * whose own pool owns every device byte, and loops that must not hit
+ * cudaMalloc/cudaFree (they can synchronise the whole device). No counterpart
+ * in the reference. Allocates nothing: the scratch is a fixed 64 MiB array
+ * that every GPU loading this library holds until exit; calls needing more
+ * (4*m*k bytes on the tensor-core path) get SI_ERR_INVALID_ARGUMENT. The
+ * first call on a device looks the array up (cudaGetSymbolAddress), so make
+ * it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race, so serialise them. */
+si_status si_matrix_multiply_static_workspace(uint32_t weight_type, const float *x, const void *weight, float *y,
+                                              int64_t m, int64_t n, int64_t k, void *stream);
+
 /* Device error word written by bounded device-side waits (a timed-out
  * mbarrier wait sets it instead of trapping). Reading clears it. */
 si_status si_device_error_take(int device, uint32_t *code);

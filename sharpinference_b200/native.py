@@ -85,6 +85,7 @@ SIGNATURES = {
     "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "si_matrix_multiply_workspace_bytes": [_u32, _i64, _i64, _i64, _pu64],
     "si_matrix_multiply": [_u32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u64, _vp],
+    "si_matrix_multiply_static_workspace": [_u32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "si_device_error_take": [_i32, _pu32],
     "si_context_create": [_i32, C.POINTER(_vp)],
     "si_context_destroy": [_vp],
