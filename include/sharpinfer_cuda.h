@@ -89,6 +89,9 @@ si_status si_synth_normal(uint64_t seed, uint64_t offset, int64_t count, float s
  * as si_synth_normal followed by si_quantize). */
 si_status si_synth_weights(uint32_t type, uint64_t seed, int64_t rows, int64_t cols, float sigma,
                            void *dst, int threads);
+/* Rows [row_begin, row_begin + rows) of the same matrix (a row shard). */
+si_status si_synth_weight_rows(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows, int64_t cols,
+                               float sigma, void *dst, int threads);
 
 /* ---------------------------------------------------------------------- */
 /* Kernel entry points on caller-owned device memory                      */
@@ -144,6 +147,28 @@ si_status si_matrix_multiply_static_workspace(uint32_t weight_type, const float 
 si_status si_device_error_take(int device, uint32_t *code);
 
 /* ---------------------------------------------------------------------- */
+/* Multi-GPU row sharding (no counterpart in the reference, which runs on  */
+/* one device): rank r of n owns weight rows [r*per, min((r+1)*per, rows))  */
+/* with per = ceil(rows / n); the output slices are all-gathered.          */
+/* ---------------------------------------------------------------------- */
+typedef struct si_comm si_comm;
+si_status si_rowshard_plan(int64_t rows, int nranks, int rank, int64_t *row_begin, int64_t *row_count,
+                           int64_t *rows_per_rank);
+/* 128-byte NCCL unique id, created on one rank and shared with the others. */
+si_status si_comm_unique_id(uint8_t *id, size_t capacity);
+/* Joins the communicator; returns SI_ERR_TIMEOUT after `timeout_ms` when a
+ * rank never joins (the half-built communicator is aborted, nothing hangs). */
+si_status si_comm_create(int device, int nranks, int rank, const uint8_t *id, int timeout_ms, si_comm **out);
+si_status si_comm_destroy(si_comm *comm);
+/* GEMV of this rank's weight rows (weight_shard = its row_count rows) into
+ * output_full[rank*per ...], then an in-place all-gather so every rank holds
+ * output_full[0 .. n*per) (the first `rows` entries are y). Both run on
+ * `stream`; output_full must hold n*per floats. */
+si_status si_rowshard_matvec_allgather(si_comm *comm, uint32_t weight_type, const void *weight_shard,
+                                       const float *input, float *output_full, int64_t rows, int64_t cols,
+                                       void *stream);
+
+/* ---------------------------------------------------------------------- */
 /* Executor: device buffers per slot, uploads/readbacks and stream        */
 /* (D3D12VmExecutor.cs:283-361,452-482 Upload / Readback / Execute /     */
 /*  ExecuteWithTransfers / MeasureGpuMicroseconds; D3D12VmResourcePool).  */
@@ -194,6 +219,19 @@ si_status si_ctx_matrix_multiply(si_context *ctx, uint32_t weight_type,
                                  si_buffer *weight, uint64_t weight_offset,
                                  si_buffer *y, uint64_t y_offset,
                                  int64_t m, int64_t n, int64_t k);
+
+/* Recorded submissions: everything issued on the context stream between
+ * si_graph_begin and si_graph_end (async uploads/readbacks from pinned
+ * memory, instruction dispatches, row-shard collectives) is captured once
+ * and replayed by si_graph_launch -- the counterpart of the pre-recorded
+ * command list D3D12VmExecutor.ExecuteWithTransfers submits per call
+ * (D3D12VmExecutor.cs:298-361). Synchronous uploads/readbacks are not
+ * allowed while capturing. */
+typedef struct si_graph si_graph;
+si_status si_graph_begin(si_context *ctx);
+si_status si_graph_end(si_context *ctx, si_graph **out);
+si_status si_graph_launch(si_context *ctx, si_graph *graph);
+si_status si_graph_destroy(si_graph *graph);
 
 /* ---------------------------------------------------------------------- */
 /* Instruction registry (InstructionCollection.cs:146-218)                */

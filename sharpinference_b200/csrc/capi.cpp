@@ -21,6 +21,12 @@ struct si_context {
     std::mutex lock;  // executor calls are serialised (D3D12VmExecutor.cs:285,307,457)
 };
 
+struct si_graph {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    si_context *owner = nullptr;
+};
+
 struct si_buffer {
     void *ptr = nullptr;
     uint64_t bytes = 0;
@@ -470,6 +476,49 @@ si_status si_ctx_matrix_multiply(si_context *ctx, uint32_t weight_type, si_buffe
                                           n, k, ctx->workspace, ctx->workspace_bytes, ctx->stream);
     if (st == SI_OK) ++ctx->submissions;
     return st;
+}
+
+// ---- recorded submissions (CUDA graphs) ----------------------------------------
+si_status si_graph_begin(si_context *ctx) {
+    if (!ctx) return fail(SI_ERR_INVALID_ARGUMENT, "null context");
+    DeviceScope scope(ctx->device);
+    return cuda_status(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+}
+
+si_status si_graph_end(si_context *ctx, si_graph **out) {
+    if (!ctx || !out) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    DeviceScope scope(ctx->device);
+    cudaGraph_t g = nullptr;
+    if (si_status st = cuda_status(cudaStreamEndCapture(ctx->stream, &g), "cudaStreamEndCapture")) return st;
+    cudaGraphExec_t exec = nullptr;
+    if (si_status st = cuda_status(cudaGraphInstantiate(&exec, g, 0), "cudaGraphInstantiate")) {
+        cudaGraphDestroy(g);
+        return st;
+    }
+    auto *graph = new si_graph();
+    graph->graph = g;
+    graph->exec = exec;
+    graph->owner = ctx;
+    *out = graph;
+    return SI_OK;
+}
+
+si_status si_graph_launch(si_context *ctx, si_graph *graph) {
+    if (!ctx || !graph || graph->owner != ctx) return fail(SI_ERR_INVALID_ARGUMENT, "graph belongs to another context");
+    std::lock_guard<std::mutex> g(ctx->lock);
+    DeviceScope scope(ctx->device);
+    const si_status st = cuda_status(cudaGraphLaunch(graph->exec, ctx->stream), "cudaGraphLaunch");
+    if (st == SI_OK) ++ctx->submissions;
+    return st;
+}
+
+si_status si_graph_destroy(si_graph *graph) {
+    if (!graph) return SI_OK;
+    if (graph->exec) cudaGraphExecDestroy(graph->exec);
+    if (graph->graph) cudaGraphDestroy(graph->graph);
+    delete graph;
+    return SI_OK;
 }
 
 // ---- instruction registry ------------------------------------------------------

@@ -75,6 +75,15 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
         : "memory");
 }
 
+// Programmatic dependent launch. `pdl_trigger` lets the next kernel in the
+// stream start launching (its CTAs still wait for free SM resources);
+// `pdl_wait` blocks until every prerequisite grid has completed and its
+// memory is visible. Kernels read their activations and write their outputs
+// only after pdl_wait; read-only weights may be prefetched before it.
+// Both are no-ops when the kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float ldf(const float *p) { return *p; }
 __device__ __forceinline__ float ldf(const __half *p) { return __half2float(*p); }
 __device__ __forceinline__ void stf(float *p, float v) { *p = v; }

@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_mma_q4k_kernel(const MmaP
     float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C][RT]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
@@ -254,6 +255,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_mma_q4k_kernel(const MmaP
     }
     if (warp == C + 1) {
         // Reducer: fixed-order sum of the C per-warp partials of each row.
+        pdl_wait();  // y may still be read by the previous kernel
         int it = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
             const int b = it & 1;
@@ -277,6 +279,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_mma_q4k_kernel(const MmaP
     SbState st1;
     const int sb0 = warp, sb1 = warp + C;
     const bool has1 = SPW == 2 && sb1 < p.nsb;
+    pdl_wait();  // x is produced by the previous kernel
     load_superblock_x(p.x, sb0, lane, st0);
     if constexpr (SPW == 2) {
         if (has1) load_superblock_x(p.x, sb1, lane, st1);
@@ -344,12 +347,10 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, MmaParams &p, size_t &s
     p.row_bytes = uint32_t(144 * nsb);
     // Row stride / 16 odd: ldmatrix's 8 row addresses hit 8 distinct bank quads.
     p.row_stride = p.row_bytes + ((nsb % 2 == 0) ? 16u : 32u);
-    const int sms = num_sms();
     const size_t budget = 220 * 1024;
-    // Tile: 48, 32 or 16 rows; the largest that keeps a ring of at least four
-    // stages and gives every SM at least two tiles.
-    int rt = 48;
-    while (rt > 16 && ((rows + rt - 1) / rt < 2 * sms || size_t(rt) * p.row_stride * 4 > budget)) rt -= 16;
+    // Tile: 32 rows when the ring still holds three stages (measured best
+    // across the Phi-4-mini shapes at K = 3072), else 16.
+    const int rt = size_t(32) * p.row_stride * 3 <= budget ? 32 : 16;
     p.rows_per_tile = rt;
     p.stage_bytes = uint32_t((uint64_t(rt) * p.row_stride + 127) / 128 * 128);
     p.num_tiles = int((rows + rt - 1) / rt);
@@ -384,13 +385,21 @@ si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, 
         cudaFuncSetAttribute(gemv_mma_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr = true;
     }
-    const int grid = std::min(p.num_tiles, num_sms());
-    const int threads = (p.compute_warps + 2) * 32;
-    if (p.spw == 2)
-        gemv_mma_q4k_kernel<2><<<grid, threads, smem, static_cast<cudaStream_t>(stream)>>>(p);
-    else
-        gemv_mma_q4k_kernel<1><<<grid, threads, smem, static_cast<cudaStream_t>(stream)>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(std::min(p.num_tiles, num_sms())));
+    cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    // The weight stream starts before the dependency wait: weights are
+    // read-only parameters, never produced by the preceding kernel.
+    cudaLaunchAttribute attr_pdl{};
+    attr_pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr_pdl.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr_pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t le = p.spw == 2 ? cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel<2>, p)
+                                      : cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel<1>, p);
+    const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
     if (e != cudaSuccess) return fail(SI_ERR_CUDA, "tensor-core Q4_K GEMV launch failed: %s", cudaGetErrorString(e));
     return SI_OK;
 }

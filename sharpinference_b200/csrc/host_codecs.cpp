@@ -295,14 +295,20 @@ si_status si_synth_normal(uint64_t seed, uint64_t offset, int64_t count, float s
 
 si_status si_synth_weights(uint32_t type, uint64_t seed, int64_t rows, int64_t cols, float sigma,
                            void *dst, int threads) {
-    if (!dst || rows <= 0 || cols <= 0) return fail(SI_ERR_INVALID_ARGUMENT, "invalid shape");
+    return si_synth_weight_rows(type, seed, 0, rows, cols, sigma, dst, threads);
+}
+
+si_status si_synth_weight_rows(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows, int64_t cols,
+                               float sigma, void *dst, int threads) {
+    if (!dst || rows <= 0 || cols <= 0 || row_begin < 0) return fail(SI_ERR_INVALID_ARGUMENT, "invalid shape");
     uint64_t rb;
     if (si_status st = byte_length(type, uint64_t(cols), &rb)) return st;
     auto *o = static_cast<uint8_t *>(dst);
     parallel_for(rows, threads, [&](int64_t r0, int64_t r1) {
         std::vector<float> row(static_cast<size_t>(cols));
         for (int64_t r = r0; r < r1; ++r) {
-            for (int64_t c = 0; c < cols; ++c) row[size_t(c)] = normal_at(seed, uint64_t(r * cols + c), sigma);
+            for (int64_t c = 0; c < cols; ++c)
+                row[size_t(c)] = normal_at(seed, uint64_t((row_begin + r) * cols + c), sigma);
             uint8_t *dr = o + uint64_t(r) * rb;
             if (type == SI_TYPE_F32) std::memcpy(dr, row.data(), rb);
             else if (type == SI_TYPE_F16) for (int64_t c = 0; c < cols; ++c) put16(dr + 2 * c, float_to_half(row[size_t(c)]));

@@ -81,6 +81,7 @@ SIGNATURES = {
     "si_dequantize": [_u32, _vp, _i64, _vp],
     "si_synth_normal": [_u64, _u64, _i64, C.c_float, _vp, _i32],
     "si_synth_weights": [_u32, _u64, _i64, _i64, C.c_float, _vp, _i32],
+    "si_synth_weight_rows": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _i32],
     "si_matvec": [_u32, _vp, _u32, _vp, _u32, _vp, _i64, _i64, _u32, _vp],
     "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "si_matrix_multiply_workspace_bytes": [_u32, _i64, _i64, _i64, _pu64],
@@ -104,6 +105,15 @@ SIGNATURES = {
     "si_ctx_matvec": [_vp, _u32, _vp, _u64, _u32, _vp, _u64, _u32, _vp, _u64, _i64, _i64, _u32],
     "si_ctx_batch_shared_matvec": [_vp, _u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _i64, _i64, _i64],
     "si_ctx_matrix_multiply": [_vp, _u32, _vp, _u64, _vp, _u64, _vp, _u64, _i64, _i64, _i64],
+    "si_rowshard_plan": [_i64, _i32, _i32, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)],
+    "si_comm_unique_id": [_vp, C.c_size_t],
+    "si_comm_create": [_i32, _i32, _i32, _vp, _i32, C.POINTER(_vp)],
+    "si_comm_destroy": [_vp],
+    "si_rowshard_matvec_allgather": [_vp, _u32, _vp, _vp, _vp, _i64, _i64, _vp],
+    "si_graph_begin": [_vp],
+    "si_graph_end": [_vp, C.POINTER(_vp)],
+    "si_graph_launch": [_vp, _vp],
+    "si_graph_destroy": [_vp],
     "si_instruction_resolve": [C.c_char_p, C.c_char_p, C.POINTER(C.c_int)],
     "si_instruction_validate": [_i32, _pu32, _i32, C.c_char_p],
 }
@@ -159,6 +169,38 @@ def tensor_byte_length(wtype: int, dims) -> int:
     return b.value
 
 
+def rowshard_plan(rows: int, nranks: int, rank: int) -> tuple[int, int, int]:
+    """(row_begin, row_count, rows_per_rank) of `rank` for a row-sharded weight."""
+    b, c, p = C.c_int64(), C.c_int64(), C.c_int64()
+    call("si_rowshard_plan", rows, nranks, rank, C.byref(b), C.byref(c), C.byref(p))
+    return b.value, c.value, p.value
+
+
+def comm_unique_id() -> bytes:
+    buf = (C.c_uint8 * 128)()
+    call("si_comm_unique_id", buf, 128)
+    return bytes(buf)
+
+
+class Comm:
+    """NCCL communicator for row-sharded mat-vec (one rank per GPU)."""
+
+    def __init__(self, device: int, nranks: int, rank: int, uid: bytes, timeout_ms: int = 60000):
+        arr = (C.c_uint8 * 128).from_buffer_copy(uid)
+        h = C.c_void_p()
+        call("si_comm_create", device, nranks, rank, arr, timeout_ms, C.byref(h))
+        self.handle, self.nranks, self.rank = h, nranks, rank
+
+    def rowshard_matvec_allgather(self, wtype, weight_shard_ptr, x_ptr, y_full_ptr, rows, cols, stream):
+        call("si_rowshard_matvec_allgather", self.handle, wtype, weight_shard_ptr, x_ptr, y_full_ptr, rows, cols,
+             C.c_void_p(stream))
+
+    def close(self):
+        if self.handle:
+            call("si_comm_destroy", self.handle)
+            self.handle = None
+
+
 def device_error_take(device: int = 0) -> int:
     v = C.c_uint32()
     call("si_device_error_take", device, C.byref(v))
@@ -182,6 +224,14 @@ def synth_weights(wtype: int, seed: int, rows: int, cols: int, sigma: float = 0.
     np = _np()
     out = np.empty(row_bytes(wtype, cols) * rows, dtype=np.uint8)
     call("si_synth_weights", wtype, seed, rows, cols, sigma, out.ctypes.data, threads)
+    return out
+
+
+def synth_weight_rows(wtype: int, seed: int, row_begin: int, rows: int, cols: int, sigma: float = 0.02,
+                      threads: int = 0):
+    np = _np()
+    out = np.empty(row_bytes(wtype, cols) * rows, dtype=np.uint8)
+    call("si_synth_weight_rows", wtype, seed, row_begin, rows, cols, sigma, out.ctypes.data, threads)
     return out
 
 
@@ -233,6 +283,21 @@ class Buffer:
             self.handle = None
 
 
+class Graph:
+    """A recorded submission replayed with one launch."""
+
+    def __init__(self, ctx: "Context", handle):
+        self.ctx, self.handle = ctx, handle
+
+    def launch(self) -> None:
+        call("si_graph_launch", self.ctx.handle, self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            call("si_graph_destroy", self.handle)
+            self.handle = None
+
+
 class Context:
     """Executor context: one device, one stream, serialised calls
     (the native counterpart of D3D12VmExecutor)."""
@@ -251,6 +316,17 @@ class Context:
 
     def synchronize(self) -> None:
         call("si_context_synchronize", self.handle)
+
+    def record(self, fn) -> "Graph":
+        """Captures everything `fn` issues on the context stream into a graph."""
+        call("si_graph_begin", self.handle)
+        try:
+            fn()
+        finally:
+            h = C.c_void_p()
+            st = lib.si_graph_end(self.handle, C.byref(h))
+        check(st)
+        return Graph(self, h)
 
     @property
     def submission_count(self) -> int:

@@ -200,3 +200,79 @@ def test_full_size_linearity_and_zero(ctx, wtype):
     combo = 2.0 * ys[0].astype(np.float64) - 0.5 * ys[1]
     d = ys[2] - combo
     assert np.linalg.norm(d) / np.linalg.norm(combo) <= 1e-4
+
+
+def test_chained_gemvs_and_async_uploads_keep_stream_order(ctx):
+    """Launch ordering of the decode GEMV (launched with programmatic
+    dependent launch): (1) an asynchronous upload of x followed by the GEMV
+    must see the new x; (2) a GEMV whose input is the previous GEMV's output
+    must see that output; (3) a GEMV that overwrites the previous GEMV's
+    input must not race with it."""
+    import ctypes as C
+    k, n1, n2 = 3072, 3072, 3072
+    w1 = native.synth_weights(N.Q4_K, 41, n1, k, 0.02)
+    w2 = native.synth_weights(N.Q4_K, 42, n2, n1, 0.02)
+    W1, W2 = ctx.buffer(w1.nbytes), ctx.buffer(w2.nbytes)
+    X, H, Y = ctx.buffer(k * 4), ctx.buffer(n1 * 4), ctx.buffer(n2 * 4)
+    px = C.c_void_p()
+    native.call("si_host_alloc_pinned", k * 4, C.byref(px))
+    try:
+        W1.upload(w1), W2.upload(w2)
+        host = np.ctypeslib.as_array(C.cast(px, C.POINTER(C.c_float)), shape=(k,))
+        for step in range(4):
+            x = native.synth_normal(900 + step, k, 1.0)
+            host[:] = x
+            native.call("si_buffer_upload_async", ctx.handle, X.handle, 0, px, k * 4)
+            ctx.matvec(N.Q4_K, W1, X, H, n1, k)     # H = W1 x
+            ctx.matvec(N.Q4_K, W2, H, Y, n2, n1)    # Y = W2 H   (reads the previous output)
+            ctx.matvec(N.Q4_K, W1, X, H, n1, k)     # rewrites H while nothing may still read it
+            y = Y.readback().view(np.float32)
+            h = H.readback().view(np.float32)
+            h_ref = oracle.matvec_f64(N.Q4_K, w1, x, n1, k)
+            y_ref = oracle.matvec_f64(N.Q4_K, w2, h.astype(np.float32), n2, n1)
+            assert np.linalg.norm(h - h_ref) / np.linalg.norm(h_ref) <= 1e-4, step
+            assert np.linalg.norm(y - y_ref) / np.linalg.norm(y_ref) <= 1e-4, step
+    finally:
+        native.call("si_host_free_pinned", px)
+        for b in (W1, W2, X, H, Y):
+            b.free()
+
+
+def test_recorded_submission_replays_with_new_pinned_inputs(ctx):
+    """si_graph_*: upload (async, pinned) -> GEMV -> readback recorded once,
+    replayed with new host inputs (ExecuteWithTransfers analog)."""
+    import ctypes as C
+    rows, cols = 3072, 3072
+    blob = native.synth_weights(N.Q4_K, 51, rows, cols, 0.02)
+    W, X, Y = ctx.buffer(blob.nbytes), ctx.buffer(cols * 4), ctx.buffer(rows * 4)
+    px, py = C.c_void_p(), C.c_void_p()
+    native.call("si_host_alloc_pinned", cols * 4, C.byref(px))
+    native.call("si_host_alloc_pinned", rows * 4, C.byref(py))
+    try:
+        W.upload(blob)
+        hx = np.ctypeslib.as_array(C.cast(px, C.POINTER(C.c_float)), shape=(cols,))
+        hy = np.ctypeslib.as_array(C.cast(py, C.POINTER(C.c_float)), shape=(rows,))
+
+        def issue():
+            native.call("si_buffer_upload_async", ctx.handle, X.handle, 0, px, cols * 4)
+            ctx.matvec(N.Q4_K, W, X, Y, rows, cols)
+            native.call("si_buffer_readback_async", ctx.handle, Y.handle, 0, py, rows * 4)
+
+        before = ctx.submission_count
+        g = ctx.record(issue)
+        try:
+            for step in range(3):
+                x = native.synth_normal(700 + step, cols, 1.0)
+                hx[:] = x
+                g.launch()
+                ctx.synchronize()
+                ref = oracle.matvec_f64(N.Q4_K, blob, x, rows, cols)
+                assert np.linalg.norm(hy - ref) / np.linalg.norm(ref) <= 1e-4
+            assert ctx.submission_count == before + 1 + 3  # the recorded dispatch + 3 replays
+        finally:
+            g.close()
+    finally:
+        native.call("si_host_free_pinned", px)
+        native.call("si_host_free_pinned", py)
+        for b in (W, X, Y):
+            b.free()
