@@ -151,7 +151,7 @@ def cpu_baseline_sample(budget_s: float = 10.0) -> dict:
     threads = oracle.online_cores()
     cpu_reference_sweep(SHAPES, weights, xs, threads)  # warm
     reps, spent = 0, 0.0
-    while spent < budget_s and reps < 200:
+    while spent < budget_s and reps < 5000:
         spent += cpu_reference_sweep(SHAPES, weights, xs, threads)
         reps += 1
     return {"value": round(step_bytes(SHAPES) * reps / spent / 1e9, 3), "unit": "GB/s", "cores": threads,

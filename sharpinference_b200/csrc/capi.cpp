@@ -401,7 +401,7 @@ si_status si_ctx_matvec(si_context *ctx, uint32_t weight_type, si_buffer *weight
         return fail(SI_ERR_INVALID_ARGUMENT, "Mixed matvec requires [rows,columns] x [columns] -> [rows].");
     uint64_t rb;
     if (si_status st = byte_length(weight_type, uint64_t(cols), &rb)) return st;
-    void *w, *x, *y;
+    void *w = nullptr, *x = nullptr, *y = nullptr;
     if (si_status st = buffer_range(ctx, weight, weight_offset, rb * uint64_t(rows), "weight", &w)) return st;
     if (si_status st = buffer_range(ctx, input, input_offset, uint64_t(cols) * elem_size(input_type), "input", &x))
         return st;
@@ -427,7 +427,7 @@ si_status si_ctx_batch_shared_matvec(si_context *ctx, uint32_t weight_type, si_b
         return fail(SI_ERR_ADAPTATION, "transformer.batch-shared-matvec: weight must be F16, Q8_0 or Q4_K.");
     uint64_t rb;
     if (si_status st = byte_length(weight_type, uint64_t(in_features), &rb)) return st;
-    void *w, *x, *c, *y;
+    void *w = nullptr, *x = nullptr, *c = nullptr, *y = nullptr;
     if (si_status st = buffer_range(ctx, weight, weight_offset, rb * uint64_t(out_features), "weight", &w)) return st;
     if (si_status st = buffer_range(ctx, input, input_offset, uint64_t(batch) * in_features * 4, "input", &x)) return st;
     if (si_status st = buffer_range(ctx, control, control_offset, 8, "control", &c)) return st;
@@ -453,7 +453,7 @@ si_status si_ctx_matrix_multiply(si_context *ctx, uint32_t weight_type, si_buffe
     if (m <= 0 || n <= 0 || k <= 0) return fail(SI_ERR_INVALID_ARGUMENT, "Incompatible matrix multiplication dimensions.");
     uint64_t rb;
     if (si_status st = byte_length(weight_type, uint64_t(k), &rb)) return st;
-    void *px, *pw, *py;
+    void *px = nullptr, *pw = nullptr, *py = nullptr;
     if (si_status st = buffer_range(ctx, x, x_offset, uint64_t(m) * k * 4, "left", &px)) return st;
     if (si_status st = buffer_range(ctx, weight, weight_offset, rb * uint64_t(n), "right", &pw)) return st;
     if (si_status st = buffer_range(ctx, y, y_offset, uint64_t(m) * n * 4, "output", &py)) return st;

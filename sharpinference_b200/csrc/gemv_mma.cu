@@ -28,6 +28,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 
 #include "device_common.cuh"
 #include "si_internal.h"
@@ -36,23 +38,58 @@ namespace si::dev {
 namespace {
 
 constexpr int kMaxComputeWarps = 16;
-constexpr int kMaxThreads = (kMaxComputeWarps + 2) * 32;  // + producer + reducer
 
 struct MmaParams {
     const uint8_t *w;
     const float *x;
     float *y;
     int rows;
-    int nsb;             // superblocks per row (K / 256)
-    int compute_warps;   // C
-    int spw;             // superblocks per compute warp (1 or 2)
-    int rows_per_tile;   // multiple of 16
+    int nsb;              // superblocks per row (K / 256)
+    int cluster;          // CTAs per cluster = K split (1, 2 or 4)
+    int nsb_cta;          // superblocks of every row one CTA covers (nsb / cluster)
+    int compute_warps;    // C
+    int spw;              // superblocks per compute warp (1 or 2)
     int stages;
-    uint32_t row_bytes;  // 144 * nsb
-    uint32_t row_stride; // padded shared-memory row stride
+    uint32_t row_bytes;   // 144 * nsb, the global row pitch
+    uint32_t cta_bytes;   // 144 * nsb_cta, bytes of each row one CTA loads
+    uint32_t row_stride;  // padded shared-memory row stride
     uint32_t stage_bytes;
     int num_tiles;
+    int groups;           // clusters (or CTAs when cluster == 1) in the grid
+    int max_local_tiles;  // ceil(num_tiles / groups): row-sum slots per CTA when cluster > 1
 };
+
+// --- thread-block cluster helpers (distributed shared memory) ---
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+// Every thread of every CTA of the cluster (hardware barrier).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -62,7 +99,10 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
+    // Not volatile: a pure register operation, so the compiler may interleave
+    // independent accumulator chains (the ldmatrix loads stay volatile and
+    // therefore ordered after the stage's mbarrier wait).
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -79,8 +119,19 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__device__ __forceinline__ float h2f_bits(uint32_t bits) {
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xffffu)));
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&bits));
+}
+
+// Two 6-bit integers v0, v1 in bits 0-5 / 16-21, OR-ed with kU6Bias (the
+// FP16 pattern of 1024 in each half), read as FP16 are 1024 + v exactly;
+// subtracting 1024 leaves v0, v1 (exact) and the pair widens to floats. The
+// bias is folded into the preceding mask, so no integer conversions are needed.
+constexpr uint32_t kU6Bias = 0x64006400u;
+__device__ __forceinline__ float2 u6pair(uint32_t biased) {
+    const uint32_t k1024 = kU6Bias;
+    const __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&biased), *reinterpret_cast<const __half2 *>(&k1024));
+    return __half22float2(v);
 }
 
 // Per-superblock state of a compute warp (B fragments stay in registers).
@@ -170,7 +221,9 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t qs_addr, const uint
     // group offset (m >> 1) (+ 2 per call).
     const int m = lane >> 3;
     const uint32_t base = qs_addr + uint32_t(((m & 1) * 8 + (lane & 7))) * row_stride + uint32_t(m >> 1) * 16;
-    float d1[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    // Four accumulator chains (one per ldmatrix group q), summed pairwise in
+    // the epilogue: shorter dependent MMA chains.
+    float dq[4][4] = {};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         uint32_t w0, w8, v0, v8;  // rows g / g+8 of groups 2q and 2q+1
@@ -181,7 +234,7 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t qs_addr, const uint
             const int gamma = 2 * q + k;
             const uint32_t a = gw[k][0], b = gw[k][1];
             const uint32_t as = a >> 8, bs = b >> 8;
-            float(&acc)[4] = gamma < 4 ? d1 : d2;
+            float(&acc)[4] = dq[q];
             // low nibbles: sub-block 2j
             mma16816(acc, codes(a, 0x000F000Fu), codes(b, 0x000F000Fu), codes(as, 0x000F000Fu),
                      codes(bs, 0x000F000Fu), st.b[2 * gamma][0], st.b[2 * gamma][1]);
@@ -190,38 +243,67 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t qs_addr, const uint
                      codes(bs, 0x00F000F0u), st.b[2 * gamma + 1][0], st.b[2 * gamma + 1][1]);
         }
     }
+    float d1[4], d2[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d1[i] = dq[0][i] + dq[1][i], d2[i] = dq[2][i] + dq[3][i];
     // Epilogue: lane (g,t) holds sub-blocks t (d1) and t+4 (d2), columns
-    // (x_hi, x_lo) for rows g (c0,c1) and g+8 (c2,c3).
+    // (x_hi, x_lo) for rows g (c0,c1) and g+8 (c2,c3). The 6-bit scales and
+    // mins of both rows are unpacked together: byte t of the row-g and
+    // row-(g+8) words goes to bits 0-7 / 16-23 (one byte permute each).
     const uint4 hg = *reinterpret_cast<const uint4 *>(hdr_g);
     const uint4 hg8 = *reinterpret_cast<const uint4 *>(hdr_g8);
-    const uint32_t sh = 8u * uint32_t(t);
+    const uint32_t sel = uint32_t(t) | (uint32_t(t + 4) << 8);
+    const uint32_t X = __byte_perm(hg.y, hg8.y, sel);  // scale bytes: low 6 bits sub-block t, top 2 of t+4
+    const uint32_t Y = __byte_perm(hg.z, hg8.z, sel);  // min bytes: low 6 bits sub-block t, top 2 of t+4
+    const uint32_t Z = __byte_perm(hg.w, hg8.w, sel);  // low nibble: scale t+4, high nibble: min t+4
+    const float2 sc_lo = u6pair((X & 0x003F003Fu) | kU6Bias);
+    const float2 mn_lo = u6pair((Y & 0x003F003Fu) | kU6Bias);
+    const float2 sc_hi = u6pair((Z & 0x000F000Fu) | ((X >> 2) & 0x00300030u) | kU6Bias);
+    const float2 mn_hi = u6pair(((Z >> 4) & 0x000F000Fu) | ((Y >> 2) & 0x00300030u) | kU6Bias);
+    const float2 dm = half2_bits_to_float2(hg.x);   // (d, dmin) of row g
+    const float2 dm8 = half2_bits_to_float2(hg8.x);  // (d, dmin) of row g+8
     float out[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const uint4 h = r ? hg8 : hg;
-        const uint32_t b0 = (h.y >> sh) & 0xffu, b1 = (h.z >> sh) & 0xffu, b2 = (h.w >> sh) & 0xffu;
-        const float sc_lo = float(b0 & 63u), mn_lo = float(b1 & 63u);
-        const float sc_hi = float((b2 & 15u) | ((b0 >> 6) << 4)), mn_hi = float((b2 >> 4) | ((b1 >> 6) << 4));
-        const float d = h2f_bits(h.x), dmin = h2f_bits(h.x >> 16);
-        const float q_lo = d1[2 * r] + d1[2 * r + 1], q_hi = d2[2 * r] + d2[2 * r + 1];
-        const float main = (sc_lo * q_lo + sc_hi * q_hi) * st.inv_scale;
-        const float mins = mn_lo * st.sx_lo_t + mn_hi * st.sx_hi_t;
-        out[r] = d * main - dmin * mins;
+    {
+        const float main = (sc_lo.x * (d1[0] + d1[1]) + sc_hi.x * (d2[0] + d2[1])) * st.inv_scale;
+        const float mins = mn_lo.x * st.sx_lo_t + mn_hi.x * st.sx_hi_t;
+        out[0] = dm.x * main - dm.y * mins;
+    }
+    {
+        const float main = (sc_lo.y * (d1[2] + d1[3]) + sc_hi.y * (d2[2] + d2[3])) * st.inv_scale;
+        const float mins = mn_lo.y * st.sx_lo_t + mn_hi.y * st.sx_hi_t;
+        out[1] = dm8.x * main - dm8.y * mins;
     }
     return make_float2(out[0], out[1]);
 }
 
-template <int SPW>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_mma_q4k_kernel(const MmaParams p) {
+// Roles (warp index): 0..C-1 compute, C producer, C+1 reducer.
+//
+// K split: with cluster size CS > 1 the CS CTAs of a cluster share every row
+// tile; CTA rank k loads and multiplies superblocks [k*nsb/CS, (k+1)*nsb/CS)
+// of each row and keeps its per-row sums in its own shared memory. After the
+// last tile one cluster barrier makes them visible, and the cluster's rows
+// are finished split over its CTAs: y = rank 0 + rank 1 + ... (DSMEM loads,
+// fixed order, deterministic). Smaller per-CTA slices let more CTAs stream a
+// small matrix at once and leave room for the next kernel's CTAs on the SM.
+// MAXW bounds the compute warps of a launch: the register budget ptxas may
+// use follows from the warps per SM sub-partition ((MAXW + 2) / 4 rounded
+// up), so the 12-warp instantiation (K = 3072 slices) gets up to 128
+// registers a thread where the 16-warp one gets 96.
+template <int SPW, int RT, int MAXW>
+__global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const MmaParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int C = p.compute_warps, RT = p.rows_per_tile;
+    const int C = p.compute_warps, CS = p.cluster;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(p.stages) * p.stage_bytes);
     uint64_t *empty = full + p.stages;
-    uint64_t *pfull = empty + p.stages;  // [2]
-    uint64_t *pempty = pfull + 2;        // [2]
+    uint64_t *pfull = empty + p.stages;  // [2] compute warps -> reducer
+    uint64_t *pempty = pfull + 2;        // [2] reducer -> compute warps
     float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C][RT]
+    float *rowsum = part + size_t(2) * C * RT;             // [max_local_tiles][RT] when CS > 1
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t crank = CS > 1 ? cluster_ctarank() : 0u;
+    const int first_tile = CS > 1 ? int(cluster_id_x()) : int(blockIdx.x);
+    const int tile_step = CS > 1 ? int(cluster_count_x()) : int(gridDim.x);
     pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
@@ -237,88 +319,117 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_mma_q4k_kernel(const MmaP
     __syncthreads();
 
     if (warp == C) {
-        // Producer: one bulk copy per row into the padded stage rows.
-        int it = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-            const int s = it % p.stages;
-            if (it >= p.stages) mbar_wait(&empty[s], ((it / p.stages) - 1) & 1, kErrEmptyBarrierTimeout);
+        // Producer: one bulk copy per row (this CTA's K slice) into the padded stage rows.
+        const uint8_t *wsrc = p.w + size_t(crank) * p.cta_bytes;
+        int it = 0, s = 0;
+        uint32_t ring_phase = 0;
+        for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
+            if (it >= p.stages) mbar_wait(&empty[s], ring_phase ^ 1u, kErrEmptyBarrierTimeout);
             const int r0 = tile * RT;
             const int nrows = min(RT, p.rows - r0);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(nrows) * p.row_bytes);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(nrows) * p.cta_bytes);
             __syncwarp();
             uint8_t *dst = smem + size_t(s) * p.stage_bytes;
             for (int r = lane; r < nrows; r += 32)
-                bulk_copy_g2s(dst + size_t(r) * p.row_stride, p.w + size_t(r0 + r) * p.row_bytes, p.row_bytes,
+                bulk_copy_g2s(dst + size_t(r) * p.row_stride, wsrc + size_t(r0 + r) * p.row_bytes, p.cta_bytes,
                               &full[s]);
+            if (++s == p.stages) s = 0, ring_phase ^= 1u;
         }
-        return;
-    }
-    if (warp == C + 1) {
-        // Reducer: fixed-order sum of the C per-warp partials of each row.
-        pdl_wait();  // y may still be read by the previous kernel
+    } else if (warp == C + 1) {
+        // Reducer: fixed-order sum of the C per-warp partials of each row
+        // (RT <= 32: lane r owns row r of the tile).
+        if (CS == 1) pdl_wait();  // y may still be read by the previous kernel
         int it = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
             const int b = it & 1;
             mbar_wait(&pfull[b], (it >> 1) & 1, kErrEpilogueTimeout);
             const int r0 = tile * RT;
             const int nrows = min(RT, p.rows - r0);
             const float *pb = part + size_t(b) * C * RT;
-            for (int r = lane; r < nrows; r += 32) {
-                float a = 0.0f;
-                for (int c = 0; c < C; ++c) a += pb[c * RT + r];
-                p.y[r0 + r] = a;
+            float a = 0.0f;
+            if (lane < nrows)
+                for (int c = 0; c < C; ++c) a += pb[c * RT + lane];
+            if (CS == 1) {
+                if (lane < nrows) p.y[r0 + lane] = a;
+            } else if (lane < RT) {
+                rowsum[it * RT + lane] = a;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&pempty[b]);
         }
-        return;
-    }
+    } else {
+        // Compute warp `warp`: superblocks warp, warp + C (SPW == 2) of this CTA's slice.
+        SbState st0;
+        SbState st1;
+        const int sb0 = warp, sb1 = warp + C;
+        const bool has1 = SPW == 2 && sb1 < p.nsb_cta;
+        const int gsb = int(crank) * p.nsb_cta;
+        pdl_wait();  // x is produced by the previous kernel
+        load_superblock_x(p.x, gsb + sb0, lane, st0);
+        if constexpr (SPW == 2) {
+            if (has1) load_superblock_x(p.x, gsb + sb1, lane, st1);
+        }
 
-    // Compute warp `warp`: superblocks warp, warp + C (when spw == 2).
-    SbState st0;
-    SbState st1;
-    const int sb0 = warp, sb1 = warp + C;
-    const bool has1 = SPW == 2 && sb1 < p.nsb;
-    pdl_wait();  // x is produced by the previous kernel
-    load_superblock_x(p.x, sb0, lane, st0);
-    if constexpr (SPW == 2) {
-        if (has1) load_superblock_x(p.x, sb1, lane, st1);
-    }
-
-    const int g = lane >> 2, t = lane & 3;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-        const int s = it % p.stages;
-        const int b = it & 1;
-        mbar_wait(&full[s], (it / p.stages) & 1, kErrFullBarrierTimeout);
-        const uint8_t *stage = smem + size_t(s) * p.stage_bytes;
-        const uint32_t stage_addr = smem_u32(stage);
-        if (it >= 2) mbar_wait(&pempty[b], ((it >> 1) - 1) & 1, kErrEpilogueTimeout);
-        float *pw = part + (size_t(b) * C + warp) * RT;
-        for (int rg = 0; rg < RT; rg += 16) {
-            const uint8_t *hdr_g = stage + size_t(rg + g) * p.row_stride;
-            const uint8_t *hdr_g8 = hdr_g + size_t(8) * p.row_stride;
-            float2 acc = superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb0 + 16u,
+        const int g = lane >> 2, t = lane & 3;
+        int it = 0, s = 0;
+        uint32_t ring_phase = 0;
+        for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
+            const int b = it & 1;
+            mbar_wait(&full[s], ring_phase, kErrFullBarrierTimeout);
+            const uint8_t *stage = smem + size_t(s) * p.stage_bytes;
+            const uint32_t stage_addr = smem_u32(stage);
+            if (it >= 2) mbar_wait(&pempty[b], ((it >> 1) - 1) & 1, kErrEpilogueTimeout);
+            float *pw = part + (size_t(b) * C + warp) * RT;
+            float2 acc[RT / 16];
+#pragma unroll
+            for (int q = 0; q < RT / 16; ++q) {
+                const int rg = 16 * q;
+                const uint8_t *hdr_g = stage + size_t(rg + g) * p.row_stride;
+                const uint8_t *hdr_g8 = hdr_g + size_t(8) * p.row_stride;
+                acc[q] = superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb0 + 16u,
                                            hdr_g + 144 * sb0, hdr_g8 + 144 * sb0, p.row_stride, lane, st0);
-            if (SPW == 2 && has1) {
-                const float2 a1 = superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb1 + 16u,
-                                                    hdr_g + 144 * sb1, hdr_g8 + 144 * sb1, p.row_stride, lane, st1);
-                acc.x += a1.x, acc.y += a1.y;
+                if (SPW == 2 && has1) {
+                    const float2 a1 =
+                        superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb1 + 16u,
+                                          hdr_g + 144 * sb1, hdr_g8 + 144 * sb1, p.row_stride, lane, st1);
+                    acc[q].x += a1.x, acc[q].y += a1.y;
+                }
             }
-            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 1);
-            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 1);
-            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 2);
-            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 2);
-            if (t == 0) {
-                pw[rg + g] = acc.x;
-                pw[rg + g + 8] = acc.y;
+#pragma unroll
+            for (int q = 0; q < RT / 16; ++q) {
+                float2 v = acc[q];
+                v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
+                v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
+                v.x += __shfl_xor_sync(0xffffffffu, v.x, 2);
+                v.y += __shfl_xor_sync(0xffffffffu, v.y, 2);
+                if (t == 0) {
+                    pw[16 * q + g] = v.x;
+                    pw[16 * q + g + 8] = v.y;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+                mbar_arrive(&pfull[b]);
+            }
+            if (++s == p.stages) s = 0, ring_phase ^= 1u;
+        }
+    }
+    if (CS > 1) {
+        pdl_wait();          // y may still be read by the previous kernel
+        cluster_sync_all();  // every CTA's row sums are complete and visible to the cluster
+        const int local_tiles = first_tile < p.num_tiles ? (p.num_tiles - 1 - first_tile) / tile_step + 1 : 0;
+        const uint32_t base = smem_u32(rowsum);
+        for (int i = int(crank) * blockDim.x + threadIdx.x; i < local_tiles * RT; i += CS * blockDim.x) {
+            const int li = i / RT, r = i - li * RT;
+            const int row = (first_tile + li * tile_step) * RT + r;
+            if (row < p.rows) {
+                float a = 0.0f;
+                for (int k = 0; k < CS; ++k) a += ld_cluster_f32(mapa_shared(base + 4u * uint32_t(i), uint32_t(k)));
+                p.y[row] = a;
             }
         }
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&empty[s]);
-            mbar_arrive(&pfull[b]);
-        }
+        cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
     }
 }
 
@@ -336,32 +447,94 @@ int num_sms() {
     return g_sms[dev];
 }
 
-bool plan_mma(int64_t rows, int64_t cols, const void *w, MmaParams &p, size_t &smem) {
+// Launch shape of one GEMV: cluster size (K split), row-tile height and the
+// shared-memory budget of one CTA.
+struct Shape {
+    int cluster;
+    int rt;
+    int budget_kb;
+};
+
+// Optional override for tuning sweeps: SI_Q4K_GEMV_PLAN="cluster,rows_per_tile,budget_kb"
+// (for example "2,16,100"); ignored when it does not fit the matrix.
+bool shape_override(Shape &s) {
+    static Shape o{0, 0, 0};
+    static bool parsed = false;
+    if (!parsed) {
+        parsed = true;
+        if (const char *e = std::getenv("SI_Q4K_GEMV_PLAN")) {
+            Shape t{};
+            if (std::sscanf(e, "%d,%d,%d", &t.cluster, &t.rt, &t.budget_kb) == 3) o = t;
+        }
+    }
+    if (o.cluster <= 0) return false;
+    s = o;
+    return true;
+}
+
+// Default launch shape: one CTA per SM with the whole shared memory as
+// ring and 32-row tiles. K is split over a cluster only when a CTA would
+// otherwise give each compute warp two superblocks (K > 4096): the one-
+// superblock warps keep the x fragments in registers without spilling.
+// (Measured on the Phi-4-mini shapes: splitting K = 3072 halves the compute
+// warps per SM and loses; K = 8192 split in two gains about 10%.)
+Shape default_shape(int64_t rows, int nsb, int sms) {
+    (void)rows;
+    (void)sms;
+    int cs = 1;
+    while (cs < 4 && nsb / cs > kMaxComputeWarps && nsb % (2 * cs) == 0) cs *= 2;
+    return {cs, 32, 220};
+}
+
+bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, size_t &smem, int &rt) {
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int nsb = int(cols / 256);
-    if (nsb > 2 * kMaxComputeWarps) return false;
-    p.nsb = nsb;
-    p.spw = nsb > kMaxComputeWarps ? 2 : 1;
-    p.compute_warps = (nsb + p.spw - 1) / p.spw;
-    p.row_bytes = uint32_t(144 * nsb);
-    // Row stride / 16 odd: ldmatrix's 8 row addresses hit 8 distinct bank quads.
-    p.row_stride = p.row_bytes + ((nsb % 2 == 0) ? 16u : 32u);
-    const size_t budget = 220 * 1024;
-    // Tile: 32 rows when the ring still holds three stages (measured best
-    // across the Phi-4-mini shapes at K = 3072), else 16.
-    const int rt = size_t(32) * p.row_stride * 3 <= budget ? 32 : 16;
-    p.rows_per_tile = rt;
-    p.stage_bytes = uint32_t((uint64_t(rt) * p.row_stride + 127) / 128 * 128);
-    p.num_tiles = int((rows + rt - 1) / rt);
-    const size_t part_bytes = size_t(2) * p.compute_warps * rt * sizeof(float);
-    int stages = int((budget - part_bytes - 512) / p.stage_bytes);
-    stages = std::min(stages, 8);
-    if (stages < 2) return false;
-    p.stages = stages;
-    p.rows = int(rows);
-    smem = size_t(stages) * p.stage_bytes + size_t(2 * stages + 4) * sizeof(uint64_t) + part_bytes;
-    return true;
+    Shape sh = default_shape(rows, nsb, sms);
+    Shape o;
+    if (shape_override(o) && (o.cluster == 1 || o.cluster == 2 || o.cluster == 4) && (o.rt == 16 || o.rt == 32) &&
+        o.budget_kb >= 32 && o.budget_kb <= 220)
+        sh = o;
+    if (nsb % sh.cluster != 0) sh.cluster = 1;
+    const size_t budget = size_t(sh.budget_kb) * 1024;
+    for (;;) {
+        const int nsb_cta = nsb / sh.cluster;
+        if (nsb_cta > 2 * kMaxComputeWarps) return false;
+        p.nsb = nsb;
+        p.cluster = sh.cluster;
+        p.nsb_cta = nsb_cta;
+        p.spw = nsb_cta > kMaxComputeWarps ? 2 : 1;
+        p.compute_warps = (nsb_cta + p.spw - 1) / p.spw;
+        p.row_bytes = uint32_t(144 * nsb);
+        p.cta_bytes = uint32_t(144 * nsb_cta);
+        // Row stride / 16 odd: ldmatrix's 8 row addresses hit 8 distinct bank quads.
+        p.row_stride = p.cta_bytes + ((nsb_cta % 2 == 0) ? 16u : 32u);
+        // Fall back to 16-row tiles when 32-row tiles leave fewer than 3 stages.
+        rt = sh.rt;
+        if (rt == 32 && size_t(32) * p.row_stride * 3 > budget) rt = 16;
+        p.stage_bytes = uint32_t((uint64_t(rt) * p.row_stride + 127) / 128 * 128);
+        p.num_tiles = int((rows + rt - 1) / rt);
+        // One CTA per SM at most: a cluster of CS CTAs takes CS SMs.
+        p.groups = std::max(1, std::min(p.num_tiles, sms / p.cluster));
+        p.max_local_tiles = (p.num_tiles + p.groups - 1) / p.groups;
+        const size_t rowsum = p.cluster > 1 ? size_t(p.max_local_tiles) * rt * sizeof(float) : 0;
+        // The K split is for small matrices: the row sums it keeps must stay small.
+        if (rowsum > 48 * 1024) {
+            sh.cluster = 1;
+            continue;
+        }
+        const size_t tail = size_t(2) * p.compute_warps * rt * sizeof(float) + rowsum;
+        const size_t bars = size_t(2 * 8 + 4) * sizeof(uint64_t);
+        if (budget < tail + bars + 2 * size_t(p.stage_bytes)) {
+            if (sh.cluster == 1) return false;
+            sh.cluster = 1;
+            continue;
+        }
+        p.stages = std::min(int((budget - tail - bars) / p.stage_bytes), 8);
+        p.rows = int(rows);
+        smem = size_t(p.stages) * p.stage_bytes + size_t(2 * p.stages + 4) * sizeof(uint64_t) + tail;
+        return true;
+    }
 }
 
 }  // namespace
@@ -375,30 +548,43 @@ using namespace si::dev;
 si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream) {
     MmaParams p{};
     size_t smem = 0;
-    if (!plan_mma(rows, cols, w, p, smem)) return SI_ERR_UNSUPPORTED;
+    int rt = 0;
+    const int sms = num_sms();
+    if (!plan_mma(rows, cols, w, sms, p, smem, rt)) return SI_ERR_UNSUPPORTED;
     p.w = static_cast<const uint8_t *>(w);
     p.x = x;
     p.y = y;
+    using Kernel = void (*)(MmaParams);
+    static const Kernel kernels[2][2][2] = {
+        {{gemv_mma_q4k_kernel<1, 16, 12>, gemv_mma_q4k_kernel<1, 32, 12>},
+         {gemv_mma_q4k_kernel<1, 16, 16>, gemv_mma_q4k_kernel<1, 32, 16>}},
+        {{gemv_mma_q4k_kernel<2, 16, 16>, gemv_mma_q4k_kernel<2, 32, 16>},
+         {gemv_mma_q4k_kernel<2, 16, 16>, gemv_mma_q4k_kernel<2, 32, 16>}}};
+    const Kernel kernel = kernels[p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(gemv_mma_q4k_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(gemv_mma_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        for (auto &a : kernels)
+            for (auto &b : a)
+                for (Kernel k : b) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr = true;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(unsigned(std::min(p.num_tiles, num_sms())));
+    cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     // The weight stream starts before the dependency wait: weights are
     // read-only parameters, never produced by the preceding kernel.
-    cudaLaunchAttribute attr_pdl{};
-    attr_pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr_pdl.val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = &attr_pdl;
-    cfg.numAttrs = 1;
-    const cudaError_t le = p.spw == 2 ? cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel<2>, p)
-                                      : cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel<1>, p);
+    cudaLaunchAttribute attrs[2]{};
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = unsigned(p.cluster);
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = p.cluster > 1 ? 2 : 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, kernel, p);
     const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
     if (e != cudaSuccess) return fail(SI_ERR_CUDA, "tensor-core Q4_K GEMV launch failed: %s", cudaGetErrorString(e));
     return SI_OK;
