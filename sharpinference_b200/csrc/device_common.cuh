@@ -20,12 +20,22 @@ enum : uint32_t {
 };
 static __device__ uint32_t g_error_word;
 
-// ~2^26 polls of try_wait (each poll may suspend the thread for a while):
-// seconds, far above any legitimate wait, far below a watchdog.
-constexpr uint32_t kMaxPolls = 1u << 26;
+// Waits suspend in hardware: each try_wait may park the warp until the
+// phase completes or kSuspendHintNs elapse, so a waiting warp takes no issue
+// slots and does not hammer the barrier that TMA completions update. Every
+// wait is still bounded: by kWaitLimitNs of %globaltimer and by kMaxPolls.
+constexpr uint32_t kSuspendHintNs = 10000000u;    // 10 ms per poll at most
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s in total
+constexpr uint32_t kMaxPolls = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -48,18 +58,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
 
 // Bounded wait on an mbarrier phase. Returns false (and records `err`) when
-// the poll budget runs out, so the caller can carry on without hanging.
+// the time or poll budget runs out, so the caller can carry on without hanging.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t err) {
-    for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < kMaxPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
     atomicOr(&g_error_word, err);
     return false;
 }

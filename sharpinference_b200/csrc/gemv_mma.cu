@@ -38,6 +38,7 @@ namespace si::dev {
 namespace {
 
 constexpr int kMaxComputeWarps = 16;
+constexpr int kMaxWps2Warps = 24;  // compute warps of the two-warps-per-column instantiation
 
 struct MmaParams {
     const uint8_t *w;
@@ -49,12 +50,25 @@ struct MmaParams {
     int nsb_cta;          // superblocks of every row one CTA covers (nsb / cluster)
     int compute_warps;    // C
     int spw;              // superblocks per compute warp (1 or 2)
+    int wps;              // compute warps per superblock column (1 or 2)
     int stages;
     uint32_t row_bytes;   // 144 * nsb, the global row pitch
     uint32_t cta_bytes;   // 144 * nsb_cta, bytes of each row one CTA loads
-    uint32_t row_stride;  // padded shared-memory row stride
+    uint32_t row_stride;  // padded shared-memory row stride (per-row copies)
+    // Shared-memory row map (see row_offset): rows come in groups of
+    // group_rows consecutive rows at pitch row_pitch, groups group_stride
+    // apart; class_period P = rows per group that fall in distinct bank
+    // classes. copy_groups: one bulk copy per group instead of per row.
+    int group_rows;       // power of two
+    int class_period;     // power of two
+    int log2_group_rows;
+    int log2_class_period;
+    uint32_t row_pitch;
+    uint32_t group_stride;
+    int copy_groups;
     uint32_t stage_bytes;
     int num_tiles;
+    int path;             // host side: 0 FP16 MMA, 1 INT8 MMA
     int groups;           // clusters (or CTAs when cluster == 1) in the grid
     int max_local_tiles;  // ceil(num_tiles / groups): row-sum slots per CTA when cluster > 1
 };
@@ -131,6 +145,13 @@ constexpr uint32_t kU6Bias = 0x64006400u;
 __device__ __forceinline__ float2 u6pair(uint32_t biased) {
     const uint32_t k1024 = kU6Bias;
     const __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&biased), *reinterpret_cast<const __half2 *>(&k1024));
+    return __half22float2(v);
+}
+// Same, divided by 16 in the same FP16 operation: (1024 + v) / 16 - 64 = v / 16 (exact).
+__device__ __forceinline__ float2 u6pair_div16(uint32_t biased) {
+    const uint32_t k16th = 0x2C002C00u, km64 = 0xD400D400u;  // 1/16, -64
+    const __half2 v = __hfma2(*reinterpret_cast<const __half2 *>(&biased), *reinterpret_cast<const __half2 *>(&k16th),
+                              *reinterpret_cast<const __half2 *>(&km64));
     return __half22float2(v);
 }
 
@@ -214,13 +235,13 @@ __device__ __forceinline__ void load_superblock_x(const float *__restrict__ x, i
 
 // One superblock column of one 16-row group. Returns this lane's partial
 // (before the cross-lane sum) for rows g (first) and g+8 (second).
-__device__ __forceinline__ float2 superblock_rows16(uint32_t qs_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
-                                                    uint32_t row_stride, int lane, const SbState &st) {
+// ldsm_addr: this lane's ldmatrix row address for the superblock's first
+// 16-byte group pair (row (lane/8 % 2) * 8 + lane % 8 of the 16-row unit,
+// group lane / 16).
+__device__ __forceinline__ float2 superblock_rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
+                                                    int lane, const SbState &st) {
     const int t = lane & 3;
-    // ldmatrix addresses: matrix m = lane / 8 -> rows (m & 1) * 8 + lane % 8,
-    // group offset (m >> 1) (+ 2 per call).
-    const int m = lane >> 3;
-    const uint32_t base = qs_addr + uint32_t(((m & 1) * 8 + (lane & 7))) * row_stride + uint32_t(m >> 1) * 16;
+    const uint32_t base = ldsm_addr;
     // Four accumulator chains (one per ldmatrix group q), summed pairwise in
     // the epilogue: shorter dependent MMA chains.
     float dq[4][4] = {};
@@ -289,16 +310,210 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t qs_addr, const uint
 // use follows from the warps per SM sub-partition ((MAXW + 2) / 4 rounded
 // up), so the 12-warp instantiation (K = 3072 slices) gets up to 128
 // registers a thread where the 16-warp one gets 96.
-template <int SPW, int RT, int MAXW>
+// FP16 path: nibble codes as FP16 subnormals, x as FP16 hi/lo pairs.
+struct F16Path {
+    using State = SbState;
+    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st) {
+        load_superblock_x(x, sb, lane, st);
+    }
+    static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
+                                                    int lane, const State &st) {
+        return superblock_rows16(ldsm_addr, hdr_g, hdr_g8, lane, st);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// INT8 path (mma.sync m16n8k32, u8 x s8 -> s32, exact integer accumulation).
+//
+//  * A = weight codes as bytes: the low nibbles of a 32-byte chunk j are the
+//    32 weights of sub-block 2j in order (k = 0..31), the high nibbles those
+//    of sub-block 2j+1. One AND yields four codes: q (mask 0x0F) or 16 q
+//    (mask 0xF0, the 1/16 goes into the sub-block scale). One ldmatrix.x4
+//    per chunk feeds two MMAs.
+//  * B = x as three base-256 digits: per superblock, v = rint(x * 2^(22-e))
+//    (|x| < 2^e, so |v| < 2^22) and v = d0 * 2^16 + d1 * 2^8 + d2 with
+//    signed 8-bit digits. Columns: sub-block s sits in half s / 4 of the n8
+//    tile (columns 0-2 or 4-6 hold d0, d1, d2; 3 and 7 stay zero), so the
+//    accumulator set s % 4 collects sub-blocks s and s + 4 side by side.
+//  * Lane (g,t) holds columns 2t, 2t+1 of set q: for even t (d0, d1) ->
+//    256 * c0 + c1 in units of 2^8, for odd t d2 (c1 is a zero column), so
+//    c0 * M + c1 with M = 256 or 1 is exact in int32 and in FP32 (< 2^24);
+//    each lane scales it by its sub-block's 6-bit scale and the per-lane
+//    digit weight / x scale, and the four lanes of a row are summed.
+// Precision: x is carried as 22-bit fixed point per superblock (relative to
+// its largest element), the products are exact, the sum is FP32.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct I8State {
+    uint32_t b[8][2];   // B fragment of sub-block s (zero unless s / 4 is this lane's column half)
+    float wt_inv;       // digit weight of this lane's accumulator columns / x scale
+    float sx_lo_t;      // sum of x over sub-block t
+    float sx_hi_t;      // sum of x over sub-block t+4
+    int digit_mul;      // 256 (even t: columns d0, d1) or 1 (odd t: column d2)
+    uint32_t sc_shift;  // scale unpack of this lane's sub-block half (t / 2): 0 / 2
+    uint32_t sc_wmask;  // 0 / 0x0F0F0F0F
+    uint32_t sc_ymask;  // 0x3F3F3F3F / 0x30303030
+};
+
+// v = d0 * 2^16 + d1 * 2^8 + d2 with d1, d2 in [-128, 127] (balanced base
+// 256): d2 is the low byte of v, d1 the low byte of (v + 2^7) >> 8 and d0 =
+// (v + 2^15 + 2^7) >> 16, because adding 128 to each lower digit makes it a
+// plain byte without carry. Only the low byte of each is kept (two's
+// complement int8), so one add and one shift give a digit.
+__device__ __forceinline__ uint32_t digit_byte(int v, int add, uint32_t shift) {
+    return uint32_t((v + add) >> shift);
+}
+// Low bytes of four words packed into one.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+}
+
+struct I8Path {
+    using State = I8State;
+    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st) {
+        const float *xs = x + size_t(sb) * 256;
+        const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
+        float v[8];
+        if (aligned) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane + 4));
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __ldg(xs + 8 * lane + i);
+        }
+        float amax = 0.0f, psum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i])), psum += v[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 2);  // lanes 4s..4s+3 hold the sum of sub-block s
+        const int t = lane & 3, g = lane >> 2;
+        st.sx_lo_t = __shfl_sync(0xffffffffu, psum, 4 * t);
+        st.sx_hi_t = __shfl_sync(0xffffffffu, psum, 4 * (t + 4));
+        // scale = 2^(22 - e) with amax < 2^e: |x * scale| < 2^22.
+        float scale = 1.0f, inv = 1.0f;
+        const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xffu;
+        if (ebits == 0xffu) {
+            inv = __int_as_float(0x7fc00000);  // non-finite activation: the rows become NaN
+        } else if (amax > 0.0f) {
+            const int e = int(ebits) - 127 + 1;
+            const int se = max(-126, min(127, 22 - e));
+            scale = __uint_as_float(uint32_t(se + 127) << 23);
+            inv = __uint_as_float(uint32_t(127 - se) << 23);
+        }
+        st.digit_mul = (t & 1) ? 1 : 256;
+        st.wt_inv = ((t & 1) ? 1.0f : 256.0f) * inv;
+        const bool hi_half = t >= 2;
+        st.sc_shift = hi_half ? 2u : 0u;
+        st.sc_wmask = hi_half ? 0x0F0F0F0Fu : 0u;
+        st.sc_ymask = hi_half ? 0x30303030u : 0x3F3F3F3Fu;
+        // B fragments: lane (g,t) holds column g = 4 * half + digit of
+        // sub-blocks 4 * half .. 4 * half + 3, k = 4t..4t+3 (b0) and
+        // 16+4t..16+4t+3 (b1); column digit 3 stays zero.
+        const int half = g >> 2, digit = g & 3;
+        const int dadd = digit == 0 ? 0x8080 : (digit == 1 ? 0x80 : 0);
+        const uint32_t dshift = digit == 0 ? 16u : (digit == 1 ? 8u : 0u);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            uint32_t b0 = 0, b1 = 0;
+            if ((s >> 2) == half && digit < 3) {
+                float q[8];
+                const float *e0 = xs + 32 * s + 4 * t;
+                if (aligned) {
+                    const float4 a = __ldg(reinterpret_cast<const float4 *>(e0));
+                    const float4 c = __ldg(reinterpret_cast<const float4 *>(e0 + 16));
+                    q[0] = a.x, q[1] = a.y, q[2] = a.z, q[3] = a.w, q[4] = c.x, q[5] = c.y, q[6] = c.z, q[7] = c.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) q[i] = __ldg(e0 + i), q[4 + i] = __ldg(e0 + 16 + i);
+                }
+                uint32_t dg[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dg[i] = digit_byte(__float2int_rn(q[i] * scale), dadd, dshift);
+                b0 = pack_low_bytes(dg[0], dg[1], dg[2], dg[3]);
+                b1 = pack_low_bytes(dg[4], dg[5], dg[6], dg[7]);
+            }
+            st.b[s][0] = b0;
+            st.b[s][1] = b1;
+        }
+    }
+
+    static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
+                                                    int lane, const State &st) {
+        const int t = lane & 3;
+        const uint32_t base = ldsm_addr;
+        int acc[4][4] = {};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t w0, w8, v0, v8;  // rows g / g+8 of the chunk's two 16-byte groups
+            ldsm_x4(base + 32u * j, w0, w8, v0, v8);
+            constexpr uint32_t L = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+            imma16832(acc[(2 * j) & 3], w0 & L, w8 & L, v0 & L, v8 & L, st.b[2 * j][0], st.b[2 * j][1]);
+            imma16832(acc[(2 * j + 1) & 3], w0 & H, w8 & H, v0 & H, v8 & H, st.b[2 * j + 1][0], st.b[2 * j + 1][1]);
+        }
+        const uint4 hg = *reinterpret_cast<const uint4 *>(hdr_g);
+        const uint4 hg8 = *reinterpret_cast<const uint4 *>(hdr_g8);
+        // Scales of this lane's sub-blocks 4 * (t / 2) + q, q = 0..3, one per byte.
+        const uint32_t pg = (hg.w & st.sc_wmask) | ((hg.y >> st.sc_shift) & st.sc_ymask);
+        const uint32_t pg8 = (hg8.w & st.sc_wmask) | ((hg8.y >> st.sc_shift) & st.sc_ymask);
+        float main0 = 0.0f, main1 = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            // Odd sets hold high-nibble sub-blocks (codes 16 q): scale / 16.
+            const uint32_t biased = (__byte_perm(pg, pg8, uint32_t(q) | (uint32_t(q + 4) << 8)) & 0x00FF00FFu) | kU6Bias;
+            const float2 sc = (q & 1) ? u6pair_div16(biased) : u6pair(biased);
+            main0 = fmaf(float(acc[q][0] * st.digit_mul + acc[q][1]), sc.x, main0);
+            main1 = fmaf(float(acc[q][2] * st.digit_mul + acc[q][3]), sc.y, main1);
+        }
+        // Mins of sub-blocks t and t+4 (rows g, g+8).
+        const uint32_t sel = uint32_t(t) | (uint32_t(t + 4) << 8);
+        const uint32_t Y = __byte_perm(hg.z, hg8.z, sel);
+        const uint32_t Z = __byte_perm(hg.w, hg8.w, sel);
+        const float2 mn_lo = u6pair((Y & 0x003F003Fu) | kU6Bias);
+        const float2 mn_hi = u6pair(((Z >> 4) & 0x000F000Fu) | ((Y >> 2) & 0x00300030u) | kU6Bias);
+        const float2 dm = half2_bits_to_float2(hg.x);
+        const float2 dm8 = half2_bits_to_float2(hg8.x);
+        const float out0 = dm.x * (main0 * st.wt_inv) - dm.y * (mn_lo.x * st.sx_lo_t + mn_hi.x * st.sx_hi_t);
+        const float out1 = dm8.x * (main1 * st.wt_inv) - dm8.y * (mn_lo.y * st.sx_lo_t + mn_hi.y * st.sx_hi_t);
+        return make_float2(out0, out1);
+    }
+};
+
+// Tile row of MMA row r (0..15) of 16-row unit u: the unit's two 8-row
+// ldmatrix sets k = 2u, 2u+1 take P rows from each of the 8/P groups, so
+// their eight row addresses fall in eight distinct bank classes.
+__device__ __forceinline__ int unit_row(const MmaParams &p, int u, int r) {
+    const int k = 2 * u + (r >> 3), e = r & 7;
+    return ((e >> p.log2_class_period) << p.log2_group_rows) + (k << p.log2_class_period) +
+           (e & (p.class_period - 1));
+}
+__device__ __forceinline__ uint32_t row_offset(const MmaParams &p, int row) {
+    return uint32_t(row >> p.log2_group_rows) * p.group_stride + uint32_t(row & (p.group_rows - 1)) * p.row_pitch;
+}
+
+// WPS compute warps share each superblock column (WPS = 2: each takes one
+// 16-row half of a 32-row tile), for more warps in flight per SM.
+template <class Path, int SPW, int RT, int WPS, int MAXW>
 __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const MmaParams p) {
+    static_assert(WPS == 1 || (WPS == 2 && SPW == 1 && RT == 32), "two warps per column need 32-row tiles");
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.compute_warps, CS = p.cluster;
+    const int C0 = C / WPS;  // superblock columns (partial sums per row)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(p.stages) * p.stage_bytes);
     uint64_t *empty = full + p.stages;
     uint64_t *pfull = empty + p.stages;  // [2] compute warps -> reducer
     uint64_t *pempty = pfull + 2;        // [2] reducer -> compute warps
-    float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C][RT]
-    float *rowsum = part + size_t(2) * C * RT;             // [max_local_tiles][RT] when CS > 1
+    float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C0][RT]
+    float *rowsum = part + size_t(2) * C0 * RT;            // [max_local_tiles][RT] when CS > 1
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = CS > 1 ? cluster_ctarank() : 0u;
@@ -330,13 +545,24 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(nrows) * p.cta_bytes);
             __syncwarp();
             uint8_t *dst = smem + size_t(s) * p.stage_bytes;
-            for (int r = lane; r < nrows; r += 32)
-                bulk_copy_g2s(dst + size_t(r) * p.row_stride, wsrc + size_t(r0 + r) * p.row_bytes, p.cta_bytes,
-                              &full[s]);
+            if (p.copy_groups) {
+                // One copy per group of consecutive rows (contiguous in global memory).
+                const int G = p.group_rows;
+                const int first = lane * G;
+                if (first < nrows) {
+                    const int cnt = min(G, nrows - first);
+                    bulk_copy_g2s(dst + size_t(lane) * p.group_stride, wsrc + size_t(r0 + first) * p.row_bytes,
+                                  uint32_t(cnt) * p.cta_bytes, &full[s]);
+                }
+            } else {
+                for (int r = lane; r < nrows; r += 32)
+                    bulk_copy_g2s(dst + size_t(r) * p.row_stride, wsrc + size_t(r0 + r) * p.row_bytes, p.cta_bytes,
+                                  &full[s]);
+            }
             if (++s == p.stages) s = 0, ring_phase ^= 1u;
         }
     } else if (warp == C + 1) {
-        // Reducer: fixed-order sum of the C per-warp partials of each row
+        // Reducer: fixed-order sum of the C0 per-column partials of each row
         // (RT <= 32: lane r owns row r of the tile).
         if (CS == 1) pdl_wait();  // y may still be read by the previous kernel
         int it = 0;
@@ -345,10 +571,10 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             mbar_wait(&pfull[b], (it >> 1) & 1, kErrEpilogueTimeout);
             const int r0 = tile * RT;
             const int nrows = min(RT, p.rows - r0);
-            const float *pb = part + size_t(b) * C * RT;
+            const float *pb = part + size_t(b) * C0 * RT;
             float a = 0.0f;
             if (lane < nrows)
-                for (int c = 0; c < C; ++c) a += pb[c * RT + lane];
+                for (int c = 0; c < C0; ++c) a += pb[c * RT + lane];
             if (CS == 1) {
                 if (lane < nrows) p.y[r0 + lane] = a;
             } else if (lane < RT) {
@@ -358,19 +584,36 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             if (lane == 0) mbar_arrive(&pempty[b]);
         }
     } else {
-        // Compute warp `warp`: superblocks warp, warp + C (SPW == 2) of this CTA's slice.
-        SbState st0;
-        SbState st1;
-        const int sb0 = warp, sb1 = warp + C;
+        // Compute warp `warp`: column col = warp % C0, i.e. superblocks col,
+        // col + C0 (SPW == 2) of this CTA's slice; row half warp / C0 (WPS == 2).
+        typename Path::State st0;
+        typename Path::State st1;
+        const int col = warp % C0, unit0 = warp / C0;
+        const int sb0 = col, sb1 = col + C0;
         const bool has1 = SPW == 2 && sb1 < p.nsb_cta;
         const int gsb = int(crank) * p.nsb_cta;
         pdl_wait();  // x is produced by the previous kernel
-        load_superblock_x(p.x, gsb + sb0, lane, st0);
+        Path::load(p.x, gsb + sb0, lane, st0);
         if constexpr (SPW == 2) {
-            if (has1) load_superblock_x(p.x, gsb + sb1, lane, st1);
+            if (has1) Path::load(p.x, gsb + sb1, lane, st1);
         }
 
         const int g = lane >> 2, t = lane & 3;
+        constexpr int kUnits = RT / 16 / WPS;  // 16-row groups per warp per tile
+        // Per unit: this lane's ldmatrix row address and the rows g, g+8 it
+        // owns in the epilogue (offsets within a stage, superblock 0).
+        uint32_t off_ldsm[kUnits], off_g[kUnits], off_g8[kUnits];
+        int row_g[kUnits], row_g8[kUnits];
+#pragma unroll
+        for (int q = 0; q < kUnits; ++q) {
+            const int u = q * WPS + unit0;
+            const int m = lane >> 3;
+            off_ldsm[q] = row_offset(p, unit_row(p, u, (m & 1) * 8 + (lane & 7))) + uint32_t(m >> 1) * 16u + 16u;
+            row_g[q] = unit_row(p, u, g);
+            row_g8[q] = unit_row(p, u, g + 8);
+            off_g[q] = row_offset(p, row_g[q]);
+            off_g8[q] = row_offset(p, row_g8[q]);
+        }
         int it = 0, s = 0;
         uint32_t ring_phase = 0;
         for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
@@ -379,32 +622,28 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             const uint8_t *stage = smem + size_t(s) * p.stage_bytes;
             const uint32_t stage_addr = smem_u32(stage);
             if (it >= 2) mbar_wait(&pempty[b], ((it >> 1) - 1) & 1, kErrEpilogueTimeout);
-            float *pw = part + (size_t(b) * C + warp) * RT;
-            float2 acc[RT / 16];
+            float *pw = part + (size_t(b) * C0 + col) * RT;
+            float2 acc[kUnits];
 #pragma unroll
-            for (int q = 0; q < RT / 16; ++q) {
-                const int rg = 16 * q;
-                const uint8_t *hdr_g = stage + size_t(rg + g) * p.row_stride;
-                const uint8_t *hdr_g8 = hdr_g + size_t(8) * p.row_stride;
-                acc[q] = superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb0 + 16u,
-                                           hdr_g + 144 * sb0, hdr_g8 + 144 * sb0, p.row_stride, lane, st0);
+            for (int q = 0; q < kUnits; ++q) {
+                acc[q] = Path::rows16(stage_addr + off_ldsm[q] + 144u * sb0, stage + off_g[q] + 144 * sb0,
+                                      stage + off_g8[q] + 144 * sb0, lane, st0);
                 if (SPW == 2 && has1) {
-                    const float2 a1 =
-                        superblock_rows16(stage_addr + uint32_t(rg) * p.row_stride + 144u * sb1 + 16u,
-                                          hdr_g + 144 * sb1, hdr_g8 + 144 * sb1, p.row_stride, lane, st1);
+                    const float2 a1 = Path::rows16(stage_addr + off_ldsm[q] + 144u * sb1, stage + off_g[q] + 144 * sb1,
+                                                   stage + off_g8[q] + 144 * sb1, lane, st1);
                     acc[q].x += a1.x, acc[q].y += a1.y;
                 }
             }
 #pragma unroll
-            for (int q = 0; q < RT / 16; ++q) {
+            for (int q = 0; q < kUnits; ++q) {
                 float2 v = acc[q];
                 v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
                 v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
                 v.x += __shfl_xor_sync(0xffffffffu, v.x, 2);
                 v.y += __shfl_xor_sync(0xffffffffu, v.y, 2);
                 if (t == 0) {
-                    pw[16 * q + g] = v.x;
-                    pw[16 * q + g + 8] = v.y;
+                    pw[row_g[q]] = v.x;
+                    pw[row_g8[q]] = v.y;
                 }
             }
             __syncwarp();
@@ -453,24 +692,36 @@ struct Shape {
     int cluster;
     int rt;
     int budget_kb;
+    int path;  // 0: FP16 MMA, 1: INT8 MMA
+    int wps;   // compute warps per superblock column (1, or 2 on the INT8 path with 32-row tiles)
+    int max_groups;  // 0: one CTA (cluster) per SM; else at most this many
 };
 
-// Optional override for tuning sweeps: SI_Q4K_GEMV_PLAN="cluster,rows_per_tile,budget_kb"
-// (for example "2,16,100"); ignored when it does not fit the matrix.
+// Optional override for tuning sweeps:
+// SI_Q4K_GEMV_PLAN="cluster,rows_per_tile,budget_kb[,path[,warps_per_column[,max_groups]]]"
+// (for example "2,16,100" or "1,32,226,1,2"); ignored when it does not fit.
 bool shape_override(Shape &s) {
-    static Shape o{0, 0, 0};
+    static Shape o{0, 0, 0, 0, 1, 0};
     static bool parsed = false;
     if (!parsed) {
         parsed = true;
         if (const char *e = std::getenv("SI_Q4K_GEMV_PLAN")) {
-            Shape t{};
-            if (std::sscanf(e, "%d,%d,%d", &t.cluster, &t.rt, &t.budget_kb) == 3) o = t;
+            Shape t{0, 0, 0, 0, 1, 0};
+            if (std::sscanf(e, "%d,%d,%d,%d,%d,%d", &t.cluster, &t.rt, &t.budget_kb, &t.path, &t.wps, &t.max_groups) >=
+                3)
+                o = t;
         }
     }
     if (o.cluster <= 0) return false;
     s = o;
     return true;
 }
+
+// Largest ring budget: the 227 KB a CTA may hold, less 1 KB of headroom.
+// The bytes in flight per SM set the bandwidth (Little's law): with one
+// stage held by the compute warps, a 4 x 55.8 KB ring (K = 3072, 32-row
+// tiles) keeps ~167 KB in flight where 3 stages kept ~111 KB.
+constexpr int kMaxBudgetKb = 226;
 
 // Default launch shape: one CTA per SM with the whole shared memory as
 // ring and 32-row tiles. K is split over a cluster only when a CTA would
@@ -483,7 +734,7 @@ Shape default_shape(int64_t rows, int nsb, int sms) {
     (void)sms;
     int cs = 1;
     while (cs < 4 && nsb / cs > kMaxComputeWarps && nsb % (2 * cs) == 0) cs *= 2;
-    return {cs, 32, 220};
+    return {cs, 32, kMaxBudgetKb, 1, 1, 0};
 }
 
 bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, size_t &smem, int &rt) {
@@ -493,7 +744,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
     Shape sh = default_shape(rows, nsb, sms);
     Shape o;
     if (shape_override(o) && (o.cluster == 1 || o.cluster == 2 || o.cluster == 4) && (o.rt == 16 || o.rt == 32) &&
-        o.budget_kb >= 32 && o.budget_kb <= 220)
+        o.budget_kb >= 32 && o.budget_kb <= kMaxBudgetKb && (o.path == 0 || o.path == 1) && (o.wps == 1 || o.wps == 2))
         sh = o;
     if (nsb % sh.cluster != 0) sh.cluster = 1;
     const size_t budget = size_t(sh.budget_kb) * 1024;
@@ -504,18 +755,45 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
         p.cluster = sh.cluster;
         p.nsb_cta = nsb_cta;
         p.spw = nsb_cta > kMaxComputeWarps ? 2 : 1;
-        p.compute_warps = (nsb_cta + p.spw - 1) / p.spw;
+        const int columns = (nsb_cta + p.spw - 1) / p.spw;
+        rt = sh.rt;
         p.row_bytes = uint32_t(144 * nsb);
         p.cta_bytes = uint32_t(144 * nsb_cta);
         // Row stride / 16 odd: ldmatrix's 8 row addresses hit 8 distinct bank quads.
         p.row_stride = p.cta_bytes + ((nsb_cta % 2 == 0) ? 16u : 32u);
         // Fall back to 16-row tiles when 32-row tiles leave fewer than 3 stages.
-        rt = sh.rt;
         if (rt == 32 && size_t(32) * p.row_stride * 3 > budget) rt = 16;
-        p.stage_bytes = uint32_t((uint64_t(rt) * p.row_stride + 127) / 128 * 128);
+        p.wps = (sh.wps == 2 && sh.path == 1 && p.spw == 1 && rt == 32 && 2 * columns <= kMaxWps2Warps) ? 2 : 1;
+        p.compute_warps = columns * p.wps;
+        if (p.cluster == 1) {
+            // Whole rows are contiguous: copy groups of rows. A row is
+            // 144 * nsb bytes = 16 * (9 nsb) with 9 nsb = nsb (mod 8), so
+            // consecutive rows repeat their bank class every P rows; 8 / P
+            // groups based 16 bytes apart give the 8 classes one ldmatrix needs.
+            const int r8 = nsb_cta % 8;
+            p.class_period = (r8 & 1) ? 8 : (r8 == 4 ? 2 : (r8 == 0 ? 1 : 4));
+            p.group_rows = rt * p.class_period / 8;
+            p.log2_class_period = p.class_period == 8 ? 3 : (p.class_period == 4 ? 2 : (p.class_period == 2 ? 1 : 0));
+            p.log2_group_rows = rt == 32 ? p.log2_class_period + 2 : p.log2_class_period + 1;
+            p.row_pitch = p.cta_bytes;
+            p.group_stride = uint32_t(p.group_rows) * p.cta_bytes + 16u;
+            p.copy_groups = 1;
+            p.stage_bytes = uint32_t((uint64_t(8 / p.class_period) * p.group_stride + 127) / 128 * 128);
+        } else {
+            // K slices of a row are not contiguous across rows: one copy per row.
+            p.class_period = 8;
+            p.group_rows = rt;
+            p.log2_class_period = 3;
+            p.log2_group_rows = rt == 32 ? 5 : 4;
+            p.row_pitch = p.row_stride;
+            p.group_stride = uint32_t(rt) * p.row_stride;
+            p.copy_groups = 0;
+            p.stage_bytes = uint32_t((uint64_t(rt) * p.row_stride + 127) / 128 * 128);
+        }
         p.num_tiles = int((rows + rt - 1) / rt);
         // One CTA per SM at most: a cluster of CS CTAs takes CS SMs.
         p.groups = std::max(1, std::min(p.num_tiles, sms / p.cluster));
+        if (sh.max_groups > 0) p.groups = std::min(p.groups, sh.max_groups);
         p.max_local_tiles = (p.num_tiles + p.groups - 1) / p.groups;
         const size_t rowsum = p.cluster > 1 ? size_t(p.max_local_tiles) * rt * sizeof(float) : 0;
         // The K split is for small matrices: the row sums it keeps must stay small.
@@ -523,7 +801,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
             sh.cluster = 1;
             continue;
         }
-        const size_t tail = size_t(2) * p.compute_warps * rt * sizeof(float) + rowsum;
+        const size_t tail = size_t(2) * columns * rt * sizeof(float) + rowsum;
         const size_t bars = size_t(2 * 8 + 4) * sizeof(uint64_t);
         if (budget < tail + bars + 2 * size_t(p.stage_bytes)) {
             if (sh.cluster == 1) return false;
@@ -532,6 +810,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
         }
         p.stages = std::min(int((budget - tail - bars) / p.stage_bytes), 8);
         p.rows = int(rows);
+        p.path = sh.path;
         smem = size_t(p.stages) * p.stage_bytes + size_t(2 * p.stages + 4) * sizeof(uint64_t) + tail;
         return true;
     }
@@ -555,17 +834,23 @@ si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, 
     p.x = x;
     p.y = y;
     using Kernel = void (*)(MmaParams);
-    static const Kernel kernels[2][2][2] = {
-        {{gemv_mma_q4k_kernel<1, 16, 12>, gemv_mma_q4k_kernel<1, 32, 12>},
-         {gemv_mma_q4k_kernel<1, 16, 16>, gemv_mma_q4k_kernel<1, 32, 16>}},
-        {{gemv_mma_q4k_kernel<2, 16, 16>, gemv_mma_q4k_kernel<2, 32, 16>},
-         {gemv_mma_q4k_kernel<2, 16, 16>, gemv_mma_q4k_kernel<2, 32, 16>}}};
-    const Kernel kernel = kernels[p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
+#define SI_GEMV_KERNELS(P)                                                                  \
+    {{{gemv_mma_q4k_kernel<P, 1, 16, 1, 12>, gemv_mma_q4k_kernel<P, 1, 32, 1, 12>},        \
+      {gemv_mma_q4k_kernel<P, 1, 16, 1, 16>, gemv_mma_q4k_kernel<P, 1, 32, 1, 16>}},       \
+     {{gemv_mma_q4k_kernel<P, 2, 16, 1, 16>, gemv_mma_q4k_kernel<P, 2, 32, 1, 16>},        \
+      {gemv_mma_q4k_kernel<P, 2, 16, 1, 16>, gemv_mma_q4k_kernel<P, 2, 32, 1, 16>}}}
+    static const Kernel kernels[2][2][2][2] = {SI_GEMV_KERNELS(F16Path), SI_GEMV_KERNELS(I8Path)};
+#undef SI_GEMV_KERNELS
+    static const Kernel kernel_wps2 = gemv_mma_q4k_kernel<I8Path, 1, 32, 2, kMaxWps2Warps>;
+    const Kernel kernel = p.wps == 2 ? kernel_wps2
+                                     : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
     static bool attr = false;
     if (!attr) {
         for (auto &a : kernels)
             for (auto &b : a)
-                for (Kernel k : b) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                for (auto &c : b)
+                    for (Kernel k : c) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(kernel_wps2, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr = true;
     }
     cudaLaunchConfig_t cfg{};
