@@ -431,8 +431,8 @@ si_status matvec_dense(uint32_t wtype, const void *w, uint32_t xtype, const void
 si_status matvec_quant(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                        void *stream) {
     auto st = static_cast<cudaStream_t>(stream);
-    if (wtype == SI_TYPE_Q4_K) {
-        const si_status ms = matvec_q4k_mma(w, x, y, rows, cols, stream);
+    {
+        const si_status ms = matvec_quant_mma(wtype, w, x, y, rows, cols, stream);
         if (ms != SI_ERR_UNSUPPORTED) return ms;
     }
     StagedParams p{};

@@ -52,8 +52,8 @@ struct MmaParams {
     int spw;              // superblocks per compute warp (1 or 2)
     int wps;              // compute warps per superblock column (1 or 2)
     int stages;
-    uint32_t row_bytes;   // 144 * nsb, the global row pitch
-    uint32_t cta_bytes;   // 144 * nsb_cta, bytes of each row one CTA loads
+    uint32_t row_bytes;   // column bytes (144 Q4_K, 272 Q8_0) * nsb, the global row pitch
+    uint32_t cta_bytes;   // column bytes * nsb_cta, bytes of each row one CTA loads
     uint32_t row_stride;  // padded shared-memory row stride (per-row copies)
     // Shared-memory row map (see row_offset): rows come in groups of
     // group_rows consecutive rows at pitch row_pitch, groups group_stride
@@ -313,7 +313,10 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t ldsm_addr, const ui
 // FP16 path: nibble codes as FP16 subnormals, x as FP16 hi/lo pairs.
 struct F16Path {
     using State = SbState;
-    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st) {
+    static constexpr uint32_t kColBytes = 144;  // one Q4_K superblock
+    static constexpr uint32_t kQsOffset = 16;   // nibbles follow the 16-byte header
+    static constexpr uint32_t kScratchBytes = 0;
+    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st, uint8_t *) {
         load_superblock_x(x, sb, lane, st);
     }
     static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
@@ -377,7 +380,10 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
 
 struct I8Path {
     using State = I8State;
-    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st) {
+    static constexpr uint32_t kColBytes = 144;
+    static constexpr uint32_t kQsOffset = 16;
+    static constexpr uint32_t kScratchBytes = 0;
+    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *) {
         const float *xs = x + size_t(sb) * 256;
         const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
         float v[8];
@@ -488,6 +494,142 @@ struct I8Path {
     }
 };
 
+// ---------------------------------------------------------------------------
+// Q8_0 path (mma.sync m16n8k32, s8 x s8 -> s32). A Q8_0 block is 34 bytes
+// (FP16 d, 32 int8 quants), so quants are not 16-byte aligned; instead of
+// unpacking, the MMA reads the raw row bytes: a column of 8 blocks (256
+// elements, 272 bytes) is covered by nine 32-byte windows (the last half
+// window overlaps the next column or the row padding), ldmatrix hands each
+// lane bytes 4t..4t+3 of every 16-byte chunk, and B holds the x digits of
+// the element at each byte position, zero at the FP16 scale bytes and
+// outside the column. Columns of the n8 tile: 2 * digit + parity, i.e. even
+// blocks in even columns (0, 2, 4), odd blocks in odd ones (1, 3, 5), 6 and 7
+// zero. Lane (g,t) then holds digit t of both block parities, so which block
+// a window's accumulator belongs to is the same for every lane: block 2j is
+// windows 2j and 2j+1 (even columns), block 2j+1 windows 2j+1 and 2j+2 (odd
+// columns). Window sums are exact integers (< 2^21); each lane scales its
+// eight block sums by the blocks' FP16 d, by its digit weight 2^16 / 2^8 / 1
+// and by the x scale, and the four lanes of a row are summed.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma16832_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct Q8State {
+    uint32_t b[9][2];  // B fragments of the column's nine windows
+    float wt_inv;      // digit weight of this lane's accumulator columns / x scale (0 for t = 3)
+};
+
+struct Q8Path {
+    using State = Q8State;
+    static constexpr uint32_t kColBytes = 272;  // eight 34-byte blocks
+    static constexpr uint32_t kQsOffset = 0;    // windows start at the column start
+    static constexpr uint32_t kImageBytes = 288;            // nine windows
+    static constexpr uint32_t kScratchBytes = 3 * kImageBytes;  // per compute warp: one image per digit
+
+    // scratch: this warp's 864-byte area. Image d holds, at each byte
+    // position of the column, digit d of the element stored there (0 at the
+    // scale bytes and beyond the column); each lane then reads its B words
+    // with aligned 32-bit loads.
+    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st,
+                                                uint8_t *scratch) {
+        const float *xs = x + size_t(sb) * 256;
+        const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
+        float v[8];
+        if (aligned) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane + 4));
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __ldg(xs + 8 * lane + i);
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        float scale = 1.0f, inv = 1.0f;
+        const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xffu;
+        if (ebits == 0xffu) {
+            inv = __int_as_float(0x7fc00000);  // non-finite activation: the rows become NaN
+        } else if (amax > 0.0f) {
+            const int e = int(ebits) - 127 + 1;
+            const int se = max(-126, min(127, 22 - e));
+            scale = __uint_as_float(uint32_t(se + 127) << 23);
+            inv = __uint_as_float(uint32_t(127 - se) << 23);
+        }
+        const int t = lane & 3, g = lane >> 2;
+        st.wt_inv = (t == 0 ? 65536.0f : (t == 1 ? 256.0f : (t == 2 ? 1.0f : 0.0f))) * inv;
+        // Images: lane l owns elements 8l..8l+7 = bytes 34 * (l / 4) + 2 + 8 * (l % 4) .. + 7 of the column.
+        int vi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vi[i] = __float2int_rn(v[i] * scale);
+        const uint32_t pos = 34u * uint32_t(lane >> 2) + 2u + 8u * uint32_t(lane & 3);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            const int add = d == 0 ? 0x8080 : (d == 1 ? 0x80 : 0);
+            const uint32_t shift = d == 0 ? 16u : (d == 1 ? 8u : 0u);
+            uint16_t *img = reinterpret_cast<uint16_t *>(scratch + d * kImageBytes + pos);  // 2-byte aligned
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                img[i] = uint16_t((digit_byte(vi[2 * i], add, shift) & 0xffu) |
+                                  ((digit_byte(vi[2 * i + 1], add, shift) & 0xffu) << 8));
+            // scale bytes of block `lane` and the tail past the column read as zero
+            if (lane < 8) *reinterpret_cast<uint16_t *>(scratch + d * kImageBytes + 34 * lane) = 0;
+            if (lane < 4) *reinterpret_cast<uint32_t *>(scratch + d * kImageBytes + 272 + 4 * lane) = 0u;
+        }
+        __syncwarp();
+        // B column g = 2 * digit + parity; digit 3 (g = 6, 7) stays zero.
+        const int parity = g & 1, digit = g >> 1;
+#pragma unroll
+        for (int w = 0; w < 9; ++w) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t p0 = 32u * w + 16u * h + 4u * t;  // 4 positions, all in block p0 / 34 or scale bytes
+                uint32_t b = 0;
+                if (digit < 3 && p0 < 272u && int((p0 / 34u) & 1u) == parity)
+                    b = *reinterpret_cast<const uint32_t *>(scratch + digit * kImageBytes + p0);
+                st.b[w][h] = b;
+            }
+        }
+        __syncwarp();
+    }
+
+    // hdr_g / hdr_g8: the column's first byte in rows g and g+8.
+    static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
+                                                    int lane, const State &st) {
+        (void)lane;
+        int acc[9][4];
+#pragma unroll
+        for (int w = 0; w < 9; ++w) {
+            uint32_t w0, w8, v0, v8;
+            ldsm_x4(ldsm_addr + 32u * w, w0, w8, v0, v8);
+            acc[w][0] = acc[w][1] = acc[w][2] = acc[w][3] = 0;
+            imma16832_s8(acc[w], w0, w8, v0, v8, st.b[w][0], st.b[w][1]);
+        }
+        const uint16_t *dg = reinterpret_cast<const uint16_t *>(hdr_g);
+        const uint16_t *dg8 = reinterpret_cast<const uint16_t *>(hdr_g8);
+        float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            // block 2j: windows 2j, 2j+1, even column (c0 row g, c2 row g+8)
+            const int e0 = acc[2 * j][0] + acc[2 * j + 1][0], e1 = acc[2 * j][2] + acc[2 * j + 1][2];
+            // block 2j+1: windows 2j+1, 2j+2, odd column (c1, c3)
+            const int o0 = acc[2 * j + 1][1] + acc[2 * j + 2][1], o1 = acc[2 * j + 1][3] + acc[2 * j + 2][3];
+            m0 = fmaf(__half2float(__ushort_as_half(dg[17 * (2 * j)])), float(e0), m0);
+            m0 = fmaf(__half2float(__ushort_as_half(dg[17 * (2 * j + 1)])), float(o0), m0);
+            m1 = fmaf(__half2float(__ushort_as_half(dg8[17 * (2 * j)])), float(e1), m1);
+            m1 = fmaf(__half2float(__ushort_as_half(dg8[17 * (2 * j + 1)])), float(o1), m1);
+        }
+        return make_float2(m0 * st.wt_inv, m1 * st.wt_inv);
+    }
+};
+
 // Tile row of MMA row r (0..15) of 16-row unit u: the unit's two 8-row
 // ldmatrix sets k = 2u, 2u+1 take P rows from each of the 8/P groups, so
 // their eight row addresses fall in eight distinct bank classes.
@@ -514,6 +656,9 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     uint64_t *pempty = pfull + 2;        // [2] reducer -> compute warps
     float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C0][RT]
     float *rowsum = part + size_t(2) * C0 * RT;            // [max_local_tiles][RT] when CS > 1
+    // Per compute warp scratch of the path (x digit images), 16-byte aligned.
+    uint8_t *scratch = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(rowsum + size_t(p.max_local_tiles) * RT * (CS > 1)) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = CS > 1 ? cluster_ctarank() : 0u;
@@ -593,9 +738,10 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         const bool has1 = SPW == 2 && sb1 < p.nsb_cta;
         const int gsb = int(crank) * p.nsb_cta;
         pdl_wait();  // x is produced by the previous kernel
-        Path::load(p.x, gsb + sb0, lane, st0);
+        uint8_t *my_scratch = scratch + size_t(warp) * Path::kScratchBytes;
+        Path::load(p.x, gsb + sb0, lane, st0, my_scratch);
         if constexpr (SPW == 2) {
-            if (has1) Path::load(p.x, gsb + sb1, lane, st1);
+            if (has1) Path::load(p.x, gsb + sb1, lane, st1, my_scratch);
         }
 
         const int g = lane >> 2, t = lane & 3;
@@ -608,7 +754,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         for (int q = 0; q < kUnits; ++q) {
             const int u = q * WPS + unit0;
             const int m = lane >> 3;
-            off_ldsm[q] = row_offset(p, unit_row(p, u, (m & 1) * 8 + (lane & 7))) + uint32_t(m >> 1) * 16u + 16u;
+            off_ldsm[q] = row_offset(p, unit_row(p, u, (m & 1) * 8 + (lane & 7))) + uint32_t(m >> 1) * 16u + Path::kQsOffset;
             row_g[q] = unit_row(p, u, g);
             row_g8[q] = unit_row(p, u, g + 8);
             off_g[q] = row_offset(p, row_g[q]);
@@ -626,11 +772,12 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             float2 acc[kUnits];
 #pragma unroll
             for (int q = 0; q < kUnits; ++q) {
-                acc[q] = Path::rows16(stage_addr + off_ldsm[q] + 144u * sb0, stage + off_g[q] + 144 * sb0,
-                                      stage + off_g8[q] + 144 * sb0, lane, st0);
+                constexpr uint32_t CB = Path::kColBytes;
+                acc[q] = Path::rows16(stage_addr + off_ldsm[q] + CB * sb0, stage + off_g[q] + CB * sb0,
+                                      stage + off_g8[q] + CB * sb0, lane, st0);
                 if (SPW == 2 && has1) {
-                    const float2 a1 = Path::rows16(stage_addr + off_ldsm[q] + 144u * sb1, stage + off_g[q] + 144 * sb1,
-                                                   stage + off_g8[q] + 144 * sb1, lane, st1);
+                    const float2 a1 = Path::rows16(stage_addr + off_ldsm[q] + CB * sb1, stage + off_g[q] + CB * sb1,
+                                                   stage + off_g8[q] + CB * sb1, lane, st1);
                     acc[q].x += a1.x, acc[q].y += a1.y;
                 }
             }
@@ -729,23 +876,36 @@ constexpr int kMaxBudgetKb = 226;
 // superblock warps keep the x fragments in registers without spilling.
 // (Measured on the Phi-4-mini shapes: splitting K = 3072 halves the compute
 // warps per SM and loses; K = 8192 split in two gains about 10%.)
-Shape default_shape(int64_t rows, int nsb, int sms) {
+Shape default_shape(int64_t rows, int nsb, int sms, int path) {
     (void)rows;
     (void)sms;
     int cs = 1;
-    while (cs < 4 && nsb / cs > kMaxComputeWarps && nsb % (2 * cs) == 0) cs *= 2;
-    return {cs, 32, kMaxBudgetKb, 1, 1, 0};
+    if (nsb > kMaxComputeWarps) {
+        cs = 0;
+        for (int c = 2; c <= 8 && !cs; ++c)
+            if (nsb % c == 0 && nsb / c <= kMaxComputeWarps) cs = c;
+        if (!cs) cs = 1;  // two superblocks per warp
+    }
+    return {cs, 32, kMaxBudgetKb, path, 1, 0};
 }
 
-bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, size_t &smem, int &rt) {
+// path: 0 FP16 / 1 INT8 (Q4_K), 2 Q8_0. col_bytes: bytes of 256 elements;
+// scratch_bytes: per compute warp scratch of the path.
+bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint32_t col_bytes,
+              uint32_t scratch_bytes, MmaParams &p, size_t &smem, int &rt) {
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int nsb = int(cols / 256);
-    Shape sh = default_shape(rows, nsb, sms);
+    Shape sh = default_shape(rows, nsb, sms, path);
     Shape o;
-    if (shape_override(o) && (o.cluster == 1 || o.cluster == 2 || o.cluster == 4) && (o.rt == 16 || o.rt == 32) &&
-        o.budget_kb >= 32 && o.budget_kb <= kMaxBudgetKb && (o.path == 0 || o.path == 1) && (o.wps == 1 || o.wps == 2))
-        sh = o;
+    if (shape_override(o) && o.cluster >= 1 && o.cluster <= 8 && (o.rt == 16 || o.rt == 32) &&
+        o.budget_kb >= 32 && o.budget_kb <= kMaxBudgetKb && (o.wps == 1 || o.wps == 2)) {
+        const int opath = path == 2 ? 2 : o.path;
+        if (opath == path || (path != 2 && (opath == 0 || opath == 1))) {
+            sh = o;
+            sh.path = opath;
+        }
+    }
     if (nsb % sh.cluster != 0) sh.cluster = 1;
     const size_t budget = size_t(sh.budget_kb) * 1024;
     for (;;) {
@@ -757,13 +917,14 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
         p.spw = nsb_cta > kMaxComputeWarps ? 2 : 1;
         const int columns = (nsb_cta + p.spw - 1) / p.spw;
         rt = sh.rt;
-        p.row_bytes = uint32_t(144 * nsb);
-        p.cta_bytes = uint32_t(144 * nsb_cta);
+        p.row_bytes = col_bytes * uint32_t(nsb);
+        p.cta_bytes = col_bytes * uint32_t(nsb_cta);
         // Row stride / 16 odd: ldmatrix's 8 row addresses hit 8 distinct bank quads.
         p.row_stride = p.cta_bytes + ((nsb_cta % 2 == 0) ? 16u : 32u);
         // Fall back to 16-row tiles when 32-row tiles leave fewer than 3 stages.
         if (rt == 32 && size_t(32) * p.row_stride * 3 > budget) rt = 16;
         p.wps = (sh.wps == 2 && sh.path == 1 && p.spw == 1 && rt == 32 && 2 * columns <= kMaxWps2Warps) ? 2 : 1;
+        const size_t scratch = size_t(columns) * p.wps * scratch_bytes;
         p.compute_warps = columns * p.wps;
         if (p.cluster == 1) {
             // Whole rows are contiguous: copy groups of rows. A row is
@@ -801,7 +962,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, MmaParams &p, 
             sh.cluster = 1;
             continue;
         }
-        const size_t tail = size_t(2) * columns * rt * sizeof(float) + rowsum;
+        const size_t tail = size_t(2) * columns * rt * sizeof(float) + rowsum + (scratch ? scratch + 16 : 0);
         const size_t bars = size_t(2 * 8 + 4) * sizeof(uint64_t);
         if (budget < tail + bars + 2 * size_t(p.stage_bytes)) {
             if (sh.cluster == 1) return false;
@@ -824,12 +985,19 @@ using namespace si::dev;
 
 // Returns SI_ERR_UNSUPPORTED (without touching the error string) when the
 // shape needs the SIMT kernel instead.
-si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream) {
+// Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
+// (without touching the error string) when the shape needs the SIMT kernel.
+si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                           void *stream) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
+    const bool q8 = wtype == SI_TYPE_Q8_0;
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
     const int sms = num_sms();
-    if (!plan_mma(rows, cols, w, sms, p, smem, rt)) return SI_ERR_UNSUPPORTED;
+    if (!plan_mma(rows, cols, w, sms, q8 ? 2 : 1, q8 ? Q8Path::kColBytes : I8Path::kColBytes,
+                  q8 ? Q8Path::kScratchBytes : 0u, p, smem, rt))
+        return SI_ERR_UNSUPPORTED;
     p.w = static_cast<const uint8_t *>(w);
     p.x = x;
     p.y = y;
@@ -839,7 +1007,8 @@ si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, 
       {gemv_mma_q4k_kernel<P, 1, 16, 1, 16>, gemv_mma_q4k_kernel<P, 1, 32, 1, 16>}},       \
      {{gemv_mma_q4k_kernel<P, 2, 16, 1, 16>, gemv_mma_q4k_kernel<P, 2, 32, 1, 16>},        \
       {gemv_mma_q4k_kernel<P, 2, 16, 1, 16>, gemv_mma_q4k_kernel<P, 2, 32, 1, 16>}}}
-    static const Kernel kernels[2][2][2][2] = {SI_GEMV_KERNELS(F16Path), SI_GEMV_KERNELS(I8Path)};
+    static const Kernel kernels[3][2][2][2] = {SI_GEMV_KERNELS(F16Path), SI_GEMV_KERNELS(I8Path),
+                                               SI_GEMV_KERNELS(Q8Path)};
 #undef SI_GEMV_KERNELS
     static const Kernel kernel_wps2 = gemv_mma_q4k_kernel<I8Path, 1, 32, 2, kMaxWps2Warps>;
     const Kernel kernel = p.wps == 2 ? kernel_wps2
@@ -871,7 +1040,8 @@ si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, 
     cfg.numAttrs = p.cluster > 1 ? 2 : 1;
     const cudaError_t le = cudaLaunchKernelEx(&cfg, kernel, p);
     const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
-    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "tensor-core Q4_K GEMV launch failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess)
+        return fail(SI_ERR_CUDA, "tensor-core %s GEMV launch failed: %s", q8 ? "Q8_0" : "Q4_K", cudaGetErrorString(e));
     return SI_OK;
 }
 

@@ -62,5 +62,6 @@ si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64
 si_status take_error_gemv(int device, uint32_t *code);
 si_status take_error_gemm(int device, uint32_t *code);
 si_status take_error_gemv_mma(int device, uint32_t *code);
-si_status matvec_q4k_mma(const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream);
+si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                           void *stream);
 }  // namespace si::kernels

@@ -1,5 +1,5 @@
-"""Every launch shape of the tensor-core Q4_K GEMV (K split over 1/2/4-CTA
-clusters, 16/32-row tiles, full or half shared-memory ring, FP16 or INT8
+"""Every launch shape of the tensor-core Q4_K and Q8_0 GEMV (K split over
+1/2/4-CTA clusters, 16/32-row tiles, full or half shared-memory ring, FP16 or INT8
 MMA path, one or two warps per superblock column) against the
 oracle on ragged shapes. The shape is forced through SI_Q4K_GEMV_PLAN, which
 the library reads once per process, so each plan runs in a child process."""
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 CHILD = Path(__file__).resolve().parent / "gemv_plan_child.py"
 PLANS = ["default", "1,16,100", "1,32,220", "2,16,100", "2,32,220", "4,16,100", "4,32,64",
          "1,16,100,1", "1,32,220,1", "2,16,100,1", "2,32,220,1", "4,32,64,1", "1,32,226,1,2", "2,32,226,1,2",
-         "4,32,120,1,2"]
+         "4,32,120,1,2", "3,16,226", "5,32,226", "8,16,160"]
 
 
 @pytest.mark.parametrize("plan", PLANS)
