@@ -30,6 +30,8 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
+#include <vector>
 
 #include "device_common.cuh"
 #include "si_internal.h"
@@ -891,8 +893,10 @@ Shape default_shape(int64_t rows, int nsb, int sms, int path) {
 
 // path: 0 FP16 / 1 INT8 (Q4_K), 2 Q8_0. col_bytes: bytes of 256 elements;
 // scratch_bytes: per compute warp scratch of the path.
+// group_cap > 0 limits the clusters (CTAs) of the grid to what can be
+// resident at once.
 bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint32_t col_bytes,
-              uint32_t scratch_bytes, MmaParams &p, size_t &smem, int &rt) {
+              uint32_t scratch_bytes, int group_cap, MmaParams &p, size_t &smem, int &rt) {
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int nsb = int(cols / 256);
@@ -955,6 +959,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint
         // One CTA per SM at most: a cluster of CS CTAs takes CS SMs.
         p.groups = std::max(1, std::min(p.num_tiles, sms / p.cluster));
         if (sh.max_groups > 0) p.groups = std::min(p.groups, sh.max_groups);
+        if (group_cap > 0) p.groups = std::min(p.groups, group_cap);
         p.max_local_tiles = (p.num_tiles + p.groups - 1) / p.groups;
         const size_t rowsum = p.cluster > 1 ? size_t(p.max_local_tiles) * rt * sizeof(float) : 0;
         // The K split is for small matrices: the row sums it keeps must stay small.
@@ -985,6 +990,47 @@ using namespace si::dev;
 
 // Returns SI_ERR_UNSUPPORTED (without touching the error string) when the
 // shape needs the SIMT kernel instead.
+// Clusters of `cluster` CTAs of `kernel` that fit on the device at once
+// (GPC boundaries leave SMs unusable for some cluster sizes); cached.
+int max_active_clusters(void (*kernel)(MmaParams), int cluster, int threads, size_t smem) {
+    struct Entry {
+        int device;
+        void (*kernel)(MmaParams);
+        int cluster, threads;
+        size_t smem;
+        int value;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> g(mu);
+        for (const Entry &e : cache)
+            if (e.device == dev && e.kernel == kernel && e.cluster == cluster && e.threads == threads && e.smem == smem)
+                return e.value;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(cluster));
+    cfg.blockDim = dim3(unsigned(threads));
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = unsigned(cluster);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    cache.push_back({dev, kernel, cluster, threads, smem, n});
+    return n;
+}
+
 // Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
 // (without touching the error string) when the shape needs the SIMT kernel.
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
@@ -995,12 +1041,6 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     size_t smem = 0;
     int rt = 0;
     const int sms = num_sms();
-    if (!plan_mma(rows, cols, w, sms, q8 ? 2 : 1, q8 ? Q8Path::kColBytes : I8Path::kColBytes,
-                  q8 ? Q8Path::kScratchBytes : 0u, p, smem, rt))
-        return SI_ERR_UNSUPPORTED;
-    p.w = static_cast<const uint8_t *>(w);
-    p.x = x;
-    p.y = y;
     using Kernel = void (*)(MmaParams);
 #define SI_GEMV_KERNELS(P)                                                                  \
     {{{gemv_mma_q4k_kernel<P, 1, 16, 1, 12>, gemv_mma_q4k_kernel<P, 1, 32, 1, 12>},        \
@@ -1011,17 +1051,33 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
                                                SI_GEMV_KERNELS(Q8Path)};
 #undef SI_GEMV_KERNELS
     static const Kernel kernel_wps2 = gemv_mma_q4k_kernel<I8Path, 1, 32, 2, kMaxWps2Warps>;
-    const Kernel kernel = p.wps == 2 ? kernel_wps2
-                                     : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
-    static bool attr = false;
-    if (!attr) {
+    static std::once_flag attr_once;
+    std::call_once(attr_once, [] {
         for (auto &a : kernels)
             for (auto &b : a)
                 for (auto &c : b)
                     for (Kernel k : c) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         cudaFuncSetAttribute(kernel_wps2, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        attr = true;
+    });
+    // Plan; with a K split, shrink the grid to the clusters that can be
+    // resident together (one wave) and plan again.
+    Kernel kernel = nullptr;
+    int cap = 0;
+    for (int attempt = 0; attempt < 4; ++attempt) {
+        if (!plan_mma(rows, cols, w, sms, q8 ? 2 : 1, q8 ? Q8Path::kColBytes : I8Path::kColBytes,
+                      q8 ? Q8Path::kScratchBytes : 0u, cap, p, smem, rt))
+            return SI_ERR_UNSUPPORTED;
+        kernel = p.wps == 2 ? kernel_wps2
+                            : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
+        if (p.cluster == 1) break;
+        const int fit = max_active_clusters(kernel, p.cluster, (p.compute_warps + 2) * 32, smem);
+        if (fit <= 0) return SI_ERR_UNSUPPORTED;
+        if (p.groups <= fit) break;
+        cap = fit;
     }
+    p.w = static_cast<const uint8_t *>(w);
+    p.x = x;
+    p.y = y;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
