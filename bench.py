@@ -36,6 +36,9 @@ sys.path.insert(0, str(ROOT))
 SHAPES = [("qkv", 5120, 3072, 0), ("o", 3072, 3072, 1), ("gate_up", 16384, 3072, 2), ("down", 3072, 8192, 3),
           ("lm_head", 200064, 3072, 4)]
 WTYPE = 12  # Q4_K
+# Secondary (1 GPU only): Q8_0 GEMV on config 1 and the Phi-4-14B decode shapes of config 5.
+Q8_SHAPES = [("config1", 8192, 3072, 0), ("qkv_14b", 7680, 5120, 11), ("o_14b", 5120, 5120, 12),
+             ("gate_up_14b", 35840, 5120, 13), ("down_14b", 5120, 17920, 14), ("lm_head_14b", 100352, 5120, 15)]
 METRIC = "quant GEMV weight GB/s (Q4_K batch-1 sweep, Phi-4-mini shapes)"
 WORKLOAD = "config2 Q4_K batch-1 GEMV sweep (Phi-4-mini qkv/o/gate_up/down/lm_head)"
 FALLBACK_HBM_GBS = 6650.0
@@ -187,6 +190,9 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+L2_ROTATE_BYTES = 384 << 20  # per-shape timing cycles through this many bytes of weight copies (3x L2)
+
+
 class Sweep:
     """Device-resident state of one rank: its row shard of every weight, the
     input vectors and the (gathered) output vectors."""
@@ -205,15 +211,29 @@ class Sweep:
             X = ctx.buffer(k * 4)
             X.upload(x)
             Y = ctx.buffer(4 * (per * world if world > 1 else n))
-            self.items.append(dict(name=name, n=n, k=k, rows_local=rows_local, W=W, X=X, Y=Y, x=x, per=per))
+            self.items.append(dict(name=name, n=n, k=k, rows_local=rows_local, W=W, X=X, Y=Y, x=x, per=per,
+                                   blob=blob, copies=[W]))
 
-    def launch(self, i: int) -> None:
+    def add_copies(self, i: int) -> None:
+        """Extra copies of weight i so that back-to-back launches cycle
+        through more bytes than L2 holds (each launch reads cold weights)."""
         it = self.items[i]
+        if it["blob"] is None:
+            return
+        want = min(64, max(1, -(-L2_ROTATE_BYTES // it["blob"].nbytes)))
+        while len(it["copies"]) < want:
+            Wc = self.ctx.buffer(it["blob"].nbytes)
+            Wc.upload(it["blob"])
+            it["copies"].append(Wc)
+
+    def launch(self, i: int, W=None, X=None, x_off: int = 0, Y=None, y_off: int = 0) -> None:
+        it = self.items[i]
+        W, X, Y = W or it["W"], X or it["X"], Y or it["Y"]
         if self.world == 1:
-            self.ctx.matvec(WTYPE, it["W"], it["X"], it["Y"], it["n"], it["k"])
+            self.ctx.matvec(WTYPE, W, X, Y, it["n"], it["k"], input_offset=x_off, output_offset=y_off)
         else:
-            self.comm.rowshard_matvec_allgather(WTYPE, it["W"].device_pointer, it["X"].device_pointer,
-                                                it["Y"].device_pointer, it["n"], it["k"], self.ctx.stream)
+            self.comm.rowshard_matvec_allgather(WTYPE, W.device_pointer, X.device_pointer + x_off,
+                                                Y.device_pointer + y_off, it["n"], it["k"], self.ctx.stream)
 
     def step(self) -> None:
         for i in range(len(self.items)):
@@ -288,19 +308,26 @@ def run_ours(args) -> None:
     clocks = sampler.summary()
     value = bytes_step * args.steps / (total_ms * 1e-3) / 1e9
 
-    # Per shape: back-to-back launches of that shape alone.
+    # Per shape: back-to-back launches of that shape alone, cycling through
+    # weight copies larger than L2 so that every launch reads cold weights.
     peak, peak_src = measured_peak()
     per_shape = {}
-    reps = 10
     graphs = [step_graph]
     for i, it in enumerate(sweep.items):
-        g = ctx.record(lambda i=i: [sweep.launch(i) for _ in range(reps)])
+        sweep.add_copies(i)
+        copies = it["copies"]
+        reps = max(10, len(copies))
+        g = ctx.record(lambda i=i, copies=copies, reps=reps: [sweep.launch(i, W=copies[r % len(copies)])
+                                                               for r in range(reps)])
         graphs.append(g)
         g.launch()
         ms = timed(g.launch, 5) / (5 * reps)
         b = shape_bytes(it["n"], it["k"])
         per_shape[it["name"]] = {"us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
-                                 "frac": round(b / (ms * 1e-3) / 1e9 / (peak * world), 3)}
+                                 "frac": round(b / (ms * 1e-3) / 1e9 / (peak * world), 3), "weight_copies": len(copies)}
+        for Wc in copies[1:]:
+            Wc.free()
+        it["copies"] = [it["W"]]
 
     # Dominant kernel: every launch of the step is the tensor-core Q4_K GEMV;
     # algorithmic bytes this rank moves per launch / average launch time.
@@ -309,23 +336,31 @@ def run_ours(args) -> None:
     achieved = rank_bytes / (total_ms / args.steps * 1e-3) / 1e9
     traffic = committed_traffic()
 
-    # e2e through the public C ABI with host buffers: x uploaded from pinned
-    # memory, the (gathered) y read back to pinned memory, every step.
-    pinned = []
+    # e2e through the public C ABI with host buffers, every step: the five
+    # inputs uploaded from one pinned host buffer in one copy, the five
+    # GEMVs (+ all-gathers), the (gathered) outputs read back into one pinned
+    # host buffer in one copy.
+    def align(v: int) -> int:
+        return (v + 255) // 256 * 256
+
+    x_off, y_off, xo, yo = [], [], 0, 0
     for it in sweep.items:
-        px, py = C.c_void_p(), C.c_void_p()
-        ny = it["n"]
-        native.call("si_host_alloc_pinned", it["k"] * 4, C.byref(px))
-        native.call("si_host_alloc_pinned", ny * 4, C.byref(py))
-        C.memmove(px, it["x"].ctypes.data, it["k"] * 4)
-        pinned.append((px, py, ny))
+        x_off.append(xo)
+        y_off.append(yo)
+        xo = align(xo + 4 * it["k"])
+        yo = align(yo + 4 * (it["per"] * world if world > 1 else it["n"]))
+    X_all, Y_all = ctx.buffer(xo), ctx.buffer(yo)
+    px, py = C.c_void_p(), C.c_void_p()
+    native.call("si_host_alloc_pinned", xo, C.byref(px))
+    native.call("si_host_alloc_pinned", yo, C.byref(py))
+    for it, off in zip(sweep.items, x_off):
+        C.memmove(px.value + off, it["x"].ctypes.data, it["k"] * 4)
 
     def e2e_issue():
-        for i, it in enumerate(sweep.items):
-            px, py, ny = pinned[i]
-            native.call("si_buffer_upload_async", ctx.handle, it["X"].handle, 0, px, it["k"] * 4)
-            sweep.launch(i)
-            native.call("si_buffer_readback_async", ctx.handle, it["Y"].handle, 0, py, ny * 4)
+        native.call("si_buffer_upload_async", ctx.handle, X_all.handle, 0, px, xo)
+        for i in range(len(sweep.items)):
+            sweep.launch(i, X=X_all, x_off=x_off[i], Y=Y_all, y_off=y_off[i])
+        native.call("si_buffer_readback_async", ctx.handle, Y_all.handle, 0, py, yo)
 
     e2e_graph = ctx.record(e2e_issue)
     graphs.append(e2e_graph)
@@ -341,17 +376,38 @@ def run_ours(args) -> None:
     e2e_ms = timed(e2e_step, args.steps)
     wall_ms = max_over_ranks((time.perf_counter() - t0) * 1e3)
     e2e_value = bytes_step * args.steps / (max(e2e_ms, 1e-9) * 1e-3) / 1e9
-    h2d = sum(4 * k for _, n, k, _ in SHAPES)
-    d2h = sum(4 * n for _, n, k, _ in SHAPES)
-    # the last e2e result equals the device-resident result
-    it = sweep.items[-1]
-    y_dev = it["Y"].readback(it["n"] * 4).view(np.float32)
-    y_host = np.ctypeslib.as_array(C.cast(pinned[-1][1], C.POINTER(C.c_float)), shape=(it["n"],))
-    assert np.array_equal(y_dev, y_host)
-    for px, py, _ in pinned:
-        native.call("si_host_free_pinned", px)
-        native.call("si_host_free_pinned", py)
+    h2d, d2h = xo, yo
+    # the e2e results equal the device-resident results of the step
+    for i, it in enumerate(sweep.items):
+        y_dev = it["Y"].readback(it["n"] * 4).view(np.float32)
+        y_host = np.ctypeslib.as_array(C.cast(py.value + y_off[i], C.POINTER(C.c_float)), shape=(it["n"],))
+        assert np.array_equal(y_dev, y_host), it["name"]
+    native.call("si_host_free_pinned", px)
+    native.call("si_host_free_pinned", py)
 
+    q8 = None
+    if world == 1 and not args.no_q8:
+        q8 = {}
+        for name, n, k, seed in Q8_SHAPES:
+            blob = native.synth_weights(8, seed, n, k, 0.02)
+            copies = []
+            for _ in range(min(64, max(1, -(-L2_ROTATE_BYTES // blob.nbytes)))):
+                Wc = ctx.buffer(blob.nbytes)
+                Wc.upload(blob)
+                copies.append(Wc)
+            Xq, Yq = ctx.buffer(4 * k), ctx.buffer(4 * n)
+            Xq.upload(native.synth_normal(1000 + seed, k, 1.0))
+            reps = max(10, len(copies))
+            g = ctx.record(lambda copies=copies, Xq=Xq, Yq=Yq, n=n, k=k, reps=reps: [
+                ctx.matvec(8, copies[r % len(copies)], Xq, Yq, n, k) for r in range(reps)])
+            g.launch()
+            ms = timed(g.launch, 5) / (5 * reps)
+            b = n * k // 32 * 34 + 4 * k + 4 * n
+            q8[name] = {"n": n, "k": k, "us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
+                        "frac": round(b / (ms * 1e-3) / 1e9 / peak, 3), "weight_copies": len(copies)}
+            g.close()
+            for Wc in copies + [Xq, Yq]:
+                Wc.free()
     err = native.device_error_take(local)
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
@@ -375,6 +431,9 @@ def run_ours(args) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "wall_ms_per_step": round(wall_ms / args.steps, 4)},
             "gpu_launches": len(SHAPES) * args.steps,
+            "q8_0_gemv": q8 and {"workload": "Q8_0 GEMV, config 1 and the Phi-4-14B decode shapes of config 5 "
+                                             "(1 GPU; back-to-back launches cycling through weight copies > L2)",
+                                 "per_shape": q8},
             "clocks": clocks,
             "device_error_word": err,
         }
@@ -397,6 +456,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-q8", action="store_true", help="skip the secondary Q8_0 GEMV measurements")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
