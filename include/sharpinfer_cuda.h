@@ -168,6 +168,33 @@ si_status si_rowshard_matvec_allgather(si_comm *comm, uint32_t weight_type, cons
                                        const float *input, float *output_full, int64_t rows, int64_t cols,
                                        void *stream);
 
+/* Fused alternative (no collective launch): row-sharded GEMV whose kernel
+ * stores every output row straight into all ranks' "arenas" over NVLink peer
+ * memory. An arena is a device buffer per rank, exported with
+ * si_ipc_export, mapped by every other rank with si_ipc_open (CUDA IPC, one
+ * process per GPU), at least 4 KB + the output vectors; its last 4 KB hold
+ * the group's flags. Create the group on every rank, then synchronise the
+ * ranks (host barrier) before the first call. si_rowshard_matvec_peer: rank r
+ * computes its rows (si_rowshard_plan; every rank must get at least one row)
+ * and, when the call completes in stream order, every rank's arena holds the
+ * whole y[rows] at byte `output_offset` (16-byte aligned). The kernel's last
+ * CTA waits, bounded by 2 s, for every rank's rows; a rank that never
+ * arrives sets bit 16 of the device error word instead of hanging. Two
+ * consecutive calls must use different output offsets (a rank can run one
+ * call ahead of another). Q4_K and Q8_0 weights on the tensor-core path. */
+typedef struct si_peer_group si_peer_group;
+si_status si_ipc_export(const void *device_ptr, uint8_t *handle, size_t capacity);  /* 64-byte handle */
+si_status si_ipc_open(int device, const uint8_t *handle, void **ptr);
+si_status si_ipc_close(int device, void *ptr);
+/* arena_addrs[q]: rank q's arena as mapped in this process (this rank's own
+ * buffer at q = rank); every arena has arena_bytes bytes. */
+si_status si_peer_group_create(int device, int nranks, int rank, const uint64_t *arena_addrs, uint64_t arena_bytes,
+                               si_peer_group **out);
+si_status si_peer_group_destroy(si_peer_group *group);
+si_status si_rowshard_matvec_peer(si_peer_group *group, uint32_t weight_type, const void *weight_shard,
+                                  const float *input, uint64_t output_offset, int64_t rows, int64_t cols,
+                                  void *stream);
+
 /* ---------------------------------------------------------------------- */
 /* Executor: device buffers per slot, uploads/readbacks and stream        */
 /* (D3D12VmExecutor.cs:283-361,452-482 Upload / Readback / Execute /     */

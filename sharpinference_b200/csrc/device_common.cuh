@@ -17,6 +17,7 @@ enum : uint32_t {
     kErrEmptyBarrierTimeout = 2u,
     kErrMmaBarrierTimeout = 4u,
     kErrEpilogueTimeout = 8u,
+    kErrPeerTimeout = 16u,  // a row-sharded GEMV's rank never published its rows
 };
 static __device__ uint32_t g_error_word;
 

@@ -46,6 +46,7 @@ struct MmaParams {
     const uint8_t *w;
     const float *x;
     float *y;
+    kernels::PeerGather peer;  // nranks == 0: plain GEMV into y
     int rows;
     int nsb;              // superblocks per row (K / 256)
     int cluster;          // CTAs per cluster = K split (1, 2 or 4)
@@ -102,6 +103,56 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
 }
+// Output row store: into y, or (row-sharded GEMV) into every rank's output
+// vector at this rank's row offset, over NVLink for the peers.
+__device__ __forceinline__ void store_y(const MmaParams &p, int row, float v) {
+    if (p.peer.nranks == 0) {
+        p.y[row] = v;
+        return;
+    }
+    const int64_t gr = p.peer.row_base + row;
+#pragma unroll
+    for (int q = 0; q < kernels::kMaxPeerRanks; ++q)
+        if (q < p.peer.nranks) p.peer.ys[q][gr] = v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// End of a row-sharded GEMV: the last CTA of this rank (ticket) publishes
+// epoch e to every rank's flag slot of this rank, then waits (bounded) until
+// every rank has published e here, so the output vector is complete when
+// the kernel completes. Every thread fenced its output stores at system
+// scope before the CTA barrier that precedes the ticket.
+__device__ __forceinline__ void peer_handshake(const MmaParams &p) {
+    const kernels::PeerGather &g = p.peer;
+    const uint32_t t = atomicAdd(g.ticket, 1u);
+    if (t != gridDim.x - 1) return;
+    __threadfence_system();
+    *g.ticket = 0u;  // every CTA of this launch has taken its ticket
+    const uint32_t e = *reinterpret_cast<volatile uint32_t *>(g.epoch) + 1u;
+    for (int q = 0; q < g.nranks; ++q) st_release_sys(g.flags[q] + g.rank, e);
+    const uint32_t *mine = g.flags[g.rank];
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < g.nranks; ++q) {
+        uint32_t polls = 0;
+        while (int32_t(ld_acquire_sys(mine + q) - e) < 0) {
+            if (++polls > kMaxPolls || globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_error_word, kErrPeerTimeout);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    *reinterpret_cast<volatile uint32_t *>(g.epoch) = e;
+}
+
 // Every thread of every CTA of the cluster (hardware barrier).
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
@@ -723,7 +774,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             if (lane < nrows)
                 for (int c = 0; c < C0; ++c) a += pb[c * RT + lane];
             if (CS == 1) {
-                if (lane < nrows) p.y[r0 + lane] = a;
+                if (lane < nrows) store_y(p, r0 + lane, a);
             } else if (lane < RT) {
                 rowsum[it * RT + lane] = a;
             }
@@ -814,10 +865,15 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             if (row < p.rows) {
                 float a = 0.0f;
                 for (int k = 0; k < CS; ++k) a += ld_cluster_f32(mapa_shared(base + 4u * uint32_t(i), uint32_t(k)));
-                p.y[row] = a;
+                store_y(p, row, a);
             }
         }
         cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
+    }
+    if (p.peer.nranks > 0) {
+        __threadfence_system();  // this thread's output stores, before the ticket
+        __syncthreads();
+        if (threadIdx.x == 0) peer_handshake(p);
     }
 }
 
@@ -1034,7 +1090,7 @@ int max_active_clusters(void (*kernel)(MmaParams), int cluster, int threads, siz
 // Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
 // (without touching the error string) when the shape needs the SIMT kernel.
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream) {
+                           void *stream, const PeerGather *peer) {
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     const bool q8 = wtype == SI_TYPE_Q8_0;
     MmaParams p{};
@@ -1078,6 +1134,7 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     p.w = static_cast<const uint8_t *>(w);
     p.x = x;
     p.y = y;
+    if (peer) p.peer = *peer;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));

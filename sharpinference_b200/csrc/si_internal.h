@@ -62,6 +62,17 @@ si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64
 si_status take_error_gemv(int device, uint32_t *code);
 si_status take_error_gemm(int device, uint32_t *code);
 si_status take_error_gemv_mma(int device, uint32_t *code);
+// Row-sharded output exchange of a fused GEMV (see si_rowshard_matvec_peer).
+constexpr int kMaxPeerRanks = 8;
+struct PeerGather {
+    float *ys[kMaxPeerRanks];         // every rank's output vector, as mapped in this process
+    uint32_t *flags[kMaxPeerRanks];   // every rank's flag array [nranks]
+    uint32_t *ticket;                 // this rank's CTA ticket counter
+    uint32_t *epoch;                  // this rank's call counter
+    int nranks;                       // 0: not a sharded call
+    int rank;
+    int64_t row_base;                 // global index of this rank's first row
+};
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream);
+                           void *stream, const PeerGather *peer = nullptr);
 }  // namespace si::kernels

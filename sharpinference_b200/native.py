@@ -110,6 +110,12 @@ SIGNATURES = {
     "si_comm_create": [_i32, _i32, _i32, _vp, _i32, C.POINTER(_vp)],
     "si_comm_destroy": [_vp],
     "si_rowshard_matvec_allgather": [_vp, _u32, _vp, _vp, _vp, _i64, _i64, _vp],
+    "si_ipc_export": [_vp, _vp, C.c_size_t],
+    "si_ipc_open": [_i32, _vp, C.POINTER(_vp)],
+    "si_ipc_close": [_i32, _vp],
+    "si_peer_group_create": [_i32, _i32, _i32, C.POINTER(C.c_uint64), C.c_uint64, C.POINTER(_vp)],
+    "si_peer_group_destroy": [_vp],
+    "si_rowshard_matvec_peer": [_vp, _u32, _vp, _vp, C.c_uint64, _i64, _i64, _vp],
     "si_graph_begin": [_vp],
     "si_graph_end": [_vp, C.POINTER(_vp)],
     "si_graph_launch": [_vp, _vp],
@@ -198,6 +204,45 @@ class Comm:
     def close(self):
         if self.handle:
             call("si_comm_destroy", self.handle)
+            self.handle = None
+
+
+def ipc_export(device_ptr: int) -> bytes:
+    """64-byte CUDA IPC handle of a device allocation (e.g. Buffer.device_pointer)."""
+    buf = (C.c_uint8 * 64)()
+    call("si_ipc_export", C.c_void_p(device_ptr), buf, 64)
+    return bytes(buf)
+
+
+def ipc_open(device: int, handle: bytes) -> int:
+    arr = (C.c_uint8 * 64).from_buffer_copy(handle)
+    p = C.c_void_p()
+    call("si_ipc_open", device, arr, C.byref(p))
+    return p.value
+
+
+def ipc_close(device: int, ptr: int) -> None:
+    call("si_ipc_close", device, C.c_void_p(ptr))
+
+
+class PeerGroup:
+    """Row-sharded GEMV whose kernel writes every rank's output arena over
+    NVLink (si_rowshard_matvec_peer). arena_addrs[q] is rank q's arena as
+    mapped in this process."""
+
+    def __init__(self, device: int, nranks: int, rank: int, arena_addrs, arena_bytes: int):
+        addrs = (C.c_uint64 * nranks)(*arena_addrs)
+        h = C.c_void_p()
+        call("si_peer_group_create", device, nranks, rank, addrs, arena_bytes, C.byref(h))
+        self.handle, self.nranks, self.rank = h, nranks, rank
+
+    def rowshard_matvec(self, wtype, weight_shard_ptr, x_ptr, output_offset, rows, cols, stream):
+        call("si_rowshard_matvec_peer", self.handle, wtype, C.c_void_p(weight_shard_ptr), C.c_void_p(x_ptr),
+             output_offset, rows, cols, C.c_void_p(stream))
+
+    def close(self):
+        if self.handle:
+            call("si_peer_group_destroy", self.handle)
             self.handle = None
 
 
