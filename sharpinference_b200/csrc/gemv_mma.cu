@@ -116,8 +116,8 @@ __device__ __forceinline__ void store_y(const MmaParams &p, int row, float v) {
         if (q < p.peer.nranks) p.peer.ys[q][gr] = v;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *addr, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *addr) {
     uint32_t v;
@@ -128,8 +128,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *addr) {
 // End of a row-sharded GEMV: the last CTA of this rank (ticket) publishes
 // epoch e to every rank's flag slot of this rank, then waits (bounded) until
 // every rank has published e here, so the output vector is complete when
-// the kernel completes. Every thread fenced its output stores at system
-// scope before the CTA barrier that precedes the ticket.
+// the kernel completes. The warp that stored output rows fenced them at
+// system scope before the CTA barrier that precedes the ticket; one more
+// system fence after the ticket orders all CTAs' rows before the flags
+// (a system fence with remote stores in flight costs ~3 us on NVLink, so
+// only the storing warp and the publishing thread fence).
 __device__ __forceinline__ void peer_handshake(const MmaParams &p) {
     const kernels::PeerGather &g = p.peer;
     const uint32_t t = atomicAdd(g.ticket, 1u);
@@ -137,7 +140,7 @@ __device__ __forceinline__ void peer_handshake(const MmaParams &p) {
     __threadfence_system();
     *g.ticket = 0u;  // every CTA of this launch has taken its ticket
     const uint32_t e = *reinterpret_cast<volatile uint32_t *>(g.epoch) + 1u;
-    for (int q = 0; q < g.nranks; ++q) st_release_sys(g.flags[q] + g.rank, e);
+    for (int q = 0; q < g.nranks; ++q) st_relaxed_sys(g.flags[q] + g.rank, e);
     const uint32_t *mine = g.flags[g.rank];
     const uint64_t t0 = globaltimer_ns();
     for (int q = 0; q < g.nranks; ++q) {
@@ -859,7 +862,9 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         cluster_sync_all();  // every CTA's row sums are complete and visible to the cluster
         const int local_tiles = first_tile < p.num_tiles ? (p.num_tiles - 1 - first_tile) / tile_step + 1 : 0;
         const uint32_t base = smem_u32(rowsum);
-        for (int i = int(crank) * blockDim.x + threadIdx.x; i < local_tiles * RT; i += CS * blockDim.x) {
+        // The reducer warps of the cluster finish the rows (one warp per CTA
+        // stores, so only it has output stores to fence on a sharded call).
+        for (int i = warp == C + 1 ? int(crank) * 32 + lane : local_tiles * RT; i < local_tiles * RT; i += CS * 32) {
             const int li = i / RT, r = i - li * RT;
             const int row = (first_tile + li * tile_step) * RT + r;
             if (row < p.rows) {
@@ -871,7 +876,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
     }
     if (p.peer.nranks > 0) {
-        __threadfence_system();  // this thread's output stores, before the ticket
+        if (warp == C + 1) __threadfence_system();  // the output stores of the reducer warp, before the ticket
         __syncthreads();
         if (threadIdx.x == 0) peer_handshake(p);
     }
