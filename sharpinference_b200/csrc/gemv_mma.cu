@@ -47,6 +47,8 @@ struct MmaParams {
     const float *x;
     float *y;
     kernels::PeerGather peer;  // nranks == 0: plain GEMV into y
+    const int32_t *control;    // batch-shared: y is written only when token < control[1]
+    int token;
     int rows;
     int nsb;              // superblocks per row (K / 256)
     int cluster;          // CTAs per cluster = K split (1, 2 or 4)
@@ -106,6 +108,7 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
 // Output row store: into y, or (row-sharded GEMV) into every rank's output
 // vector at this rank's row offset, over NVLink for the peers.
 __device__ __forceinline__ void store_y(const MmaParams &p, int row, float v) {
+    if (p.control && p.token >= p.control[1]) return;  // read after the dependency wait
     if (p.peer.nranks == 0) {
         p.y[row] = v;
         return;
@@ -1095,7 +1098,7 @@ int max_active_clusters(void (*kernel)(MmaParams), int cluster, int threads, siz
 // Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
 // (without touching the error string) when the shape needs the SIMT kernel.
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream, const PeerGather *peer) {
+                           void *stream, const PeerGather *peer, const int32_t *control, int token) {
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     const bool q8 = wtype == SI_TYPE_Q8_0;
     MmaParams p{};
@@ -1140,6 +1143,8 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     p.x = x;
     p.y = y;
     if (peer) p.peer = *peer;
+    p.control = control;
+    p.token = token;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));

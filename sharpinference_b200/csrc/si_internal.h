@@ -73,6 +73,8 @@ struct PeerGather {
     int rank;
     int64_t row_base;                 // global index of this rank's first row
 };
+// control/token: batch-shared use, y is written only when token < control[1].
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream, const PeerGather *peer = nullptr);
+                           void *stream, const PeerGather *peer = nullptr, const int32_t *control = nullptr,
+                           int token = 0);
 }  // namespace si::kernels

@@ -164,6 +164,16 @@ using namespace si::dev;
 si_status shared_weight_matvec(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y,
                                int64_t m, int64_t n, int64_t k, void *stream) {
     auto st = static_cast<cudaStream_t>(stream);
+    // Quantised weights: one tensor-core GEMV per input row (the weights are
+    // re-read per row, from L2 when they fit, which still beats the SIMT
+    // kernel by an order of magnitude). Rows at or past control[1] are not
+    // written (the check runs on the device, after the dependency wait).
+    if ((wtype == SI_TYPE_Q4_K || wtype == SI_TYPE_Q8_0) && m <= 1024) {
+        si_status ms = SI_OK;
+        for (int64_t b = 0; b < m && ms == SI_OK; ++b)
+            ms = matvec_quant_mma(wtype, w, x + b * k, y + b * n, n, k, stream, nullptr, control, int(b));
+        if (ms != SI_ERR_UNSUPPORTED) return ms;  // the first call decides: the shape is the same for every row
+    }
     switch (wtype) {
     case SI_TYPE_F32: return launch_shared<SI_TYPE_F32>(w, x, y, control, m, n, k, st);
     case SI_TYPE_F16: return launch_shared<SI_TYPE_F16>(w, x, y, control, m, n, k, st);
