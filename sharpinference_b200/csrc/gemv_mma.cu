@@ -48,7 +48,10 @@ struct MmaParams {
     float *y;
     kernels::PeerGather peer;  // nranks == 0: plain GEMV into y
     const int32_t *control;    // batch-shared: y is written only when token < control[1]
-    int token;
+    int token;                 // index of this launch's first input row (batched: of its 8 rows)
+    int ntok;                  // batched paths: input rows in this launch (<= 8)
+    int64_t x_stride;          // batched paths: floats between input rows (K)
+    int64_t y_stride;          // batched paths: floats between output rows (N)
     int rows;
     int nsb;              // superblocks per row (K / 256)
     int cluster;          // CTAs per cluster = K split (1, 2 or 4)
@@ -107,10 +110,10 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
 }
 // Output row store: into y, or (row-sharded GEMV) into every rank's output
 // vector at this rank's row offset, over NVLink for the peers.
-__device__ __forceinline__ void store_y(const MmaParams &p, int row, float v) {
-    if (p.control && p.token >= p.control[1]) return;  // read after the dependency wait
+__device__ __forceinline__ void store_y(const MmaParams &p, int row, float v, int tok = 0) {
+    if (p.control && p.token + tok >= p.control[1]) return;  // read after the dependency wait
     if (p.peer.nranks == 0) {
-        p.y[row] = v;
+        p.y[tok * p.y_stride + row] = v;
         return;
     }
     const int64_t gr = p.peer.row_base + row;
@@ -372,14 +375,18 @@ __device__ __forceinline__ float2 superblock_rows16(uint32_t ldsm_addr, const ui
 // FP16 path: nibble codes as FP16 subnormals, x as FP16 hi/lo pairs.
 struct F16Path {
     using State = SbState;
+    static constexpr int kTokens = 1;
+    using Out = float2;
+    static __device__ __forceinline__ void accumulate(Out &a, const Out &b) { a.x += b.x, a.y += b.y; }
     static constexpr uint32_t kColBytes = 144;  // one Q4_K superblock
     static constexpr uint32_t kQsOffset = 16;   // nibbles follow the 16-byte header
     static constexpr uint32_t kScratchBytes = 0;
-    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st, uint8_t *) {
+    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st, uint8_t *, int64_t, int) {
         load_superblock_x(x, sb, lane, st);
     }
     static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
-                                                    int lane, const State &st) {
+                                                    int lane, const State &st,
+                                                    const uint8_t * = nullptr) {
         return superblock_rows16(ldsm_addr, hdr_g, hdr_g8, lane, st);
     }
 };
@@ -439,10 +446,14 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
 
 struct I8Path {
     using State = I8State;
+    static constexpr int kTokens = 1;
+    using Out = float2;
+    static __device__ __forceinline__ void accumulate(Out &a, const Out &b) { a.x += b.x, a.y += b.y; }
     static constexpr uint32_t kColBytes = 144;
     static constexpr uint32_t kQsOffset = 16;
     static constexpr uint32_t kScratchBytes = 0;
-    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *) {
+    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *,
+                                                int64_t, int) {
         const float *xs = x + size_t(sb) * 256;
         const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
         float v[8];
@@ -513,7 +524,8 @@ struct I8Path {
     }
 
     static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
-                                                    int lane, const State &st) {
+                                                    int lane, const State &st,
+                                                    const uint8_t * = nullptr) {
         const int t = lane & 3;
         const uint32_t base = ldsm_addr;
         int acc[4][4] = {};
@@ -554,6 +566,181 @@ struct I8Path {
 };
 
 // ---------------------------------------------------------------------------
+// Batched INT8 path (Q4_K, up to 8 input rows "tokens" per launch). The n8
+// tile of mma.m16n8k32.u8.s8 holds the 8 tokens (column g = token g), one
+// tile per base-256 digit of x, so the weight codes of a 16-row unit are
+// unpacked once and meet all 8 tokens in 3 MMAs per 32-weight sub-block.
+// Lane (g,t) accumulates rows g, g+8 x tokens 2t, 2t+1 (complete sums, no
+// cross-lane reduction). The 6-bit sub-block scales are applied in integer
+// arithmetic (16 x scale for low-nibble sub-blocks, whose codes are q where
+// high-nibble codes are 16 q), exact up to one float conversion per digit
+// and superblock. The mins term sum_s m_s * sum(x over s) is three more
+// MMAs: A = the packed 6-bit mins (k = sub-block), B = the per-token
+// sub-block sums of x as exact digits.
+// ---------------------------------------------------------------------------
+struct I8T8State {
+    uint32_t b[8][3][2];  // [sub-block][digit][b0, b1]
+    uint32_t bm[3];       // mins B fragment per digit (k = sub-block 4t..4t+3; b1 = 0)
+    float inv[2];         // 1 / x scale of tokens 2t, 2t+1 (0 when absent)
+    float inv_m[2];       // 1 / scale of their sub-block sums
+};
+
+struct I8T8Path {
+    using State = I8T8State;
+    static constexpr int kTokens = 8;
+    using Out = float4;  // (row g, token 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+    static __device__ __forceinline__ void accumulate(Out &a, const Out &b) {
+        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    static constexpr uint32_t kColBytes = 144;
+    static constexpr uint32_t kQsOffset = 16;
+    static constexpr uint32_t kScratchBytes = 0;
+
+    // power-of-two scale with |v * scale| < 2^22 for |v| <= amax; inv = 1 / scale
+    static __device__ __forceinline__ void fixed_point(float amax, float &scale, float &inv) {
+        scale = 1.0f, inv = 1.0f;
+        const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xffu;
+        if (ebits == 0xffu) {
+            inv = __int_as_float(0x7fc00000);
+        } else if (amax > 0.0f) {
+            const int e = int(ebits) - 127 + 1;
+            const int se = max(-126, min(127, 22 - e));
+            scale = __uint_as_float(uint32_t(se + 127) << 23);
+            inv = __uint_as_float(uint32_t(127 - se) << 23);
+        }
+    }
+
+    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *,
+                                                int64_t x_stride, int ntok) {
+        const int t = lane & 3, g = lane >> 2;
+        const bool present = g < ntok;
+        const float *xs = x + size_t(present ? g : 0) * x_stride + size_t(sb) * 256;
+        // This lane's 64 elements of token g: sub-block s, k = 4t..4t+3 and 16+4t..16+4t+3.
+        float amax = 0.0f, ps[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            ps[s] = 0.0f;
+            if (present) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 4 * t));
+                const float4 c = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 16 + 4 * t));
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))));
+                ps[s] = ((a.x + a.y) + (a.z + a.w)) + ((c.x + c.y) + (c.z + c.w));
+            }
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        float smax = 0.0f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            ps[s] += __shfl_xor_sync(0xffffffffu, ps[s], 1);
+            ps[s] += __shfl_xor_sync(0xffffffffu, ps[s], 2);  // sum of token g over sub-block s
+            smax = fmaxf(smax, fabsf(ps[s]));
+        }
+        float scale, inv, scale_m, inv_m;
+        fixed_point(amax, scale, inv);
+        fixed_point(smax, scale_m, inv_m);
+        if (!present) inv = 0.0f, inv_m = 0.0f;
+        // accumulator side: tokens 2t, 2t+1 live in lanes 8t and 8t+4
+        st.inv[0] = __shfl_sync(0xffffffffu, inv, 8 * t);
+        st.inv[1] = __shfl_sync(0xffffffffu, inv, 8 * t + 4);
+        st.inv_m[0] = __shfl_sync(0xffffffffu, inv_m, 8 * t);
+        st.inv_m[1] = __shfl_sync(0xffffffffu, inv_m, 8 * t + 4);
+        constexpr int kAdd[3] = {0x8080, 0x80, 0};
+        constexpr uint32_t kShift[3] = {16u, 8u, 0u};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            int v[8];
+            if (present) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 4 * t));
+                const float4 c = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 16 + 4 * t));
+                v[0] = __float2int_rn(a.x * scale), v[1] = __float2int_rn(a.y * scale);
+                v[2] = __float2int_rn(a.z * scale), v[3] = __float2int_rn(a.w * scale);
+                v[4] = __float2int_rn(c.x * scale), v[5] = __float2int_rn(c.y * scale);
+                v[6] = __float2int_rn(c.z * scale), v[7] = __float2int_rn(c.w * scale);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0;
+            }
+#pragma unroll
+            for (int d = 0; d < 3; ++d) {
+                st.b[s][d][0] = pack_low_bytes(digit_byte(v[0], kAdd[d], kShift[d]), digit_byte(v[1], kAdd[d], kShift[d]),
+                                               digit_byte(v[2], kAdd[d], kShift[d]), digit_byte(v[3], kAdd[d], kShift[d]));
+                st.b[s][d][1] = pack_low_bytes(digit_byte(v[4], kAdd[d], kShift[d]), digit_byte(v[5], kAdd[d], kShift[d]),
+                                               digit_byte(v[6], kAdd[d], kShift[d]), digit_byte(v[7], kAdd[d], kShift[d]));
+            }
+        }
+        // mins B: k = sub-block s (t = 0: s 0..3, t = 1: s 4..7, t >= 2: zero), column g = token g
+        int vm[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float sv = t == 0 ? ps[i] : ps[4 + i];
+            vm[i] = (present && t < 2) ? __float2int_rn(sv * scale_m) : 0;
+        }
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            st.bm[d] = pack_low_bytes(digit_byte(vm[0], kAdd[d], kShift[d]), digit_byte(vm[1], kAdd[d], kShift[d]),
+                                      digit_byte(vm[2], kAdd[d], kShift[d]), digit_byte(vm[3], kAdd[d], kShift[d]));
+    }
+
+    static __device__ __forceinline__ Out rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
+                                                 int lane, const State &st, const uint8_t * = nullptr) {
+        const int t = lane & 3;
+        const uint4 hg = *reinterpret_cast<const uint4 *>(hdr_g);
+        const uint4 hg8 = *reinterpret_cast<const uint4 *>(hdr_g8);
+        // 6-bit scales: sub-blocks 0..3 in sl, 4..7 in sh (one per byte); mins likewise.
+        const uint32_t sl0 = hg.y & 0x3F3F3F3Fu, sl8 = hg8.y & 0x3F3F3F3Fu;
+        const uint32_t sh0 = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+        const uint32_t sh8 = (hg8.w & 0x0F0F0F0Fu) | ((hg8.y >> 2) & 0x30303030u);
+        int tot[3][4];
+#pragma unroll
+        for (int d = 0; d < 3; ++d) tot[d][0] = tot[d][1] = tot[d][2] = tot[d][3] = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t w0, w8, v0, v8;
+            ldsm_x4(ldsm_addr + 32u * j, w0, w8, v0, v8);
+            constexpr uint32_t L = 0x0F0F0F0Fu, H = 0xF0F0F0F0u;
+            const uint32_t p0 = j < 2 ? sl0 : sh0, p8 = j < 2 ? sl8 : sh8;
+            const uint32_t sh_lo = 16u * (j & 1), sh_hi = sh_lo + 8u;  // bytes 2(j%2), 2(j%2)+1
+            const int s_lo0 = int(((p0 >> sh_lo) & 0xffu) << 4), s_lo8 = int(((p8 >> sh_lo) & 0xffu) << 4);
+            const int s_hi0 = int((p0 >> sh_hi) & 0xffu), s_hi8 = int((p8 >> sh_hi) & 0xffu);
+#pragma unroll
+            for (int d = 0; d < 3; ++d) {
+                int lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+                imma16832(lo, w0 & L, w8 & L, v0 & L, v8 & L, st.b[2 * j][d][0], st.b[2 * j][d][1]);
+                imma16832(hi, w0 & H, w8 & H, v0 & H, v8 & H, st.b[2 * j + 1][d][0], st.b[2 * j + 1][d][1]);
+                tot[d][0] += lo[0] * s_lo0 + hi[0] * s_hi0;
+                tot[d][1] += lo[1] * s_lo0 + hi[1] * s_hi0;
+                tot[d][2] += lo[2] * s_lo8 + hi[2] * s_hi8;
+                tot[d][3] += lo[3] * s_lo8 + hi[3] * s_hi8;
+            }
+        }
+        // mins: A = 6-bit mins (k = sub-block: lane t = 0 holds 0..3, t = 1 holds 4..7)
+        const uint32_t ml0 = hg.z & 0x3F3F3F3Fu, ml8 = hg8.z & 0x3F3F3F3Fu;
+        const uint32_t mh0 = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+        const uint32_t mh8 = ((hg8.w >> 4) & 0x0F0F0F0Fu) | ((hg8.z >> 2) & 0x30303030u);
+        const uint32_t am0 = t == 0 ? ml0 : (t == 1 ? mh0 : 0u), am8 = t == 0 ? ml8 : (t == 1 ? mh8 : 0u);
+        int mt[3][4];
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            mt[d][0] = mt[d][1] = mt[d][2] = mt[d][3] = 0;
+            imma16832(mt[d], am0, am8, 0u, 0u, st.bm[d], 0u);
+        }
+        const float2 dm = half2_bits_to_float2(hg.x), dm8 = half2_bits_to_float2(hg8.x);
+        float r[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float main = (float(tot[0][i]) * 65536.0f + float(tot[1][i]) * 256.0f + float(tot[2][i])) * 0.0625f;
+            const float mins = float(mt[0][i]) * 65536.0f + float(mt[1][i]) * 256.0f + float(mt[2][i]);
+            const float2 dd = i < 2 ? dm : dm8;
+            const int u = i & 1;
+            r[i] = dd.x * main * st.inv[u] - dd.y * mins * st.inv_m[u];
+        }
+        return make_float4(r[0], r[1], r[2], r[3]);
+    }
+};
+
+// ---------------------------------------------------------------------------
 // Q8_0 path (mma.sync m16n8k32, s8 x s8 -> s32). A Q8_0 block is 34 bytes
 // (FP16 d, 32 int8 quants), so quants are not 16-byte aligned; instead of
 // unpacking, the MMA reads the raw row bytes: a column of 8 blocks (256
@@ -585,6 +772,9 @@ struct Q8State {
 
 struct Q8Path {
     using State = Q8State;
+    static constexpr int kTokens = 1;
+    using Out = float2;
+    static __device__ __forceinline__ void accumulate(Out &a, const Out &b) { a.x += b.x, a.y += b.y; }
     static constexpr uint32_t kColBytes = 272;  // eight 34-byte blocks
     static constexpr uint32_t kQsOffset = 0;    // windows start at the column start
     static constexpr uint32_t kImageBytes = 288;            // nine windows
@@ -595,7 +785,7 @@ struct Q8Path {
     // scale bytes and beyond the column); each lane then reads its B words
     // with aligned 32-bit loads.
     static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st,
-                                                uint8_t *scratch) {
+                                                uint8_t *scratch, int64_t, int) {
         const float *xs = x + size_t(sb) * 256;
         const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
         float v[8];
@@ -661,7 +851,8 @@ struct Q8Path {
 
     // hdr_g / hdr_g8: the column's first byte in rows g and g+8.
     static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
-                                                    int lane, const State &st) {
+                                                    int lane, const State &st,
+                                                    const uint8_t * = nullptr) {
         (void)lane;
         int acc[9][4];
 #pragma unroll
@@ -709,15 +900,17 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.compute_warps, CS = p.cluster;
     const int C0 = C / WPS;  // superblock columns (partial sums per row)
+    constexpr int TK = Path::kTokens;  // input rows per launch (1: GEMV)
+    constexpr int RTK = RT * TK;       // outputs per tile
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(p.stages) * p.stage_bytes);
     uint64_t *empty = full + p.stages;
     uint64_t *pfull = empty + p.stages;  // [2] compute warps -> reducer
     uint64_t *pempty = pfull + 2;        // [2] reducer -> compute warps
-    float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C0][RT]
-    float *rowsum = part + size_t(2) * C0 * RT;            // [max_local_tiles][RT] when CS > 1
-    // Per compute warp scratch of the path (x digit images), 16-byte aligned.
+    float *part = reinterpret_cast<float *>(pempty + 2);  // [2][C0][RT][TK]
+    float *rowsum = part + size_t(2) * C0 * RTK;           // [max_local_tiles][RT][TK] when CS > 1
+    // Per compute warp scratch of the path, 16-byte aligned.
     uint8_t *scratch = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(rowsum + size_t(p.max_local_tiles) * RT * (CS > 1)) + 15) & ~uintptr_t(15));
+        (reinterpret_cast<uintptr_t>(rowsum + size_t(p.max_local_tiles) * RTK * (CS > 1)) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = CS > 1 ? cluster_ctarank() : 0u;
@@ -766,8 +959,8 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             if (++s == p.stages) s = 0, ring_phase ^= 1u;
         }
     } else if (warp == C + 1) {
-        // Reducer: fixed-order sum of the C0 per-column partials of each row
-        // (RT <= 32: lane r owns row r of the tile).
+        // Reducer: fixed-order sum of the C0 per-column partials of each
+        // output (row r, input row u) = index r * TK + u of the tile.
         if (CS == 1) pdl_wait();  // y may still be read by the previous kernel
         int it = 0;
         for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
@@ -775,14 +968,18 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             mbar_wait(&pfull[b], (it >> 1) & 1, kErrEpilogueTimeout);
             const int r0 = tile * RT;
             const int nrows = min(RT, p.rows - r0);
-            const float *pb = part + size_t(b) * C0 * RT;
-            float a = 0.0f;
-            if (lane < nrows)
-                for (int c = 0; c < C0; ++c) a += pb[c * RT + lane];
-            if (CS == 1) {
-                if (lane < nrows) store_y(p, r0 + lane, a);
-            } else if (lane < RT) {
-                rowsum[it * RT + lane] = a;
+            const float *pb = part + size_t(b) * C0 * RTK;
+#pragma unroll
+            for (int o0 = 0; o0 < RTK; o0 += 32) {
+                const int o = o0 + lane, r = o / TK, u = o % TK;
+                float a = 0.0f;
+                if (r < nrows)
+                    for (int c = 0; c < C0; ++c) a += pb[c * RTK + o];
+                if (CS == 1) {
+                    if (r < nrows && (TK == 1 || u < p.ntok)) store_y(p, r0 + r, a, u);
+                } else {
+                    rowsum[it * RTK + o] = a;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&pempty[b]);
@@ -798,9 +995,9 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         const int gsb = int(crank) * p.nsb_cta;
         pdl_wait();  // x is produced by the previous kernel
         uint8_t *my_scratch = scratch + size_t(warp) * Path::kScratchBytes;
-        Path::load(p.x, gsb + sb0, lane, st0, my_scratch);
+        Path::load(p.x, gsb + sb0, lane, st0, my_scratch, p.x_stride, p.ntok);
         if constexpr (SPW == 2) {
-            if (has1) Path::load(p.x, gsb + sb1, lane, st1, my_scratch);
+            if (has1) Path::load(p.x, gsb + sb1, lane, st1, my_scratch, p.x_stride, p.ntok);
         }
 
         const int g = lane >> 2, t = lane & 3;
@@ -827,29 +1024,37 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
             const uint8_t *stage = smem + size_t(s) * p.stage_bytes;
             const uint32_t stage_addr = smem_u32(stage);
             if (it >= 2) mbar_wait(&pempty[b], ((it >> 1) - 1) & 1, kErrEpilogueTimeout);
-            float *pw = part + (size_t(b) * C0 + col) * RT;
-            float2 acc[kUnits];
+            float *pw = part + (size_t(b) * C0 + col) * RTK;
+            typename Path::Out acc[kUnits];
 #pragma unroll
             for (int q = 0; q < kUnits; ++q) {
                 constexpr uint32_t CB = Path::kColBytes;
                 acc[q] = Path::rows16(stage_addr + off_ldsm[q] + CB * sb0, stage + off_g[q] + CB * sb0,
-                                      stage + off_g8[q] + CB * sb0, lane, st0);
+                                      stage + off_g8[q] + CB * sb0, lane, st0, my_scratch);
                 if (SPW == 2 && has1) {
-                    const float2 a1 = Path::rows16(stage_addr + off_ldsm[q] + CB * sb1, stage + off_g[q] + CB * sb1,
-                                                   stage + off_g8[q] + CB * sb1, lane, st1);
-                    acc[q].x += a1.x, acc[q].y += a1.y;
+                    const typename Path::Out a1 =
+                        Path::rows16(stage_addr + off_ldsm[q] + CB * sb1, stage + off_g[q] + CB * sb1,
+                                     stage + off_g8[q] + CB * sb1, lane, st1, my_scratch);
+                    Path::accumulate(acc[q], a1);
                 }
             }
 #pragma unroll
             for (int q = 0; q < kUnits; ++q) {
-                float2 v = acc[q];
-                v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
-                v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
-                v.x += __shfl_xor_sync(0xffffffffu, v.x, 2);
-                v.y += __shfl_xor_sync(0xffffffffu, v.y, 2);
-                if (t == 0) {
-                    pw[row_g[q]] = v.x;
-                    pw[row_g8[q]] = v.y;
+                if constexpr (TK == 1) {
+                    float2 v = acc[q];
+                    v.x += __shfl_xor_sync(0xffffffffu, v.x, 1);
+                    v.y += __shfl_xor_sync(0xffffffffu, v.y, 1);
+                    v.x += __shfl_xor_sync(0xffffffffu, v.x, 2);
+                    v.y += __shfl_xor_sync(0xffffffffu, v.y, 2);
+                    if (t == 0) {
+                        pw[row_g[q]] = v.x;
+                        pw[row_g8[q]] = v.y;
+                    }
+                } else {
+                    // lane (g,t) owns rows g, g+8 x input rows 2t, 2t+1 (complete sums)
+                    const float4 v = acc[q];
+                    *reinterpret_cast<float2 *>(pw + row_g[q] * TK + 2 * t) = make_float2(v.x, v.y);
+                    *reinterpret_cast<float2 *>(pw + row_g8[q] * TK + 2 * t) = make_float2(v.z, v.w);
                 }
             }
             __syncwarp();
@@ -867,13 +1072,14 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         const uint32_t base = smem_u32(rowsum);
         // The reducer warps of the cluster finish the rows (one warp per CTA
         // stores, so only it has output stores to fence on a sharded call).
-        for (int i = warp == C + 1 ? int(crank) * 32 + lane : local_tiles * RT; i < local_tiles * RT; i += CS * 32) {
-            const int li = i / RT, r = i - li * RT;
+        for (int i = warp == C + 1 ? int(crank) * 32 + lane : local_tiles * RTK; i < local_tiles * RTK;
+             i += CS * 32) {
+            const int li = i / RTK, rem = i - li * RTK, r = rem / TK, u = rem % TK;
             const int row = (first_tile + li * tile_step) * RT + r;
-            if (row < p.rows) {
+            if (row < p.rows && (TK == 1 || u < p.ntok)) {
                 float a = 0.0f;
                 for (int k = 0; k < CS; ++k) a += ld_cluster_f32(mapa_shared(base + 4u * uint32_t(i), uint32_t(k)));
-                store_y(p, row, a);
+                store_y(p, row, a, u);
             }
         }
         cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
@@ -960,7 +1166,7 @@ Shape default_shape(int64_t rows, int nsb, int sms, int path) {
 // group_cap > 0 limits the clusters (CTAs) of the grid to what can be
 // resident at once.
 bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint32_t col_bytes,
-              uint32_t scratch_bytes, int group_cap, MmaParams &p, size_t &smem, int &rt) {
+              uint32_t scratch_bytes, int group_cap, MmaParams &p, size_t &smem, int &rt, int tokens = 1) {
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int nsb = int(cols / 256);
@@ -968,8 +1174,8 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint
     Shape o;
     if (shape_override(o) && o.cluster >= 1 && o.cluster <= 8 && (o.rt == 16 || o.rt == 32) &&
         o.budget_kb >= 32 && o.budget_kb <= kMaxBudgetKb && (o.wps == 1 || o.wps == 2)) {
-        const int opath = path == 2 ? 2 : o.path;
-        if (opath == path || (path != 2 && (opath == 0 || opath == 1))) {
+        const int opath = path >= 2 ? path : o.path;
+        if (opath == path || (path < 2 && (opath == 0 || opath == 1))) {
             sh = o;
             sh.path = opath;
         }
@@ -1025,13 +1231,14 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint
         if (sh.max_groups > 0) p.groups = std::min(p.groups, sh.max_groups);
         if (group_cap > 0) p.groups = std::min(p.groups, group_cap);
         p.max_local_tiles = (p.num_tiles + p.groups - 1) / p.groups;
-        const size_t rowsum = p.cluster > 1 ? size_t(p.max_local_tiles) * rt * sizeof(float) : 0;
+        const size_t rowsum = p.cluster > 1 ? size_t(p.max_local_tiles) * rt * tokens * sizeof(float) : 0;
         // The K split is for small matrices: the row sums it keeps must stay small.
         if (rowsum > 48 * 1024) {
             sh.cluster = 1;
             continue;
         }
-        const size_t tail = size_t(2) * columns * rt * sizeof(float) + rowsum + (scratch ? scratch + 16 : 0);
+        const size_t tail =
+            size_t(2) * columns * rt * tokens * sizeof(float) + rowsum + (scratch ? scratch + 16 : 0);
         const size_t bars = size_t(2 * 8 + 4) * sizeof(uint64_t);
         if (budget < tail + bars + 2 * size_t(p.stage_bytes)) {
             if (sh.cluster == 1) return false;
@@ -1095,12 +1302,13 @@ int max_active_clusters(void (*kernel)(MmaParams), int cluster, int threads, siz
     return n;
 }
 
-// Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
-// (without touching the error string) when the shape needs the SIMT kernel.
-si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream, const PeerGather *peer, const int32_t *control, int token) {
-    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
-    const bool q8 = wtype == SI_TYPE_Q8_0;
+namespace {
+
+// One launch of the tensor-core GEMV skeleton. path: 1 Q4_K INT8 (or FP16
+// by override), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
+si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream,
+                     const PeerGather *peer, const int32_t *control, int token, int ntok, int64_t x_stride,
+                     int64_t y_stride) {
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
@@ -1114,6 +1322,10 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     static const Kernel kernels[3][2][2][2] = {SI_GEMV_KERNELS(F16Path), SI_GEMV_KERNELS(I8Path),
                                                SI_GEMV_KERNELS(Q8Path)};
 #undef SI_GEMV_KERNELS
+    // batched: one superblock per warp only ([max warps 12 / 16][rows per tile 16 / 32])
+    static const Kernel kernels_t8[2][2] = {
+        {gemv_mma_q4k_kernel<I8T8Path, 1, 16, 1, 12>, gemv_mma_q4k_kernel<I8T8Path, 1, 32, 1, 12>},
+        {gemv_mma_q4k_kernel<I8T8Path, 1, 16, 1, 16>, gemv_mma_q4k_kernel<I8T8Path, 1, 32, 1, 16>}};
     static const Kernel kernel_wps2 = gemv_mma_q4k_kernel<I8Path, 1, 32, 2, kMaxWps2Warps>;
     static std::once_flag attr_once;
     std::call_once(attr_once, [] {
@@ -1121,18 +1333,27 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
             for (auto &b : a)
                 for (auto &c : b)
                     for (Kernel k : c) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        for (auto &a : kernels_t8)
+            for (Kernel k : a) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         cudaFuncSetAttribute(kernel_wps2, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
+    const bool q8 = path == 2, batched = path == 3;
+    const uint32_t col_bytes = q8 ? Q8Path::kColBytes : I8Path::kColBytes;
     // Plan; with a K split, shrink the grid to the clusters that can be
     // resident together (one wave) and plan again.
     Kernel kernel = nullptr;
     int cap = 0;
     for (int attempt = 0; attempt < 4; ++attempt) {
-        if (!plan_mma(rows, cols, w, sms, q8 ? 2 : 1, q8 ? Q8Path::kColBytes : I8Path::kColBytes,
-                      q8 ? Q8Path::kScratchBytes : 0u, cap, p, smem, rt))
+        if (!plan_mma(rows, cols, w, sms, path, col_bytes, q8 ? Q8Path::kScratchBytes : 0u, cap, p, smem, rt,
+                      batched ? I8T8Path::kTokens : 1))
             return SI_ERR_UNSUPPORTED;
-        kernel = p.wps == 2 ? kernel_wps2
-                            : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
+        if (batched) {
+            if (p.spw != 1 || p.wps != 1) return SI_ERR_UNSUPPORTED;
+            kernel = kernels_t8[p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
+        } else {
+            kernel = p.wps == 2 ? kernel_wps2
+                                : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
+        }
         if (p.cluster == 1) break;
         const int fit = max_active_clusters(kernel, p.cluster, (p.compute_warps + 2) * 32, smem);
         if (fit <= 0) return SI_ERR_UNSUPPORTED;
@@ -1145,6 +1366,9 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     if (peer) p.peer = *peer;
     p.control = control;
     p.token = token;
+    p.ntok = ntok;
+    p.x_stride = x_stride;
+    p.y_stride = y_stride;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
@@ -1165,6 +1389,31 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
     if (e != cudaSuccess)
         return fail(SI_ERR_CUDA, "tensor-core %s GEMV launch failed: %s", q8 ? "Q8_0" : "Q4_K", cudaGetErrorString(e));
+    return SI_OK;
+}
+
+}  // namespace
+
+// Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
+// (without touching the error string) when the shape needs the SIMT kernel.
+si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                           void *stream, const PeerGather *peer, const int32_t *control, int token) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
+    return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, control, token, 1, cols,
+                      rows);
+}
+
+// Q4_K batch: y[b] = W x[b] for the m input rows, eight per launch (each
+// weight byte read once per eight rows). x rows 16-byte aligned.
+si_status matvec_q4k_batched(const void *w, const float *x, float *y, int64_t m, int64_t rows, int64_t cols,
+                             void *stream, const int32_t *control) {
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || cols % 4 != 0 || m < 2) return SI_ERR_UNSUPPORTED;
+    for (int64_t b0 = 0; b0 < m; b0 += I8T8Path::kTokens) {
+        const int n = int(std::min<int64_t>(I8T8Path::kTokens, m - b0));
+        const si_status st = launch_mma(3, w, x + b0 * cols, y + b0 * rows, rows, cols, stream, nullptr, control,
+                                        int(b0), n, cols, rows);
+        if (st != SI_OK) return st;  // the first launch decides (same shape for every group)
+    }
     return SI_OK;
 }
 

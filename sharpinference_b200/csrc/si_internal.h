@@ -77,4 +77,8 @@ struct PeerGather {
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                            void *stream, const PeerGather *peer = nullptr, const int32_t *control = nullptr,
                            int token = 0);
+// Q4_K batch on the tensor cores, eight input rows per launch; SI_ERR_UNSUPPORTED
+// when the shape or alignment needs another kernel (nothing launched then).
+si_status matvec_q4k_batched(const void *w, const float *x, float *y, int64_t m, int64_t rows, int64_t cols,
+                             void *stream, const int32_t *control);
 }  // namespace si::kernels

@@ -164,10 +164,15 @@ using namespace si::dev;
 si_status shared_weight_matvec(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y,
                                int64_t m, int64_t n, int64_t k, void *stream) {
     auto st = static_cast<cudaStream_t>(stream);
-    // Quantised weights: one tensor-core GEMV per input row (the weights are
+    // Q4_K: the batched tensor-core GEMV (eight input rows per weight pass).
+    // Otherwise quantised weights: one tensor-core GEMV per input row (the weights are
     // re-read per row, from L2 when they fit, which still beats the SIMT
     // kernel by an order of magnitude). Rows at or past control[1] are not
     // written (the check runs on the device, after the dependency wait).
+    if (wtype == SI_TYPE_Q4_K && m >= 2 && m <= 1024) {
+        const si_status bs = matvec_q4k_batched(w, x, y, m, n, k, stream, control);
+        if (bs != SI_ERR_UNSUPPORTED) return bs;
+    }
     if ((wtype == SI_TYPE_Q4_K || wtype == SI_TYPE_Q8_0) && m <= 1024) {
         si_status ms = SI_OK;
         for (int64_t b = 0; b < m && ms == SI_OK; ++b)

@@ -68,6 +68,21 @@ def test_batch_shared_quant_parity_and_valid_mask(ctx, wtype, batch, valid):
         north_star_gate(y[b], ref, x[b], rn, k)
 
 
+@pytest.mark.parametrize("wtype", [N.Q4_K, N.Q8_0])
+@pytest.mark.parametrize("batch,valid,n,k", [(13, 13, 5120, 3072), (9, 7, 3072, 8192), (32, 30, 2000, 1024),
+                                             (8, 8, 4099, 768)])
+def test_batch_shared_tensor_core_shapes(ctx, wtype, batch, valid, n, k):
+    """Q4_K runs the batched tensor-core GEMV (eight input rows per weight
+    pass, K split over clusters for K = 8192), Q8_0 one GEMV per row."""
+    blob, x, y = _shared_case(ctx, wtype, batch, n, k, valid, seed=batch * 7 + n)
+    assert np.all(y[valid:] == -31.0), "rows at or beyond validCount were written"
+    rn = row_norm_max(wtype, blob, n, k)
+    for b in range(valid):
+        ref = oracle.matvec_f64(wtype, blob, x[b], n, k)
+        north_star_gate(y[b], ref, x[b], rn, k)
+    assert native.device_error_take(0) == 0
+
+
 @pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K])
 @pytest.mark.parametrize("m,n,k", [(1, 64, 256), (33, 129, 512), (64, 1000, 768), (300, 200, 256), (257, 128, 1024),
                                    (64, 7, 256)])
