@@ -37,6 +37,10 @@ sys.path.insert(0, str(ROOT))
 SHAPES = [("qkv", 5120, 3072, 0), ("o", 3072, 3072, 1), ("gate_up", 16384, 3072, 2), ("down", 3072, 8192, 3),
           ("lm_head", 200064, 3072, 4)]
 WTYPE = 12  # Q4_K
+# Secondary (1 GPU only): batch-shared mat-vec (transformer.batch-shared-matvec) at the reference's
+# batch 16 and config 5's 32 streams: (name, weight type, N, K, seed, batch).
+BATCH_SHAPES = [("qkv", 12, 5120, 3072, 0, 16), ("lm_head", 12, 200064, 3072, 4, 16), ("lm_head", 12, 200064, 3072, 4, 32),
+                ("gate_up_14b", 8, 35840, 5120, 13, 32)]
 # Secondary (1 GPU only): Q8_0 GEMV on config 1 and the Phi-4-14B decode shapes of config 5.
 Q8_SHAPES = [("config1", 8192, 3072, 0), ("qkv_14b", 7680, 5120, 11), ("o_14b", 5120, 5120, 12),
              ("gate_up_14b", 35840, 5120, 13), ("down_14b", 5120, 17920, 14), ("lm_head_14b", 100352, 5120, 15)]
@@ -472,6 +476,32 @@ def run_ours(args) -> None:
             g.close()
             for Wc in copies + [Xq, Yq]:
                 Wc.free()
+    bs = None
+    if world == 1 and not args.no_q8:
+        bs = {}
+        for name, wt, n, k, seed, batch in BATCH_SHAPES:
+            blob = native.synth_weights(wt, seed, n, k, 0.02)
+            copies = []
+            for _ in range(min(16, max(1, -(-L2_ROTATE_BYTES // blob.nbytes)))):
+                Wc = ctx.buffer(blob.nbytes)
+                Wc.upload(blob)
+                copies.append(Wc)
+            xb = np.concatenate([native.synth_normal(2000 + seed * 64 + b, k, 1.0) for b in range(batch)])
+            Xb, Yb, Cb = ctx.buffer(xb.nbytes), ctx.buffer(4 * batch * n), ctx.buffer(8)
+            Xb.upload(xb)
+            Cb.upload(np.array([0, batch], np.int32))
+            reps = max(4, len(copies))
+            g = ctx.record(lambda copies=copies, Xb=Xb, Yb=Yb, Cb=Cb, n=n, k=k, wt=wt, batch=batch, reps=reps: [
+                ctx.batch_shared_matvec(wt, copies[r % len(copies)], Xb, Cb, Yb, batch, n, k) for r in range(reps)])
+            g.launch()
+            ms = timed(g.launch, 3) / (3 * reps)
+            wb = blob.nbytes
+            bs[f"{name}_b{batch}"] = {"type": "Q4_K" if wt == 12 else "Q8_0", "n": n, "k": k, "batch": batch,
+                                      "us": round(ms * 1e3, 1), "weight_GB/s": round(wb / (ms * 1e-3) / 1e9, 1),
+                                      "weight_stream_frac": round(wb / (ms * 1e-3) / 1e9 / peak, 3)}
+            g.close()
+            for Wc in copies + [Xb, Yb, Cb]:
+                Wc.free()
     err = native.device_error_take(local)
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
@@ -499,6 +529,9 @@ def run_ours(args) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "wall_ms_per_step": round(wall_ms / args.steps, 4)},
             "gpu_launches": len(SHAPES) * args.steps,
+            "batch_shared": bs and {"workload": "transformer.batch-shared-matvec: all rows valid, weights read "
+                                                 "from copies > L2; roofline = the weight stream read once",
+                                     "per_shape": bs},
             "q8_0_gemv": q8 and {"workload": "Q8_0 GEMV, config 1 and the Phi-4-14B decode shapes of config 5 "
                                              "(1 GPU; back-to-back launches cycling through weight copies > L2)",
                                  "per_shape": q8},

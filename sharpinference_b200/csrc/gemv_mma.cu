@@ -972,6 +972,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
 #pragma unroll
             for (int o0 = 0; o0 < RTK; o0 += 32) {
                 const int o = o0 + lane, r = o / TK, u = o % TK;
+                if (o >= RTK) break;  // RT * TK = 16: lanes 16..31 have no output
                 float a = 0.0f;
                 if (r < nrows)
                     for (int c = 0; c < C0; ++c) a += pb[c * RTK + o];
