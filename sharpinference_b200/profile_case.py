@@ -1,0 +1,47 @@
+"""Runs one hot-path case twice on GPU 0 (for ncu captures of a single
+launch with `-s 1 -c 1`): synthetic seeded weights and inputs, device-resident.
+
+  python -m sharpinference_b200.profile_case gemv Q4_K 200064 3072
+  python -m sharpinference_b200.profile_case gemv Q8_0 100352 5120
+  python -m sharpinference_b200.profile_case batch Q4_K 200064 3072 16
+  python -m sharpinference_b200.profile_case gemm Q4_K 200064 3072 512
+"""
+from __future__ import annotations
+
+import sys
+
+import numpy as np
+
+from . import native
+
+TYPES = {"Q4_K": native.Q4_K, "Q8_0": native.Q8_0, "F16": native.F16, "F32": native.F32}
+
+
+def main(argv: list[str]) -> None:
+    kind, tname, n, k = argv[0], argv[1], int(argv[2]), int(argv[3])
+    m = int(argv[4]) if len(argv) > 4 else 1
+    wt = TYPES[tname]
+    blob = native.synth_weights(wt, 4, n, k, 0.02)
+    x = native.synth_normal(1004, m * k, 1.0)
+    with native.Context(0) as ctx:
+        W, X, Y = ctx.buffer(blob.nbytes), ctx.buffer(x.nbytes), ctx.buffer(4 * m * n)
+        W.upload(blob), X.upload(x)
+        C = ctx.buffer(8)
+        C.upload(np.array([0, m], np.int32))
+        for _ in range(2):
+            if kind == "gemv":
+                ctx.matvec(wt, W, X, Y, n, k)
+            elif kind == "batch":
+                ctx.batch_shared_matvec(wt, W, X, C, Y, m, n, k)
+            elif kind == "gemm":
+                ctx.matrix_multiply(wt, X, W, Y, m, n, k)
+            else:
+                raise SystemExit(f"unknown case {kind}")
+        ctx.synchronize()
+        y = Y.readback().view(np.float32)
+        print(f"{kind} {tname} {n}x{k} m={m}: finite={bool(np.all(np.isfinite(y)))} "
+              f"device_error={native.device_error_take(0)}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
