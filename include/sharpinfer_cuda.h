@@ -273,6 +273,143 @@ si_status si_instruction_resolve(const char *collection_id, const char *name, in
 si_status si_instruction_validate(int instruction_id, const uint32_t *port_types, int port_count,
                                   const char *configuration);
 
+/* ---------------------------------------------------------------------- */
+/* Transformer instructions (collection TransformerFloat32,               */
+/* GpuTransformerInstructionCollection.cs:8-33) and core.gather-row       */
+/* ---------------------------------------------------------------------- */
+/* Device pointers, FP32 tensors, enqueued on `stream` (NULL = legacy
+ * default stream). Shape checks return SI_ERR_ADAPTATION as the
+ * instruction's Generate throws InstructionAdaptationException; pointers
+ * are checked against their device allocations. `position` and `control`
+ * live in device memory, so one recorded graph serves every decode step.
+ * Batch forms take control = (start position, validCount): rows
+ * b >= validCount are left untouched (GpuBatchTransformerInstructions.cs:78-82). */
+
+/* core.gather-row (GpuTierZeroInstruction.cs:397-407; Phi4D3D12TextSession.cs:510-516):
+ * output[c] = table[*index, c] dequantised to FP32 (table F32, F16, Q8_0 or
+ * Q4_K in GGUF layout), NaN in every element for an index outside [0, rows). */
+si_status si_gather_row(uint32_t table_type, const void *table, int64_t rows, int64_t cols, const int32_t *index,
+                        float *output, void *stream);
+/* transformer.rms-norm (GpuTransformerInstructionCollection.cs:323-368). */
+si_status si_rms_norm(const float *input, const float *weight, float *output, int64_t count, float epsilon,
+                      void *stream);
+/* transformer.residual-rms-norm (GpuTransformerInstructionCollection.cs:370-417):
+ * updated = hidden + residual; output = updated * rsqrt(mean(updated^2) + eps) * weight. */
+si_status si_residual_rms_norm(const float *hidden, const float *residual, const float *weight, float *updated,
+                               float *output, int64_t count, float epsilon, void *stream);
+/* transformer.swiglu (GpuTransformerInstructionCollection.cs:419-443): gate_up = [gate | up],
+ * output[i] = gate / (1 + exp(-gate)) * up, count = output length. */
+si_status si_swiglu(const float *gate_up, float *output, int64_t count, void *stream);
+/* transformer.scaled-add (GpuTransformerInstructionCollection.cs:151-182); scale > 0 and finite. */
+si_status si_scaled_add(const float *input, const float *update, float *output, int64_t count, float scale,
+                        void *stream);
+/* transformer.rope-kv-write (GpuTransformerInstructionCollection.cs:445-543): qkv = [query |
+ * key | value]; rotates the first rotary_size channels of every query/key head (pairs d,
+ * d + rotary/2, angle = position * frequencies[d mod rotary/2], cos/sin scaled by rope_scale),
+ * writes query and the cache rows [context, kv_heads, head_size] at *position; nothing is
+ * written for a position outside [0, context). */
+si_status si_rope_kv_write(const float *qkv, const int32_t *position, const float *frequencies, float *query,
+                           float *key_cache, float *value_cache, int64_t query_size, int32_t kv_heads,
+                           int32_t head_size, int32_t rotary_size, int64_t context, float rope_scale, void *stream);
+/* transformer.grouped-query-attention (GpuTransformerInstructionCollection.cs:46-148): causal
+ * attention of one query over cache tokens 0..min(max(0,*position), context-1), query head h
+ * reading kv head h / (query_heads / kv_heads), scores scaled by 1/sqrt(head_size). */
+si_status si_grouped_query_attention(const float *query, const float *key_cache, const float *value_cache,
+                                     const int32_t *position, float *output, int32_t query_heads, int32_t kv_heads,
+                                     int32_t head_size, int64_t context, void *stream);
+/* transformer.gqa-scores / causal-softmax / gqa-values
+ * (GpuTransformerInstructionCollection.cs:545-695): the unfused attention, scores and
+ * probabilities [query_heads, context]; token t takes part when (uint)t <= (uint)*position. */
+si_status si_gqa_scores(const float *query, const float *key_cache, const int32_t *position, float *scores,
+                        int32_t query_heads, int32_t kv_heads, int32_t head_size, int64_t context, void *stream);
+si_status si_causal_softmax(const float *scores, const int32_t *position, float *probabilities, int32_t heads,
+                            int64_t context, void *stream);
+si_status si_gqa_values(const float *probabilities, const float *value_cache, const int32_t *position, float *output,
+                        int32_t query_heads, int32_t kv_heads, int32_t head_size, int64_t context, void *stream);
+/* transformer.argmax (GpuTransformerInstructionCollection.cs:697-744): the smallest index of
+ * the largest value; NaN never wins; 0 when no value exceeds -FLT_MAX. */
+si_status si_argmax(const float *input, int64_t count, int32_t *output, void *stream);
+/* transformer.embedding-gather-batch (GpuTransformerInstructionCollection.cs:184-219): output
+ * row r = FP16 table row indices[r] as FP32; an index outside the table gives zeros. */
+si_status si_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *output,
+                                    int64_t batch, int64_t width, void *stream);
+/* transformer.copy-embedding-rows (GpuTransformerInstructionCollection.cs:221-280):
+ * output[output_start * width + e] = input[e], e < rows * width. */
+si_status si_copy_embedding_rows(const float *input, float *output, int64_t output_rows, int64_t rows,
+                                 int64_t width, int64_t output_start, void *stream);
+/* Batch forms (GpuBatchTransformerInstructions.cs:101-679). */
+si_status si_batch_rms_norm(const float *input, const float *weight, const int32_t *control, float *output,
+                            int64_t batch, int64_t width, float epsilon, void *stream);
+si_status si_batch_residual_rms_norm(const float *hidden, const float *residual, const float *weight,
+                                     const int32_t *control, float *updated, float *output, int64_t batch,
+                                     int64_t width, float epsilon, void *stream);
+si_status si_batch_swiglu(const float *gate_up, const int32_t *control, float *output, int64_t batch, int64_t width,
+                          void *stream);
+/* Row b is the token at position control[0] + b. */
+si_status si_batch_rope_kv_write(const float *qkv, const int32_t *control, const float *frequencies, float *query,
+                                 float *key_cache, float *value_cache, int64_t batch, int64_t query_size,
+                                 int32_t kv_heads, int32_t head_size, int32_t rotary_size, int64_t context,
+                                 float rope_scale, void *stream);
+si_status si_batch_gqa_scores(const float *query, const float *key_cache, const int32_t *control, float *scores,
+                              int64_t batch, int32_t query_heads, int32_t kv_heads, int32_t head_size,
+                              int64_t context, void *stream);
+si_status si_batch_causal_softmax(const float *scores, const int32_t *control, float *probabilities, int64_t batch,
+                                  int32_t heads, int64_t context, void *stream);
+si_status si_batch_gqa_values(const float *probabilities, const float *value_cache, const int32_t *control,
+                              float *output, int64_t batch, int32_t query_heads, int32_t kv_heads, int32_t head_size,
+                              int64_t context, void *stream);
+/* output = input row control[1] - 1 when 0 < control[1] <= batch. */
+si_status si_batch_select_last(const float *input, const int32_t *control, float *output, int64_t batch,
+                               int64_t width, void *stream);
+/* output row b = table row control[0] + b for b < control[1] when that row exists. */
+si_status si_batch_gather_rows(const float *table, int64_t rows, const int32_t *control, float *output,
+                               int64_t batch, int64_t width, void *stream);
+
+/* ---------------------------------------------------------------------- */
+/* Phi-4 text decoder session (Phi4D3D12TextSession.cs)                   */
+/* ---------------------------------------------------------------------- */
+/* The decode program of Phi4D3D12TextSession.Build (:307-920) as one CUDA
+ * graph per token: gather-row, rms-norm, then per layer qkv mat-vec,
+ * rope-kv-write, grouped-query-attention, output mat-vec, residual-rms-norm,
+ * gate_up mat-vec, swiglu, down mat-vec, residual-rms-norm; vocabulary
+ * mat-vec over the tied token_embedding and argmax. Weights keep their GGUF
+ * bytes; KV caches are FP32 [context, kv_heads, head_size] per layer
+ * (:420-425). query_heads * head_size must equal hidden. */
+typedef struct si_decoder_config {
+    int32_t layers, hidden, query_heads, kv_heads, head_size, rotary_size, intermediate, vocab;
+    int64_t context;          /* maximumContext */
+    float epsilon;            /* phi3.attention.layer_norm_rms_epsilon */
+    float rope_base;          /* phi3.rope.freq_base */
+    float rope_scale;         /* phi3.rope.scaling.attn_factor */
+    uint32_t weight_type;     /* qkv / attn_output / ffn_up / ffn_down: F16, F32, Q8_0 or Q4_K */
+    uint32_t embedding_type;  /* token_embedding (gathered and used as the vocabulary projection) */
+} si_decoder_config;
+typedef struct si_decoder si_decoder;
+si_status si_decoder_create(int device, const si_decoder_config *config, si_decoder **out);
+si_status si_decoder_destroy(si_decoder *decoder);
+/* Slots by the reference's names (Phi4D3D12TextSession.cs:391-425, 427-446):
+ * token_embedding, output_norm, attn_norm_L, ffn_norm_L, qkv_weight_L,
+ * attn_output_weight_L, ffn_up_weight_L, ffn_down_weight_L, rope_frequencies
+ * (filled from rope_base at creation), key_cache_L, value_cache_L, hidden,
+ * hidden_after_attention, normalized, qkv, query, attention, projected,
+ * gate_up, activated, down, logits, next_token, control. */
+si_status si_decoder_slot(si_decoder *decoder, const char *name, void **device_pointer, uint64_t *bytes);
+si_status si_decoder_upload(si_decoder *decoder, const char *name, uint64_t offset, const void *host, uint64_t bytes);
+si_status si_decoder_read(si_decoder *decoder, const char *name, uint64_t offset, void *host, uint64_t bytes);
+si_status si_decoder_stream(si_decoder *decoder, void **stream);
+/* ForwardToken (Phi4D3D12TextSession.cs:212-227): upload (token, position),
+ * run the decode graph, read back the argmax; position advances by one.
+ * SI_ERR_INVALID_ARGUMENT for a token outside the vocabulary or a full cache. */
+si_status si_decoder_forward_token(si_decoder *decoder, int32_t token, int32_t *next_token);
+/* Device-resident greedy loop: feeds prompt[0..prompt_tokens) and then its
+ * own argmax for `steps` more positions, without host round trips between
+ * tokens. tokens[k] = argmax after the k-th forward (prompt_tokens + steps
+ * entries); position advances by prompt_tokens + steps. */
+si_status si_decoder_generate(si_decoder *decoder, const int32_t *prompt, int32_t prompt_tokens, int32_t steps,
+                              int32_t *tokens);
+si_status si_decoder_reset(si_decoder *decoder);  /* Reset(): position = 0 */
+si_status si_decoder_position(si_decoder *decoder, int32_t *position);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,60 @@ int or_matrix_multiply_tr(uint32_t wtype, const float *x, const void *w, float *
 
 int or_online_cores(void);
 
+/* ---- transformer instructions (oracle/transformer.c) -------------------- */
+void or_rms_norm(const float *in, const float *weight, float *out, int64_t n, float eps);
+void or_residual_rms_norm(const float *hidden, const float *residual, const float *weight, float *updated,
+                          float *out, int64_t n, float eps);
+void or_swiglu(const float *gate_up, float *out, int64_t n);
+void or_scaled_add(const float *in, const float *update, float *out, int64_t n, float scale);
+int or_gather_row(uint32_t table_type, const void *table, int64_t rows, int64_t cols, int32_t index, float *out);
+void or_rope_kv_write(const float *qkv, int32_t position, const float *freq, float *query, float *key_cache,
+                      float *value_cache, int64_t query_size, int64_t kv_size, int head_size, int rotary_size,
+                      int64_t context, float rope_scale);
+void or_grouped_query_attention(const float *query, const float *key_cache, const float *value_cache,
+                                int32_t position, float *out, int query_heads, int kv_heads, int head_size,
+                                int64_t context);
+void or_gqa_scores(const float *query, const float *key_cache, int32_t position, float *scores, int query_heads,
+                   int kv_heads, int head_size, int64_t context);
+void or_causal_softmax(const float *scores, int32_t position, float *probs, int heads, int64_t context);
+void or_gqa_values(const float *probs, const float *value_cache, int32_t position, float *out, int query_heads,
+                   int kv_heads, int head_size, int64_t context);
+int32_t or_argmax(const float *in, int64_t n);
+void or_batch_rms_norm(const float *in, const float *weight, const int32_t *control, float *out, int64_t batch,
+                       int64_t width, float eps);
+void or_batch_residual_rms_norm(const float *hidden, const float *residual, const float *weight,
+                                const int32_t *control, float *updated, float *out, int64_t batch, int64_t width,
+                                float eps);
+void or_batch_swiglu(const float *gate_up, const int32_t *control, float *out, int64_t batch, int64_t width);
+void or_batch_rope_kv_write(const float *qkv, const int32_t *control, const float *freq, float *query,
+                            float *key_cache, float *value_cache, int64_t batch, int64_t query_size,
+                            int64_t kv_size, int head_size, int rotary_size, int64_t context, float rope_scale);
+void or_batch_gqa_scores(const float *query, const float *key_cache, const int32_t *control, float *scores,
+                         int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context);
+void or_batch_causal_softmax(const float *scores, const int32_t *control, float *probs, int64_t batch, int heads,
+                             int64_t context);
+void or_batch_gqa_values(const float *probs, const float *value_cache, const int32_t *control, float *out,
+                         int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context);
+void or_batch_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width);
+void or_batch_gather_rows(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,
+                          int64_t width);
+void or_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
+                               int64_t batch, int64_t width);
+void or_copy_embedding_rows(const float *in, float *out, int64_t rows, int64_t width, int64_t output_start);
+
+/* ---- Phi-4 decode program (Phi4D3D12TextSession.cs:866-920) ------------- */
+typedef struct or_decoder_config {
+    int32_t layers, hidden, query_heads, kv_heads, head_size, rotary_size, intermediate, vocab;
+    int64_t context;
+    float epsilon, rope_base, rope_scale;
+    uint32_t weight_type;     /* linear projections */
+    uint32_t embedding_type;  /* token_embedding (tied vocabulary projection) */
+} or_decoder_config;
+void or_rope_frequencies(float base, int rotary_size, float *out);
+int or_decoder_step(const or_decoder_config *cfg, const void *const *w, const float *freq, float *key_cache,
+                    float *value_cache, int32_t token, int32_t position, float *logits, int32_t *next_token,
+                    int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -196,7 +196,40 @@ constexpr const char *kTierZeroFloat32 = "00000000-0000-0000-0000-000000000000";
 constexpr const char *kTierZeroFloat16 = "00000000-0000-0000-0000-000000000001";
 constexpr const char *kTransformerFloat32 = "824d0f9c-16c7-46d8-b49d-0f91d6a4ec83";
 
-enum InstructionId { kMatVec32 = 1, kMatVec16 = 2, kMatrixMultiply = 3, kBatchSharedMatVec = 4 };
+enum InstructionId { kMatVec32 = 1, kMatVec16 = 2, kMatrixMultiply = 3, kBatchSharedMatVec = 4, kGatherRow = 5,
+                     kTransformerBase = 16 };
+
+// Port element types of the FP32 transformer instructions, in port order
+// (GpuTransformerInstructionCollection.cs, GpuBatchTransformerInstructions.cs):
+// f = F32, i = Int32, h = F16.
+struct TransformerSignature {
+    const char *name;
+    const char *ports;
+};
+constexpr TransformerSignature kTransformer[] = {
+    {"transformer.rms-norm", "fff"},
+    {"transformer.residual-rms-norm", "fffff"},
+    {"transformer.swiglu", "ff"},
+    {"transformer.rope-kv-write", "fiffff"},
+    {"transformer.gqa-scores", "ffif"},
+    {"transformer.causal-softmax", "fif"},
+    {"transformer.gqa-values", "ffif"},
+    {"transformer.grouped-query-attention", "fffif"},
+    {"transformer.argmax", "fi"},
+    {"transformer.scaled-add", "fff"},
+    {"transformer.embedding-gather-batch", "hif"},
+    {"transformer.copy-embedding-rows", "ff"},
+    {"transformer.batch-rms-norm", "ffif"},
+    {"transformer.batch-residual-rms-norm", "fffiff"},
+    {"transformer.batch-swiglu", "fif"},
+    {"transformer.batch-rope-kv-write", "fiffff"},
+    {"transformer.batch-gqa-scores", "ffif"},
+    {"transformer.batch-causal-softmax", "fif"},
+    {"transformer.batch-gqa-values", "ffif"},
+    {"transformer.batch-select-last", "fif"},
+    {"transformer.batch-gather-rows", "fif"},
+};
+constexpr int kTransformerCount = int(sizeof(kTransformer) / sizeof(kTransformer[0]));
 
 bool iequal(const char *a, const char *b) {
     for (; *a && *b; ++a, ++b)
@@ -205,6 +238,14 @@ bool iequal(const char *a, const char *b) {
 }
 
 }  // namespace
+
+// Shared with the other host translation units (si_internal.h).
+si_status device_range(const char *port, const void *ptr, uint64_t bytes) {
+    return check_device_range(port, ptr, bytes);
+}
+bool ranges_overlap(const void *a, uint64_t an, const void *b, uint64_t bn) { return overlaps(a, an, b, bn); }
+si_status cuda_error(int error, const char *what) { return cuda_status(static_cast<cudaError_t>(error), what); }
+
 }  // namespace si
 
 using namespace si;
@@ -533,6 +574,10 @@ si_status si_instruction_resolve(const char *collection_id, const char *name, in
     if ((t0f32 || t0f16) && std::strcmp(name, "core.mat-vec") == 0) id = t0f32 ? kMatVec32 : kMatVec16;
     else if (t0f32 && std::strcmp(name, "core.matrix-multiply") == 0) id = kMatrixMultiply;
     else if (tr && std::strcmp(name, "transformer.batch-shared-matvec") == 0) id = kBatchSharedMatVec;
+    else if (t0f32 && std::strcmp(name, "core.gather-row") == 0) id = kGatherRow;
+    else if (tr)
+        for (int i = 0; i < kTransformerCount; ++i)
+            if (std::strcmp(name, kTransformer[i].name) == 0) id = kTransformerBase + i;
     if (!id) return fail(SI_ERR_UNSUPPORTED, "No cuda implementation for '%s/%s'.", collection_id, name);
     *instruction_id = id;
     return SI_OK;
@@ -573,7 +618,27 @@ si_status si_instruction_validate(int instruction_id, const uint32_t *t, int n, 
         if (!*cfg) return SI_OK;
         return fail(SI_ERR_ADAPTATION, "Unsupported CUDA execution configuration '%s'.", cfg);
     }
-    default: return fail(SI_ERR_UNSUPPORTED, "unknown instruction id %d", instruction_id);
+    case kGatherRow: {
+        // table, index, output: [f32|f16|q8_0|q4_k, Int32] -> [f32] (TierZeroOperationContracts.cs:159)
+        const bool ok = n == 3 && (t[0] == SI_TYPE_F32 || t[0] == SI_TYPE_F16 || quant(t[0])) &&
+                        t[1] == SI_TYPE_I32 && t[2] == SI_TYPE_F32;
+        if (!ok) return fail(SI_ERR_ADAPTATION, "core.gather-row: no supported parameter/precision signature.");
+        if (!*cfg) return SI_OK;
+        return fail(SI_ERR_ADAPTATION, "Unsupported CUDA execution configuration '%s'.", cfg);
+    }
+    default: {
+        const int i = instruction_id - kTransformerBase;
+        if (i < 0 || i >= kTransformerCount) return fail(SI_ERR_UNSUPPORTED, "unknown instruction id %d", instruction_id);
+        const char *ports = kTransformer[i].ports;
+        bool ok = int(std::strlen(ports)) == n;
+        for (int p = 0; ok && p < n; ++p) {
+            const uint32_t want = ports[p] == 'f' ? SI_TYPE_F32 : ports[p] == 'i' ? SI_TYPE_I32 : SI_TYPE_F16;
+            ok = t[p] == want;
+        }
+        if (!ok) return fail(SI_ERR_ADAPTATION, "%s: no supported parameter/precision signature.", kTransformer[i].name);
+        if (!*cfg) return SI_OK;
+        return fail(SI_ERR_ADAPTATION, "Unsupported CUDA execution configuration '%s'.", cfg);
+    }
     }
 }
 

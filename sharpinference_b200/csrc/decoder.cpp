@@ -1,0 +1,417 @@
+// Phi-4 text decoder session on CUDA: the decode program that
+// Phi4D3D12TextSession.Build assembles from core.* and transformer.*
+// instructions (Phi4D3D12TextSession.cs:307-920), recorded once into a CUDA
+// graph and replayed per token. ForwardToken semantics (one host round trip
+// per token) and a device-resident greedy loop (the argmax kernel writes the
+// next step's control) share the same recorded step.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "si_internal.h"
+
+using si::fail;
+namespace k = si::kernels;
+
+struct si_decoder {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    si_decoder_config cfg{};
+    struct Slot {
+        void *ptr;
+        uint64_t bytes;
+    };
+    std::vector<void *> allocations;
+    std::unordered_map<std::string, Slot> slots;
+    // Resolved slot pointers.
+    const void *embedding = nullptr;
+    const float *output_norm = nullptr;
+    std::vector<const float *> attn_norm, ffn_norm;
+    std::vector<const void *> w_qkv, w_out, w_up, w_down;
+    std::vector<float *> key_cache, value_cache;
+    float *freq = nullptr;
+    int32_t *control = nullptr, *next_token = nullptr, *prompt = nullptr, *history = nullptr;
+    k::DecodeFeed *feed = nullptr;
+    float *hidden = nullptr, *after = nullptr, *normalized = nullptr, *qkv = nullptr, *query = nullptr,
+          *attention = nullptr, *projected = nullptr, *gate_up = nullptr, *activated = nullptr, *down = nullptr,
+          *logits = nullptr;
+    // Pinned host staging: [0,1] control, [2] next token, then the feed
+    // descriptor, then prompt / history staging of `context` entries each.
+    int32_t *pinned = nullptr;
+    k::DecodeFeed *pinned_feed = nullptr;
+    int32_t *pinned_prompt = nullptr, *pinned_history = nullptr;
+    cudaGraphExec_t step_exec = nullptr, feed_exec = nullptr;
+    int32_t position = 0;
+    std::mutex lock;  // session calls are serialised, as the executor's are
+};
+
+namespace {
+
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+si_status cuda(cudaError_t e, const char *what) { return si::cuda_error(int(e), what); }
+
+si_status alloc_slot(si_decoder *d, const std::string &name, uint64_t bytes, void **out) {
+    void *p = nullptr;
+    if (si_status st = cuda(cudaMalloc(&p, bytes), "cudaMalloc")) return st;
+    d->allocations.push_back(p);
+    if (si_status st = cuda(cudaMemset(p, 0, bytes), "cudaMemset")) return st;
+    d->slots[name] = {p, bytes};
+    *out = p;
+    return SI_OK;
+}
+
+template <class T>
+si_status alloc_typed(si_decoder *d, const std::string &name, uint64_t bytes, T **out) {
+    void *p = nullptr;
+    si_status st = alloc_slot(d, name, bytes, &p);
+    *out = static_cast<T *>(p);
+    return st;
+}
+
+si_status fill_ones(float *p, int64_t n) {
+    std::vector<float> ones(size_t(n), 1.0f);
+    return cuda(cudaMemcpy(p, ones.data(), size_t(n) * 4, cudaMemcpyHostToDevice), "cudaMemcpy");
+}
+
+void destroy(si_decoder *d) {
+    DeviceScope scope(d->device);
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    if (d->step_exec) cudaGraphExecDestroy(d->step_exec);
+    if (d->feed_exec) cudaGraphExecDestroy(d->feed_exec);
+    for (void *p : d->allocations) cudaFree(p);
+    if (d->pinned) cudaFreeHost(d->pinned);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    delete d;
+}
+
+si_status project(uint32_t type, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                  cudaStream_t s) {
+    if (type == SI_TYPE_Q8_0 || type == SI_TYPE_Q4_K) return k::matvec_quant(type, w, x, y, rows, cols, s);
+    return k::matvec_dense(type, w, SI_TYPE_F32, x, SI_TYPE_F32, y, rows, cols, s);
+}
+
+// One decode step (Phi4D3D12TextSession.cs:866-920), enqueued on d->stream.
+si_status record_step(si_decoder *d, k::DecodeFeed *feed) {
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
+    cudaStream_t s = d->stream;
+    int32_t *position = d->control + 1;
+    if (si_status st = k::tr_gather_row(c.embedding_type, d->embedding, c.vocab, H, d->control, d->hidden, s)) return st;
+    if (si_status st = k::tr_rms_norm(d->hidden, nullptr, d->attn_norm[0], nullptr, nullptr, d->normalized, 1, H,
+                                      c.epsilon, s))
+        return st;
+    for (int l = 0; l < c.layers; ++l) {
+        if (si_status st = project(c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H, s)) return st;
+        if (si_status st = k::tr_rope_kv_write(d->qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
+                                               d->value_cache[l], 1, H, KV, c.head_size, c.rotary_size, c.context,
+                                               c.rope_scale, s))
+            return st;
+        if (si_status st = k::tr_attention_decode(d->query, d->key_cache[l], d->value_cache[l], position, d->attention,
+                                                  c.query_heads, c.kv_heads, c.head_size, c.context, s))
+            return st;
+        if (si_status st = project(c.weight_type, d->w_out[l], d->attention, d->projected, H, H, s)) return st;
+        if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
+                                          H, c.epsilon, s))
+            return st;
+        if (si_status st = project(c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H, s)) return st;
+        if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, 1, F, s)) return st;
+        if (si_status st = project(c.weight_type, d->w_down[l], d->activated, d->down, H, F, s)) return st;
+        const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
+        if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
+                                          c.epsilon, s))
+            return st;
+    }
+    if (si_status st = project(c.embedding_type, d->embedding, d->normalized, d->logits, c.vocab, H, s)) return st;
+    return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
+}
+
+si_status build_graph(si_decoder *d, k::DecodeFeed *feed, cudaGraphExec_t *out) {
+    if (si_status st = cuda(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture"))
+        return st;
+    const si_status rec = record_step(d, feed);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(d->stream, &g);
+    if (rec != SI_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rec;
+    }
+    if (e != cudaSuccess) return cuda(e, "cudaStreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return cuda(ie, "cudaGraphInstantiate");
+}
+
+si_status validate(const si_decoder_config *c) {
+    if (!c) return fail(SI_ERR_INVALID_ARGUMENT, "null config");
+    if (c->layers <= 0 || c->hidden <= 0 || c->query_heads <= 0 || c->kv_heads <= 0 || c->head_size <= 0 ||
+        c->rotary_size <= 0 || c->intermediate <= 0 || c->vocab <= 0 || c->context <= 0 || c->context > INT32_MAX)
+        return fail(SI_ERR_INVALID_ARGUMENT, "decoder dimensions must be positive");
+    if (int64_t(c->query_heads) * c->head_size != c->hidden)
+        return fail(SI_ERR_ADAPTATION, "query_heads * head_size (%d * %d) must equal hidden (%d)", c->query_heads,
+                    c->head_size, c->hidden);
+    if (c->query_heads % c->kv_heads) return fail(SI_ERR_ADAPTATION, "Query heads must be divisible by key/value heads.");
+    if (c->query_heads / c->kv_heads > 8 || c->head_size > 256)
+        return fail(SI_ERR_UNSUPPORTED, "attention supports up to 8 query heads per key/value head and head_size <= 256");
+    if (c->rotary_size > c->head_size || c->rotary_size % 2)
+        return fail(SI_ERR_ADAPTATION, "Invalid query, cache, head, or rotary dimensions.");
+    if (!(std::isfinite(c->epsilon) && c->epsilon > 0) || !(std::isfinite(c->rope_scale) && c->rope_scale > 0) ||
+        !(std::isfinite(c->rope_base) && c->rope_base > 0))
+        return fail(SI_ERR_ADAPTATION, "epsilon, rope_base and rope_scale must be finite and positive");
+    if (!si::known_type(c->weight_type) || !si::known_type(c->embedding_type))
+        return fail(SI_ERR_UNSUPPORTED, "unsupported weight type");
+    uint64_t b;
+    for (int64_t cols : {int64_t(c->hidden), int64_t(c->intermediate)})
+        if (si_status st = si::byte_length(c->weight_type, uint64_t(cols), &b)) return st;
+    return si::byte_length(c->embedding_type, uint64_t(c->hidden), &b);
+}
+
+si_status create(int device, const si_decoder_config *c, si_decoder **out) {
+    auto *d = new si_decoder();
+    d->device = device;
+    d->cfg = *c;
+    auto cleanup = [&](si_status st) {
+        destroy(d);
+        return st;
+    };
+    if (si_status st = cuda(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreate"))
+        return cleanup(st);
+    const int64_t H = c->hidden, KV = int64_t(c->kv_heads) * c->head_size, QKV = H + 2 * KV, F = c->intermediate;
+    uint64_t rb_h = 0, rb_f = 0, rb_e = 0;
+    si::byte_length(c->weight_type, uint64_t(H), &rb_h);
+    si::byte_length(c->weight_type, uint64_t(F), &rb_f);
+    si::byte_length(c->embedding_type, uint64_t(H), &rb_e);
+    void *p = nullptr;
+    if (si_status st = alloc_slot(d, "token_embedding", rb_e * uint64_t(c->vocab), &p)) return cleanup(st);
+    d->embedding = p;
+    float *f = nullptr;
+    if (si_status st = alloc_typed(d, "output_norm", H * 4, &f)) return cleanup(st);
+    if (si_status st = fill_ones(f, H)) return cleanup(st);
+    d->output_norm = f;
+    for (int l = 0; l < c->layers; ++l) {
+        const std::string L = std::to_string(l);
+        if (si_status st = alloc_typed(d, "attn_norm_" + L, H * 4, &f)) return cleanup(st);
+        if (si_status st = fill_ones(f, H)) return cleanup(st);
+        d->attn_norm.push_back(f);
+        if (si_status st = alloc_typed(d, "ffn_norm_" + L, H * 4, &f)) return cleanup(st);
+        if (si_status st = fill_ones(f, H)) return cleanup(st);
+        d->ffn_norm.push_back(f);
+        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(QKV), &p)) return cleanup(st);
+        d->w_qkv.push_back(p);
+        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(H), &p)) return cleanup(st);
+        d->w_out.push_back(p);
+        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(2 * F), &p)) return cleanup(st);
+        d->w_up.push_back(p);
+        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(H), &p)) return cleanup(st);
+        d->w_down.push_back(p);
+        if (si_status st = alloc_typed(d, "key_cache_" + L, uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
+        d->key_cache.push_back(f);
+        if (si_status st = alloc_typed(d, "value_cache_" + L, uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
+        d->value_cache.push_back(f);
+    }
+    // rope_frequencies initializer (Phi4D3D12TextSession.cs:394-398).
+    if (si_status st = alloc_typed(d, "rope_frequencies", uint64_t(c->rotary_size / 2) * 4, &d->freq)) return cleanup(st);
+    {
+        std::vector<float> fr(size_t(c->rotary_size / 2));
+        for (int i = 0; i < c->rotary_size / 2; ++i)
+            fr[size_t(i)] = 1.0f / std::pow(c->rope_base, 2.0f * float(i) / float(c->rotary_size));
+        if (si_status st = cuda(cudaMemcpy(d->freq, fr.data(), fr.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy"))
+            return cleanup(st);
+    }
+    struct A {
+        const char *name;
+        float **dst;
+        int64_t n;
+    } acts[] = {{"hidden", &d->hidden, H},         {"hidden_after_attention", &d->after, H},
+                {"normalized", &d->normalized, H}, {"qkv", &d->qkv, QKV},
+                {"query", &d->query, H},           {"attention", &d->attention, H},
+                {"projected", &d->projected, H},   {"gate_up", &d->gate_up, 2 * F},
+                {"activated", &d->activated, F},   {"down", &d->down, H},
+                {"logits", &d->logits, c->vocab}};
+    for (const A &a : acts)
+        if (si_status st = alloc_typed(d, a.name, uint64_t(a.n) * 4, a.dst)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "control", 8, &d->control)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "next_token", 4, &d->next_token)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "prompt", uint64_t(c->context) * 4, &d->prompt)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "history", uint64_t(c->context) * 4, &d->history)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "feed", sizeof(k::DecodeFeed), &d->feed)) return cleanup(st);
+    const size_t pinned_bytes = 64 + sizeof(k::DecodeFeed) + 2 * size_t(c->context) * 4;
+    if (si_status st = cuda(cudaMallocHost(reinterpret_cast<void **>(&d->pinned), pinned_bytes), "cudaMallocHost"))
+        return cleanup(st);
+    d->pinned_feed = reinterpret_cast<k::DecodeFeed *>(reinterpret_cast<uint8_t *>(d->pinned) + 64);
+    d->pinned_prompt = reinterpret_cast<int32_t *>(d->pinned_feed + 1);
+    d->pinned_history = d->pinned_prompt + c->context;
+    if (si_status st = cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return cleanup(st);
+    *out = d;
+    return SI_OK;
+}
+
+si_status ensure_graphs(si_decoder *d) {
+    if (!d->step_exec)
+        if (si_status st = build_graph(d, nullptr, &d->step_exec)) return st;
+    if (!d->feed_exec)
+        if (si_status st = build_graph(d, d->feed, &d->feed_exec)) return st;
+    return SI_OK;
+}
+
+si_status slot_range(si_decoder *d, const char *name, uint64_t offset, uint64_t bytes, uint8_t **p) {
+    if (!name) return fail(SI_ERR_INVALID_ARGUMENT, "null slot name");
+    auto it = d->slots.find(name);
+    if (it == d->slots.end()) return fail(SI_ERR_INVALID_ARGUMENT, "No slot named '%s'.", name);
+    if (offset > it->second.bytes || bytes > it->second.bytes - offset)
+        return fail(SI_ERR_INVALID_ARGUMENT, "slot '%s': %llu bytes at offset %llu exceed its %llu bytes", name,
+                    (unsigned long long)bytes, (unsigned long long)offset, (unsigned long long)it->second.bytes);
+    *p = static_cast<uint8_t *>(it->second.ptr) + offset;
+    return SI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+si_status si_decoder_create(int device, const si_decoder_config *config, si_decoder **out) {
+    if (!out) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (si_status st = validate(config)) return st;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SI_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
+    DeviceScope scope(device);
+    return create(device, config, out);
+}
+
+si_status si_decoder_destroy(si_decoder *decoder) {
+    if (decoder) destroy(decoder);
+    return SI_OK;
+}
+
+si_status si_decoder_slot(si_decoder *d, const char *name, void **device_pointer, uint64_t *bytes) {
+    if (!d || !device_pointer || !bytes) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    uint8_t *p = nullptr;
+    if (si_status st = slot_range(d, name, 0, 0, &p)) return st;
+    *device_pointer = p;
+    *bytes = d->slots[name].bytes;
+    return SI_OK;
+}
+
+si_status si_decoder_upload(si_decoder *d, const char *name, uint64_t offset, const void *host, uint64_t bytes) {
+    if (!d || (!host && bytes)) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    uint8_t *p = nullptr;
+    if (si_status st = slot_range(d, name, offset, bytes, &p)) return st;
+    DeviceScope scope(d->device);
+    if (si_status st = cuda(cudaMemcpyAsync(p, host, bytes, cudaMemcpyHostToDevice, d->stream), "cudaMemcpyAsync"))
+        return st;
+    return cuda(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+}
+
+si_status si_decoder_read(si_decoder *d, const char *name, uint64_t offset, void *host, uint64_t bytes) {
+    if (!d || (!host && bytes)) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    uint8_t *p = nullptr;
+    if (si_status st = slot_range(d, name, offset, bytes, &p)) return st;
+    DeviceScope scope(d->device);
+    if (si_status st = cuda(cudaMemcpyAsync(host, p, bytes, cudaMemcpyDeviceToHost, d->stream), "cudaMemcpyAsync"))
+        return st;
+    return cuda(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+}
+
+si_status si_decoder_stream(si_decoder *d, void **stream) {
+    if (!d || !stream) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *stream = d->stream;
+    return SI_OK;
+}
+
+si_status si_decoder_forward_token(si_decoder *d, int32_t token, int32_t *next_token) {
+    if (!d || !next_token) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (token < 0 || token >= d->cfg.vocab)
+        return fail(SI_ERR_INVALID_ARGUMENT, "token %d outside the vocabulary of %d", token, d->cfg.vocab);
+    if (d->position >= d->cfg.context)
+        return fail(SI_ERR_INVALID_ARGUMENT, "The GPU KV cache capacity of %lld tokens has been reached.",
+                    (long long)d->cfg.context);
+    DeviceScope scope(d->device);
+    if (si_status st = ensure_graphs(d)) return st;
+    d->pinned[0] = token;
+    d->pinned[1] = d->position;
+    if (si_status st = cuda(cudaMemcpyAsync(d->control, d->pinned, 8, cudaMemcpyHostToDevice, d->stream), "upload"))
+        return st;
+    if (si_status st = cuda(cudaGraphLaunch(d->step_exec, d->stream), "cudaGraphLaunch")) return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->pinned + 2, d->next_token, 4, cudaMemcpyDeviceToHost, d->stream),
+                            "readback"))
+        return st;
+    if (si_status st = cuda(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) return st;
+    ++d->position;
+    *next_token = d->pinned[2];
+    return SI_OK;
+}
+
+si_status si_decoder_generate(si_decoder *d, const int32_t *prompt, int32_t prompt_tokens, int32_t steps,
+                              int32_t *tokens) {
+    if (!d || !prompt || !tokens) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (prompt_tokens <= 0 || steps < 0) return fail(SI_ERR_INVALID_ARGUMENT, "prompt_tokens must be positive, steps >= 0");
+    const int64_t n = int64_t(prompt_tokens) + steps;
+    if (d->position + n > d->cfg.context)
+        return fail(SI_ERR_INVALID_ARGUMENT, "The GPU KV cache capacity of %lld tokens has been reached.",
+                    (long long)d->cfg.context);
+    for (int32_t i = 0; i < prompt_tokens; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->cfg.vocab)
+            return fail(SI_ERR_INVALID_ARGUMENT, "prompt token %d (%d) outside the vocabulary", i, prompt[i]);
+    DeviceScope scope(d->device);
+    if (si_status st = ensure_graphs(d)) return st;
+    std::memcpy(d->pinned_prompt, prompt, size_t(prompt_tokens) * 4);
+    *d->pinned_feed = k::DecodeFeed{d->control, d->prompt, d->history, d->position, prompt_tokens, int32_t(n), 0};
+    d->pinned[0] = prompt[0];
+    d->pinned[1] = d->position;
+    cudaStream_t s = d->stream;
+    if (si_status st = cuda(cudaMemcpyAsync(d->prompt, d->pinned_prompt, size_t(prompt_tokens) * 4,
+                                            cudaMemcpyHostToDevice, s), "upload"))
+        return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->feed, d->pinned_feed, sizeof(k::DecodeFeed), cudaMemcpyHostToDevice, s),
+                            "upload"))
+        return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->control, d->pinned, 8, cudaMemcpyHostToDevice, s), "upload")) return st;
+    for (int64_t i = 0; i < n; ++i)
+        if (si_status st = cuda(cudaGraphLaunch(d->feed_exec, s), "cudaGraphLaunch")) return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->pinned_history, d->history, size_t(n) * 4, cudaMemcpyDeviceToHost, s),
+                            "readback"))
+        return st;
+    if (si_status st = cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return st;
+    std::memcpy(tokens, d->pinned_history, size_t(n) * 4);
+    d->position += int32_t(n);
+    return SI_OK;
+}
+
+si_status si_decoder_reset(si_decoder *d) {
+    if (!d) return fail(SI_ERR_INVALID_ARGUMENT, "null decoder");
+    std::lock_guard<std::mutex> g(d->lock);
+    d->position = 0;
+    return SI_OK;
+}
+
+si_status si_decoder_position(si_decoder *d, int32_t *position) {
+    if (!d || !position) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *position = d->position;
+    return SI_OK;
+}
+
+}  // extern "C"

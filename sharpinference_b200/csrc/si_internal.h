@@ -43,6 +43,13 @@ si_status byte_length(uint32_t type, uint64_t elements, uint64_t *bytes);
 float half_to_float(uint16_t h);
 uint16_t float_to_half(float f);
 
+// The tensor [ptr, ptr + bytes) lies inside one device allocation of the
+// current device (SI_ERR_INVALID_ARGUMENT naming `port` otherwise).
+si_status device_range(const char *port, const void *ptr, uint64_t bytes);
+bool ranges_overlap(const void *a, uint64_t an, const void *b, uint64_t bn);
+// Maps a cudaError_t onto si_status with the runtime's message.
+si_status cuda_error(int error, const char *what);
+
 }  // namespace si
 
 // Launch wrappers implemented in the .cu files (host side of each kernel).
@@ -81,4 +88,49 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
 // when the shape or alignment needs another kernel (nothing launched then).
 si_status matvec_q4k_batched(const void *w, const float *x, float *y, int64_t m, int64_t rows, int64_t cols,
                              void *stream, const int32_t *control);
+// ---- transformer instructions (transformer.cu) ------------------------------
+// Device-side greedy loop state read by the argmax kernel after each decode
+// step: it stores the step's token in history[position - base] and writes
+// the next step's control = (next token, position + 1), where the next token
+// is prompt[k + 1] while prompt tokens remain, else the argmax.
+struct DecodeFeed {
+    int32_t *control;       // [token, position] read by the decode step
+    const int32_t *prompt;  // prompt tokens, prompt[0] at position `base`
+    int32_t *history;       // argmax of every step, `capacity` entries
+    int32_t base;
+    int32_t prompt_tokens;
+    int32_t capacity;
+    int32_t pad;
+};
+si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
+                        void *stream);
+si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
+                                    int64_t batch, int64_t width, void *stream);
+si_status tr_copy_rows(const float *in, float *out, int64_t count, void *stream);
+// residual == nullptr: rms-norm; otherwise residual-rms-norm (updated written).
+// control == nullptr: every row; otherwise rows < control[1].
+si_status tr_rms_norm(const float *in, const float *residual, const float *weight, const int32_t *control,
+                      float *updated, float *out, int64_t batch, int64_t width, float eps, void *stream);
+si_status tr_swiglu(const float *gate_up, const int32_t *control, float *out, int64_t batch, int64_t width,
+                    void *stream);
+si_status tr_scaled_add(const float *in, const float *update, float *out, int64_t count, float scale, void *stream);
+// control == nullptr: single form at *position; otherwise the batch form.
+si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int32_t *control, const float *freq,
+                           float *query, float *key_cache, float *value_cache, int64_t batch, int64_t qsize,
+                           int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale, void *stream);
+si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
+                              int query_heads, int kv_heads, int head_size, int64_t context, void *stream);
+si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *position, const int32_t *control,
+                        float *scores, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
+                        void *stream);
+si_status tr_causal_softmax(const float *scores, const int32_t *position, const int32_t *control, float *probs,
+                            int64_t batch, int heads, int64_t context, void *stream);
+si_status tr_gqa_values(const float *probs, const float *vc, const int32_t *position, const int32_t *control,
+                        float *out, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
+                        void *stream);
+si_status tr_argmax(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, void *stream);
+si_status tr_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width,
+                         void *stream);
+si_status tr_gather_rows(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,
+                         int64_t width, void *stream);
 }  // namespace si::kernels

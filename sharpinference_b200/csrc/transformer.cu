@@ -1,0 +1,762 @@
+// FP32 transformer instructions of SharpInference (collection
+// TransformerFloat32, GpuTransformerInstructionCollection.cs and
+// GpuBatchTransformerInstructions.cs) and core.gather-row with quantised
+// tables, as sm_100a kernels.
+//
+// Every kernel is launched with programmatic dependent launch: it lets its
+// successor start launching at once (pdl_trigger) and reads its inputs only
+// after pdl_wait, so inside the decode graph a GEMV's weight stream overlaps
+// the small kernels in front of it. Arithmetic is FP32 with explicit
+// round-to-nearest intrinsics where the instruction body fixes an order
+// (no contraction into FMA).
+//
+// Decode attention (transformer.grouped-query-attention) is split over
+// tokens: one 8-CTA cluster per key/value head, each CTA an online softmax
+// over its share of the cache for all query heads of the group, combined
+// through distributed shared memory. No workspace, no atomics.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+
+#include "device_common.cuh"
+#include "si_internal.h"
+
+namespace si::kernels {
+namespace {
+
+using namespace si::dev;
+
+constexpr float kNegMax = -3.402823466e+38f;
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float dsmem_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t dsmem_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+// All threads of all CTAs of the cluster. Every CTA of a cluster is resident
+// at once and every thread reaches each call, so the barrier completes.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over the block (blockDim.x a multiple of 32, at most 1024); every
+// thread gets the total. `red` holds 33 floats of shared memory.
+__device__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// ---- element access of a table row ----------------------------------------
+// Element c of a row in GGUF layout, dequantised exactly as the CPU codecs
+// do it: Q8_0 d*q; Q4_K (d*sc)*q - (dmin*m).
+__device__ __forceinline__ float row_element(uint32_t type, const uint8_t *row, int64_t c) {
+    switch (type) {
+    case SI_TYPE_F32: return reinterpret_cast<const float *>(row)[c];
+    case SI_TYPE_F16: return __half2float(reinterpret_cast<const __half *>(row)[c]);
+    case SI_TYPE_Q8_0: {
+        const uint8_t *b = row + (c >> 5) * kQ8_0Bytes;
+        const float d = __half2float(*reinterpret_cast<const __half *>(b));
+        return __fmul_rn(d, float(int8_t(b[2 + (c & 31)])));
+    }
+    default: {  // SI_TYPE_Q4_K
+        const uint8_t *b = row + (c >> 8) * kQ4KBytes;
+        const float d = __half2float(*reinterpret_cast<const __half *>(b));
+        const float dmin = __half2float(*reinterpret_cast<const __half *>(b + 2));
+        const uint8_t *sc = b + 4;
+        const int e = int(c & 255), s = e >> 5;
+        int scale, mn;
+        if (s < 4) {
+            scale = sc[s] & 63;
+            mn = sc[s + 4] & 63;
+        } else {
+            scale = (sc[s + 4] & 0x0f) | ((sc[s - 4] >> 6) << 4);
+            mn = (sc[s + 4] >> 4) | ((sc[s] >> 6) << 4);
+        }
+        const int q = (b[16 + 32 * (s >> 1) + (e & 31)] >> (4 * (s & 1))) & 15;
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, float(scale)), float(q)), __fmul_rn(dmin, float(mn)));
+    }
+    }
+}
+
+// core.gather-row: out = table[index], NaN everywhere for an index outside
+// [0, rows) (GpuTierZeroInstruction.cs:397-407).
+__global__ void gather_row_kernel(uint32_t type, const uint8_t *table, int64_t rows, int64_t cols, uint64_t row_bytes,
+                                  const int32_t *index, float *out) {
+    pdl_trigger();
+    pdl_wait();
+    const int32_t r = *index;
+    const bool ok = r >= 0 && r < rows;
+    const uint8_t *row = table + (ok ? uint64_t(r) * row_bytes : 0);
+    for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < cols; c += int64_t(gridDim.x) * blockDim.x)
+        out[c] = ok ? row_element(type, row, c) : __int_as_float(0x7fc00000);
+}
+
+// transformer.embedding-gather-batch: FP16 table rows by index; an index
+// outside the table reads 0, as an out-of-range raw-buffer load does under
+// Direct3D 12 (GpuTransformerInstructionCollection.cs:184-219).
+__global__ void embedding_gather_batch_kernel(const __half *table, int64_t rows, const int32_t *indices, float *out,
+                                              int64_t count, int64_t width) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / width, col = e - row * width;
+        const int64_t t = int64_t(uint32_t(indices[row]));
+        out[e] = t < rows ? __half2float(table[t * width + col]) : 0.0f;
+    }
+}
+
+// transformer.copy-embedding-rows (GpuTransformerInstructionCollection.cs:221-248).
+__global__ void copy_rows_kernel(const float *in, float *out, int64_t count) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x)
+        out[e] = in[e];
+}
+
+// transformer.rms-norm / residual-rms-norm and their batch forms: one CTA
+// per row; rows at or beyond control[1] are skipped (batch forms only).
+// updated = hidden + residual is stored before the norm reads it back, so
+// `updated` may alias `hidden`.
+template <bool kResidual>
+__global__ void __launch_bounds__(1024) rms_norm_kernel(const float *in, const float *residual, const float *weight,
+                                                        const int32_t *control, float *updated, float *out,
+                                                        int64_t width, float eps) {
+    __shared__ float red[33];
+    pdl_trigger();
+    pdl_wait();
+    const int64_t row = blockIdx.x;
+    if (control && row >= control[1]) return;
+    const float *x = in + row * width;
+    float *u = kResidual ? updated + row * width : nullptr;
+    float s = 0.0f;
+    for (int64_t j = threadIdx.x; j < width; j += blockDim.x) {
+        float v = x[j];
+        if (kResidual) {
+            v = __fadd_rn(v, residual[row * width + j]);
+            u[j] = v;
+        }
+        s = __fadd_rn(s, __fmul_rn(v, v));
+    }
+    s = block_sum(s, red);
+    const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s, float(width)), eps));
+    float *o = out + row * width;
+    for (int64_t j = threadIdx.x; j < width; j += blockDim.x) {
+        const float v = kResidual ? u[j] : x[j];
+        o[j] = __fmul_rn(__fmul_rn(v, scale), weight[j]);
+    }
+}
+
+// transformer.swiglu / batch-swiglu: out = gate / (1 + exp(-gate)) * up with
+// gate_up = [gate | up] per row.
+__global__ void swiglu_kernel(const float *gate_up, const int32_t *control, float *out, int64_t batch, int64_t width) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t count = batch * width;
+    const int64_t valid = control ? int64_t(control[1]) : batch;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / width, col = e - row * width;
+        if (row >= valid) continue;
+        const float g = gate_up[row * 2 * width + col], up = gate_up[row * 2 * width + width + col];
+        out[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+    }
+}
+
+// transformer.scaled-add: out = in + scale * update.
+__global__ void scaled_add_kernel(const float *in, const float *update, float *out, int64_t count, float scale) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x)
+        out[e] = __fadd_rn(in[e], __fmul_rn(scale, update[e]));
+}
+
+// transformer.rope-kv-write / batch-rope-kv-write. Single form: the token
+// position is *position and there is one row; batch form: row b is the
+// token at control[0] + b, rows b >= control[1] are skipped. Rows whose
+// position is outside [0, context) write nothing.
+__global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const int32_t *control, const float *freq,
+                               float *query, float *key_cache, float *value_cache, int64_t batch, int64_t qsize,
+                               int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t width = qsize + 2 * kvsize, count = batch * width;
+    const int half = rotary / 2;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / width, local = e - row * width;
+        int32_t pos;
+        if (control) {
+            if (row >= control[1]) continue;
+            pos = control[0] + int32_t(row);
+        } else {
+            pos = *position;
+        }
+        if (pos < 0 || pos >= context) continue;
+        float v = qkv[e];
+        const bool is_query = local < qsize, is_key = !is_query && local < qsize + kvsize;
+        if (is_query || is_key) {
+            const int d = int((is_query ? local : local - qsize) % head_size);
+            if (d < rotary) {
+                const int ri = d < half ? d : d - half;
+                const float other = qkv[d < half ? e + half : e - half];
+                const float angle = __fmul_rn(float(pos), freq[ri]);
+                const float c = __fmul_rn(cosf(angle), rope_scale), s = __fmul_rn(sinf(angle), rope_scale);
+                v = d < half ? __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, s))
+                             : __fadd_rn(__fmul_rn(v, c), __fmul_rn(other, s));
+            }
+            if (is_query) query[row * qsize + local] = v;
+            else key_cache[int64_t(pos) * kvsize + (local - qsize)] = v;
+        } else {
+            value_cache[int64_t(pos) * kvsize + (local - qsize - kvsize)] = v;
+        }
+    }
+}
+
+// ---- decode attention --------------------------------------------------------
+constexpr int kAttnCluster = 8;
+constexpr int kAttnWarps = 8;
+
+// One cluster of kAttnCluster CTAs per key/value head. Tokens 0..active,
+// active = min(max(0, *position), context - 1), are split into contiguous
+// per-CTA ranges; inside a CTA each warp takes tiles of kTile tokens and
+// keeps an online softmax (running max m, denominator l, weighted values)
+// for the G query heads of the group. Lane j holds channels j + 32 i.
+template <int NPL, int MAXG, int kTile>
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
+    gqa_decode_kernel(const float *query, const float *key_cache, const float *value_cache, const int32_t *position,
+                      float *out, int group, int kv_heads, int head_size, int64_t context, float scale) {
+    extern __shared__ float smem[];
+    const int G = group, hs = head_size;
+    float *w_acc = smem;                                 // [warps][G][hs]
+    float *w_m = w_acc + kAttnWarps * G * hs;            // [warps][G]
+    float *w_l = w_m + kAttnWarps * G;                   // [warps][G]
+    float *c_acc = w_l + kAttnWarps * G;                 // [G][hs]
+    float *c_m = c_acc + G * hs;                         // [G]
+    float *c_l = c_m + G;                                // [G]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kvh = blockIdx.x / kAttnCluster;
+    const uint32_t rank = cta_rank_in_cluster();
+    pdl_trigger();
+    pdl_wait();
+    int64_t active = *position;
+    active = active < 0 ? 0 : (active > context - 1 ? context - 1 : active);
+    const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
+    const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
+
+    float q[MAXG][NPL], acc[MAXG][NPL], m[MAXG], l[MAXG];
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int d = lane + 32 * i;
+            q[g][i] = (g < G && d < hs) ? query[(int64_t(kvh) * G + g) * hs + d] : 0.0f;
+            acc[g][i] = 0.0f;
+        }
+    }
+    const int64_t stride = int64_t(kv_heads) * hs;
+    for (int64_t tb = t0 + int64_t(warp) * kTile; tb < t1; tb += int64_t(kAttnWarps) * kTile) {
+        float kr[kTile][NPL], vr[kTile][NPL];
+#pragma unroll
+        for (int u = 0; u < kTile; ++u) {
+            const int64_t t = tb + u;
+            const float *kp = key_cache + t * stride + int64_t(kvh) * hs;
+            const float *vp = value_cache + t * stride + int64_t(kvh) * hs;
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                const int d = lane + 32 * i;
+                const bool ok = t < t1 && d < hs;
+                kr[u][i] = ok ? kp[d] : 0.0f;
+                vr[u][i] = ok ? vp[d] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g) {
+            if (g >= G) break;
+            float s[kTile];
+            float tile_max = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < kTile; ++u) {
+                float p = 0.0f;
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) p = __fadd_rn(p, __fmul_rn(q[g][i], kr[u][i]));
+                s[u] = __fmul_rn(warp_sum(p), scale);
+                if (tb + u < t1) tile_max = fmaxf(tile_max, s[u]);
+            }
+            const float m_new = fmaxf(m[g], tile_max);
+            const float corr = m[g] == -INFINITY ? 0.0f : expf(__fsub_rn(m[g], m_new));
+            float lsum = __fmul_rn(l[g], corr);
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) acc[g][i] = __fmul_rn(acc[g][i], corr);
+#pragma unroll
+            for (int u = 0; u < kTile; ++u) {
+                if (tb + u >= t1) break;
+                const float p = expf(__fsub_rn(s[u], m_new));
+                lsum = __fadd_rn(lsum, p);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) acc[g][i] = __fadd_rn(acc[g][i], __fmul_rn(p, vr[u][i]));
+            }
+            l[g] = lsum;
+            m[g] = m_new;
+        }
+    }
+    // Warp partials -> CTA partial.
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) {
+        if (g >= G) break;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int d = lane + 32 * i;
+            if (d < hs) w_acc[(warp * G + g) * hs + d] = acc[g][i];
+        }
+        if (lane == 0) {
+            w_m[warp * G + g] = m[g];
+            w_l[warp * G + g] = l[g];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * hs; idx += blockDim.x) {
+        const int g = idx / hs, d = idx - g * hs;
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, w_m[w * G + g]);
+        float A = 0.0f, L = 0.0f;
+        if (M != -INFINITY)
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float mw = w_m[w * G + g];
+                if (mw == -INFINITY) continue;
+                const float f = expf(__fsub_rn(mw, M));
+                A = __fadd_rn(A, __fmul_rn(w_acc[(w * G + g) * hs + d], f));
+                L = __fadd_rn(L, __fmul_rn(w_l[w * G + g], f));
+            }
+        c_acc[idx] = A;
+        if (d == 0) {
+            c_m[g] = M;
+            c_l[g] = L;
+        }
+    }
+    cluster_sync();
+    // CTA partials of the cluster -> output; rank r finishes a slice.
+    const int total = G * hs, chunk = (total + kAttnCluster - 1) / kAttnCluster;
+    const int lo = int(rank) * chunk, hi = lo + chunk < total ? lo + chunk : total;
+    for (int idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
+        const int g = idx / hs, d = idx - g * hs;
+        float mr[kAttnCluster];
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            mr[r] = dsmem_f32(dsmem_addr(c_m + g, uint32_t(r)));
+            M = fmaxf(M, mr[r]);
+        }
+        float A = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            if (mr[r] == -INFINITY) continue;
+            const float f = expf(__fsub_rn(mr[r], M));
+            A = __fadd_rn(A, __fmul_rn(dsmem_f32(dsmem_addr(c_acc + idx, uint32_t(r))), f));
+            L = __fadd_rn(L, __fmul_rn(dsmem_f32(dsmem_addr(c_l + g, uint32_t(r))), f));
+        }
+        out[(int64_t(kvh) * G + g) * hs + d] = __fdiv_rn(A, L);
+    }
+    cluster_sync();  // no CTA leaves while a peer may still read its partials
+}
+
+// ---- unfused attention instructions (single and batch forms) --------------
+// transformer.gqa-scores / batch-gqa-scores. Single form (control null):
+// active = *position and the token test is the instruction's unsigned
+// token <= uint(active). Batch form: rows b < control[1], active =
+// control[0] + b and a negative active scores nothing.
+__global__ void gqa_scores_kernel(const float *query, const float *key_cache, const int32_t *position,
+                                  const int32_t *control, float *scores, int64_t batch, int query_heads, int group,
+                                  int kv_heads, int head_size, int64_t context, float scale) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t count = batch * query_heads * context;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / (int64_t(query_heads) * context);
+        const int64_t local = e - row * query_heads * context;
+        const int head = int(local / context);
+        const int64_t token = local - int64_t(head) * context;
+        bool take;
+        if (control) {
+            if (row >= control[1]) continue;
+            const int32_t active = control[0] + int32_t(row);
+            take = active >= 0 && uint32_t(token) <= uint32_t(active);
+        } else {
+            take = uint32_t(token) <= uint32_t(*position);
+        }
+        float s = kNegMax;
+        if (take) {
+            const int kvh = head / group;
+            const float *qp = query + (row * query_heads + head) * head_size;
+            const float *kp = key_cache + (token * kv_heads + kvh) * head_size;
+            s = 0.0f;
+            for (int d = 0; d < head_size; ++d) s = __fadd_rn(s, __fmul_rn(qp[d], kp[d]));
+            s = __fmul_rn(s, scale);
+        }
+        scores[e] = s;
+    }
+}
+
+// transformer.causal-softmax / batch-causal-softmax: one CTA per (row, head).
+__global__ void causal_softmax_kernel(const float *scores, const int32_t *position, const int32_t *control,
+                                      float *probs, int heads, int64_t context) {
+    __shared__ float red[33];
+    pdl_trigger();
+    pdl_wait();
+    const int64_t row = blockIdx.x / heads;
+    int32_t active;
+    bool valid = true;
+    if (control) {
+        if (row >= control[1]) return;
+        active = control[0] + int32_t(row);
+        valid = active >= 0;
+    } else {
+        active = *position;
+    }
+    const float *s = scores + int64_t(blockIdx.x) * context;
+    float *p = probs + int64_t(blockIdx.x) * context;
+    float mx = kNegMax;
+    if (valid)
+        for (int64_t t = threadIdx.x; uint32_t(t) <= uint32_t(active) && t < context; t += blockDim.x) mx = fmaxf(mx, s[t]);
+    // block max
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : kNegMax;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) red[32] = v;
+    }
+    __syncthreads();
+    const float maximum = red[32];
+    __syncthreads();
+    float sum = 0.0f;
+    if (valid)
+        for (int64_t t = threadIdx.x; uint32_t(t) <= uint32_t(active) && t < context; t += blockDim.x)
+            sum = __fadd_rn(sum, expf(__fsub_rn(s[t], maximum)));
+    const float denominator = block_sum(sum, red);
+    for (int64_t t = threadIdx.x; t < context; t += blockDim.x)
+        p[t] = valid && uint32_t(t) <= uint32_t(active) ? __fdiv_rn(expf(__fsub_rn(s[t], maximum)), denominator) : 0.0f;
+}
+
+// transformer.gqa-values / batch-gqa-values: one thread per output element.
+__global__ void gqa_values_kernel(const float *probs, const float *value_cache, const int32_t *position,
+                                  const int32_t *control, float *out, int64_t batch, int query_heads, int group,
+                                  int kv_heads, int head_size, int64_t context) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t width = int64_t(query_heads) * head_size, count = batch * width;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / width, local = e - row * width;
+        const int head = int(local / head_size), d = int(local - int64_t(head) * head_size);
+        int32_t active;
+        bool valid = true;
+        if (control) {
+            if (row >= control[1]) continue;
+            active = control[0] + int32_t(row);
+            valid = active >= 0;
+        } else {
+            active = *position;
+        }
+        const int kvh = head / group;
+        const float *pp = probs + (row * query_heads + head) * context;
+        float s = 0.0f;
+        if (valid)
+            for (int64_t t = 0; uint32_t(t) <= uint32_t(active) && t < context; ++t)
+                s = __fadd_rn(s, __fmul_rn(pp[t], value_cache[(t * kv_heads + kvh) * head_size + d]));
+        out[e] = s;
+    }
+}
+
+// ---- argmax -----------------------------------------------------------------
+constexpr int kArgmaxCluster = 8;
+constexpr int kArgmaxThreads = 1024;
+
+// The instruction's merge rule: a candidate replaces the best when greater,
+// or equal with a smaller index (GpuTransformerInstructionCollection.cs:697-744).
+__device__ __forceinline__ void argmax_merge(float &b, uint32_t &bi, float o, uint32_t oi) {
+    if (o > b || (o == b && oi < bi)) {
+        b = o;
+        bi = oi;
+    }
+}
+
+// transformer.argmax over one 8-CTA cluster. With `feed` set (device-side
+// greedy loop) it also records the token and prepares the next step's
+// control: position + 1 and the next prompt token or the argmax.
+__global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
+    argmax_kernel(const float *in, int64_t n, int32_t *out, DecodeFeed *feed) {
+    __shared__ float sb[32];
+    __shared__ uint32_t si[32];
+    pdl_trigger();
+    pdl_wait();
+    float b = kNegMax;
+    uint32_t bi = 0;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t j = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; j < n; j += stride)
+        argmax_merge(b, bi, in[j], uint32_t(j));
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(b, bi, ob, oi);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sb[warp] = b;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        b = lane < int(blockDim.x >> 5) ? sb[lane] : kNegMax;
+        bi = lane < int(blockDim.x >> 5) ? si[lane] : 0u;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            argmax_merge(b, bi, ob, oi);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        sb[0] = b;
+        si[0] = bi;
+    }
+    cluster_sync();
+    if (cta_rank_in_cluster() == 0 && threadIdx.x == 0) {
+        float best = sb[0];
+        uint32_t idx = si[0];
+        for (uint32_t r = 1; r < kArgmaxCluster; ++r)
+            argmax_merge(best, idx, dsmem_f32(dsmem_addr(sb, r)), dsmem_u32(dsmem_addr(si, r)));
+        *out = int32_t(idx);
+        if (feed) {
+            const int32_t pos = feed->control[1], k = pos - feed->base;
+            if (k >= 0 && k < feed->capacity) feed->history[k] = int32_t(idx);
+            feed->control[1] = pos + 1;
+            feed->control[0] = k + 1 < feed->prompt_tokens ? feed->prompt[k + 1] : int32_t(idx);
+        }
+    }
+    cluster_sync();  // rank 0 has read every CTA's candidate
+}
+
+// transformer.batch-select-last: out = input row control[1] - 1.
+__global__ void select_last_kernel(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width) {
+    pdl_trigger();
+    pdl_wait();
+    const int32_t valid = control[1];
+    if (valid <= 0 || valid > batch) return;
+    for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < width; c += int64_t(gridDim.x) * blockDim.x)
+        out[c] = in[int64_t(valid - 1) * width + c];
+}
+
+// transformer.batch-gather-rows: output row b = table row control[0] + b.
+__global__ void gather_rows_kernel(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,
+                                   int64_t width) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t count = batch * width;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = e / width, col = e - row * width, src = int64_t(control[0]) + row;
+        if (row < control[1] && src >= 0 && src < rows) out[e] = table[src * width + col];
+    }
+}
+
+// ---- launch helpers -----------------------------------------------------------
+int sm_count_cached() {
+    static int n = [] {
+        int dev = 0, v = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v;
+    }();
+    return n;
+}
+
+int elementwise_grid(int64_t count, int threads) {
+    const int64_t blocks = (count + threads - 1) / threads;
+    const int64_t cap = int64_t(sm_count_cached()) * 8;
+    return int(std::max<int64_t>(1, std::min(blocks, cap)));
+}
+
+template <class... KArgs, class... Args>
+si_status launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
+                 Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+    return SI_OK;
+}
+
+}  // namespace
+
+si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
+                        void *stream) {
+    uint64_t row_bytes = 0;
+    if (si_status st = byte_length(type, uint64_t(cols), &row_bytes)) return st;
+    return launch("core.gather-row", gather_row_kernel, dim3(elementwise_grid(cols, 256)), dim3(256), 0, stream, type,
+                  static_cast<const uint8_t *>(table), rows, cols, row_bytes, index, out);
+}
+
+si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
+                                    int64_t batch, int64_t width, void *stream) {
+    const int64_t count = batch * width;
+    return launch("transformer.embedding-gather-batch", embedding_gather_batch_kernel,
+                  dim3(elementwise_grid(count, 256)), dim3(256), 0, stream, reinterpret_cast<const __half *>(table),
+                  rows, indices, out, count, width);
+}
+
+si_status tr_copy_rows(const float *in, float *out, int64_t count, void *stream) {
+    return launch("transformer.copy-embedding-rows", copy_rows_kernel, dim3(elementwise_grid(count, 256)), dim3(256),
+                  0, stream, in, out, count);
+}
+
+si_status tr_rms_norm(const float *in, const float *residual, const float *weight, const int32_t *control,
+                      float *updated, float *out, int64_t batch, int64_t width, float eps, void *stream) {
+    const int threads = width >= 1024 ? 1024 : int(std::max<int64_t>(32, (width + 31) / 32 * 32));
+    if (residual)
+        return launch("transformer.residual-rms-norm", rms_norm_kernel<true>, dim3(unsigned(batch)), dim3(threads), 0,
+                      stream, in, residual, weight, control, updated, out, width, eps);
+    return launch("transformer.rms-norm", rms_norm_kernel<false>, dim3(unsigned(batch)), dim3(threads), 0, stream, in,
+                  residual, weight, control, updated, out, width, eps);
+}
+
+si_status tr_swiglu(const float *gate_up, const int32_t *control, float *out, int64_t batch, int64_t width,
+                    void *stream) {
+    return launch("transformer.swiglu", swiglu_kernel, dim3(elementwise_grid(batch * width, 256)), dim3(256), 0,
+                  stream, gate_up, control, out, batch, width);
+}
+
+si_status tr_scaled_add(const float *in, const float *update, float *out, int64_t count, float scale, void *stream) {
+    return launch("transformer.scaled-add", scaled_add_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+                  stream, in, update, out, count, scale);
+}
+
+si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int32_t *control, const float *freq,
+                           float *query, float *key_cache, float *value_cache, int64_t batch, int64_t qsize,
+                           int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale,
+                           void *stream) {
+    const int64_t count = batch * (qsize + 2 * kvsize);
+    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+                  stream, qkv, position, control, freq, query, key_cache, value_cache, batch, qsize, kvsize, head_size,
+                  rotary, context, rope_scale);
+}
+
+namespace {
+template <int NPL, int MAXG, int kTile>
+si_status launch_gqa(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
+                     int group, int kv_heads, int head_size, int64_t context, float scale, void *stream) {
+    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile>;
+    const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
+                               2 * group) * sizeof(float);
+    if (smem > 48 * 1024) {
+        static bool raised = false;
+        if (!raised) {
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            raised = true;
+        }
+    }
+    return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(kv_heads * kAttnCluster)),
+                  dim3(kAttnWarps * 32), smem, stream, query, kc, vc, position, out, group, kv_heads, head_size,
+                  context, scale);
+}
+}  // namespace
+
+si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
+                              int query_heads, int kv_heads, int head_size, int64_t context, void *stream) {
+    const int group = query_heads / kv_heads;
+    const float scale = 1.0f / sqrtf(float(head_size));
+    const int npl = (head_size + 31) / 32;
+    if (group <= 4) {
+        if (npl <= 1) return launch_gqa<1, 4, 8>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+        if (npl <= 2) return launch_gqa<2, 4, 8>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+        if (npl <= 4) return launch_gqa<4, 4, 8>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+        return launch_gqa<8, 4, 4>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+    }
+    if (npl <= 1) return launch_gqa<1, 8, 8>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+    if (npl <= 2) return launch_gqa<2, 8, 4>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+    if (npl <= 4) return launch_gqa<4, 8, 4>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+    return launch_gqa<8, 8, 2>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream);
+}
+
+si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *position, const int32_t *control,
+                        float *scores, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
+                        void *stream) {
+    const int64_t count = batch * query_heads * context;
+    return launch("transformer.gqa-scores", gqa_scores_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+                  stream, query, kc, position, control, scores, batch, query_heads, query_heads / kv_heads, kv_heads,
+                  head_size, context, 1.0f / sqrtf(float(head_size)));
+}
+
+si_status tr_causal_softmax(const float *scores, const int32_t *position, const int32_t *control, float *probs,
+                            int64_t batch, int heads, int64_t context, void *stream) {
+    return launch("transformer.causal-softmax", causal_softmax_kernel, dim3(unsigned(batch * heads)), dim3(256), 0,
+                  stream, scores, position, control, probs, heads, context);
+}
+
+si_status tr_gqa_values(const float *probs, const float *vc, const int32_t *position, const int32_t *control,
+                        float *out, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
+                        void *stream) {
+    const int64_t count = batch * query_heads * head_size;
+    return launch("transformer.gqa-values", gqa_values_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+                  stream, probs, vc, position, control, out, batch, query_heads, query_heads / kv_heads, kv_heads,
+                  head_size, context);
+}
+
+si_status tr_argmax(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, void *stream) {
+    return launch("transformer.argmax", argmax_kernel, dim3(kArgmaxCluster), dim3(kArgmaxThreads), 0, stream, in, n,
+                  out, feed);
+}
+
+si_status tr_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width,
+                         void *stream) {
+    return launch("transformer.batch-select-last", select_last_kernel, dim3(elementwise_grid(width, 256)), dim3(256),
+                  0, stream, in, control, out, batch, width);
+}
+
+si_status tr_gather_rows(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,
+                         int64_t width, void *stream) {
+    return launch("transformer.batch-gather-rows", gather_rows_kernel, dim3(elementwise_grid(batch * width, 256)),
+                  dim3(256), 0, stream, table, rows, control, out, batch, width);
+}
+
+}  // namespace si::kernels

@@ -122,6 +122,40 @@ SIGNATURES = {
     "si_graph_destroy": [_vp],
     "si_instruction_resolve": [C.c_char_p, C.c_char_p, C.POINTER(C.c_int)],
     "si_instruction_validate": [_i32, _pu32, _i32, C.c_char_p],
+    # transformer instructions (device pointers, stream last)
+    "si_gather_row": [_u32, _vp, _i64, _i64, _vp, _vp, _vp],
+    "si_rms_norm": [_vp, _vp, _vp, _i64, C.c_float, _vp],
+    "si_residual_rms_norm": [_vp, _vp, _vp, _vp, _vp, _i64, C.c_float, _vp],
+    "si_swiglu": [_vp, _vp, _i64, _vp],
+    "si_scaled_add": [_vp, _vp, _vp, _i64, C.c_float, _vp],
+    "si_rope_kv_write": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, C.c_float, _vp],
+    "si_grouped_query_attention": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],
+    "si_gqa_scores": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],
+    "si_causal_softmax": [_vp, _vp, _vp, _i32, _i64, _vp],
+    "si_gqa_values": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],
+    "si_argmax": [_vp, _i64, _vp, _vp],
+    "si_embedding_gather_batch": [_vp, _i64, _vp, _vp, _i64, _i64, _vp],
+    "si_copy_embedding_rows": [_vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "si_batch_rms_norm": [_vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _vp],
+    "si_batch_residual_rms_norm": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _vp],
+    "si_batch_swiglu": [_vp, _vp, _vp, _i64, _i64, _vp],
+    "si_batch_rope_kv_write": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _i64, C.c_float, _vp],
+    "si_batch_gqa_scores": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp],
+    "si_batch_causal_softmax": [_vp, _vp, _vp, _i64, _i32, _i64, _vp],
+    "si_batch_gqa_values": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp],
+    "si_batch_select_last": [_vp, _vp, _vp, _i64, _i64, _vp],
+    "si_batch_gather_rows": [_vp, _i64, _vp, _vp, _i64, _i64, _vp],
+    # decoder session
+    "si_decoder_create": [_i32, _vp, C.POINTER(_vp)],
+    "si_decoder_destroy": [_vp],
+    "si_decoder_slot": [_vp, C.c_char_p, C.POINTER(_vp), _pu64],
+    "si_decoder_upload": [_vp, C.c_char_p, _u64, _vp, _u64],
+    "si_decoder_read": [_vp, C.c_char_p, _u64, _vp, _u64],
+    "si_decoder_stream": [_vp, C.POINTER(_vp)],
+    "si_decoder_forward_token": [_vp, C.c_int32, C.POINTER(C.c_int32)],
+    "si_decoder_generate": [_vp, _vp, C.c_int32, C.c_int32, _vp],
+    "si_decoder_reset": [_vp],
+    "si_decoder_position": [_vp, C.POINTER(C.c_int32)],
 }
 _RESTYPE = {"si_abi_version": C.c_int}
 
@@ -432,3 +466,86 @@ def header_functions(header: Path | None = None) -> list[str]:
     text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
     return sorted(set(re.findall(r"\b(si_[a-z0-9_]+)\s*\(", text)))
 
+
+
+# ---- Phi-4 decoder session -----------------------------------------------------------
+class DecoderConfig(C.Structure):
+    """si_decoder_config."""
+    _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("query_heads", C.c_int32), ("kv_heads", C.c_int32),
+                ("head_size", C.c_int32), ("rotary_size", C.c_int32), ("intermediate", C.c_int32),
+                ("vocab", C.c_int32), ("context", C.c_int64), ("epsilon", C.c_float), ("rope_base", C.c_float),
+                ("rope_scale", C.c_float), ("weight_type", C.c_uint32), ("embedding_type", C.c_uint32)]
+
+
+def decoder_slot_names(layers: int) -> list[str]:
+    """Weight slots of the decode program (Phi4D3D12TextSession.cs:391-410)."""
+    names = ["token_embedding", "output_norm"]
+    for layer in range(layers):
+        names += [f"attn_norm_{layer}", f"ffn_norm_{layer}", f"qkv_weight_{layer}", f"attn_output_weight_{layer}",
+                  f"ffn_up_weight_{layer}", f"ffn_down_weight_{layer}"]
+    return names
+
+
+class Decoder:
+    """Phi4D3D12TextSession on CUDA: ForwardToken, Reset, Position, plus a
+    device-resident greedy loop (generate)."""
+
+    def __init__(self, cfg: dict, device: int = 0):
+        self.cfg = DecoderConfig(**cfg)
+        h = C.c_void_p()
+        call("si_decoder_create", device, C.byref(self.cfg), C.byref(h))
+        self.handle = h
+        s = C.c_void_p()
+        call("si_decoder_stream", h, C.byref(s))
+        self.stream = s.value
+
+    def slot(self, name: str) -> tuple[int, int]:
+        p, n = C.c_void_p(), C.c_uint64()
+        call("si_decoder_slot", self.handle, name.encode(), C.byref(p), C.byref(n))
+        return p.value, n.value
+
+    def upload(self, name: str, data, offset: int = 0) -> None:
+        np = _np()
+        arr = np.ascontiguousarray(data)
+        call("si_decoder_upload", self.handle, name.encode(), offset, arr.ctypes.data, arr.nbytes)
+
+    def read(self, name: str, dtype=None, count: int | None = None, offset: int = 0):
+        np = _np()
+        dtype = np.dtype(dtype or np.float32)
+        if count is None:
+            count = (self.slot(name)[1] - offset) // dtype.itemsize
+        out = np.empty(count, dtype=dtype)
+        call("si_decoder_read", self.handle, name.encode(), offset, out.ctypes.data, out.nbytes)
+        return out
+
+    def forward_token(self, token: int) -> int:
+        v = C.c_int32()
+        call("si_decoder_forward_token", self.handle, token, C.byref(v))
+        return v.value
+
+    def generate(self, prompt, steps: int):
+        np = _np()
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(p.size + steps, dtype=np.int32)
+        call("si_decoder_generate", self.handle, p.ctypes.data, p.size, steps, out.ctypes.data)
+        return out
+
+    def reset(self) -> None:
+        call("si_decoder_reset", self.handle)
+
+    @property
+    def position(self) -> int:
+        v = C.c_int32()
+        call("si_decoder_position", self.handle, C.byref(v))
+        return v.value
+
+    def close(self) -> None:
+        if self.handle:
+            call("si_decoder_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

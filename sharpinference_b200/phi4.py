@@ -1,0 +1,78 @@
+"""Phi-4 text decoder shapes and seeded random-init weights for the CUDA
+decoder session (native.Decoder, the counterpart of Phi4D3D12TextSession).
+
+The dimensions follow Phi4D3D12TextSession.cs:14-25 (Phi-4-mini); the 14B
+shape is the Phi-4 (14B) text model. Weights are synthetic: every linear
+slot is N(0, sigma) quantised to the configured GGUF type with its own seed
+(slot ordinal i of native.decoder_slot_names -> seed * 1_000_003 + i), norm
+weights are ones. Weights are generated and uploaded one slot at a time so
+host memory stays at one slot.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import native
+
+# Phi4D3D12TextSession.cs:14-25; epsilon / rope metadata of the Phi-4-mini GGUF
+# (phi3.attention.layer_norm_rms_epsilon, phi3.rope.freq_base,
+# phi3.rope.scaling.attn_factor = sqrt(1 + ln(32) / ln(4096))).
+PHI4_MINI = dict(layers=32, hidden=3072, query_heads=24, kv_heads=8, head_size=128, rotary_size=96,
+                 intermediate=8192, vocab=200064, context=4096, epsilon=1e-5, rope_base=10000.0,
+                 rope_scale=1.1902381, weight_type=native.Q4_K, embedding_type=native.Q4_K)
+PHI4_14B = dict(layers=40, hidden=5120, query_heads=40, kv_heads=10, head_size=128, rotary_size=128,
+                intermediate=17920, vocab=100352, context=4096, epsilon=1e-5, rope_base=250000.0, rope_scale=1.0,
+                weight_type=native.Q8_0, embedding_type=native.Q8_0)
+TINY = dict(layers=2, hidden=256, query_heads=2, kv_heads=1, head_size=128, rotary_size=96, intermediate=512,
+            vocab=640, context=128, epsilon=1e-5, rope_base=10000.0, rope_scale=1.1902381, weight_type=native.Q4_K,
+            embedding_type=native.Q4_K)
+
+
+def linear_shapes(cfg: dict) -> dict[str, tuple[int, int]]:
+    """(rows, cols) of every quantised slot (Phi4D3D12TextSession.cs:391-410)."""
+    h, f = cfg["hidden"], cfg["intermediate"]
+    kv = cfg["kv_heads"] * cfg["head_size"]
+    shapes = {"token_embedding": (cfg["vocab"], h)}
+    for layer in range(cfg["layers"]):
+        shapes[f"qkv_weight_{layer}"] = (h + 2 * kv, h)
+        shapes[f"attn_output_weight_{layer}"] = (h, h)
+        shapes[f"ffn_up_weight_{layer}"] = (2 * f, h)
+        shapes[f"ffn_down_weight_{layer}"] = (h, f)
+    return shapes
+
+
+def weight_bytes(cfg: dict) -> int:
+    """Bytes of weights one decode step reads: every linear slot once (the
+    tied token_embedding as the vocabulary projection) plus the norms."""
+    total = 0
+    for name, (rows, cols) in linear_shapes(cfg).items():
+        wt = cfg["embedding_type"] if name == "token_embedding" else cfg["weight_type"]
+        total += rows * native.row_bytes(wt, cols)
+    return total + (2 * cfg["layers"] + 1) * cfg["hidden"] * 4
+
+
+def synthetic_weights(cfg: dict, seed: int, sigma: float = 0.02, threads: int = 0):
+    """Yields (slot name, bytes) for every linear slot, one at a time."""
+    shapes = linear_shapes(cfg)
+    for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
+        if name not in shapes:
+            continue
+        rows, cols = shapes[name]
+        wt = cfg["embedding_type"] if name == "token_embedding" else cfg["weight_type"]
+        yield name, native.synth_weights(wt, seed * 1_000_003 + i, rows, cols, sigma, threads)
+
+
+def load_synthetic(decoder: "native.Decoder", cfg: dict, seed: int, sigma: float = 0.02, threads: int = 0) -> None:
+    for name, blob in synthetic_weights(cfg, seed, sigma, threads):
+        decoder.upload(name, blob)
+
+
+def random_prompt(seed: int, tokens: int, vocab: int) -> np.ndarray:
+    """Uniform random token ids (splitmix64 of the index, modulo vocab)."""
+    idx = np.arange(tokens, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = idx * np.uint64(0x9E3779B97F4A7C15) + np.uint64(seed * 0x632BE59BD9B4E019 & 0xFFFFFFFFFFFFFFFF)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    return (z % np.uint64(vocab)).astype(np.int32)

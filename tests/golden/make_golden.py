@@ -9,6 +9,9 @@ exactly as that test constructs them; cited per case):
   cooperative_matvec.npz        GpuMatVecTests shapes x signatures, with the
                                 double-precision expected values that test
                                 computes
+  transformer_known_answers.json  GpuTransformerInstructionTests cases, with
+                                the expected values computed the way each
+                                test computes them
 
 Run:  python tests/golden/make_golden.py   (deterministic; no inputs needed)
 """
@@ -95,6 +98,86 @@ def known_answers() -> dict:
     return cases
 
 
+def _avg_f32(values) -> np.float32:
+    """Enumerable.Average over floats: double accumulation, float result."""
+    return np.float32(np.sum(np.asarray(values, dtype=np.float64)) / len(values))
+
+
+def _rms_expected(row, weight, eps=np.float32(1e-5)):
+    row = np.asarray(row, dtype=np.float32)
+    scale = np.float32(1.0) / np.sqrt(_avg_f32(row * row) + eps, dtype=np.float32)
+    return (row * scale * np.asarray(weight, dtype=np.float32)).astype(np.float32)
+
+
+def _attention_reference(qkv, key_cache, value_cache, batch, qh, kvh, hs, start):
+    """AttentionReference of GpuTransformerInstructionTests.cs:514-559."""
+    qsize, kvsize = qh * hs, kvh * hs
+    width = qsize + 2 * kvsize
+    out = np.zeros(batch * qsize, dtype=np.float64)
+    for row in range(batch):
+        active = start + row
+        for head in range(qh):
+            kv = head // (qh // kvh)
+            scores = np.array([sum(qkv[row * width + head * hs + d] * key_cache[(t * kvh + kv) * hs + d]
+                                   for d in range(hs)) for t in range(active + 1)]) / np.sqrt(hs)
+            e = np.exp(scores - scores.max())
+            for d in range(hs):
+                out[row * qsize + head * hs + d] = sum(e[t] / e.sum() * value_cache[(t * kvh + kv) * hs + d]
+                                                       for t in range(active + 1))
+    return out
+
+
+def transformer_known_answers() -> dict:
+    src = "src/SharpInference.Tests/GpuTransformerInstructionTests.cs"
+    cases = {}
+    hidden = [1, -2, 3, -4, 5, -6, 7, -8]
+    residual = [0.5, 1, -1.5, 2, -2.5, 3, -3.5, 4]
+    weight = [1, 0.5, 1.5, 2, 0.75, 1.25, 0.25, 1.75]
+    updated = (np.float32(hidden) + np.float32(residual)).astype(np.float32)
+    cases["residual_rms_norm"] = {
+        "source": f"{src}:12-78", "epsilon": 1e-5, "hidden": hidden, "residual": residual, "weight": weight,
+        "expected_updated": updated.tolist(), "expected_output": _rms_expected(updated, weight).tolist(),
+        "tolerance": 1e-5,
+    }
+    gate_up = np.float32([-2, -1, 1, 2, 0.5, 1.5, -2, 3])
+    g, u = gate_up[:4], gate_up[4:]
+    cases["swiglu"] = {
+        "source": f"{src}:80-137", "gate_up": gate_up.tolist(),
+        "expected": (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float32).tolist(), "tolerance": 1e-5,
+    }
+    cases["scaled_add"] = {
+        "source": f"{src}:139-185", "input": [1, -2, 3, -4], "update": [0.5, 1, -1.5, 2], "scale": 2.0,
+        "expected": [2, 0, 0, 0], "tolerance": 1e-5,
+    }
+    rms_in = np.float32([1, -2, 3, -4, 5, 2, 4, -1, -3, 0.5, 9, 9, 9, 9, 9]).reshape(3, 5)
+    rms_w = [1, 0.5, 1.5, 2, 0.25]
+    expected = np.full((3, 5), -77.0, dtype=np.float32)
+    for row in range(2):
+        expected[row] = _rms_expected(rms_in[row], rms_w)
+    cases["batch_rms_norm"] = {
+        "source": f"{src}:187-235", "epsilon": 1e-5, "batch": 3, "width": 5, "input": rms_in.reshape(-1).tolist(),
+        "weight": rms_w, "control": [7, 2], "fill": -77.0, "expected": expected.reshape(-1).tolist(),
+        "tolerance": 1e-5,
+    }
+    cases["batch_gather_rows"] = {
+        "source": f"{src}:237-277", "rows": 5, "batch": 4, "width": 3,
+        "table": [0, 1, 2, 10, 11, 12, 20, 21, 22, 30, 31, 32, 40, 41, 42], "control": [2, 2], "fill": -17.0,
+        "expected": [20, 21, 22, 30, 31, 32, -17, -17, -17, -17, -17, -17], "tolerance": 1e-5,
+    }
+    qkv = [1, 0, 0, 1, 1, 1, 10, 20, 1, 1, 2, 0, 0, 2, 30, 40]
+    exp_k = [1, 0, 1, 1, 0, 2, -9, -9]
+    exp_v = [2, 4, 10, 20, 30, 40, -8, -8]
+    cases["batch_attention"] = {
+        "source": f"{src}:327-441,514-559", "batch": 2, "query_heads": 2, "kv_heads": 1, "head_size": 2,
+        "context": 4, "rotary_size": 2, "rope_scale": 1.0, "frequencies": [0.0], "qkv": qkv, "control": [1, 2],
+        "key_cache": [1, 0, -9, -9, -9, -9, -9, -9], "value_cache": [2, 4, -8, -8, -8, -8, -8, -8],
+        "expected_key_cache": exp_k, "expected_value_cache": exp_v,
+        "expected_output": _attention_reference(qkv, exp_k, exp_v, 2, 2, 1, 2, 1).tolist(),
+        "cache_tolerance": 1e-5, "output_tolerance": 2e-5,
+    }
+    return cases
+
+
 # GpuMatVecTests.cs:13-39: shapes x signatures, values (i%9-4)*0.125 and
 # (i%7-3)*0.25, expected = (float) double-precision row sum, rounded through
 # Half for an FP16 output; padding sentinel 13 around every buffer.
@@ -117,7 +200,9 @@ def cooperative_fixture() -> dict:
 def main() -> None:
     (HERE / "reference_known_answers.json").write_text(json.dumps(known_answers(), indent=1) + "\n")
     np.savez_compressed(HERE / "cooperative_matvec.npz", **cooperative_fixture())
-    print("wrote", HERE / "reference_known_answers.json", HERE / "cooperative_matvec.npz")
+    (HERE / "transformer_known_answers.json").write_text(json.dumps(transformer_known_answers(), indent=1) + "\n")
+    print("wrote", HERE / "reference_known_answers.json", HERE / "cooperative_matvec.npz",
+          HERE / "transformer_known_answers.json")
 
 
 if __name__ == "__main__":

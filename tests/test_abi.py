@@ -112,7 +112,86 @@ def test_registry_resolves_cuda_instructions():
     with pytest.raises(native.NotSupportedError):
         native.resolve("11111111-2222-3333-4444-555555555555", "core.mat-vec")
     with pytest.raises(native.NotSupportedError):
-        native.resolve(native.TIER_ZERO_FLOAT32, "core.gather-row")
+        native.resolve(native.TIER_ZERO_FLOAT32, "core.copy")
+    with pytest.raises(native.NotSupportedError):
+        native.resolve(native.TRANSFORMER_FLOAT32, "core.gather-row")  # a tier-zero instruction
+
+
+# The 22 names of GpuTransformerInstructionCollection.cs:8-33 with their port types.
+TRANSFORMER_PORTS = {
+    "transformer.rms-norm": "fff", "transformer.residual-rms-norm": "fffff", "transformer.swiglu": "ff",
+    "transformer.rope-kv-write": "fiffff", "transformer.gqa-scores": "ffif", "transformer.causal-softmax": "fif",
+    "transformer.gqa-values": "ffif", "transformer.grouped-query-attention": "fffif", "transformer.argmax": "fi",
+    "transformer.scaled-add": "fff", "transformer.embedding-gather-batch": "hif",
+    "transformer.copy-embedding-rows": "ff", "transformer.batch-rms-norm": "ffif",
+    "transformer.batch-residual-rms-norm": "fffiff", "transformer.batch-shared-matvec": "hfif",
+    "transformer.batch-swiglu": "fif", "transformer.batch-rope-kv-write": "fiffff",
+    "transformer.batch-gqa-scores": "ffif", "transformer.batch-causal-softmax": "fif",
+    "transformer.batch-gqa-values": "ffif", "transformer.batch-select-last": "fif",
+    "transformer.batch-gather-rows": "fif",
+}
+
+
+def test_registry_covers_every_transformer_instruction():
+    code = {"f": N.F32, "i": N.I32, "h": N.F16}
+    ids = set()
+    for name, ports in TRANSFORMER_PORTS.items():
+        iid = native.resolve(native.TRANSFORMER_FLOAT32, name)
+        ids.add(iid)
+        types = [code[c] for c in ports]
+        native.validate(iid, types)
+        wrong = list(types)
+        wrong[-1] = N.F16 if wrong[-1] != N.F16 else N.F32
+        with pytest.raises(native.InstructionAdaptationError):
+            native.validate(iid, wrong)
+        with pytest.raises(native.InstructionAdaptationError):
+            native.validate(iid, types[:-1])
+        with pytest.raises(native.InstructionAdaptationError):
+            native.validate(iid, types, "some-config")
+    assert len(ids) == len(TRANSFORMER_PORTS) == 22
+    gr = native.resolve(native.TIER_ZERO_FLOAT32, "core.gather-row")
+    for t in (N.F32, N.F16, N.Q8_0, N.Q4_K):
+        native.validate(gr, [t, N.I32, N.F32])
+    with pytest.raises(native.InstructionAdaptationError):
+        native.validate(gr, [N.F32, N.F32, N.F32])
+
+
+def test_transformer_entry_points_reject_bad_shapes_on_the_host():
+    lib = native.lib
+    f = FAKE
+    # rope: odd rotary size, rotary above head size, query not whole heads (rope-kv-write Generate)
+    assert lib.si_rope_kv_write(f, f, f, f, f, f, 256, 1, 128, 95, 16, 1.0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_rope_kv_write(f, f, f, f, f, f, 256, 1, 128, 130, 16, 1.0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_rope_kv_write(f, f, f, f, f, f, 200, 1, 128, 96, 16, 1.0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_rope_kv_write(f, f, f, f, f, f, 256, 1, 128, 96, 16, 0.0, None) == N.SI_ERR_ADAPTATION
+    # attention: heads not divisible
+    assert lib.si_grouped_query_attention(f, f, f, f, f, 24, 7, 128, 64, None) == N.SI_ERR_ADAPTATION
+    assert "divisible" in native.last_error()
+    assert lib.si_gqa_scores(f, f, f, f, 6, 4, 32, 16, None) == N.SI_ERR_ADAPTATION
+    # norms: epsilon must be finite and positive
+    assert lib.si_rms_norm(f, f, f, 16, 0.0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_residual_rms_norm(f, f, f, f, f, 16, float("nan"), None) == N.SI_ERR_ADAPTATION
+    assert lib.si_scaled_add(f, f, f, 16, -2.0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_copy_embedding_rows(f, f, 4, 0, 8, 0, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_copy_embedding_rows(f, f, 4, 2, 8, 3, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_argmax(f, 0, f, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_gather_row(N.Q4_K, f, 4, 300, f, f, None) == N.SI_ERR_INVALID_DATA
+    assert lib.si_gather_row(99, f, 4, 256, f, f, None) == N.SI_ERR_UNSUPPORTED
+
+
+def test_decoder_config_is_validated_before_any_device_call():
+    base = dict(layers=2, hidden=256, query_heads=2, kv_heads=1, head_size=128, rotary_size=96, intermediate=512,
+                vocab=640, context=64, epsilon=1e-5, rope_base=10000.0, rope_scale=1.0, weight_type=N.Q4_K,
+                embedding_type=N.Q4_K)
+    for change, err in [({"query_heads": 3}, native.InstructionAdaptationError),
+                        ({"kv_heads": 3, "query_heads": 2}, native.InstructionAdaptationError),
+                        ({"rotary_size": 97}, native.InstructionAdaptationError),
+                        ({"intermediate": 500}, native.InvalidDataError),
+                        ({"layers": 0}, native.ArgumentError),
+                        ({"weight_type": 99}, native.NotSupportedError)]:
+        cfg = dict(base, **change)
+        with pytest.raises(err):
+            native.Decoder(cfg)
 
 
 def test_registry_signatures_and_configurations():

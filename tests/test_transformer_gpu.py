@@ -1,0 +1,319 @@
+"""CUDA transformer instructions against the CPU oracle and the reference's
+known answers (GpuTransformerInstructionTests.cs), called through the C ABI
+on device buffers. FP32 elementwise work is compared to 1e-5 (the
+reference's AssertClose bound); reductions whose summation order differs
+from the instruction's 64-lane tree (norm, attention, softmax) to a
+relative 2e-5; gather, cache writes and argmax are exact."""
+import json
+
+import numpy as np
+import pytest
+
+import oracle
+from helpers import GOLDEN
+from sharpinference_b200 import native
+
+pytestmark = pytest.mark.gpu
+N = native
+
+
+class Dev:
+    """Device buffers for one test, freed at the end."""
+
+    def __init__(self, ctx):
+        self.ctx, self.bufs = ctx, []
+
+    def put(self, arr, dtype=None):
+        a = np.ascontiguousarray(arr if dtype is None else np.asarray(arr, dtype=dtype))
+        b = self.ctx.buffer(max(a.nbytes, 16))
+        if a.nbytes:
+            b.upload(a)
+        b.count, b.dtype = a.size, a.dtype
+        self.bufs.append(b)
+        return b
+
+    def zeros(self, count, dtype=np.float32, fill=0):
+        return self.put(np.full(count, fill, dtype=dtype))
+
+    def get(self, b, count=None, dtype=None):
+        self.ctx.synchronize()
+        dtype = np.dtype(dtype or b.dtype)
+        count = b.count if count is None else count
+        return b.readback(count * dtype.itemsize).view(dtype).copy()
+
+    def close(self):
+        for b in self.bufs:
+            b.free()
+
+
+@pytest.fixture
+def dev(ctx):
+    d = Dev(ctx)
+    yield d
+    d.close()
+
+
+def p(b):
+    return b.device_pointer
+
+
+def S(ctx):
+    return ctx.stream
+
+
+def _cases():
+    return json.loads((GOLDEN / "transformer_known_answers.json").read_text())
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+# ---- known answers ------------------------------------------------------------------
+def test_residual_rms_norm_known_answer(ctx, dev):
+    c = _cases()["residual_rms_norm"]
+    n = len(c["hidden"])
+    h, r, w = dev.put(c["hidden"], np.float32), dev.put(c["residual"], np.float32), dev.put(c["weight"], np.float32)
+    u, o = dev.zeros(n), dev.zeros(n)
+    N.call("si_residual_rms_norm", p(h), p(r), p(w), p(u), p(o), n, c["epsilon"], S(ctx))
+    assert np.max(np.abs(dev.get(u) - c["expected_updated"])) <= c["tolerance"]
+    assert np.max(np.abs(dev.get(o) - c["expected_output"])) <= c["tolerance"]
+
+
+def test_swiglu_and_scaled_add_known_answers(ctx, dev):
+    c = _cases()
+    g = dev.put(c["swiglu"]["gate_up"], np.float32)
+    o = dev.zeros(4)
+    N.call("si_swiglu", p(g), p(o), 4, S(ctx))
+    assert np.max(np.abs(dev.get(o) - c["swiglu"]["expected"])) <= c["swiglu"]["tolerance"]
+    s = c["scaled_add"]
+    a, u, o = dev.put(s["input"], np.float32), dev.put(s["update"], np.float32), dev.zeros(4)
+    N.call("si_scaled_add", p(a), p(u), p(o), 4, s["scale"], S(ctx))
+    assert np.max(np.abs(dev.get(o) - s["expected"])) <= s["tolerance"]
+
+
+def test_batch_rms_norm_known_answer(ctx, dev):
+    c = _cases()["batch_rms_norm"]
+    x, w = dev.put(c["input"], np.float32), dev.put(c["weight"], np.float32)
+    ctl, o = dev.put(c["control"], np.int32), dev.zeros(c["batch"] * c["width"], fill=c["fill"])
+    N.call("si_batch_rms_norm", p(x), p(w), p(ctl), p(o), c["batch"], c["width"], c["epsilon"], S(ctx))
+    assert np.max(np.abs(dev.get(o) - c["expected"])) <= c["tolerance"]
+
+
+def test_batch_gather_rows_known_answer(ctx, dev):
+    c = _cases()["batch_gather_rows"]
+    t, ctl = dev.put(c["table"], np.float32), dev.put(c["control"], np.int32)
+    o = dev.zeros(c["batch"] * c["width"], fill=c["fill"])
+    N.call("si_batch_gather_rows", p(t), c["rows"], p(ctl), p(o), c["batch"], c["width"], S(ctx))
+    np.testing.assert_array_equal(dev.get(o), c["expected"])
+
+
+def test_batch_attention_known_answer(ctx, dev):
+    c = _cases()["batch_attention"]
+    b, qh, kvh, hs, T = c["batch"], c["query_heads"], c["kv_heads"], c["head_size"], c["context"]
+    qkv, ctl, fr = dev.put(c["qkv"], np.float32), dev.put(c["control"], np.int32), dev.put(c["frequencies"], np.float32)
+    q, kc, vc = dev.zeros(b * qh * hs), dev.put(c["key_cache"], np.float32), dev.put(c["value_cache"], np.float32)
+    sc, pr, out = dev.zeros(b * qh * T), dev.zeros(b * qh * T), dev.zeros(b * qh * hs)
+    N.call("si_batch_rope_kv_write", p(qkv), p(ctl), p(fr), p(q), p(kc), p(vc), b, qh * hs, kvh, hs,
+           c["rotary_size"], T, c["rope_scale"], S(ctx))
+    N.call("si_batch_gqa_scores", p(q), p(kc), p(ctl), p(sc), b, qh, kvh, hs, T, S(ctx))
+    N.call("si_batch_causal_softmax", p(sc), p(ctl), p(pr), b, qh, T, S(ctx))
+    N.call("si_batch_gqa_values", p(pr), p(vc), p(ctl), p(out), b, qh, kvh, hs, T, S(ctx))
+    np.testing.assert_allclose(dev.get(kc), c["expected_key_cache"], atol=c["cache_tolerance"])
+    np.testing.assert_allclose(dev.get(vc), c["expected_value_cache"], atol=c["cache_tolerance"])
+    np.testing.assert_allclose(dev.get(out), c["expected_output"], atol=c["output_tolerance"])
+
+
+# ---- seeded parity against the oracle ---------------------------------------------------
+@pytest.mark.parametrize("width", [8, 3072, 5120, 8193])
+def test_rms_norms_match_oracle(ctx, dev, width):
+    rng = np.random.default_rng(width)
+    x, r = rng.standard_normal(width).astype(np.float32), rng.standard_normal(width).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
+    bx, br, bw, bu, bo = dev.put(x), dev.put(r), dev.put(w), dev.zeros(width), dev.zeros(width)
+    N.call("si_rms_norm", p(bx), p(bw), p(bo), width, 1e-5, S(ctx))
+    assert _rel(dev.get(bo), oracle.rms_norm(x, w, 1e-5)) < 2e-5
+    N.call("si_residual_rms_norm", p(bx), p(br), p(bw), p(bu), p(bo), width, 1e-5, S(ctx))
+    u_ref, o_ref = oracle.residual_rms_norm(x, r, w, 1e-5)
+    np.testing.assert_array_equal(dev.get(bu), u_ref)
+    assert _rel(dev.get(bo), o_ref) < 2e-5
+    # in place: updated aliases hidden
+    N.call("si_residual_rms_norm", p(bx), p(br), p(bw), p(bx), p(bo), width, 1e-5, S(ctx))
+    np.testing.assert_array_equal(dev.get(bx), u_ref)
+    assert _rel(dev.get(bo), o_ref) < 2e-5
+
+
+def test_swiglu_matches_oracle(ctx, dev):
+    rng = np.random.default_rng(1)
+    g = (3 * rng.standard_normal(2 * 8192)).astype(np.float32)
+    bg, bo = dev.put(g), dev.zeros(8192)
+    N.call("si_swiglu", p(bg), p(bo), 8192, S(ctx))
+    np.testing.assert_allclose(dev.get(bo), oracle.swiglu(g), rtol=2e-6, atol=1e-6)
+
+
+PHI4_MINI = dict(qh=24, kvh=8, hs=128, rot=96)
+PHI4_14B = dict(qh=40, kvh=10, hs=128, rot=128)
+
+
+@pytest.mark.parametrize("shape", [PHI4_MINI, PHI4_14B], ids=["mini", "14b"])
+@pytest.mark.parametrize("pos", [0, 17, 63, 64, -1])
+def test_rope_kv_write_matches_oracle(ctx, dev, shape, pos):
+    qh, kvh, hs, rot, T = shape["qh"], shape["kvh"], shape["hs"], shape["rot"], 64
+    rng = np.random.default_rng(pos + 100)
+    qkv = rng.standard_normal(qh * hs + 2 * kvh * hs).astype(np.float32)
+    freq = oracle.rope_frequencies(10000.0, rot)
+    kc0 = np.full(T * kvh * hs, -3, np.float32)
+    posb, bq = dev.put([pos], np.int32), dev.zeros(qh * hs, fill=-7)
+    bkc, bvc = dev.put(kc0), dev.put(kc0)
+    N.call("si_rope_kv_write", p(dev.put(qkv)), p(posb), p(dev.put(freq)), p(bq), p(bkc), p(bvc), qh * hs, kvh, hs,
+           rot, T, 1.1902381, S(ctx))
+    q_ref, kc_ref, vc_ref = oracle.rope_kv_write(qkv, pos, freq, kc0, kc0, qh * hs, kvh, hs, rot, T, 1.1902381)
+    if not 0 <= pos < T:
+        assert np.all(dev.get(bq) == -7) and np.all(dev.get(bkc) == -3) and np.all(dev.get(bvc) == -3)
+        return
+    np.testing.assert_allclose(dev.get(bq), q_ref, rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(dev.get(bkc), kc_ref, rtol=1e-5, atol=2e-6)
+    np.testing.assert_array_equal(dev.get(bvc), vc_ref)
+
+
+ATTN_SHAPES = [
+    dict(qh=24, kvh=8, hs=128),   # Phi-4-mini
+    dict(qh=40, kvh=10, hs=128),  # Phi-4-14B
+    dict(qh=8, kvh=8, hs=64),
+    dict(qh=16, kvh=2, hs=96),
+    dict(qh=4, kvh=1, hs=256),
+    dict(qh=6, kvh=2, hs=2),
+]
+
+
+@pytest.mark.parametrize("shape", ATTN_SHAPES, ids=lambda s: f"{s['qh']}x{s['kvh']}x{s['hs']}")
+@pytest.mark.parametrize("pos", [0, 1, 7, 8, 9, 300, 1023, 5000, -4])
+def test_grouped_query_attention_matches_oracle(ctx, dev, shape, pos):
+    qh, kvh, hs, T = shape["qh"], shape["kvh"], shape["hs"], 1024
+    rng = np.random.default_rng(pos + 7 * hs)
+    q = rng.standard_normal(qh * hs).astype(np.float32)
+    kc = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    vc = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    out = dev.zeros(qh * hs)
+    N.call("si_grouped_query_attention", p(dev.put(q)), p(dev.put(kc)), p(dev.put(vc)), p(dev.put([pos], np.int32)),
+           p(out), qh, kvh, hs, T, S(ctx))
+    ref = oracle.grouped_query_attention(q, kc, vc, pos, qh, kvh, hs, T)
+    np.testing.assert_allclose(dev.get(out), ref, rtol=2e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("pos", [0, 5, 31, -1])
+def test_unfused_attention_matches_oracle(ctx, dev, pos):
+    qh, kvh, hs, T = 6, 2, 32, 32
+    rng = np.random.default_rng(pos + 50)
+    q = rng.standard_normal(qh * hs).astype(np.float32)
+    kc = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    vc = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    bq, bkc, bvc, bp = dev.put(q), dev.put(kc), dev.put(vc), dev.put([pos], np.int32)
+    sc, pr, out = dev.zeros(qh * T), dev.zeros(qh * T), dev.zeros(qh * hs)
+    N.call("si_gqa_scores", p(bq), p(bkc), p(bp), p(sc), qh, kvh, hs, T, S(ctx))
+    N.call("si_causal_softmax", p(sc), p(bp), p(pr), qh, T, S(ctx))
+    N.call("si_gqa_values", p(pr), p(bvc), p(bp), p(out), qh, kvh, hs, T, S(ctx))
+    s_ref = oracle.gqa_scores(q, kc, pos, qh, kvh, hs, T)
+    p_ref = oracle.causal_softmax(s_ref, pos, qh, T)
+    np.testing.assert_allclose(dev.get(sc), s_ref, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(dev.get(pr), p_ref, rtol=2e-5, atol=1e-7)
+    np.testing.assert_allclose(dev.get(out), oracle.gqa_values(p_ref, vc, pos, qh, kvh, hs, T), rtol=2e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("start,valid", [(0, 3), (5, 2), (-2, 3), (30, 4)])
+def test_batch_attention_forms_match_oracle(ctx, dev, start, valid):
+    B, qh, kvh, hs, rot, T = 4, 6, 2, 32, 16, 32
+    rng = np.random.default_rng(start + 40)
+    qkv = rng.standard_normal((B, qh * hs + 2 * kvh * hs)).astype(np.float32)
+    kc0 = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    vc0 = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    freq = oracle.rope_frequencies(10000.0, rot)
+    ctl = [start, valid]
+    bctl, bq = dev.put(ctl, np.int32), dev.zeros(B * qh * hs, fill=-1)
+    bkc, bvc = dev.put(kc0), dev.put(vc0)
+    sc, pr, out = dev.zeros(B * qh * T, fill=-2), dev.zeros(B * qh * T, fill=-3), dev.zeros(B * qh * hs, fill=-4)
+    N.call("si_batch_rope_kv_write", p(dev.put(qkv)), p(bctl), p(dev.put(freq)), p(bq), p(bkc), p(bvc), B, qh * hs,
+           kvh, hs, rot, T, 1.0, S(ctx))
+    N.call("si_batch_gqa_scores", p(bq), p(bkc), p(bctl), p(sc), B, qh, kvh, hs, T, S(ctx))
+    N.call("si_batch_causal_softmax", p(sc), p(bctl), p(pr), B, qh, T, S(ctx))
+    N.call("si_batch_gqa_values", p(pr), p(bvc), p(bctl), p(out), B, qh, kvh, hs, T, S(ctx))
+    q_ref, kc_ref, vc_ref = oracle.batch_rope_kv_write(qkv, ctl, freq, np.full((B, qh * hs), -1, np.float32), kc0,
+                                                       vc0, qh * hs, kvh, hs, rot, T, 1.0)
+    np.testing.assert_allclose(dev.get(bq), q_ref.reshape(-1), rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(dev.get(bkc), kc_ref, rtol=1e-5, atol=2e-6)
+    np.testing.assert_array_equal(dev.get(bvc), vc_ref)
+    s_ref = oracle.batch_gqa_scores(q_ref, kc_ref, ctl, np.full((B, qh, T), -2, np.float32), qh, kvh, hs, T)
+    p_ref = oracle.batch_causal_softmax(s_ref, ctl, np.full((B, qh, T), -3, np.float32), qh, T)
+    o_ref = oracle.batch_gqa_values(p_ref, vc_ref, ctl, np.full((B, qh * hs), -4, np.float32), qh, kvh, hs, T)
+    np.testing.assert_allclose(dev.get(sc), s_ref.reshape(-1), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(dev.get(pr), p_ref.reshape(-1), rtol=2e-5, atol=1e-7)
+    np.testing.assert_allclose(dev.get(out), o_ref.reshape(-1), rtol=2e-5, atol=2e-6)
+
+
+def test_batch_norms_swiglu_select_match_oracle(ctx, dev):
+    B, W, ctl = 5, 3072, [0, 3]
+    rng = np.random.default_rng(9)
+    x, r = rng.standard_normal((B, W)).astype(np.float32), rng.standard_normal((B, W)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(W)).astype(np.float32)
+    bx, br, bw, bc = dev.put(x), dev.put(r), dev.put(w), dev.put(ctl, np.int32)
+    bu, bo = dev.zeros(B * W, fill=5), dev.zeros(B * W, fill=6)
+    N.call("si_batch_residual_rms_norm", p(bx), p(br), p(bw), p(bc), p(bu), p(bo), B, W, 1e-5, S(ctx))
+    u_ref, o_ref = oracle.batch_residual_rms_norm(x, r, w, ctl, np.full((B, W), 5, np.float32),
+                                                  np.full((B, W), 6, np.float32), 1e-5)
+    np.testing.assert_array_equal(dev.get(bu), u_ref.reshape(-1))
+    assert _rel(dev.get(bo), o_ref.reshape(-1)) < 2e-5
+    assert np.all(dev.get(bo).reshape(B, W)[3:] == 6)
+    g = rng.standard_normal((B, 2 * W)).astype(np.float32)
+    bs = dev.zeros(B * W, fill=8)
+    N.call("si_batch_swiglu", p(dev.put(g)), p(bc), p(bs), B, W, S(ctx))
+    s_ref = oracle.batch_swiglu(g, ctl, np.full((B, W), 8, np.float32))
+    np.testing.assert_allclose(dev.get(bs), s_ref.reshape(-1), rtol=2e-6, atol=1e-6)
+    last = dev.zeros(W, fill=9)
+    N.call("si_batch_select_last", p(bx), p(bc), p(last), B, W, S(ctx))
+    np.testing.assert_array_equal(dev.get(last), x[2])
+
+
+def test_argmax_matches_oracle_and_tie_rules(ctx, dev):
+    rng = np.random.default_rng(2)
+    cases = [rng.standard_normal(200064).astype(np.float32)]
+    tie = np.zeros(200064, np.float32)
+    tie[[150000, 70001, 199999]] = 3.0
+    cases.append(tie)
+    nan = rng.standard_normal(1000).astype(np.float32)
+    nan[::3] = np.nan
+    cases += [nan, np.full(77, -np.inf, np.float32), np.float32([-1, -0.0, 0.0]), np.float32([np.nan] * 5)]
+    for x in cases:
+        out = dev.zeros(1, np.int32, fill=-1)
+        N.call("si_argmax", p(dev.put(x)), x.size, p(out), S(ctx))
+        assert int(dev.get(out)[0]) == oracle.argmax(x)
+
+
+@pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K])
+def test_gather_row_is_exact(ctx, dev, wtype):
+    rows, cols = 37, 3072
+    rng = np.random.default_rng(wtype)
+    table = (0.02 * rng.standard_normal((rows, cols))).astype(np.float32)
+    blob = oracle.quantize(wtype, table) if wtype != N.F16 else table.astype(np.float16).view(np.uint8)
+    bt = dev.put(blob)
+    for idx in (0, 5, rows - 1, rows, -1):
+        out = dev.zeros(cols, fill=123)
+        N.call("si_gather_row", wtype, p(bt), rows, cols, p(dev.put([idx], np.int32)), p(out), S(ctx))
+        got = dev.get(out)
+        if 0 <= idx < rows:
+            np.testing.assert_array_equal(got, oracle.gather_row(wtype, blob, rows, cols, idx))
+        else:
+            assert np.all(np.isnan(got))
+
+
+def test_embedding_gather_batch_and_copy_rows(ctx, dev):
+    rng = np.random.default_rng(3)
+    table = rng.standard_normal((50, 96)).astype(np.float16)
+    idx = np.int32([3, 49, 0, 50, -1])
+    out = dev.zeros(idx.size * 96)
+    N.call("si_embedding_gather_batch", p(dev.put(table)), 50, p(dev.put(idx)), p(out), idx.size, 96, S(ctx))
+    np.testing.assert_array_equal(dev.get(out), oracle.embedding_gather_batch(table, 50, idx, 96))
+    x = rng.standard_normal(2 * 96).astype(np.float32)
+    o = dev.zeros(5 * 96, fill=1)
+    N.call("si_copy_embedding_rows", p(dev.put(x)), p(o), 5, 2, 96, 3, S(ctx))
+    np.testing.assert_array_equal(dev.get(o), oracle.copy_embedding_rows(x, np.ones(5 * 96, np.float32), 2, 96, 3))
