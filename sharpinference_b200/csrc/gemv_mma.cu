@@ -79,6 +79,67 @@ struct MmaParams {
     int path;             // host side: 0 FP16 MMA, 1 INT8 MMA
     int groups;           // clusters (or CTAs when cluster == 1) in the grid
     int max_local_tiles;  // ceil(num_tiles / groups): row-sum slots per CTA when cluster > 1
+    // Input transform applied while x is loaded (the decode step's fused
+    // prologue; kernels::XForm): 0 x as is; 1 rms-norm, x_j = (x_j + x_res_j)
+    // * s * x_norm_w_j with s = 1 / sqrt(mean over all K of (x + x_res)^2 +
+    // x_eps), CTA 0 also storing x + x_res to x_updated; 2 swiglu, x_j =
+    // g_j / (1 + exp(-g_j)) * u_j with g = x[0, K) and u = x[K, 2K).
+    int x_mode;
+    float x_eps;
+    const float *x_res;
+    const float *x_norm_w;
+    float *x_updated;
+    // Weights of the next projection to pull into L2 once this CTA's ring
+    // is full (decode step; null: none).
+    const uint8_t *prefetch;
+    uint64_t prefetch_bytes;
+};
+
+// Source of the GEMV input as the load paths see it: element i of the
+// (transformed) vector. The transform is a template parameter so the plain
+// load (M = 0) compiles to bare vector loads the compiler can batch. Modes
+// 1 and 2 need 16-byte aligned vectors.
+template <int M>
+struct XSrc {
+    const float *x;
+    const float *res;
+    const float *w;
+    float scale;
+    int64_t up;  // mode 2: offset of u
+    __device__ __forceinline__ bool aligned(int64_t i) const {
+        return M != 0 || (reinterpret_cast<uintptr_t>(x + i) & 15u) == 0;
+    }
+    static __device__ __forceinline__ float swish_mul(float g, float u) {
+        return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    }
+    __device__ __forceinline__ float get(int64_t i) const {
+        const float a = __ldg(x + i);
+        if constexpr (M == 0) {
+            return a;
+        } else if constexpr (M == 1) {
+            const float v = res ? __fadd_rn(a, __ldg(res + i)) : a;
+            return __fmul_rn(__fmul_rn(v, scale), __ldg(w + i));
+        } else {
+            return swish_mul(a, __ldg(x + up + i));
+        }
+    }
+    __device__ __forceinline__ float4 get4(int64_t i) const {
+        float4 a = __ldg(reinterpret_cast<const float4 *>(x + i));
+        if constexpr (M == 0) {
+            return a;
+        } else if constexpr (M == 1) {
+            if (res) {
+                const float4 r = __ldg(reinterpret_cast<const float4 *>(res + i));
+                a = make_float4(__fadd_rn(a.x, r.x), __fadd_rn(a.y, r.y), __fadd_rn(a.z, r.z), __fadd_rn(a.w, r.w));
+            }
+            const float4 m = __ldg(reinterpret_cast<const float4 *>(w + i));
+            return make_float4(__fmul_rn(__fmul_rn(a.x, scale), m.x), __fmul_rn(__fmul_rn(a.y, scale), m.y),
+                               __fmul_rn(__fmul_rn(a.z, scale), m.z), __fmul_rn(__fmul_rn(a.w, scale), m.w));
+        } else {
+            const float4 u = __ldg(reinterpret_cast<const float4 *>(x + up + i));
+            return make_float4(swish_mul(a.x, u.x), swish_mul(a.y, u.y), swish_mul(a.z, u.z), swish_mul(a.w, u.w));
+        }
+    }
 };
 
 // --- thread-block cluster helpers (distributed shared memory) ---
@@ -225,18 +286,19 @@ struct SbState {
     float sx_hi_t;      // sum of x over sub-block t+4
 };
 
-__device__ __forceinline__ void load_superblock_x(const float *__restrict__ x, int sb, int lane, SbState &st) {
-    const float *xs = x + size_t(sb) * 256;
+template <class XS>
+__device__ __forceinline__ void load_superblock_x(const XS &X, int sb, int lane, SbState &st) {
+    const int64_t xb = int64_t(sb) * 256;
     // 8 consecutive x per lane: lane l covers elements 8l .. 8l+7 (sub-block l/4).
     float v[8];
-    const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
+    const bool aligned = X.aligned(xb);
     if (aligned) {
-        const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane));
-        const float4 b = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane + 4));
+        const float4 a = X.get4(xb + 8 * lane);
+        const float4 b = X.get4(xb + 8 * lane + 4);
         v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
     } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __ldg(xs + 8 * lane + i);
+        for (int i = 0; i < 8; ++i) v[i] = X.get(xb + 8 * lane + i);
     }
     float amax = 0.0f, psum = 0.0f;
 #pragma unroll
@@ -272,11 +334,11 @@ __device__ __forceinline__ void load_superblock_x(const float *__restrict__ x, i
                 const int e0 = 64 * j + 32 * h + 16 * p + 4 * t;
                 float q[4];
                 if (aligned) {
-                    const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + e0));
+                    const float4 a = X.get4(xb + e0);
                     q[0] = a.x, q[1] = a.y, q[2] = a.z, q[3] = a.w;
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = __ldg(xs + e0 + i);
+                    for (int i = 0; i < 4; ++i) q[i] = X.get(xb + e0 + i);
                 }
                 const float f = h ? scale * 0.0625f : scale;  // high nibbles carry codes 16 q
                 float part[4];
@@ -381,7 +443,8 @@ struct F16Path {
     static constexpr uint32_t kColBytes = 144;  // one Q4_K superblock
     static constexpr uint32_t kQsOffset = 16;   // nibbles follow the 16-byte header
     static constexpr uint32_t kScratchBytes = 0;
-    static __device__ __forceinline__ void load(const float *x, int sb, int lane, State &st, uint8_t *, int64_t, int) {
+    template <class XS>
+    static __device__ __forceinline__ void load(const XS &x, int sb, int lane, State &st, uint8_t *, int64_t, int) {
         load_superblock_x(x, sb, lane, st);
     }
     static __device__ __forceinline__ float2 rows16(uint32_t ldsm_addr, const uint8_t *hdr_g, const uint8_t *hdr_g8,
@@ -452,18 +515,18 @@ struct I8Path {
     static constexpr uint32_t kColBytes = 144;
     static constexpr uint32_t kQsOffset = 16;
     static constexpr uint32_t kScratchBytes = 0;
-    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *,
-                                                int64_t, int) {
-        const float *xs = x + size_t(sb) * 256;
-        const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
+    template <class XS>
+    static __device__ __forceinline__ void load(const XS &X, int sb, int lane, State &st, uint8_t *, int64_t, int) {
+        const int64_t xb = int64_t(sb) * 256;
+        const bool aligned = X.aligned(xb);
         float v[8];
         if (aligned) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane));
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane + 4));
+            const float4 a = X.get4(xb + 8 * lane);
+            const float4 b = X.get4(xb + 8 * lane + 4);
             v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __ldg(xs + 8 * lane + i);
+            for (int i = 0; i < 8; ++i) v[i] = X.get(xb + 8 * lane + i);
         }
         float amax = 0.0f, psum = 0.0f;
 #pragma unroll
@@ -503,14 +566,14 @@ struct I8Path {
             uint32_t b0 = 0, b1 = 0;
             if ((s >> 2) == half && digit < 3) {
                 float q[8];
-                const float *e0 = xs + 32 * s + 4 * t;
+                const int64_t e0 = xb + 32 * s + 4 * t;
                 if (aligned) {
-                    const float4 a = __ldg(reinterpret_cast<const float4 *>(e0));
-                    const float4 c = __ldg(reinterpret_cast<const float4 *>(e0 + 16));
+                    const float4 a = X.get4(e0);
+                    const float4 c = X.get4(e0 + 16);
                     q[0] = a.x, q[1] = a.y, q[2] = a.z, q[3] = a.w, q[4] = c.x, q[5] = c.y, q[6] = c.z, q[7] = c.w;
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = __ldg(e0 + i), q[4 + i] = __ldg(e0 + 16 + i);
+                    for (int i = 0; i < 4; ++i) q[i] = X.get(e0 + i), q[4 + i] = X.get(e0 + 16 + i);
                 }
                 uint32_t dg[8];
 #pragma unroll
@@ -610,8 +673,10 @@ struct I8T8Path {
         }
     }
 
-    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st, uint8_t *,
+    template <class XS>
+    static __device__ __forceinline__ void load(const XS &X, int sb, int lane, State &st, uint8_t *,
                                                 int64_t x_stride, int ntok) {
+        const float *__restrict__ x = X.x;  // batched launches take x as is (mode 0)
         const int t = lane & 3, g = lane >> 2;
         const bool present = g < ntok;
         const float *xs = x + size_t(present ? g : 0) * x_stride + size_t(sb) * 256;
@@ -784,18 +849,18 @@ struct Q8Path {
     // position of the column, digit d of the element stored there (0 at the
     // scale bytes and beyond the column); each lane then reads its B words
     // with aligned 32-bit loads.
-    static __device__ __forceinline__ void load(const float *__restrict__ x, int sb, int lane, State &st,
-                                                uint8_t *scratch, int64_t, int) {
-        const float *xs = x + size_t(sb) * 256;
-        const bool aligned = (reinterpret_cast<uintptr_t>(xs) & 15u) == 0;
+    template <class XS>
+    static __device__ __forceinline__ void load(const XS &X, int sb, int lane, State &st, uint8_t *scratch,
+                                                int64_t, int) {
+        const int64_t xb = int64_t(sb) * 256;
         float v[8];
-        if (aligned) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane));
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(xs + 8 * lane + 4));
+        if (X.aligned(xb)) {
+            const float4 a = X.get4(xb + 8 * lane);
+            const float4 b = X.get4(xb + 8 * lane + 4);
             v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __ldg(xs + 8 * lane + i);
+            for (int i = 0; i < 8; ++i) v[i] = X.get(xb + 8 * lane + i);
         }
         float amax = 0.0f;
 #pragma unroll
@@ -892,6 +957,37 @@ __device__ __forceinline__ uint32_t row_offset(const MmaParams &p, int row) {
     return uint32_t(row >> p.log2_group_rows) * p.group_stride + uint32_t(row & (p.group_rows - 1)) * p.row_pitch;
 }
 
+// Fused rms-norm prologue (x_mode 1): the C compute warps of every CTA
+// reduce the sum of squares of x + x_res over all K in one fixed order, so
+// every CTA derives the same scale; CTA 0 also stores x + x_res to
+// x_updated. `red` is C floats of shared memory the pipeline has not used
+// yet; named barrier 1 spans the C compute warps only.
+__device__ __forceinline__ float rms_prologue(const MmaParams &p, int warp, int lane, int C, float *red) {
+    const int64_t K = int64_t(p.nsb) * 256;
+    const bool store = p.x_updated != nullptr && blockIdx.x == 0;
+    float s = 0.0f;
+    for (int64_t i = (int64_t(warp) * 32 + lane) * 4; i < K; i += int64_t(C) * 128) {
+        float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + i));
+        if (p.x_res) {
+            const float4 r = __ldg(reinterpret_cast<const float4 *>(p.x_res + i));
+            a = make_float4(__fadd_rn(a.x, r.x), __fadd_rn(a.y, r.y), __fadd_rn(a.z, r.z), __fadd_rn(a.w, r.w));
+        }
+        if (store) *reinterpret_cast<float4 *>(p.x_updated + i) = a;
+        s = __fadd_rn(s, __fmul_rn(a.x, a.x));
+        s = __fadd_rn(s, __fmul_rn(a.y, a.y));
+        s = __fadd_rn(s, __fmul_rn(a.z, a.z));
+        s = __fadd_rn(s, __fmul_rn(a.w, a.w));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    if (lane == 0) red[warp] = s;
+    asm volatile("bar.sync 1, %0;" ::"r"(C * 32) : "memory");
+    float total = 0.0f;
+    for (int w = 0; w < C; ++w) total = __fadd_rn(total, red[w]);
+    asm volatile("bar.sync 1, %0;" ::"r"(C * 32) : "memory");  // red returns to the pipeline
+    return 1.0f / sqrtf(__fadd_rn(__fdiv_rn(total, float(K)), p.x_eps));
+}
+
 // WPS compute warps share each superblock column (WPS = 2: each takes one
 // 16-row half of a 32-row tile), for more warps in flight per SM.
 template <class Path, int SPW, int RT, int WPS, int MAXW>
@@ -956,8 +1052,10 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                     bulk_copy_g2s(dst + size_t(r) * p.row_stride, wsrc + size_t(r0 + r) * p.row_bytes, p.cta_bytes,
                                   &full[s]);
             }
+            if (it == p.stages - 1) prefetch_l2_share(p.prefetch, p.prefetch_bytes, lane);
             if (++s == p.stages) s = 0, ring_phase ^= 1u;
         }
+        if (it < p.stages) prefetch_l2_share(p.prefetch, p.prefetch_bytes, lane);  // fewer tiles than stages
     } else if (warp == C + 1) {
         // Reducer: fixed-order sum of the C0 per-column partials of each
         // output (row r, input row u) = index r * TK + u of the tile.
@@ -996,9 +1094,20 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         const int gsb = int(crank) * p.nsb_cta;
         pdl_wait();  // x is produced by the previous kernel
         uint8_t *my_scratch = scratch + size_t(warp) * Path::kScratchBytes;
-        Path::load(p.x, gsb + sb0, lane, st0, my_scratch, p.x_stride, p.ntok);
-        if constexpr (SPW == 2) {
-            if (has1) Path::load(p.x, gsb + sb1, lane, st1, my_scratch, p.x_stride, p.ntok);
+        auto load_x = [&](const auto &X) {
+            Path::load(X, gsb + sb0, lane, st0, my_scratch, p.x_stride, p.ntok);
+            if constexpr (SPW == 2) {
+                if (has1) Path::load(X, gsb + sb1, lane, st1, my_scratch, p.x_stride, p.ntok);
+            }
+        };
+        const int64_t K = int64_t(p.nsb) * 256;
+        if (Path::kTokens > 1 || p.x_mode == 0) {
+            load_x(XSrc<0>{p.x, nullptr, nullptr, 1.0f, K});
+        } else if (p.x_mode == 1) {
+            const float scale = rms_prologue(p, warp, lane, C, part);
+            load_x(XSrc<1>{p.x, p.x_res, p.x_norm_w, scale, K});
+        } else {
+            load_x(XSrc<2>{p.x, nullptr, nullptr, 1.0f, K});
         }
 
         const int g = lane >> 2, t = lane & 3;
@@ -1309,7 +1418,15 @@ namespace {
 // by override), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
 si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream,
                      const PeerGather *peer, const int32_t *control, int token, int ntok, int64_t x_stride,
-                     int64_t y_stride) {
+                     int64_t y_stride, const XForm *xf = nullptr) {
+    if (xf && xf->mode) {
+        // The transforms read 16-byte vectors of x, the residual and the norm weight.
+        auto misaligned = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+        if (path == 3 || (xf->mode != 1 && xf->mode != 2) || misaligned(x) ||
+            (xf->mode == 1 && (!xf->norm_weight || misaligned(xf->norm_weight) ||
+                               (xf->residual && misaligned(xf->residual)) || (xf->updated && misaligned(xf->updated)))))
+            return SI_ERR_UNSUPPORTED;
+    }
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
@@ -1370,6 +1487,17 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
     p.ntok = ntok;
     p.x_stride = x_stride;
     p.y_stride = y_stride;
+    if (xf && xf->mode) {
+        p.x_mode = xf->mode;
+        p.x_eps = xf->eps;
+        p.x_res = xf->residual;
+        p.x_norm_w = xf->norm_weight;
+        p.x_updated = xf->updated;
+    }
+    if (xf && xf->prefetch && xf->prefetch_bytes >= 16 && !(reinterpret_cast<uintptr_t>(xf->prefetch) & 15u)) {
+        p.prefetch = static_cast<const uint8_t *>(xf->prefetch);
+        p.prefetch_bytes = xf->prefetch_bytes & ~uint64_t(15);
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
@@ -1398,10 +1526,11 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
 // Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
 // (without touching the error string) when the shape needs the SIMT kernel.
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream, const PeerGather *peer, const int32_t *control, int token) {
+                           void *stream, const PeerGather *peer, const int32_t *control, int token,
+                           const XForm *xform) {
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, control, token, 1, cols,
-                      rows);
+                      rows, xform);
 }
 
 // Q4_K batch: y[b] = W x[b] for the m input rows, eight per launch (each

@@ -5,6 +5,9 @@ launch with `-s 1 -c 1`): synthetic seeded weights and inputs, device-resident.
   python -m sharpinference_b200.profile_case gemv Q8_0 100352 5120
   python -m sharpinference_b200.profile_case batch Q4_K 200064 3072 16
   python -m sharpinference_b200.profile_case gemm Q4_K 200064 3072 512
+  python -m sharpinference_b200.profile_case decode mini 64 2
+      (Phi-4-mini random-init decoder: 64 prompt steps, then 2 more decode
+      steps; each step is one graph of 292 kernel launches)
 """
 from __future__ import annotations
 
@@ -17,7 +20,22 @@ from . import native
 TYPES = {"Q4_K": native.Q4_K, "Q8_0": native.Q8_0, "F16": native.F16, "F32": native.F32}
 
 
+def decode(preset: str, prompt_tokens: int, steps: int) -> None:
+    from . import phi4
+    cfg = dict(phi4.PHI4_MINI if preset == "mini" else phi4.PHI4_14B)
+    cfg["context"] = prompt_tokens + steps + 1
+    with native.Decoder(cfg) as dec:
+        phi4.load_synthetic(dec, cfg, seed=7)
+        prompt = phi4.random_prompt(7, prompt_tokens, cfg["vocab"])
+        toks = dec.generate(prompt, steps)
+        print(f"decode {preset} prompt={prompt_tokens} steps={steps}: last tokens {toks[-3:].tolist()} "
+              f"device_error={native.device_error_take(0)}")
+
+
 def main(argv: list[str]) -> None:
+    if argv[0] == "decode":
+        decode(argv[1], int(argv[2]), int(argv[3]))
+        return
     kind, tname, n, k = argv[0], argv[1], int(argv[2]), int(argv[3])
     m = int(argv[4]) if len(argv) > 4 else 1
     wt = TYPES[tname]

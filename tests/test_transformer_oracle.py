@@ -197,7 +197,9 @@ def tiny_decoder_weights(cfg, seed=7):
         if name in shapes:
             rows, cols = shapes[name]
             wt = cfg["embedding_type"] if name == "token_embedding" else cfg["weight_type"]
-            weights[name] = oracle.quantize(wt, oracle.normal(seed * 1000 + i, rows * cols, 0.02))
+            values = oracle.normal(seed * 1000 + i, rows * cols, 0.02)
+            weights[name] = (values.astype(np.float16).view(np.uint8) if wt == oracle.F16
+                             else oracle.quantize(wt, values))
         else:
             weights[name] = (1.0 + oracle.normal(seed * 1000 + i, h, 0.1)).astype(np.float32)
     return weights
