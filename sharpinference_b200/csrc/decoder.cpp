@@ -50,17 +50,7 @@ struct si_decoder {
     k::DecodeFeed *pinned_feed = nullptr;
     int32_t *pinned_prompt = nullptr, *pinned_history = nullptr;
     cudaGraphExec_t step_exec = nullptr, feed_exec = nullptr;
-    // Bytes of each projection slot; every decode-step launch pulls the
-    // weights of an upcoming projection into L2 (prefetch = false: none).
-    uint64_t qkv_bytes = 0, out_bytes = 0, up_bytes = 0, down_bytes = 0, embedding_bytes = 0;
-    bool prefetch = false;
-    // fuse = false records the program instruction by instruction, as the
-    // reference dispatches it (nine launches per layer); true fuses it into
-    // five (see record_step). Measured on B200 (Phi-4-mini, position ~600):
-    // 1.69 ms/token unfused, 2.02 fused: back-to-back GEMVs each need every
-    // SM's shared memory, so the next GEMV cannot stream its weights while
-    // the previous one runs, where a one-CTA norm kernel in between lets it.
-    bool fuse = false;
+
     // The persistent decode step (one cooperative launch per token) where the
     // model allows it; `direct`: its launches could not be recorded into a
     // graph and are issued per token instead.
@@ -127,46 +117,12 @@ si_status project(uint32_t type, const void *w, const float *x, float *y, int64_
     return k::matvec_dense(type, w, SI_TYPE_F32, x, SI_TYPE_F32, y, rows, cols, s);
 }
 
-// A projection with the instruction in front of it fused into the GEMV's
-// input load (residual-rms-norm, rms-norm or swiglu). Where the tensor-core
-// GEMV cannot take the transform (dense weights), the instruction runs as its
-// own kernel into `staging` and the plain mat-vec follows.
-si_status project_fused(si_decoder *d, uint32_t type, const void *w, const float *x, const k::XForm &xf, float *y,
-                        int64_t rows, int64_t cols, float *staging) {
-    cudaStream_t s = d->stream;
-    if (xf.mode == 0) {
-        if (type == SI_TYPE_Q8_0 || type == SI_TYPE_Q4_K) {
-            const si_status st = k::matvec_quant_mma(type, w, x, y, rows, cols, s, nullptr, nullptr, 0, &xf);
-            if (st != SI_ERR_UNSUPPORTED) return st;
-        }
-        return project(type, w, x, y, rows, cols, s);
-    }
-    if (type == SI_TYPE_Q8_0 || type == SI_TYPE_Q4_K) {
-        const si_status st = k::matvec_quant_mma(type, w, x, y, rows, cols, s, nullptr, nullptr, 0, &xf);
-        if (st != SI_ERR_UNSUPPORTED) return st;
-    }
-    si_status st;
-    if (xf.mode == 2)
-        st = k::tr_swiglu(x, nullptr, staging, 1, cols, s);
-    else if (xf.residual)
-        st = k::tr_rms_norm(x, xf.residual, xf.norm_weight, nullptr, xf.updated, staging, 1, cols, xf.eps, s);
-    else
-        st = k::tr_rms_norm(x, nullptr, xf.norm_weight, nullptr, nullptr, staging, 1, cols, xf.eps, s);
-    if (st) return st;
-    return project(type, w, staging, y, rows, cols, s);
-}
-
-// One decode step (Phi4D3D12TextSession.cs:866-920), enqueued on d->stream.
-// The program's instructions run fused, five launches per layer:
-//   qkv mat-vec  <- (residual-)rms-norm of the previous layer's output
-//   grouped-query-attention <- rope-kv-write
-//   attention-output mat-vec
-//   ffn_up mat-vec <- residual-rms-norm (stores hidden_after_attention)
-//   ffn_down mat-vec <- swiglu
-// and the vocabulary mat-vec takes the last residual-rms-norm with
-// output_norm. The residual stream alternates between `hidden` and
-// `hidden_after_attention` exactly as the reference's slots do.
 // The decode program one instruction per launch (Phi4D3D12TextSession.cs:866-920).
+// Measured on B200 (Phi-4-mini, position ~600): 1.69-1.75 ms per token.
+// A variant with the norms, swiglu and rope fused into the neighbouring
+// kernels (five launches per layer) measured 2.02 ms: back-to-back GEMVs
+// each need every SM's shared memory, so a GEMV could no longer stream its
+// weights during the previous kernel the way it does during a one-CTA norm.
 si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
     const si_decoder_config &c = d->cfg;
     const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
@@ -201,67 +157,12 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
     return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
 }
 
+// One decode step on d->stream: the persistent step's launch, or the
+// program instruction by instruction (nine launches per layer, each
+// programmatically dependent on the previous one).
 si_status record_step(si_decoder *d, k::DecodeFeed *feed) {
     if (d->step) return k::decode_step_launch(d->step, feed, d->stream);
-    if (!d->fuse) return record_step_unfused(d, feed);
-    const si_decoder_config &c = d->cfg;
-    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
-    cudaStream_t s = d->stream;
-    int32_t *position = d->control + 1;
-    // L2 prefetch schedule: each launch pulls an upcoming projection, so the
-    // weight stream keeps HBM busy through the latency-bound launches:
-    //   gather -> qkv_0; qkv_l -> out_l; attention_l -> up_l; out_l -> down_l;
-    //   up_l -> qkv_l+1; down_l -> up_l+1 (the last layer: the vocabulary).
-    const bool pf = d->prefetch;
-    const uint64_t vocab_half = std::min<uint64_t>(d->embedding_bytes / 2, uint64_t(48) << 20) & ~uint64_t(15);
-    auto next_qkv = [&](int l) -> std::pair<const void *, uint64_t> {
-        if (!pf) return {nullptr, 0};
-        if (l + 1 < c.layers) return {d->w_qkv[l + 1], d->qkv_bytes};
-        return {d->embedding, vocab_half};
-    };
-    auto next_up = [&](int l) -> std::pair<const void *, uint64_t> {
-        if (!pf) return {nullptr, 0};
-        if (l + 1 < c.layers) return {d->w_up[l + 1], d->up_bytes};
-        return {static_cast<const uint8_t *>(d->embedding) + vocab_half, vocab_half};
-    };
-    if (si_status st = k::tr_gather_row(c.embedding_type, d->embedding, c.vocab, H, d->control, d->hidden, s,
-                                        pf ? d->w_qkv[0] : nullptr, pf ? d->qkv_bytes : 0))
-        return st;
-    for (int l = 0; l < c.layers; ++l) {
-        // qkv <- rms(hidden, attn_norm_0), or residual-rms(after + down, attn_norm_l) storing hidden
-        k::XForm pre_attn = l == 0 ? k::XForm{1, nullptr, d->attn_norm[0], nullptr, c.epsilon}
-                                   : k::XForm{1, d->down, d->attn_norm[l], d->hidden, c.epsilon};
-        if (pf) pre_attn.prefetch = d->w_out[l], pre_attn.prefetch_bytes = d->out_bytes;
-        const float *attn_in = l == 0 ? d->hidden : d->after;
-        if (si_status st = project_fused(d, c.weight_type, d->w_qkv[l], attn_in, pre_attn, d->qkv, QKV, H,
-                                         d->normalized))
-            return st;
-        if (si_status st = k::tr_attention_decode_rope(d->qkv, d->freq, c.rotary_size, c.rope_scale, d->key_cache[l],
-                                                       d->value_cache[l], position, d->attention, c.query_heads,
-                                                       c.kv_heads, c.head_size, c.context, s,
-                                                       pf ? d->w_up[l] : nullptr, pf ? d->up_bytes : 0))
-            return st;
-        k::XForm plain{0, nullptr, nullptr, nullptr, 0.0f};
-        if (pf) plain.prefetch = d->w_down[l], plain.prefetch_bytes = d->down_bytes;
-        if (si_status st = project_fused(d, c.weight_type, d->w_out[l], d->attention, plain, d->projected, H, H,
-                                         d->normalized))
-            return st;
-        k::XForm pre_ffn{1, d->projected, d->ffn_norm[l], d->after, c.epsilon};
-        std::tie(pre_ffn.prefetch, pre_ffn.prefetch_bytes) = next_qkv(l);
-        if (si_status st = project_fused(d, c.weight_type, d->w_up[l], d->hidden, pre_ffn, d->gate_up, 2 * F, H,
-                                         d->normalized))
-            return st;
-        k::XForm act{2, nullptr, nullptr, nullptr, 0.0f};
-        std::tie(act.prefetch, act.prefetch_bytes) = next_up(l);
-        if (si_status st = project_fused(d, c.weight_type, d->w_down[l], d->gate_up, act, d->down, H, F,
-                                         d->activated))
-            return st;
-    }
-    const k::XForm final_norm{1, d->down, d->output_norm, nullptr, c.epsilon};
-    if (si_status st = project_fused(d, c.embedding_type, d->embedding, d->after, final_norm, d->logits, c.vocab, H,
-                                     d->normalized))
-        return st;
-    return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
+    return record_step_unfused(d, feed);
 }
 
 si_status build_graph(si_decoder *d, k::DecodeFeed *feed, cudaGraphExec_t *out) {
@@ -333,13 +234,7 @@ si_status create(int device, const si_decoder_config *c, si_decoder **out) {
     void *p = nullptr;
     if (si_status st = alloc_slot(d, "token_embedding", rb_e * uint64_t(c->vocab), &p)) return cleanup(st);
     d->embedding = p;
-    d->embedding_bytes = rb_e * uint64_t(c->vocab);
-    d->qkv_bytes = rb_h * uint64_t(QKV);
-    d->out_bytes = rb_h * uint64_t(H);
-    d->up_bytes = rb_h * uint64_t(2 * F);
-    d->down_bytes = rb_f * uint64_t(H);
-    if (const char *e = std::getenv("SI_DECODE_PREFETCH")) d->prefetch = std::atoi(e) != 0;
-    if (const char *e = std::getenv("SI_DECODE_FUSE")) d->fuse = std::atoi(e) != 0;
+
     float *f = nullptr;
     if (si_status st = alloc_typed(d, "output_norm", H * 4, &f)) return cleanup(st);
     if (si_status st = fill_ones(f, H)) return cleanup(st);

@@ -90,23 +90,6 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
         : "memory");
 }
 
-// L2 prefetch of this CTA's share of `bytes` bytes at `src` (16-byte
-// aligned, bytes a multiple of 16): fire-and-forget bulk prefetches of up to
-// 16 KB, issued by the calling warp's lanes. Used to pull the next
-// projection's weights into L2 while the current kernel runs.
-__device__ __forceinline__ void prefetch_l2_share(const void *src, uint64_t bytes, int lane) {
-    if (!src || !bytes) return;
-    const uint64_t units = bytes >> 4, per = (units + gridDim.x - 1) / gridDim.x;
-    const uint64_t b = per * blockIdx.x, e = b + per < units ? b + per : units;
-    constexpr uint64_t kChunk = 1024;  // 16-byte units per prefetch
-    for (uint64_t u = b + uint64_t(lane) * kChunk; u < e; u += 32 * kChunk) {
-        const uint32_t n = uint32_t((e - u < kChunk ? e - u : kChunk) << 4);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t *>(src) + (u << 4)),
-                     "r"(n)
-                     : "memory");
-    }
-}
-
 // Programmatic dependent launch. `pdl_trigger` lets the next kernel in the
 // stream start launching (its CTAs still wait for free SM resources);
 // `pdl_wait` blocks until every prerequisite grid has completed and its

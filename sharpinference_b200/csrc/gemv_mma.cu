@@ -80,20 +80,6 @@ struct MmaParams {
     int path;             // host side: 0 FP16 MMA, 1 INT8 MMA
     int groups;           // clusters (or CTAs when cluster == 1) in the grid
     int max_local_tiles;  // ceil(num_tiles / groups): row-sum slots per CTA when cluster > 1
-    // Input transform applied while x is loaded (the decode step's fused
-    // prologue; kernels::XForm): 0 x as is; 1 rms-norm, x_j = (x_j + x_res_j)
-    // * s * x_norm_w_j with s = 1 / sqrt(mean over all K of (x + x_res)^2 +
-    // x_eps), CTA 0 also storing x + x_res to x_updated; 2 swiglu, x_j =
-    // g_j / (1 + exp(-g_j)) * u_j with g = x[0, K) and u = x[K, 2K).
-    int x_mode;
-    float x_eps;
-    const float *x_res;
-    const float *x_norm_w;
-    float *x_updated;
-    // Weights of the next projection to pull into L2 once this CTA's ring
-    // is full (decode step; null: none).
-    const uint8_t *prefetch;
-    uint64_t prefetch_bytes;
 };
 
 // --- thread-block cluster helpers (distributed shared memory) ---
@@ -194,37 +180,6 @@ __device__ __forceinline__ uint32_t row_offset(const MmaParams &p, int row) {
     return uint32_t(row >> p.log2_group_rows) * p.group_stride + uint32_t(row & (p.group_rows - 1)) * p.row_pitch;
 }
 
-// Fused rms-norm prologue (x_mode 1): the C compute warps of every CTA
-// reduce the sum of squares of x + x_res over all K in one fixed order, so
-// every CTA derives the same scale; CTA 0 also stores x + x_res to
-// x_updated. `red` is C floats of shared memory the pipeline has not used
-// yet; named barrier 1 spans the C compute warps only.
-__device__ __forceinline__ float rms_prologue(const MmaParams &p, int warp, int lane, int C, float *red) {
-    const int64_t K = int64_t(p.nsb) * 256;
-    const bool store = p.x_updated != nullptr && blockIdx.x == 0;
-    float s = 0.0f;
-    for (int64_t i = (int64_t(warp) * 32 + lane) * 4; i < K; i += int64_t(C) * 128) {
-        float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + i));
-        if (p.x_res) {
-            const float4 r = __ldg(reinterpret_cast<const float4 *>(p.x_res + i));
-            a = make_float4(__fadd_rn(a.x, r.x), __fadd_rn(a.y, r.y), __fadd_rn(a.z, r.z), __fadd_rn(a.w, r.w));
-        }
-        if (store) *reinterpret_cast<float4 *>(p.x_updated + i) = a;
-        s = __fadd_rn(s, __fmul_rn(a.x, a.x));
-        s = __fadd_rn(s, __fmul_rn(a.y, a.y));
-        s = __fadd_rn(s, __fmul_rn(a.z, a.z));
-        s = __fadd_rn(s, __fmul_rn(a.w, a.w));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    if (lane == 0) red[warp] = s;
-    asm volatile("bar.sync 1, %0;" ::"r"(C * 32) : "memory");
-    float total = 0.0f;
-    for (int w = 0; w < C; ++w) total = __fadd_rn(total, red[w]);
-    asm volatile("bar.sync 1, %0;" ::"r"(C * 32) : "memory");  // red returns to the pipeline
-    return 1.0f / sqrtf(__fadd_rn(__fdiv_rn(total, float(K)), p.x_eps));
-}
-
 // WPS compute warps share each superblock column (WPS = 2: each takes one
 // 16-row half of a 32-row tile), for more warps in flight per SM.
 template <class Path, int SPW, int RT, int WPS, int MAXW>
@@ -289,10 +244,8 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                     bulk_copy_g2s(dst + size_t(r) * p.row_stride, wsrc + size_t(r0 + r) * p.row_bytes, p.cta_bytes,
                                   &full[s]);
             }
-            if (it == p.stages - 1) prefetch_l2_share(p.prefetch, p.prefetch_bytes, lane);
             if (++s == p.stages) s = 0, ring_phase ^= 1u;
         }
-        if (it < p.stages) prefetch_l2_share(p.prefetch, p.prefetch_bytes, lane);  // fewer tiles than stages
     } else if (warp == C + 1) {
         // Reducer: fixed-order sum of the C0 per-column partials of each
         // output (row r, input row u) = index r * TK + u of the tile.
@@ -337,15 +290,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                 if (has1) Path::load(X, gsb + sb1, lane, st1, my_scratch, p.x_stride, p.ntok);
             }
         };
-        const int64_t K = int64_t(p.nsb) * 256;
-        if (Path::kTokens > 1 || p.x_mode == 0) {
-            load_x(XSrc<0>{p.x, nullptr, nullptr, 1.0f, K});
-        } else if (p.x_mode == 1) {
-            const float scale = rms_prologue(p, warp, lane, C, part);
-            load_x(XSrc<1>{p.x, p.x_res, p.x_norm_w, scale, K});
-        } else {
-            load_x(XSrc<2>{p.x, nullptr, nullptr, 1.0f, K});
-        }
+        load_x(XSrc<0>{p.x, nullptr, nullptr, 1.0f, int64_t(p.nsb) * 256});
 
         const int g = lane >> 2, t = lane & 3;
         constexpr int kUnits = RT / 16 / WPS;  // 16-row groups per warp per tile
@@ -655,15 +600,7 @@ namespace {
 // by override), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
 si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream,
                      const PeerGather *peer, const int32_t *control, int token, int ntok, int64_t x_stride,
-                     int64_t y_stride, const XForm *xf = nullptr) {
-    if (xf && xf->mode) {
-        // The transforms read 16-byte vectors of x, the residual and the norm weight.
-        auto misaligned = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
-        if (path == 3 || (xf->mode != 1 && xf->mode != 2) || misaligned(x) ||
-            (xf->mode == 1 && (!xf->norm_weight || misaligned(xf->norm_weight) ||
-                               (xf->residual && misaligned(xf->residual)) || (xf->updated && misaligned(xf->updated)))))
-            return SI_ERR_UNSUPPORTED;
-    }
+                     int64_t y_stride) {
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
@@ -724,17 +661,6 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
     p.ntok = ntok;
     p.x_stride = x_stride;
     p.y_stride = y_stride;
-    if (xf && xf->mode) {
-        p.x_mode = xf->mode;
-        p.x_eps = xf->eps;
-        p.x_res = xf->residual;
-        p.x_norm_w = xf->norm_weight;
-        p.x_updated = xf->updated;
-    }
-    if (xf && xf->prefetch && xf->prefetch_bytes >= 16 && !(reinterpret_cast<uintptr_t>(xf->prefetch) & 15u)) {
-        p.prefetch = static_cast<const uint8_t *>(xf->prefetch);
-        p.prefetch_bytes = xf->prefetch_bytes & ~uint64_t(15);
-    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(p.groups * p.cluster));
     cfg.blockDim = dim3(unsigned((p.compute_warps + 2) * 32));
@@ -763,11 +689,10 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
 // Tensor-core quantised GEMV (Q4_K or Q8_0). Returns SI_ERR_UNSUPPORTED
 // (without touching the error string) when the shape needs the SIMT kernel.
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
-                           void *stream, const PeerGather *peer, const int32_t *control, int token,
-                           const XForm *xform) {
+                           void *stream, const PeerGather *peer, const int32_t *control, int token) {
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, control, token, 1, cols,
-                      rows, xform);
+                      rows);
 }
 
 // Q4_K batch: y[b] = W x[b] for the m input rows, eight per launch (each

@@ -80,27 +80,10 @@ struct PeerGather {
     int rank;
     int64_t row_base;                 // global index of this rank's first row
 };
-// Transform of the GEMV input applied while it is loaded (decode-step
-// fusion): mode 1 = transformer.residual-rms-norm / rms-norm in front of the
-// mat-vec (x := (x + residual) * rsqrt(mean((x + residual)^2) + eps) *
-// norm_weight, residual may be null, (x + residual) stored to `updated`
-// when non-null); mode 2 = transformer.swiglu in front (x = [gate | up] of
-// 2K floats, x := gate / (1 + exp(-gate)) * up). All vectors 16-byte aligned.
-// `prefetch`: weights of the next projection, pulled into L2 by this launch
-// (any mode, 16-byte aligned; null for none).
-struct XForm {
-    int mode;
-    const float *residual;
-    const float *norm_weight;
-    float *updated;
-    float eps;
-    const void *prefetch = nullptr;
-    uint64_t prefetch_bytes = 0;
-};
 // control/token: batch-shared use, y is written only when token < control[1].
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                            void *stream, const PeerGather *peer = nullptr, const int32_t *control = nullptr,
-                           int token = 0, const XForm *xform = nullptr);
+                           int token = 0);
 // Q4_K batch on the tensor cores, eight input rows per launch; SI_ERR_UNSUPPORTED
 // when the shape or alignment needs another kernel (nothing launched then).
 si_status matvec_q4k_batched(const void *w, const float *x, float *y, int64_t m, int64_t rows, int64_t cols,
@@ -119,9 +102,8 @@ struct DecodeFeed {
     int32_t capacity;
     int32_t pad;
 };
-// prefetch / prefetch_bytes (decode step): weights pulled into L2 by the launch.
 si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
-                        void *stream, const void *prefetch = nullptr, uint64_t prefetch_bytes = 0);
+                        void *stream);
 si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
                                     int64_t batch, int64_t width, void *stream);
 si_status tr_copy_rows(const float *in, float *out, int64_t count, void *stream);
@@ -138,13 +120,6 @@ si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int3
                            int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale, void *stream);
 si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                               int query_heads, int kv_heads, int head_size, int64_t context, void *stream);
-// rope-kv-write fused into the decode attention: qkv = [query | key | value],
-// the key/value rows at *position (0 <= *position < context) are written to
-// the caches by the kernel itself.
-si_status tr_attention_decode_rope(const float *qkv, const float *freq, int rotary, float rope_scale, float *kc,
-                                   float *vc, const int32_t *position, float *out, int query_heads, int kv_heads,
-                                   int head_size, int64_t context, void *stream, const void *prefetch = nullptr,
-                                   uint64_t prefetch_bytes = 0);
 si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *position, const int32_t *control,
                         float *scores, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
                         void *stream);

@@ -114,9 +114,8 @@ __device__ __forceinline__ float row_element(uint32_t type, const uint8_t *row, 
 // core.gather-row: out = table[index], NaN everywhere for an index outside
 // [0, rows) (GpuTierZeroInstruction.cs:397-407).
 __global__ void gather_row_kernel(uint32_t type, const uint8_t *table, int64_t rows, int64_t cols, uint64_t row_bytes,
-                                  const int32_t *index, float *out, const void *prefetch, uint64_t prefetch_bytes) {
+                                  const int32_t *index, float *out) {
     pdl_trigger();
-    if (threadIdx.x < 32) prefetch_l2_share(prefetch, prefetch_bytes, int(threadIdx.x));
     pdl_wait();
     const int32_t r = *index;
     const bool ok = r >= 0 && r < rows;
@@ -255,35 +254,11 @@ constexpr int kAttnWarps = 8;
 // per-CTA ranges; inside a CTA each warp takes tiles of kTile tokens and
 // keeps an online softmax (running max m, denominator l, weighted values)
 // for the G query heads of the group. Lane j holds channels j + 32 i.
-//
-// kRope (the decode step's fusion of rope-kv-write into the attention):
-// `query` is the qkv projection [query | key | value]; every CTA rotates its
-// query heads itself and the CTA whose token range holds *position rotates
-// this head's key, stores key and value rows at *position into the caches
-// and reads them back like any other row. The caller guarantees
-// 0 <= *position < context (the session checks it before every step).
-struct RopeArgs {
-    const float *freq;
-    int rotary;
-    float rope_scale;
-    const void *prefetch;  // weights pulled into L2 by the launch (decode step)
-    uint64_t prefetch_bytes;
-};
 
-__device__ __forceinline__ float rope_rotate(const float *head, int d, int rotary, int32_t pos, const RopeArgs &r) {
-    const float v = head[d];
-    if (d >= rotary) return v;
-    const int half = rotary >> 1, ri = d < half ? d : d - half;
-    const float other = head[d < half ? d + half : d - half];
-    const float angle = __fmul_rn(float(pos), r.freq[ri]);
-    const float c = __fmul_rn(cosf(angle), r.rope_scale), s = __fmul_rn(sinf(angle), r.rope_scale);
-    return d < half ? __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, s)) : __fadd_rn(__fmul_rn(v, c), __fmul_rn(other, s));
-}
-
-template <int NPL, int MAXG, int kTile, bool kRope>
+template <int NPL, int MAXG, int kTile>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
-    gqa_decode_kernel(const float *query, float *key_cache, float *value_cache, const int32_t *position, float *out,
-                      int group, int kv_heads, int head_size, int64_t context, float scale, RopeArgs rope) {
+    gqa_decode_kernel(const float *query, const float *key_cache, const float *value_cache, const int32_t *position,
+                      float *out, int group, int kv_heads, int head_size, int64_t context, float scale) {
     extern __shared__ float smem[];
     const int G = group, hs = head_size;
     float *w_acc = smem;                                 // [warps][G][hs]
@@ -296,26 +271,13 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
     const int kvh = blockIdx.x / kAttnCluster;
     const uint32_t rank = cta_rank_in_cluster();
     pdl_trigger();
-    if (warp == 0) prefetch_l2_share(rope.prefetch, rope.prefetch_bytes, lane);
     pdl_wait();
     int64_t active = *position;
     active = active < 0 ? 0 : (active > context - 1 ? context - 1 : active);
     const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
 
-    const int32_t pos = *position;
     const int64_t stride = int64_t(kv_heads) * hs;
-    if (kRope) {
-        if (t0 <= int64_t(pos) && int64_t(pos) < t1) {
-            const float *kin = query + int64_t(kv_heads) * G * hs + int64_t(kvh) * hs;
-            const float *vin = kin + stride;
-            for (int d = threadIdx.x; d < hs; d += blockDim.x) {
-                key_cache[int64_t(pos) * stride + int64_t(kvh) * hs + d] = rope_rotate(kin, d, rope.rotary, pos, rope);
-                value_cache[int64_t(pos) * stride + int64_t(kvh) * hs + d] = vin[d];
-            }
-        }
-        __syncthreads();  // the row at pos is read back below by this CTA's warps
-    }
     float q[MAXG][NPL], acc[MAXG][NPL], m[MAXG], l[MAXG];
 #pragma unroll
     for (int g = 0; g < MAXG; ++g) {
@@ -324,8 +286,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 #pragma unroll
         for (int i = 0; i < NPL; ++i) {
             const int d = lane + 32 * i;
-            const float *qh = query + (int64_t(kvh) * G + g) * hs;
-            q[g][i] = (g < G && d < hs) ? (kRope ? rope_rotate(qh, d, rope.rotary, pos, rope) : qh[d]) : 0.0f;
+            q[g][i] = (g < G && d < hs) ? query[(int64_t(kvh) * G + g) * hs + d] : 0.0f;
             acc[g][i] = 0.0f;
         }
     }
@@ -672,13 +633,11 @@ si_status launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 blo
 }  // namespace
 
 si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
-                        void *stream, const void *prefetch, uint64_t prefetch_bytes) {
+                        void *stream) {
     uint64_t row_bytes = 0;
     if (si_status st = byte_length(type, uint64_t(cols), &row_bytes)) return st;
-    if (reinterpret_cast<uintptr_t>(prefetch) & 15u) prefetch = nullptr;
     return launch("core.gather-row", gather_row_kernel, dim3(elementwise_grid(cols, 256)), dim3(256), 0, stream, type,
-                  static_cast<const uint8_t *>(table), rows, cols, row_bytes, index, out, prefetch,
-                  prefetch_bytes & ~uint64_t(15));
+                  static_cast<const uint8_t *>(table), rows, cols, row_bytes, index, out);
 }
 
 si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
@@ -726,10 +685,10 @@ si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int3
 }
 
 namespace {
-template <int NPL, int MAXG, int kTile, bool kRope>
-si_status launch_gqa(const float *query, float *kc, float *vc, const int32_t *position, float *out, int group,
-                     int kv_heads, int head_size, int64_t context, float scale, RopeArgs rope, void *stream) {
-    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile, kRope>;
+template <int NPL, int MAXG, int kTile>
+si_status launch_gqa(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
+                     int group, int kv_heads, int head_size, int64_t context, float scale, void *stream) {
+    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile>;
     const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
                                2 * group) * sizeof(float);
     if (smem > 48 * 1024) {
@@ -741,17 +700,17 @@ si_status launch_gqa(const float *query, float *kc, float *vc, const int32_t *po
     }
     return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(kv_heads * kAttnCluster)),
                   dim3(kAttnWarps * 32), smem, stream, query, kc, vc, position, out, group, kv_heads, head_size,
-                  context, scale, rope);
+                  context, scale);
 }
+}  // namespace
 
-template <bool kRope>
-si_status dispatch_gqa(const float *query, float *kc, float *vc, const int32_t *position, float *out, int query_heads,
-                       int kv_heads, int head_size, int64_t context, RopeArgs rope, void *stream) {
+si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
+                              int query_heads, int kv_heads, int head_size, int64_t context, void *stream) {
     const int group = query_heads / kv_heads;
     const float scale = 1.0f / sqrtf(float(head_size));
     const int npl = (head_size + 31) / 32;
 #define SI_GQA(NPL, MAXG, TILE) \
-    launch_gqa<NPL, MAXG, TILE, kRope>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, rope, stream)
+    launch_gqa<NPL, MAXG, TILE>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream)
     if (group <= 4) {
         if (npl <= 1) return SI_GQA(1, 4, 8);
         if (npl <= 2) return SI_GQA(2, 4, 8);
@@ -763,22 +722,6 @@ si_status dispatch_gqa(const float *query, float *kc, float *vc, const int32_t *
     if (npl <= 4) return SI_GQA(4, 8, 4);
     return SI_GQA(8, 8, 2);
 #undef SI_GQA
-}
-}  // namespace
-
-si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
-                              int query_heads, int kv_heads, int head_size, int64_t context, void *stream) {
-    return dispatch_gqa<false>(query, const_cast<float *>(kc), const_cast<float *>(vc), position, out, query_heads,
-                               kv_heads, head_size, context, RopeArgs{nullptr, 0, 1.0f, nullptr, 0}, stream);
-}
-
-si_status tr_attention_decode_rope(const float *qkv, const float *freq, int rotary, float rope_scale, float *kc,
-                                   float *vc, const int32_t *position, float *out, int query_heads, int kv_heads,
-                                   int head_size, int64_t context, void *stream, const void *prefetch,
-                                   uint64_t prefetch_bytes) {
-    if (reinterpret_cast<uintptr_t>(prefetch) & 15u) prefetch = nullptr;
-    return dispatch_gqa<true>(qkv, kc, vc, position, out, query_heads, kv_heads, head_size, context,
-                              RopeArgs{freq, rotary, rope_scale, prefetch, prefetch_bytes & ~uint64_t(15)}, stream);
 }
 
 si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *position, const int32_t *control,

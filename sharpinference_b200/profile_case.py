@@ -8,6 +8,9 @@ launch with `-s 1 -c 1`): synthetic seeded weights and inputs, device-resident.
   python -m sharpinference_b200.profile_case decode mini 64 2
       (Phi-4-mini random-init decoder: 64 prompt steps, then 2 more decode
       steps; each step is one graph of 292 kernel launches)
+  python -m sharpinference_b200.profile_case decode-trace mini 512
+      (the persistent decode step: one step at position 512 with its
+      per-phase trace, averaged per phase kind over the layers, CTA 0)
 """
 from __future__ import annotations
 
@@ -32,9 +35,43 @@ def decode(preset: str, prompt_tokens: int, steps: int) -> None:
               f"device_error={native.device_error_take(0)}")
 
 
+def decode_trace(preset: str, position: int) -> None:
+    import os
+    from . import phi4
+    os.environ["SI_DECODE_STEP"] = "1"
+    os.environ["SI_DECODE_TRACE"] = "1"
+    cfg = dict(phi4.PHI4_MINI if preset == "mini" else phi4.PHI4_14B)
+    cfg["context"] = position + 2
+    with native.Decoder(cfg) as dec:
+        phi4.load_synthetic(dec, cfg, seed=7)
+        prompt = phi4.random_prompt(7, position + 1, cfg["vocab"])
+        dec.generate(prompt[:position], 0)
+        dec.generate(prompt[position:], 0)  # the traced step
+        t = dec.read("step_trace", dtype=np.uint64).astype(np.int64)
+    phases = t.size // 24
+    t = t.reshape(3, phases, 8)
+    kinds = ["gather"] + ["qkv", "attention", "combine", "out", "gate_up", "down"] * cfg["layers"] + ["lm_head",
+                                                                                                   "argmax"]
+    rows = {}
+    for ph in range(1, phases - 1):
+        r = t[0, ph]
+        staged = (r[7] - r[0]) / 1e3 if r[7] else 0.0
+        rows.setdefault(kinds[ph], []).append(
+            [(r[1] - r[0]) / 1e3, (r[0] - t[0, ph - 1, 2]) / 1e3, staged, r[3] / 1e3, r[4] / 1e3, r[5] / 1e3,
+             r[6] / 1e3])
+    print(f"persistent decode step, {preset}, position {position}: {(t[0, phases - 1, 1] - t[0, 0, 0]) / 1e3:.1f} us")
+    print("phase      work  grid-wait  input  | waits: full  pempty  producer-empty  reducer-pfull   (us, CTA 0)")
+    for k, v in rows.items():
+        a = np.mean(np.array(v), axis=0)
+        print(f"{k:9s} " + " ".join(f"{x:7.2f}" for x in a))
+
+
 def main(argv: list[str]) -> None:
     if argv[0] == "decode":
         decode(argv[1], int(argv[2]), int(argv[3]))
+        return
+    if argv[0] == "decode-trace":
+        decode_trace(argv[1], int(argv[2]))
         return
     kind, tname, n, k = argv[0], argv[1], int(argv[2]), int(argv[3])
     m = int(argv[4]) if len(argv) > 4 else 1
