@@ -410,6 +410,38 @@ si_status si_decoder_generate(si_decoder *decoder, const int32_t *prompt, int32_
 si_status si_decoder_reset(si_decoder *decoder);  /* Reset(): position = 0 */
 si_status si_decoder_position(si_decoder *decoder, int32_t *position);
 
+/* ---------------------------------------------------------------------- */
+/* GGUF model files (GgufModelFile.cs)                                    */
+/* ---------------------------------------------------------------------- */
+/* si_gguf_open parses a GGUF v3 file as GgufModelFile.Open does
+ * (GgufModelFile.cs:57-160) and maps it read-only; SI_ERR_INVALID_DATA for
+ * a malformed file (InvalidDataException), SI_ERR_UNSUPPORTED for an
+ * unknown tensor type (NotSupportedException). Tensor data pointers point
+ * into the mapping and stay valid until si_gguf_close; their bytes are
+ * uploaded unchanged (Phi4D3D12TextSession.cs:56-57). Tensor types are GGUF
+ * ids (GgufModelTensorType, GgufModelFile.cs:24-46); byte lengths follow
+ * GetByteLength (:301-331) plus the K-quant superblocks (Q2_K..Q8_K). */
+typedef struct si_gguf si_gguf;
+si_status si_gguf_open(const char *path, si_gguf **out);
+si_status si_gguf_close(si_gguf *file);
+si_status si_gguf_tensor_count(si_gguf *file, int64_t *count);
+si_status si_gguf_find_tensor(si_gguf *file, const char *name, int64_t *index);
+/* dims: 8 entries (unused ones 0), in file order (fastest dimension first). */
+si_status si_gguf_tensor_info(si_gguf *file, int64_t index, char *name, size_t name_capacity, uint32_t *type,
+                              int32_t *rank, uint64_t *dims, uint64_t *bytes, const void **data);
+/* Metadata in file order; type = GgufMetadataType (:7-22); arrays report
+ * their element type and count. */
+si_status si_gguf_metadata_count(si_gguf *file, int64_t *count);
+si_status si_gguf_metadata_key(si_gguf *file, int64_t index, char *key, size_t capacity, uint32_t *type,
+                               uint32_t *element_type, uint64_t *count);
+/* Numeric and Bool values as double (GetMetadata<T>'s conversion). */
+si_status si_gguf_metadata_number(si_gguf *file, const char *key, double *value);
+si_status si_gguf_metadata_string(si_gguf *file, const char *key, char *buffer, size_t capacity, size_t *length);
+/* Arrays of fixed-size elements: a pointer to the packed little-endian
+ * elements in the mapping; String arrays: count and element type only. */
+si_status si_gguf_metadata_array(si_gguf *file, const char *key, uint32_t *element_type, uint64_t *count,
+                                 const void **data);
+
 #ifdef __cplusplus
 }
 #endif

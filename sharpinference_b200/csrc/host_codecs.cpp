@@ -28,27 +28,39 @@ void clear_error() { g_last_error.clear(); }
 
 const std::string &last_error() { return g_last_error; }
 
+// GgufModelFile.GetByteLength (GgufModelFile.cs:301-331), extended with the
+// K-quant superblocks of the GGUF format (256 elements: Q2_K 84 B, Q3_K 110,
+// Q4_K 144, Q5_K 176, Q6_K 210, Q8_K 292), which the reference rejects.
 si_status byte_length(uint32_t type, uint64_t elements, uint64_t *bytes) {
+    uint64_t block = 1, per = 0;
     switch (type) {
-    case SI_TYPE_F32: *bytes = elements * 4; return SI_OK;
-    case SI_TYPE_F16: *bytes = elements * 2; return SI_OK;
-    case SI_TYPE_Q8_0:
-        if (elements % kQ8_0Block)
-            return fail(SI_ERR_INVALID_DATA,
-                        "Quantized tensor element count %llu is not divisible by block size %d.",
-                        (unsigned long long)elements, kQ8_0Block);
-        *bytes = elements / kQ8_0Block * kQ8_0Bytes;
-        return SI_OK;
-    case SI_TYPE_Q4_K:
-        if (elements % kQ4KBlock)
-            return fail(SI_ERR_INVALID_DATA,
-                        "Quantized tensor element count %llu is not divisible by block size %d.",
-                        (unsigned long long)elements, kQ4KBlock);
-        *bytes = elements / kQ4KBlock * kQ4KBytes;
-        return SI_OK;
-    default:
-        return fail(SI_ERR_UNSUPPORTED, "GGUF tensor type '%u' is not supported.", type);
+    case 0: per = 4; break;                      // F32
+    case 1: case 30: per = 2; break;             // F16, BF16
+    case 24: per = 1; break;                     // I8
+    case 25: per = 2; break;                     // I16
+    case 26: per = 4; break;                     // I32
+    case 27: case 28: per = 8; break;            // I64, F64
+    case 2: block = 32, per = 18; break;         // Q4_0
+    case 3: block = 32, per = 20; break;         // Q4_1
+    case 6: block = 32, per = 22; break;         // Q5_0
+    case 7: block = 32, per = 24; break;         // Q5_1
+    case 8: block = 32, per = 34; break;         // Q8_0
+    case 9: block = 32, per = 36; break;         // Q8_1
+    case 10: block = 256, per = 84; break;       // Q2_K
+    case 11: block = 256, per = 110; break;      // Q3_K
+    case 12: block = 256, per = 144; break;      // Q4_K
+    case 13: block = 256, per = 176; break;      // Q5_K
+    case 14: block = 256, per = 210; break;      // Q6_K
+    case 15: block = 256, per = 292; break;      // Q8_K
+    default: return fail(SI_ERR_UNSUPPORTED, "GGUF tensor type '%u' is not supported.", type);
     }
+    if (elements % block)
+        return fail(SI_ERR_INVALID_DATA, "Quantized tensor element count %llu is not divisible by block size %llu.",
+                    (unsigned long long)elements, (unsigned long long)block);
+    const uint64_t blocks = elements / block;
+    if (blocks > UINT64_MAX / per) return fail(SI_ERR_INVALID_DATA, "tensor byte length overflows");
+    *bytes = blocks * per;
+    return SI_OK;
 }
 
 static inline uint32_t bits_of(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }

@@ -14,6 +14,7 @@ namespace si {
 // Thread-local last-error message; every failing entry point sets it.
 si_status fail(si_status status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 void clear_error();
+const std::string &last_error();
 
 constexpr int kQ8_0Block = 32;
 constexpr int kQ8_0Bytes = 34;

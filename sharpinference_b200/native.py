@@ -156,6 +156,18 @@ SIGNATURES = {
     "si_decoder_generate": [_vp, _vp, C.c_int32, C.c_int32, _vp],
     "si_decoder_reset": [_vp],
     "si_decoder_position": [_vp, C.POINTER(C.c_int32)],
+    # GGUF files
+    "si_gguf_open": [C.c_char_p, C.POINTER(_vp)],
+    "si_gguf_close": [_vp],
+    "si_gguf_tensor_count": [_vp, C.POINTER(_i64)],
+    "si_gguf_find_tensor": [_vp, C.c_char_p, C.POINTER(_i64)],
+    "si_gguf_tensor_info": [_vp, _i64, C.c_char_p, C.c_size_t, _pu32, C.POINTER(C.c_int32), _pu64, _pu64,
+                            C.POINTER(_vp)],
+    "si_gguf_metadata_count": [_vp, C.POINTER(_i64)],
+    "si_gguf_metadata_key": [_vp, _i64, C.c_char_p, C.c_size_t, _pu32, _pu32, _pu64],
+    "si_gguf_metadata_number": [_vp, C.c_char_p, C.POINTER(C.c_double)],
+    "si_gguf_metadata_string": [_vp, C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
+    "si_gguf_metadata_array": [_vp, C.c_char_p, _pu32, _pu64, C.POINTER(_vp)],
 }
 _RESTYPE = {"si_abi_version": C.c_int}
 
@@ -542,6 +554,87 @@ class Decoder:
     def close(self) -> None:
         if self.handle:
             call("si_decoder_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+# ---- GGUF model files ----------------------------------------------------------------
+GGUF_SCALARS = {0: "u1", 1: "i1", 2: "<u2", 3: "<i2", 4: "<u4", 5: "<i4", 6: "<f4", 7: "u1", 10: "<u8", 11: "<i8",
+                12: "<f8"}
+
+
+class GgufTensor:
+    def __init__(self, name, type_, dims, nbytes, address, owner):
+        self.name, self.type, self.dims, self.nbytes, self._address, self._owner = name, type_, dims, nbytes, address, owner
+
+    @property
+    def data(self):
+        """The tensor's bytes in the mapping (read-only view, no copy)."""
+        np = _np()
+        buf = (C.c_uint8 * self.nbytes).from_address(self._address)
+        arr = np.frombuffer(buf, dtype=np.uint8)
+        arr.flags.writeable = False
+        return arr
+
+
+class GgufFile:
+    """GgufModelFile: metadata and tensors of a GGUF v3 file (si_gguf_*)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        call("si_gguf_open", str(path).encode(), C.byref(h))
+        self.handle = h
+        n = C.c_int64()
+        call("si_gguf_tensor_count", h, C.byref(n))
+        self.tensors = {}
+        name = C.create_string_buffer(4096)
+        t, rank, nbytes, data = C.c_uint32(), C.c_int32(), C.c_uint64(), C.c_void_p()
+        dims = (C.c_uint64 * 8)()
+        for i in range(n.value):
+            call("si_gguf_tensor_info", h, i, name, 4096, C.byref(t), C.byref(rank), dims, C.byref(nbytes),
+                 C.byref(data))
+            nm = name.value.decode()
+            self.tensors[nm] = GgufTensor(nm, t.value, [dims[d] for d in range(rank.value)], nbytes.value,
+                                          data.value, self)
+        call("si_gguf_metadata_count", h, C.byref(n))
+        self.metadata = {}
+        et, cnt = C.c_uint32(), C.c_uint64()
+        for i in range(n.value):
+            call("si_gguf_metadata_key", h, i, name, 4096, C.byref(t), C.byref(et), C.byref(cnt))
+            key = name.value.decode()
+            self.metadata[key] = self._value(key, t.value, et.value, cnt.value)
+
+    def _value(self, key, type_, elem, count):
+        np = _np()
+        k = key.encode()
+        if type_ == 8:
+            n = C.c_size_t()
+            call("si_gguf_metadata_string", self.handle, k, None, 0, C.byref(n))
+            buf = C.create_string_buffer(n.value + 1)
+            call("si_gguf_metadata_string", self.handle, k, buf, n.value + 1, None)
+            return buf.raw[:n.value].decode("utf-8")
+        if type_ == 9:
+            if elem not in GGUF_SCALARS:
+                return ("array", elem, count)
+            p = C.c_void_p()
+            call("si_gguf_metadata_array", self.handle, k, None, None, C.byref(p))
+            dt = np.dtype(GGUF_SCALARS[elem])
+            arr = np.frombuffer((C.c_uint8 * (count * dt.itemsize)).from_address(p.value), dtype=dt).copy()
+            return arr.astype(bool) if elem == 7 else arr
+        v = C.c_double()
+        call("si_gguf_metadata_number", self.handle, k, C.byref(v))
+        if type_ == 7:
+            return bool(v.value)
+        return v.value if type_ in (6, 12) else int(v.value)
+
+    def close(self):
+        if self.handle:
+            call("si_gguf_close", self.handle)
             self.handle = None
 
     def __enter__(self):

@@ -76,3 +76,70 @@ def random_prompt(seed: int, tokens: int, vocab: int) -> np.ndarray:
         z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
         z = z ^ (z >> np.uint64(31))
     return (z % np.uint64(vocab)).astype(np.int32)
+
+
+# ---- GGUF files: the session's weights by the reference's tensor names ------------
+# Phi4D3D12TextSession.cs:391-410: slot <- GGUF tensor.
+def gguf_tensor_name(slot: str) -> str:
+    if slot == "token_embedding":
+        return "token_embd.weight"
+    if slot == "output_norm":
+        return "output_norm.weight"
+    name, layer = slot.rsplit("_", 1)
+    return {"attn_norm": f"blk.{layer}.attn_norm.weight", "ffn_norm": f"blk.{layer}.ffn_norm.weight",
+            "qkv_weight": f"blk.{layer}.attn_qkv.weight", "attn_output_weight": f"blk.{layer}.attn_output.weight",
+            "ffn_up_weight": f"blk.{layer}.ffn_up.weight", "ffn_down_weight": f"blk.{layer}.ffn_down.weight"}[name]
+
+
+def config_from_gguf(f: "native.GgufFile", context: int = 4096) -> dict:
+    """The decoder configuration of a phi3-architecture GGUF file: the
+    metadata the reference session reads (phi3.rope.freq_base,
+    phi3.attention.layer_norm_rms_epsilon, phi3.rope.scaling.attn_factor),
+    the shape keys, and the weight types of the tensors themselves."""
+    m = f.metadata
+    emb = f.tensors["token_embd.weight"]
+    heads = int(m.get("phi3.attention.head_count", PHI4_MINI["query_heads"]))
+    hidden = int(m.get("phi3.embedding_length", emb.dims[0]))
+    cfg = dict(layers=int(m.get("phi3.block_count", PHI4_MINI["layers"])), hidden=hidden, query_heads=heads,
+               kv_heads=int(m.get("phi3.attention.head_count_kv", heads)), head_size=hidden // heads,
+               rotary_size=int(m.get("phi3.rope.dimension_count", hidden // heads)),
+               intermediate=int(m.get("phi3.feed_forward_length", PHI4_MINI["intermediate"])), vocab=int(emb.dims[1]),
+               context=context, epsilon=float(m["phi3.attention.layer_norm_rms_epsilon"]),
+               rope_base=float(m["phi3.rope.freq_base"]),
+               rope_scale=float(m.get("phi3.rope.scaling.attn_factor", 1.0)),
+               weight_type=f.tensors["blk.0.attn_qkv.weight"].type, embedding_type=emb.type)
+    return cfg
+
+
+def load_gguf(decoder: "native.Decoder", f: "native.GgufFile") -> None:
+    """Uploads every slot's GGUF tensor unchanged (Phi4D3D12TextSession.cs:56-57)."""
+    for slot in native.decoder_slot_names(decoder.cfg.layers):
+        t = f.tensors[gguf_tensor_name(slot)]
+        size = decoder.slot(slot)[1]
+        if t.nbytes != size:
+            raise native.InvalidDataError(f"GGUF tensor '{t.name}' has {t.nbytes} bytes, slot '{slot}' {size}")
+        decoder.upload(slot, t.data)
+
+
+def save_gguf(path, cfg: dict, weights: dict) -> None:
+    """Writes a model (the session's slots -> arrays) as a phi3 GGUF file."""
+    from . import gguf
+    h, f_ = cfg["hidden"], cfg["intermediate"]
+    shapes = linear_shapes(cfg)
+    meta = {"general.architecture": "phi3", "general.alignment": (gguf.U32, 32),
+            "phi3.block_count": (gguf.U32, cfg["layers"]), "phi3.embedding_length": (gguf.U32, h),
+            "phi3.feed_forward_length": (gguf.U32, f_), "phi3.attention.head_count": (gguf.U32, cfg["query_heads"]),
+            "phi3.attention.head_count_kv": (gguf.U32, cfg["kv_heads"]),
+            "phi3.rope.dimension_count": (gguf.U32, cfg["rotary_size"]),
+            "phi3.attention.layer_norm_rms_epsilon": (gguf.F32, cfg["epsilon"]),
+            "phi3.rope.freq_base": (gguf.F32, cfg["rope_base"]),
+            "phi3.rope.scaling.attn_factor": (gguf.F32, cfg["rope_scale"])}
+    tensors = []
+    for slot in native.decoder_slot_names(cfg["layers"]):
+        if slot in shapes:
+            rows, cols = shapes[slot]
+            t = cfg["embedding_type"] if slot == "token_embedding" else cfg["weight_type"]
+            tensors.append((gguf_tensor_name(slot), t, [cols, rows], weights[slot]))
+        else:
+            tensors.append((gguf_tensor_name(slot), 0, [h], np.asarray(weights[slot], dtype=np.float32)))
+    gguf.write(path, meta, tensors)

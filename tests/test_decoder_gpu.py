@@ -134,3 +134,20 @@ def test_persistent_step_matches_oracle(monkeypatch, wtype):
         rest = dec.generate([got[-1]], 19)
         assert got + list(rest) == want
     assert native.device_error_take(0) == 0
+
+
+def test_session_from_gguf_file(tmp_path):
+    """A model saved as a phi3 GGUF file, opened by the library's reader and
+    uploaded byte-for-byte into the session, decodes the oracle's tokens."""
+    from sharpinference_b200 import phi4
+    cfg = tiny_decoder_config()
+    weights = tiny_decoder_weights(cfg, seed=33)
+    path = tmp_path / "tiny.gguf"
+    phi4.save_gguf(path, cfg, weights)
+    prompt = np.random.default_rng(33).integers(0, cfg["vocab"], 10)
+    want = oracle.Decoder(cfg, weights).generate(prompt, 10)
+    with native.GgufFile(path) as f:
+        gcfg = phi4.config_from_gguf(f, context=cfg["context"])
+        with native.Decoder(gcfg) as dec:
+            phi4.load_gguf(dec, f)
+            assert list(dec.generate(prompt, 10)) == want
