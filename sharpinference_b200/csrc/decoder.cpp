@@ -118,6 +118,9 @@ si_status project(uint32_t type, const void *w, const float *x, float *y, int64_
 }
 
 // The decode program one instruction per launch (Phi4D3D12TextSession.cs:866-920).
+// Fusing rope-kv-write into the attention launch measured slower (1.69 vs
+// 1.59 ms per token): the one-wave rope kernel is another window in which
+// the next GEMV streams its weights.
 // Measured on B200 (Phi-4-mini, position ~600): 1.69-1.75 ms per token.
 // A variant with the norms, swiglu and rope fused into the neighbouring
 // kernels (five launches per layer) measured 2.02 ms: back-to-back GEMVs

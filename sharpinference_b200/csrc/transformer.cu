@@ -41,9 +41,12 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
+// Remote shared-memory load. Volatile keeps it after the cluster barrier
+// (also a volatile asm); without a memory clobber, loads written back to
+// back are issued back to back.
 __device__ __forceinline__ float dsmem_f32(uint32_t addr) {
     float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
 }
 __device__ __forceinline__ uint32_t dsmem_u32(uint32_t addr) {
@@ -151,6 +154,8 @@ __global__ void copy_rows_kernel(const float *in, float *out, int64_t count) {
 // updated = hidden + residual is stored before the norm reads it back, so
 // `updated` may alias `hidden`; a null `updated` (internal callers only)
 // recomputes the sum instead of storing it.
+constexpr int kRmsHeld = 8;  // elements per thread held in registers (rows <= 8192 at 1024 threads)
+
 template <bool kResidual>
 __global__ void __launch_bounds__(1024) rms_norm_kernel(const float *in, const float *residual, const float *weight,
                                                         const int32_t *control, float *updated, float *out,
@@ -163,6 +168,34 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const float *in, const f
     const float *x = in + row * width;
     const float *r = kResidual ? residual + row * width : nullptr;
     float *u = kResidual && updated ? updated + row * width : nullptr;
+    float *o = out + row * width;
+    // Rows up to kRmsHeld * blockDim elements keep their values and weights in
+    // registers: every load is issued before the reduction (one round trip).
+    if (width <= int64_t(kRmsHeld) * blockDim.x) {
+        float v[kRmsHeld], w[kRmsHeld];
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kRmsHeld; ++k) {
+            const int64_t j = threadIdx.x + int64_t(k) * blockDim.x;
+            const bool ok = j < width;
+            v[k] = ok ? (kResidual ? __fadd_rn(x[j], r[j]) : x[j]) : 0.0f;
+            w[k] = ok ? weight[j] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kRmsHeld; ++k) {
+            const int64_t j = threadIdx.x + int64_t(k) * blockDim.x;
+            if (kResidual && u && j < width) u[j] = v[k];
+            s = __fadd_rn(s, __fmul_rn(v[k], v[k]));
+        }
+        s = block_sum(s, red);
+        const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s, float(width)), eps));
+#pragma unroll
+        for (int k = 0; k < kRmsHeld; ++k) {
+            const int64_t j = threadIdx.x + int64_t(k) * blockDim.x;
+            if (j < width) o[j] = __fmul_rn(__fmul_rn(v[k], scale), w[k]);
+        }
+        return;
+    }
     float s = 0.0f;
     for (int64_t j = threadIdx.x; j < width; j += blockDim.x) {
         float v = x[j];
@@ -174,7 +207,6 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const float *in, const f
     }
     s = block_sum(s, red);
     const float scale = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s, float(width)), eps));
-    float *o = out + row * width;
     for (int64_t j = threadIdx.x; j < width; j += blockDim.x) {
         const float v = !kResidual ? x[j] : (u ? u[j] : __fadd_rn(x[j], r[j]));
         o[j] = __fmul_rn(__fmul_rn(v, scale), weight[j]);
@@ -254,6 +286,7 @@ constexpr int kAttnWarps = 8;
 // per-CTA ranges; inside a CTA each warp takes tiles of kTile tokens and
 // keeps an online softmax (running max m, denominator l, weighted values)
 // for the G query heads of the group. Lane j holds channels j + 32 i.
+
 
 template <int NPL, int MAXG, int kTile>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
@@ -375,20 +408,23 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
     const int lo = int(rank) * chunk, hi = lo + chunk < total ? lo + chunk : total;
     for (int idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
         const int g = idx / hs, d = idx - g * hs;
-        float mr[kAttnCluster];
+        float mr[kAttnCluster], ar[kAttnCluster], lr[kAttnCluster];
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {  // all 3 x 8 remote loads first
+            mr[r] = dsmem_f32(dsmem_addr(c_m + g, uint32_t(r)));
+            ar[r] = dsmem_f32(dsmem_addr(c_acc + idx, uint32_t(r)));
+            lr[r] = dsmem_f32(dsmem_addr(c_l + g, uint32_t(r)));
+        }
         float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) {
-            mr[r] = dsmem_f32(dsmem_addr(c_m + g, uint32_t(r)));
-            M = fmaxf(M, mr[r]);
-        }
+        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, mr[r]);
         float A = 0.0f, L = 0.0f;
 #pragma unroll
         for (int r = 0; r < kAttnCluster; ++r) {
             if (mr[r] == -INFINITY) continue;
             const float f = expf(__fsub_rn(mr[r], M));
-            A = __fadd_rn(A, __fmul_rn(dsmem_f32(dsmem_addr(c_acc + idx, uint32_t(r))), f));
-            L = __fadd_rn(L, __fmul_rn(dsmem_f32(dsmem_addr(c_l + g, uint32_t(r))), f));
+            A = __fadd_rn(A, __fmul_rn(ar[r], f));
+            L = __fadd_rn(L, __fmul_rn(lr[r], f));
         }
         out[(int64_t(kvh) * G + g) * hs + d] = __fdiv_rn(A, L);
     }
