@@ -563,7 +563,9 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
     """Config 4: the Phi-4-mini-shaped random-init decoder (32 layers, Q4_K
     linears and tied Q4_K token embedding, seed 7) through the decoder
     session: a 512-token uniform-random prompt fed step by step (each step
-    one graph of the decode program), then 128 greedy decode steps in the
+    one graph of the decode program; its ids are checked against the
+    oracle's), then the same prompt again through the batched prefill
+    (timed: prefill tok/s), then 128 greedy decode steps in the
     device-resident loop. decode tok/s = 128 / device time of the 128 steps;
     e2e = the same through the public call (si_decoder_generate: the seed
     token uploaded, the 128 token ids read back) by the host clock."""
@@ -583,18 +585,30 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
         for name, blob in weights.items():
             dec.upload(name, blob)
         stream = torch.cuda.ExternalStream(dec.stream, device=torch.device("cuda", local))
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         with ClockSampler(local) as clk:
+            # the prompt through the decode program token by token (the
+            # greedy ids checked against the oracle below)
             e[0].record(stream)
             hist = dec.generate(prompt, 0)
             e[1].record(stream)
+            dec.reset()
+            dec.prefill(prompt)  # warm-up: chunk buffers, kernel attributes
+            dec.reset()
+            e[4].record(stream)
+            t0 = time.perf_counter()
+            nxt = dec.prefill(prompt)  # batched prefill (two chunks of 256 rows)
+            prefill_wall = time.perf_counter() - t0
+            e[5].record(stream)
             e[2].record(stream)
             t0 = time.perf_counter()
-            toks = dec.generate(hist[-1:], steps - 1)
+            toks = dec.generate([nxt], steps - 1)
             wall = time.perf_counter() - t0
             e[3].record(stream)
             e[3].synchronize()
-        prefill_ms, decode_ms = e[0].elapsed_time(e[1]), e[2].elapsed_time(e[3])
+        stepwise_ms, decode_ms = e[0].elapsed_time(e[1]), e[2].elapsed_time(e[3])
+        prefill_ms = e[4].elapsed_time(e[5])
+        linear_params = sum(r * c for n, (r, c) in phi4.linear_shapes(cfg).items() if n != "token_embedding")
         kv_row = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_size"] * 4  # K and V rows of all layers
         kv_bytes = sum(kv_row * (p + 1) for p in range(512, 512 + steps))
         wbytes = phi4.weight_bytes(cfg)
@@ -602,7 +616,11 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
         tok_s = steps / (decode_ms * 1e-3)
         out.update({
             "decode_tok_s": round(tok_s, 1), "decode_ms_per_token": round(decode_ms / steps, 4),
-            "prefill_ms_per_token": round(prefill_ms / 512, 4),
+            "prompt_stepwise_ms_per_token": round(stepwise_ms / 512, 4),
+            "prefill_tok_s": round(512 / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 3),
+            "prefill_e2e_tok_s": round(512 / prefill_wall, 1),
+            "prefill_linear_tflops": round(2 * linear_params * 512 / (prefill_ms * 1e-3) / 1e12, 1),
+            "prefill_next_equals_stepwise": bool(nxt == int(hist[-1])),
             "e2e_decode_tok_s": round(steps / wall, 1),
             "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_per_token),
                          "bytes": "all GGUF weight bytes read once per token + the KV-cache rows attended",

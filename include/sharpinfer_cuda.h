@@ -358,6 +358,15 @@ si_status si_batch_causal_softmax(const float *scores, const int32_t *control, f
 si_status si_batch_gqa_values(const float *probabilities, const float *value_cache, const int32_t *control,
                               float *output, int64_t batch, int32_t query_heads, int32_t kv_heads, int32_t head_size,
                               int64_t context, void *stream);
+/* batch-gqa-scores -> batch-causal-softmax -> batch-gqa-values in one pass
+ * (the prefill chunk's attention, GpuBatchTransformerInstructions.cs:320-551
+ * composed): query [count, query_heads * head_size] holds rows at positions
+ * start .. start + count - 1; row b attends cache tokens 0..start + b.
+ * 0 <= start, start + count <= context; head_size 64, 128, 192 or 256
+ * (SI_ERR_UNSUPPORTED otherwise); buffers 16-byte aligned. */
+si_status si_batch_grouped_query_attention(const float *query, const float *key_cache, const float *value_cache,
+                                           int32_t start, int32_t count, float *output, int32_t query_heads,
+                                           int32_t kv_heads, int32_t head_size, int64_t context, void *stream);
 /* output = input row control[1] - 1 when 0 < control[1] <= batch. */
 si_status si_batch_select_last(const float *input, const int32_t *control, float *output, int64_t batch,
                                int64_t width, void *stream);
@@ -407,6 +416,21 @@ si_status si_decoder_forward_token(si_decoder *decoder, int32_t token, int32_t *
  * entries); position advances by prompt_tokens + steps. */
 si_status si_decoder_generate(si_decoder *decoder, const int32_t *prompt, int32_t prompt_tokens, int32_t steps,
                               int32_t *tokens);
+/* Batched prompt prefill (the prefill_fused_16 program,
+ * Phi4D3D12TextSession.cs:267-286 and :1018-1155): the prompt in chunks of
+ * up to 256 rows with control = (position, rows) per chunk; projections as
+ * GEMMs, batch rope-kv-write, the batch scores / causal-softmax / values
+ * instructions fused into one attention pass, batch residual norms; after
+ * the last chunk select-last, vocabulary mat-vec and argmax. *next_token =
+ * the prediction after the last prompt token; position advances by
+ * prompt_tokens. Head sizes other than 64/128/192/256 run the decode
+ * program once per token instead. */
+si_status si_decoder_prefill(si_decoder *decoder, const int32_t *prompt, int32_t prompt_tokens, int32_t *next_token);
+/* PrefillFusedEmbeddings (Phi4D3D12TextSession.cs:267-286): the same
+ * program on `rows` ready FP32 embedding rows [rows, hidden] from host
+ * memory instead of gathered token rows. */
+si_status si_decoder_prefill_embeddings(si_decoder *decoder, const float *embeddings, int32_t rows,
+                                        int32_t *next_token);
 si_status si_decoder_reset(si_decoder *decoder);  /* Reset(): position = 0 */
 si_status si_decoder_position(si_decoder *decoder, int32_t *position);
 

@@ -56,6 +56,16 @@ struct si_decoder {
     // graph and are issued per token instead.
     k::DecodeStep *step = nullptr;
     bool direct = false;
+    // Prompt prefill in chunks of up to kPrefillRows rows (buffers allocated
+    // by the first prefill call): the chunk's activations, one (start,
+    // count) control pair per chunk, the split-operand GEMM workspace.
+    struct Prefill {
+        float *hidden, *after, *normalized, *qkv, *query, *attention, *projected, *gate_up, *activated, *down;
+        int32_t *control;
+        void *workspace;
+        uint64_t workspace_bytes;
+    } pf{};
+    bool pf_ready = false;
     int32_t position = 0;
     std::mutex lock;  // session calls are serialised, as the executor's are
 };
@@ -191,6 +201,135 @@ si_status build_graph(si_decoder *d, k::DecodeFeed *feed, cudaGraphExec_t *out) 
     const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     return cuda(ie, "cudaGraphInstantiate");
+}
+
+// Prefill chunk rows: one tcgen05 GEMM tile of input rows (N = 256), so
+// every weight tile is read once per chunk.
+constexpr int64_t kPrefillRows = 256;
+
+si_status ensure_prefill(si_decoder *d) {
+    if (d->pf_ready) return SI_OK;
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
+    const int64_t R = kPrefillRows;
+    auto &P = d->pf;
+    struct A {
+        const char *name;
+        float **dst;
+        int64_t n;
+    } acts[] = {{"batch_hidden", &P.hidden, R * H},       {"batch_hidden_after_attention", &P.after, R * H},
+                {"batch_normalized", &P.normalized, R * H}, {"batch_qkv", &P.qkv, R * QKV},
+                {"batch_query", &P.query, R * H},         {"batch_attention", &P.attention, R * H},
+                {"batch_projected", &P.projected, R * H}, {"batch_gate_up", &P.gate_up, R * 2 * F},
+                {"batch_activated", &P.activated, R * F}, {"batch_down", &P.down, R * H}};
+    for (const A &a : acts)
+        if (si_status st = alloc_typed(d, a.name, uint64_t(a.n) * 4, a.dst)) return st;
+    const int64_t chunks = (c.context + R - 1) / R;
+    if (si_status st = alloc_typed(d, "prefill_control", uint64_t(chunks) * 8, &P.control)) return st;
+    uint64_t ws = 0;
+    for (auto [n, kk] : {std::pair<int64_t, int64_t>{QKV, H}, {H, H}, {2 * F, H}, {H, F}})
+        for (int64_t rows = 64; rows <= R; rows += 64) {  // the split count depends on the rows
+            uint64_t b = 0;
+            k::gemm_workspace_bytes(c.weight_type, rows, n, kk, &b);
+            ws = std::max(ws, b);
+        }
+    if (ws) {
+        void *p = nullptr;
+        if (si_status st = alloc_slot(d, "gemm_workspace", ws, &p)) return st;
+        P.workspace = p;
+        P.workspace_bytes = ws;
+    }
+    d->pf_ready = true;
+    return SI_OK;
+}
+
+// Y[rows, n] = X[rows, k] W^T: the tcgen05 GEMM from 64 rows, the batch
+// GEMV below that.
+si_status batch_project(si_decoder *d, const void *w, const float *x, float *y, int64_t rows, int64_t n, int64_t k) {
+    return k::gemm_tn(d->cfg.weight_type, x, w, y, rows, n, k, d->pf.workspace, d->pf.workspace_bytes, d->stream);
+}
+
+// The prefill program of one chunk (Phi4D3D12TextSession.cs:1018-1155) on
+// rows [start, start + rows) whose hidden rows are already in pf.hidden:
+// batch instructions with control = (start, rows), the three attention
+// instructions fused, and after the last chunk select-last -> vocabulary
+// projection -> argmax into next_token.
+si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, int32_t rows, bool last) {
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
+    auto &P = d->pf;
+    cudaStream_t s = d->stream;
+    if (si_status st = k::tr_rms_norm(P.hidden, nullptr, d->attn_norm[0], control, nullptr, P.normalized, rows, H,
+                                      c.epsilon, s))
+        return st;
+    for (int l = 0; l < c.layers; ++l) {
+        if (si_status st = batch_project(d, d->w_qkv[l], P.normalized, P.qkv, rows, QKV, H)) return st;
+        if (si_status st = k::tr_rope_kv_write(P.qkv, nullptr, control, d->freq, P.query, d->key_cache[l],
+                                               d->value_cache[l], rows, H, KV, c.head_size, c.rotary_size, c.context,
+                                               c.rope_scale, s))
+            return st;
+        if (si_status st = k::tr_prefill_attention(P.query, d->key_cache[l], d->value_cache[l], start, rows,
+                                                   P.attention, c.query_heads, c.kv_heads, c.head_size, c.context, s))
+            return st;
+        if (si_status st = batch_project(d, d->w_out[l], P.attention, P.projected, rows, H, H)) return st;
+        if (si_status st = k::tr_rms_norm(P.hidden, P.projected, d->ffn_norm[l], control, P.after, P.normalized, rows,
+                                          H, c.epsilon, s))
+            return st;
+        if (si_status st = batch_project(d, d->w_up[l], P.normalized, P.gate_up, rows, 2 * F, H)) return st;
+        if (si_status st = k::tr_swiglu(P.gate_up, control, P.activated, rows, F, s)) return st;
+        if (si_status st = batch_project(d, d->w_down[l], P.activated, P.down, rows, H, F)) return st;
+        const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
+        if (si_status st = k::tr_rms_norm(P.after, P.down, next_norm, control, P.hidden, P.normalized, rows, H,
+                                          c.epsilon, s))
+            return st;
+    }
+    if (!last) return SI_OK;
+    if (si_status st = k::tr_select_last(P.normalized, control, d->normalized, rows, H, s)) return st;
+    if (si_status st = project(c.embedding_type, d->embedding, d->normalized, d->logits, c.vocab, H, s)) return st;
+    return k::tr_argmax(d->logits, c.vocab, d->next_token, nullptr, s);
+}
+
+// Prefill of `count` rows from the session position: token ids (gathered
+// from token_embedding) or ready embedding rows from the host.
+si_status prefill(si_decoder *d, const int32_t *tokens, const float *embeddings, int32_t count, int32_t *next_token) {
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden;
+    if (si_status st = ensure_prefill(d)) return st;
+    cudaStream_t s = d->stream;
+    const int32_t chunks = int32_t((count + kPrefillRows - 1) / kPrefillRows);
+    std::vector<int32_t> pairs(size_t(chunks) * 2);
+    for (int32_t i = 0; i < chunks; ++i) {
+        pairs[size_t(2 * i)] = d->position + int32_t(i * kPrefillRows);
+        pairs[size_t(2 * i + 1)] = int32_t(std::min<int64_t>(kPrefillRows, count - i * kPrefillRows));
+    }
+    if (si_status st = cuda(cudaMemcpyAsync(d->pf.control, pairs.data(), pairs.size() * 4, cudaMemcpyHostToDevice, s),
+                            "upload"))
+        return st;
+    if (tokens) {
+        std::memcpy(d->pinned_prompt, tokens, size_t(count) * 4);
+        if (si_status st = cuda(cudaMemcpyAsync(d->prompt, d->pinned_prompt, size_t(count) * 4,
+                                                cudaMemcpyHostToDevice, s), "upload"))
+            return st;
+    }
+    for (int32_t i = 0; i < chunks; ++i) {
+        const int32_t start = pairs[size_t(2 * i)], rows = pairs[size_t(2 * i + 1)];
+        const int64_t first = int64_t(i) * kPrefillRows;
+        if (tokens) {
+            if (si_status st = k::tr_gather_rows_quant(c.embedding_type, d->embedding, c.vocab, H, d->prompt + first,
+                                                       rows, d->pf.hidden, s))
+                return st;
+        } else if (si_status st = cuda(cudaMemcpyAsync(d->pf.hidden, embeddings + first * H, size_t(rows) * H * 4,
+                                                       cudaMemcpyHostToDevice, s), "upload")) {
+            return st;
+        }
+        if (si_status st = prefill_chunk(d, d->pf.control + 2 * i, start, rows, i + 1 == chunks)) return st;
+    }
+    if (si_status st = cuda(cudaMemcpyAsync(d->pinned + 2, d->next_token, 4, cudaMemcpyDeviceToHost, s), "readback"))
+        return st;
+    if (si_status st = cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return st;
+    d->position += count;
+    *next_token = d->pinned[2];
+    return SI_OK;
 }
 
 si_status validate(const si_decoder_config *c) {
@@ -480,6 +619,43 @@ si_status si_decoder_generate(si_decoder *d, const int32_t *prompt, int32_t prom
     std::memcpy(tokens, d->pinned_history, size_t(n) * 4);
     d->position += int32_t(n);
     return SI_OK;
+}
+
+si_status si_decoder_prefill(si_decoder *d, const int32_t *prompt, int32_t prompt_tokens, int32_t *next_token) {
+    if (!d || !prompt || !next_token) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    if (prompt_tokens <= 0) return fail(SI_ERR_INVALID_ARGUMENT, "prompt_tokens must be positive");
+    {
+        std::lock_guard<std::mutex> g(d->lock);
+        if (d->position + int64_t(prompt_tokens) > d->cfg.context)
+            return fail(SI_ERR_INVALID_ARGUMENT, "The GPU KV cache capacity of %lld tokens has been reached.",
+                        (long long)d->cfg.context);
+        for (int32_t i = 0; i < prompt_tokens; ++i)
+            if (prompt[i] < 0 || prompt[i] >= d->cfg.vocab)
+                return fail(SI_ERR_INVALID_ARGUMENT, "prompt token %d (%d) outside the vocabulary", i, prompt[i]);
+        if (k::tr_prefill_attention_supported(d->cfg.head_size)) {
+            DeviceScope scope(d->device);
+            return prefill(d, prompt, nullptr, prompt_tokens, next_token);
+        }
+    }
+    // Head sizes the fused prefill attention does not cover: the decode
+    // program once per prompt token.
+    std::vector<int32_t> history(static_cast<size_t>(prompt_tokens));
+    if (si_status st = si_decoder_generate(d, prompt, prompt_tokens, 0, history.data())) return st;
+    *next_token = history.back();
+    return SI_OK;
+}
+
+si_status si_decoder_prefill_embeddings(si_decoder *d, const float *embeddings, int32_t rows, int32_t *next_token) {
+    if (!d || !embeddings || !next_token) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    if (rows <= 0) return fail(SI_ERR_INVALID_ARGUMENT, "rows must be positive");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (d->position + int64_t(rows) > d->cfg.context)
+        return fail(SI_ERR_INVALID_ARGUMENT, "The GPU KV cache capacity of %lld tokens has been reached.",
+                    (long long)d->cfg.context);
+    if (!k::tr_prefill_attention_supported(d->cfg.head_size))
+        return fail(SI_ERR_UNSUPPORTED, "prefill attention supports head sizes 64, 128, 192 and 256");
+    DeviceScope scope(d->device);
+    return prefill(d, nullptr, embeddings, rows, next_token);
 }
 
 si_status si_decoder_reset(si_decoder *d) {

@@ -94,16 +94,50 @@ __device__ __forceinline__ float h16(uint32_t bits) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xffffu)));
 }
 
-// 64 consecutive weights of one row, columns k0 .. k0+63 (k0 % 64 == 0).
+// 64 consecutive weights of one row, columns k0 .. k0+63 (k0 % 64 == 0), in
+// two steps so that the producer issues the next stage's loads before it
+// decodes this one: fetch_weights64 loads the raw bytes into registers,
+// decode_weights64 turns them into FP32 values.
 template <int FMT>
-__device__ __forceinline__ void load_weights64(const uint8_t *row, int k0, float (&w)[64]) {
+struct RawWeights {
+    uint4 v[FMT == SI_TYPE_Q4_K ? 3 : FMT == SI_TYPE_Q8_0 ? 5 : FMT == SI_TYPE_F16 ? 8 : 16];
+    int j;  // Q4_K: 64-column group within the super-block
+};
+
+template <int FMT>
+__device__ __forceinline__ void fetch_weights64(const uint8_t *row, int k0, RawWeights<FMT> &r) {
     if constexpr (FMT == SI_TYPE_Q4_K) {
         const uint8_t *sb = row + (k0 >> 8) * 144;
-        const int j = (k0 >> 6) & 3;
-        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(sb));
-        const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(sb + 16 + 32 * j));
-        const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(sb + 32 + 32 * j));
-        const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        r.j = (k0 >> 6) & 3;
+        r.v[0] = __ldg(reinterpret_cast<const uint4 *>(sb));
+        r.v[1] = __ldg(reinterpret_cast<const uint4 *>(sb + 16 + 32 * r.j));
+        r.v[2] = __ldg(reinterpret_cast<const uint4 *>(sb + 32 + 32 * r.j));
+    } else if constexpr (FMT == SI_TYPE_Q8_0) {
+        const uint32_t *u = reinterpret_cast<const uint32_t *>(row + (k0 >> 5) * 34);  // 68 bytes, 4-byte aligned
+#pragma unroll
+        for (int i = 0; i < 5; ++i) {
+            r.v[i].x = __ldg(u + 4 * i);
+            r.v[i].y = i < 4 ? __ldg(u + 4 * i + 1) : 0u;
+            r.v[i].z = i < 4 ? __ldg(u + 4 * i + 2) : 0u;
+            r.v[i].w = i < 4 ? __ldg(u + 4 * i + 3) : 0u;
+        }
+    } else if constexpr (FMT == SI_TYPE_F16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0) * 2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r.v[i] = __ldg(p + i);
+    } else {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0) * 4);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r.v[i] = __ldg(p + i);
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void decode_weights64(const RawWeights<FMT> &r, float (&w)[64]) {
+    if constexpr (FMT == SI_TYPE_Q4_K) {
+        const uint4 h = r.v[0];
+        const uint32_t q[8] = {r.v[1].x, r.v[1].y, r.v[1].z, r.v[1].w, r.v[2].x, r.v[2].y, r.v[2].z, r.v[2].w};
+        const int j = r.j;
         const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
         const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
         const uint32_t mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
@@ -121,11 +155,12 @@ __device__ __forceinline__ void load_weights64(const uint8_t *row, int k0, float
                 w[32 + 4 * i + b] = a1 * float(byte >> 4) - c1;
             }
     } else if constexpr (FMT == SI_TYPE_Q8_0) {
-        const uint8_t *blk = row + (k0 >> 5) * 34;  // two blocks, 68 bytes, 4-byte aligned
-        const uint32_t *u = reinterpret_cast<const uint32_t *>(blk);
         uint32_t wv[17];
 #pragma unroll
-        for (int i = 0; i < 17; ++i) wv[i] = __ldg(u + i);
+        for (int i = 0; i < 4; ++i) {
+            wv[4 * i] = r.v[i].x, wv[4 * i + 1] = r.v[i].y, wv[4 * i + 2] = r.v[i].z, wv[4 * i + 3] = r.v[i].w;
+        }
+        wv[16] = r.v[4].x;
         const float d0 = h16(wv[0]), d1 = h16(wv[8] >> 16);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -134,11 +169,9 @@ __device__ __forceinline__ void load_weights64(const uint8_t *row, int k0, float
             w[32 + e] = d1 * float(int8_t((wv[b1 >> 2] >> (8 * (b1 & 3))) & 0xffu));
         }
     } else if constexpr (FMT == SI_TYPE_F16) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0) * 2);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint4 v = __ldg(p + i);
-            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t vv[4] = {r.v[i].x, r.v[i].y, r.v[i].z, r.v[i].w};
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 w[8 * i + 2 * t] = h16(vv[t]);
@@ -146,11 +179,10 @@ __device__ __forceinline__ void load_weights64(const uint8_t *row, int k0, float
             }
         }
     } else {
-        const float4 *p = reinterpret_cast<const float4 *>(row + size_t(k0) * 4);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float4 v = __ldg(p + i);
-            w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+            w[4 * i] = __uint_as_float(r.v[i].x), w[4 * i + 1] = __uint_as_float(r.v[i].y);
+            w[4 * i + 2] = __uint_as_float(r.v[i].z), w[4 * i + 3] = __uint_as_float(r.v[i].w);
         }
     }
 }
@@ -162,9 +194,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 struct GemmParams {
     const uint8_t *w;
-    float *y;
+    float *y;            // splits == 1: Y; otherwise the partial sums [splits][m][n]
     uint64_t row_bytes;
     int m, n, k;
+    int splits;          // K split over gridDim.z CTAs
 };
 
 template <int FMT>
@@ -181,7 +214,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kBM, t0 = blockIdx.y * kBN;
-    const int iters = p.k / kBK;
+    // K stages [it0, it0 + iters) of this CTA's split
+    const int total_iters = p.k / kBK;
+    const int it0 = int(int64_t(total_iters) * blockIdx.z / p.splits);
+    const int iters = int(int64_t(total_iters) * (blockIdx.z + 1) / p.splits) - it0;
+    float *const y = p.y + size_t(blockIdx.z) * size_t(p.m) * size_t(p.n);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -209,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
                 uint8_t *st = smem + s * kStageBytes;
                 mbar_arrive_expect_tx(&full[s], 2 * kBTile);
-                tma_load_2d(st + 2 * kATile, &map_hi, it * kBK, t0, &full[s]);
-                tma_load_2d(st + 2 * kATile + kBTile, &map_lo, it * kBK, t0, &full[s]);
+                tma_load_2d(st + 2 * kATile, &map_hi, (it0 + it) * kBK, t0, &full[s]);
+                tma_load_2d(st + 2 * kATile + kBTile, &map_lo, (it0 + it) * kBK, t0, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -239,15 +276,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = threadIdx.x - 64;  // weight row within the tile, 0..127
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
+        RawWeights<FMT> raw, next;
+        if (valid_row && iters > 0) fetch_weights64<FMT>(wrow, it0 * kBK, raw);
         for (int it = 0; it < iters; ++it) {
             const int s = it % kStages;
+            // the next stage's bytes are in flight while this one is decoded
+            if (valid_row && it + 1 < iters) fetch_weights64<FMT>(wrow, (it0 + it + 1) * kBK, next);
             float w[64];
             if (valid_row) {
-                load_weights64<FMT>(wrow, it * kBK, w);
+                decode_weights64<FMT>(raw, w);
             } else {
 #pragma unroll
                 for (int i = 0; i < 64; ++i) w[i] = 0.0f;
             }
+            raw = next;
             if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
             uint8_t *st = smem + s * kStageBytes;
             uint8_t *hi_row = st + (r >> 3) * 1024 + (r & 7) * 128;
@@ -283,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int t = t0 + c0 + j;
-                    if (t < p.m) p.y[size_t(t) * p.n + row] = __uint_as_float(v[j]);
+                    if (t < p.m) y[size_t(t) * p.n + row] = __uint_as_float(v[j]);
                 }
             }
         }
@@ -306,6 +348,27 @@ __global__ void split_bf16_kernel(const float4 *__restrict__ x, uint2 *__restric
         const uint32_t l23 = pack_bf16(v.z - __uint_as_float(h23 << 16), v.w - __uint_as_float(h23 & 0xffff0000u));
         hi[i] = make_uint2(h01, h23);
         lo[i] = make_uint2(l01, l23);
+    }
+}
+
+// Y = sum of the K-split partial sums, in split order (deterministic).
+// vec: count % 4 == 0 and y 16-byte aligned (float4 accesses), else scalar.
+__global__ void reduce_splits_kernel(const float *__restrict__ part, float *__restrict__ y, int64_t count, int splits,
+                                     bool vec) {
+    const int64_t n4 = vec ? count / 4 : 0;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        float4 acc = reinterpret_cast<const float4 *>(part)[i];
+        for (int s = 1; s < splits; ++s) {
+            const float4 v = reinterpret_cast<const float4 *>(part + size_t(s) * count)[i];
+            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        }
+        reinterpret_cast<float4 *>(y)[i] = acc;
+    }
+    for (int64_t i = n4 * 4 + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        float acc = part[i];
+        for (int s = 1; s < splits; ++s) acc += part[size_t(s) * count + i];
+        y[i] = acc;
     }
 }
 
@@ -349,16 +412,39 @@ bool tensor_core_shape(uint32_t wtype, int64_t m, int64_t n, int64_t k) {
 
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
+// K splits for an m x n output: one CTA per SM at most per wave (the
+// two-stage ring takes 193 KB of shared memory), so pick the split that
+// minimises waves x (stages per CTA + a fixed cost of about four stages
+// for the TMEM drain and pipeline fill), keeping at least two stages per CTA.
+int gemm_splits(int64_t m, int64_t n, int64_t k) {
+    static const int sms = [] {
+        int dev = 0, v = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v;
+    }();
+    const int64_t tiles = ((n + kBM - 1) / kBM) * ((m + kBN - 1) / kBN);
+    const int64_t iters = k / kBK;
+    int best = 1;
+    double best_cost = 1e30;
+    for (int s = 1; s <= 16 && iters / s >= 2; ++s) {
+        const int64_t waves = (tiles * s + sms - 1) / sms;
+        const double cost = double(waves) * (double(iters) / s + 4.0);
+        if (cost < best_cost - 1e-9) best_cost = cost, best = s;
+    }
+    return best;
+}
+
 template <int FMT>
-si_status launch_gemm(const void *w, float *y, uint64_t rb, int m, int n, int k, const CUtensorMap &hi,
+si_status launch_gemm(const void *w, float *y, uint64_t rb, int m, int n, int k, int splits, const CUtensorMap &hi,
                       const CUtensorMap &lo, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(gemm_tcgen05_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem));
         attr = true;
     }
-    GemmParams p{static_cast<const uint8_t *>(w), y, rb, m, n, k};
-    const dim3 grid(unsigned((n + kBM - 1) / kBM), unsigned((m + kBN - 1) / kBN));
+    GemmParams p{static_cast<const uint8_t *>(w), y, rb, m, n, k, splits};
+    const dim3 grid(unsigned((n + kBM - 1) / kBM), unsigned((m + kBN - 1) / kBN), unsigned(splits));
     gemm_tcgen05_kernel<FMT><<<grid, kThreads, kGemmSmem, st>>>(hi, lo, p);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SI_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
@@ -372,7 +458,11 @@ namespace si::kernels {
 using namespace si::dev;
 
 si_status gemm_workspace_bytes(uint32_t wtype, int64_t m, int64_t n, int64_t k, uint64_t *bytes) {
-    *bytes = tensor_core_shape(wtype, m, n, k) ? 2 * align256(uint64_t(m) * uint64_t(k) * 2) : 0;
+    *bytes = 0;
+    if (!tensor_core_shape(wtype, m, n, k)) return SI_OK;
+    const int splits = gemm_splits(m, n, k);
+    *bytes = 2 * align256(uint64_t(m) * uint64_t(k) * 2) +
+             (splits > 1 ? align256(uint64_t(splits) * uint64_t(m) * uint64_t(n) * 4) : 0);
     return SI_OK;
 }
 
@@ -381,8 +471,6 @@ si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64
     auto st = static_cast<cudaStream_t>(stream);
     uint64_t need = 0;
     gemm_workspace_bytes(wtype, m, n, k, &need);
-    const uint64_t rb_check = wtype == SI_TYPE_Q4_K ? 144 * (k / 256) : 0;
-    (void)rb_check;
     if (!need || reinterpret_cast<uintptr_t>(w) % 16 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0)
         return shared_weight_matvec(wtype, w, x, nullptr, y, m, n, k, stream);
     uint64_t rb;
@@ -401,12 +489,23 @@ si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64
     CUtensorMap map_hi, map_lo;
     if (si_status s = make_x_map(&map_hi, hi, int(m), int(k))) return s;
     if (si_status s = make_x_map(&map_lo, lo, int(m), int(k))) return s;
+    const int splits = gemm_splits(m, n, k);
+    float *out = splits > 1 ? reinterpret_cast<float *>(lo + align256(uint64_t(m) * uint64_t(k) * 2)) : y;
+    si_status ls;
     switch (wtype) {
-    case SI_TYPE_Q4_K: return launch_gemm<SI_TYPE_Q4_K>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
-    case SI_TYPE_Q8_0: return launch_gemm<SI_TYPE_Q8_0>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
-    case SI_TYPE_F16: return launch_gemm<SI_TYPE_F16>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
-    default: return launch_gemm<SI_TYPE_F32>(w, y, rb, int(m), int(n), int(k), map_hi, map_lo, st);
+    case SI_TYPE_Q4_K: ls = launch_gemm<SI_TYPE_Q4_K>(w, out, rb, int(m), int(n), int(k), splits, map_hi, map_lo, st); break;
+    case SI_TYPE_Q8_0: ls = launch_gemm<SI_TYPE_Q8_0>(w, out, rb, int(m), int(n), int(k), splits, map_hi, map_lo, st); break;
+    case SI_TYPE_F16: ls = launch_gemm<SI_TYPE_F16>(w, out, rb, int(m), int(n), int(k), splits, map_hi, map_lo, st); break;
+    default: ls = launch_gemm<SI_TYPE_F32>(w, out, rb, int(m), int(n), int(k), splits, map_hi, map_lo, st); break;
     }
+    if (ls != SI_OK || splits == 1) return ls;
+    const int64_t count = m * n;
+    const int rblocks = int(std::min<int64_t>((count / 4 + 255) / 256 + 1, 148 * 8));
+    const bool vec = count % 4 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+    reduce_splits_kernel<<<rblocks, 256, 0, st>>>(out, y, count, splits, vec);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "split reduction launch failed: %s", cudaGetErrorString(e));
+    return SI_OK;
 }
 
 si_status take_error_gemm(int device, uint32_t *code) {

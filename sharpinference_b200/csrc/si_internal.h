@@ -105,6 +105,9 @@ struct DecodeFeed {
 };
 si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
                         void *stream);
+// core.gather-row for `count` indices at once (rows of a prefill chunk).
+si_status tr_gather_rows_quant(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *indices,
+                               int64_t count, float *out, void *stream);
 si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
                                     int64_t batch, int64_t width, void *stream);
 si_status tr_copy_rows(const float *in, float *out, int64_t count, void *stream);
@@ -129,6 +132,13 @@ si_status tr_causal_softmax(const float *scores, const int32_t *position, const 
 si_status tr_gqa_values(const float *probs, const float *vc, const int32_t *position, const int32_t *control,
                         float *out, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
                         void *stream);
+// batch-gqa-scores -> batch-causal-softmax -> batch-gqa-values fused for
+// the rows [start, start + count) of a prefill chunk (head sizes for which
+// tr_prefill_attention_supported is true).
+bool tr_prefill_attention_supported(int head_size);
+si_status tr_prefill_attention(const float *query, const float *kc, const float *vc, int32_t start, int32_t count,
+                               float *out, int query_heads, int kv_heads, int head_size, int64_t context,
+                               void *stream);
 si_status tr_argmax(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, void *stream);
 si_status tr_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width,
                          void *stream);

@@ -127,6 +127,21 @@ __global__ void gather_row_kernel(uint32_t type, const uint8_t *table, int64_t r
         out[c] = ok ? row_element(type, row, c) : __int_as_float(0x7fc00000);
 }
 
+// core.gather-row over a list of indices (the prompt's rows of a prefill
+// chunk): out[r] = table[indices[r]], a NaN row for an invalid index.
+__global__ void gather_rows_quant_kernel(uint32_t type, const uint8_t *table, int64_t rows, int64_t cols,
+                                         uint64_t row_bytes, const int32_t *indices, int64_t count, float *out) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t total = count * cols;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = e / cols, c = e - r * cols;
+        const int32_t t = indices[r];
+        out[e] = (t >= 0 && t < rows) ? row_element(type, table + uint64_t(t) * row_bytes, c)
+                                      : __int_as_float(0x7fc00000);
+    }
+}
+
 // transformer.embedding-gather-batch: FP16 table rows by index; an index
 // outside the table reads 0, as an out-of-range raw-buffer load does under
 // Direct3D 12 (GpuTransformerInstructionCollection.cs:184-219).
@@ -539,6 +554,188 @@ __global__ void gqa_values_kernel(const float *probs, const float *value_cache, 
     }
 }
 
+// ---- prefill attention ---------------------------------------------------------
+// batch-gqa-scores -> batch-causal-softmax -> batch-gqa-values of a prefill
+// chunk in one pass, without the [batch, heads, context] score and
+// probability buffers: row b (position start + b, b < count) of query head h
+// attends cache tokens 0..start + b of key/value head h / group with an
+// online softmax (running maximum and denominator per row, the accumulator
+// rescaled when the maximum grows). One CTA = kPfRows query rows of one
+// head; key/value tiles of kPfKeys tokens are double-buffered in shared
+// memory with cp.async. 256 threads as 16 x 16: thread (ty, tx) scores rows
+// ty + 16 i against keys tx + 16 j and accumulates rows ty + 16 i, columns
+// 4 tx + 64 c of the output.
+constexpr int kPfRows = 64;
+constexpr int kPfKeys = 32;
+constexpr int kPfThreads = 256;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    const uint32_t dst = uint32_t(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int HS>
+__global__ void __launch_bounds__(kPfThreads, HS <= 128 ? 2 : 1)
+prefill_attention_kernel(const float *__restrict__ query, const float *__restrict__ key_cache,
+                         const float *__restrict__ value_cache, int32_t start, int32_t count, float *__restrict__ out,
+                         int query_heads, int group, int kv_heads, float scale) {
+    constexpr int QS = HS + 4;       // padded row stride of the query and key tiles
+    constexpr int PS = kPfKeys + 4;  // padded row stride of the probability tile
+    constexpr int C4 = HS / 64;      // float4 output columns per thread
+    constexpr int JK = kPfKeys / 16; // keys per thread per tile
+    extern __shared__ __align__(16) float pf_smem[];
+    float *qs = pf_smem;                       // [kPfRows][QS]
+    float *ks = qs + kPfRows * QS;             // [2][kPfKeys][QS]
+    float *vs = ks + 2 * kPfKeys * QS;         // [2][kPfKeys][HS]
+    float *ps = vs + 2 * kPfKeys * HS;         // [kPfRows][PS]
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int head = blockIdx.x, kvh = head / group;
+    // heavier (later) row tiles first
+    const int row0 = (int(gridDim.y) - 1 - int(blockIdx.y)) * kPfRows;
+    const int last_row = min(row0 + kPfRows, count) - 1;
+    const int64_t qstride = int64_t(query_heads) * HS, kstride = int64_t(kv_heads) * HS;
+    const int nkeys = start + last_row + 1;
+    const int tiles = (nkeys + kPfKeys - 1) / kPfKeys;
+
+    auto load_tile = [&](int t, int buf) {
+        float *kd = ks + buf * kPfKeys * QS, *vd = vs + buf * kPfKeys * HS;
+        for (int e = tid; e < kPfKeys * (HS / 4); e += kPfThreads) {
+            const int key = e / (HS / 4), c = (e - key * (HS / 4)) * 4;
+            const int token = t * kPfKeys + key;
+            const bool valid = token < nkeys;
+            const int64_t off = valid ? int64_t(token) * kstride + int64_t(kvh) * HS + c : 0;
+            cp_async16(kd + key * QS + c, key_cache + off, valid);
+            cp_async16(vd + key * HS + c, value_cache + off, valid);
+        }
+        cp_async_commit();
+    };
+    load_tile(0, 0);
+    for (int e = tid; e < kPfRows * (HS / 4); e += kPfThreads) {
+        const int r = e / (HS / 4), c = (e - r * (HS / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row0 + r < count) v = *reinterpret_cast<const float4 *>(query + int64_t(row0 + r) * qstride +
+                                                                      int64_t(head) * HS + c);
+        *reinterpret_cast<float4 *>(qs + r * QS + c) = v;
+    }
+
+    float acc[4][C4 * 4];
+    float mrow[4], lrow[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        mrow[i] = -INFINITY;
+        lrow[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < C4 * 4; ++c) acc[i][c] = 0.0f;
+    }
+    for (int t = 0; t < tiles; ++t) {
+        const int buf = t & 1;
+        if (t + 1 < tiles) {
+            load_tile(t + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *kt = ks + buf * kPfKeys * QS, *vt = vs + buf * kPfKeys * HS;
+        float sc[4][JK];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < JK; ++j) sc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < HS; d += 4) {
+            float4 q[4], k[JK];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4 *>(qs + (ty + 16 * i) * QS + d);
+#pragma unroll
+            for (int j = 0; j < JK; ++j) k[j] = *reinterpret_cast<const float4 *>(kt + (tx + 16 * j) * QS + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < JK; ++j) {
+                    sc[i][j] = fmaf(q[i].x, k[j].x, sc[i][j]);
+                    sc[i][j] = fmaf(q[i].y, k[j].y, sc[i][j]);
+                    sc[i][j] = fmaf(q[i].z, k[j].z, sc[i][j]);
+                    sc[i][j] = fmaf(q[i].w, k[j].w, sc[i][j]);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = row0 + ty + 16 * i;
+            const int active = start + row;  // tokens 0..active
+            float tile_max = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < JK; ++j) {
+                const int token = t * kPfKeys + tx + 16 * j;
+                const bool valid = row < count && token <= active;
+                sc[i][j] = valid ? sc[i][j] * scale : -INFINITY;
+                tile_max = fmaxf(tile_max, sc[i][j]);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) tile_max = fmaxf(tile_max, __shfl_xor_sync(0xffffffffu, tile_max, o));
+            const float m_new = fmaxf(mrow[i], tile_max);
+            // all keys of this row masked so far: nothing to rescale or add
+            const float alpha = m_new == -INFINITY ? 1.0f : expf(mrow[i] - m_new);
+            mrow[i] = m_new;
+            lrow[i] *= alpha;
+#pragma unroll
+            for (int c = 0; c < C4 * 4; ++c) acc[i][c] *= alpha;
+#pragma unroll
+            for (int j = 0; j < JK; ++j) {
+                const float p = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - m_new);
+                lrow[i] += p;
+                ps[(ty + 16 * i) * PS + tx + 16 * j] = p;
+            }
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int key = 0; key < kPfKeys; key += 4) {
+            float4 p[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = *reinterpret_cast<const float4 *>(ps + (ty + 16 * i) * PS + key);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                for (int c = 0; c < C4; ++c) {
+                    const float4 v = *reinterpret_cast<const float4 *>(vt + (key + kk) * HS + 4 * tx + 64 * c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float pv = kk == 0 ? p[i].x : kk == 1 ? p[i].y : kk == 2 ? p[i].z : p[i].w;
+                        acc[i][4 * c + 0] = fmaf(pv, v.x, acc[i][4 * c + 0]);
+                        acc[i][4 * c + 1] = fmaf(pv, v.y, acc[i][4 * c + 1]);
+                        acc[i][4 * c + 2] = fmaf(pv, v.z, acc[i][4 * c + 2]);
+                        acc[i][4 * c + 3] = fmaf(pv, v.w, acc[i][4 * c + 3]);
+                    }
+                }
+            }
+        }
+        __syncthreads();  // the tile's buffers and the probabilities are rewritten next
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float l = lrow[i];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        const int row = row0 + ty + 16 * i;
+        if (row >= count) continue;
+        const float inv = 1.0f / l;
+        float *dst = out + int64_t(row) * qstride + int64_t(head) * HS;
+#pragma unroll
+        for (int c = 0; c < C4; ++c)
+            *reinterpret_cast<float4 *>(dst + 4 * tx + 64 * c) =
+                make_float4(acc[i][4 * c] * inv, acc[i][4 * c + 1] * inv, acc[i][4 * c + 2] * inv,
+                            acc[i][4 * c + 3] * inv);
+    }
+}
+
 // ---- argmax -----------------------------------------------------------------
 constexpr int kArgmaxCluster = 8;
 constexpr int kArgmaxThreads = 1024;
@@ -676,6 +873,14 @@ si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t 
                   static_cast<const uint8_t *>(table), rows, cols, row_bytes, index, out);
 }
 
+si_status tr_gather_rows_quant(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *indices,
+                               int64_t count, float *out, void *stream) {
+    uint64_t row_bytes = 0;
+    if (si_status st = byte_length(type, uint64_t(cols), &row_bytes)) return st;
+    return launch("core.gather-row", gather_rows_quant_kernel, dim3(elementwise_grid(count * cols, 256)), dim3(256), 0,
+                  stream, type, static_cast<const uint8_t *>(table), rows, cols, row_bytes, indices, count, out);
+}
+
 si_status tr_embedding_gather_batch(const uint16_t *table, int64_t rows, const int32_t *indices, float *out,
                                     int64_t batch, int64_t width, void *stream) {
     const int64_t count = batch * width;
@@ -767,6 +972,50 @@ si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *posi
     return launch("transformer.gqa-scores", gqa_scores_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
                   stream, query, kc, position, control, scores, batch, query_heads, query_heads / kv_heads, kv_heads,
                   head_size, context, 1.0f / sqrtf(float(head_size)));
+}
+
+namespace {
+template <int HS>
+si_status launch_prefill_attention(const float *query, const float *kc, const float *vc, int32_t start, int32_t count,
+                                   float *out, int query_heads, int kv_heads, void *stream) {
+    constexpr size_t smem = size_t(kPfRows * (HS + 4) + 2 * kPfKeys * (HS + 4) + 2 * kPfKeys * HS +
+                                   kPfRows * (kPfKeys + 4)) * sizeof(float);
+    static bool raised = false;
+    if (!raised) {
+        cudaFuncSetAttribute(prefill_attention_kernel<HS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        raised = true;
+    }
+    const dim3 grid(unsigned(query_heads), unsigned((count + kPfRows - 1) / kPfRows));
+    return launch("transformer.batch-grouped-query-attention", prefill_attention_kernel<HS>, grid, dim3(kPfThreads),
+                  smem, stream, query, kc, vc, start, count, out, query_heads, query_heads / kv_heads, kv_heads,
+                  1.0f / sqrtf(float(HS)));
+}
+}  // namespace
+
+bool tr_prefill_attention_supported(int head_size) {
+    return head_size == 64 || head_size == 128 || head_size == 192 || head_size == 256;
+}
+
+si_status tr_prefill_attention(const float *query, const float *kc, const float *vc, int32_t start, int32_t count,
+                               float *out, int query_heads, int kv_heads, int head_size, int64_t context,
+                               void *stream) {
+    if (count <= 0) return SI_OK;
+    if ((int64_t(count) + kPfRows - 1) / kPfRows > 65535)
+        return fail(SI_ERR_UNSUPPORTED, "prefill attention takes at most %d rows per call", 65535 * kPfRows);
+    if (start < 0 || int64_t(start) + count > context)
+        return fail(SI_ERR_INVALID_ARGUMENT, "prefill rows [%d, %d) outside the context of %lld", start,
+                    start + count, (long long)context);
+    for (const void *p : {static_cast<const void *>(query), static_cast<const void *>(kc),
+                          static_cast<const void *>(vc), static_cast<const void *>(out)})
+        if (reinterpret_cast<uintptr_t>(p) % 16)
+            return fail(SI_ERR_INVALID_ARGUMENT, "prefill attention buffers must be 16-byte aligned");
+    switch (head_size) {
+    case 64: return launch_prefill_attention<64>(query, kc, vc, start, count, out, query_heads, kv_heads, stream);
+    case 128: return launch_prefill_attention<128>(query, kc, vc, start, count, out, query_heads, kv_heads, stream);
+    case 192: return launch_prefill_attention<192>(query, kc, vc, start, count, out, query_heads, kv_heads, stream);
+    case 256: return launch_prefill_attention<256>(query, kc, vc, start, count, out, query_heads, kv_heads, stream);
+    default: return fail(SI_ERR_UNSUPPORTED, "prefill attention supports head sizes 64, 128, 192 and 256");
+    }
 }
 
 si_status tr_causal_softmax(const float *scores, const int32_t *position, const int32_t *control, float *probs,

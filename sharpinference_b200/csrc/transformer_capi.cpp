@@ -276,6 +276,24 @@ si_status si_batch_gqa_values(const float *probabilities, const float *value_cac
                                   head_size, context, stream);
 }
 
+si_status si_batch_grouped_query_attention(const float *query, const float *key_cache, const float *value_cache,
+                                           int32_t start, int32_t count, float *output, int32_t query_heads,
+                                           int32_t kv_heads, int32_t head_size, int64_t context, void *stream) {
+    const char *op = "transformer.batch-grouped-query-attention";
+    if (count <= 0) return adapt(op, "count must be positive.");
+    if (si_status st = attention_shape(op, query_heads, kv_heads, head_size, context)) return st;
+    if (!kernels::tr_prefill_attention_supported(head_size))
+        return fail(SI_ERR_UNSUPPORTED, "%s supports head sizes 64, 128, 192 and 256", op);
+    const uint64_t width = uint64_t(query_heads) * head_size;
+    if (si_status st = ports({{"query", query, uint64_t(count) * width * F},
+                              {"key_cache", key_cache, uint64_t(context) * kv_heads * head_size * F},
+                              {"value_cache", value_cache, uint64_t(context) * kv_heads * head_size * F},
+                              {"output", output, uint64_t(count) * width * F}}))
+        return st;
+    return kernels::tr_prefill_attention(query, key_cache, value_cache, start, count, output, query_heads, kv_heads,
+                                         head_size, context, stream);
+}
+
 si_status si_batch_select_last(const float *input, const int32_t *control, float *output, int64_t batch,
                                int64_t width, void *stream) {
     if (batch <= 0 || width <= 0) return adapt("transformer.batch-select-last", "Expected input [B,H] and output [H].");

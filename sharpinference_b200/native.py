@@ -143,6 +143,7 @@ SIGNATURES = {
     "si_batch_gqa_scores": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp],
     "si_batch_causal_softmax": [_vp, _vp, _vp, _i64, _i32, _i64, _vp],
     "si_batch_gqa_values": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _vp],
+    "si_batch_grouped_query_attention": [_vp, _vp, _vp, _i32, _i32, _vp, _i32, _i32, _i32, _i64, _vp],
     "si_batch_select_last": [_vp, _vp, _vp, _i64, _i64, _vp],
     "si_batch_gather_rows": [_vp, _i64, _vp, _vp, _i64, _i64, _vp],
     # decoder session
@@ -154,6 +155,8 @@ SIGNATURES = {
     "si_decoder_stream": [_vp, C.POINTER(_vp)],
     "si_decoder_forward_token": [_vp, C.c_int32, C.POINTER(C.c_int32)],
     "si_decoder_generate": [_vp, _vp, C.c_int32, C.c_int32, _vp],
+    "si_decoder_prefill": [_vp, _vp, C.c_int32, _vp],
+    "si_decoder_prefill_embeddings": [_vp, _vp, C.c_int32, _vp],
     "si_decoder_reset": [_vp],
     "si_decoder_position": [_vp, C.POINTER(C.c_int32)],
     # GGUF files
@@ -541,6 +544,24 @@ class Decoder:
         out = np.empty(p.size + steps, dtype=np.int32)
         call("si_decoder_generate", self.handle, p.ctypes.data, p.size, steps, out.ctypes.data)
         return out
+
+    def prefill(self, prompt) -> int:
+        """Batched prompt prefill; returns the prediction after the last token."""
+        np = _np()
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        v = C.c_int32()
+        call("si_decoder_prefill", self.handle, p.ctypes.data, p.size, C.byref(v))
+        return v.value
+
+    def prefill_embeddings(self, rows) -> int:
+        """Prefill from ready FP32 embedding rows [n, hidden]."""
+        np = _np()
+        r = np.ascontiguousarray(rows, dtype=np.float32)
+        if r.ndim != 2 or r.shape[1] != self.cfg.hidden:
+            raise ArgumentError(f"embedding rows must be [n, {self.cfg.hidden}], got {r.shape}")
+        v = C.c_int32()
+        call("si_decoder_prefill_embeddings", self.handle, r.ctypes.data, r.shape[0], C.byref(v))
+        return v.value
 
     def reset(self) -> None:
         call("si_decoder_reset", self.handle)

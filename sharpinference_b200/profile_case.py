@@ -8,6 +8,9 @@ launch with `-s 1 -c 1`): synthetic seeded weights and inputs, device-resident.
   python -m sharpinference_b200.profile_case decode mini 64 2
       (Phi-4-mini random-init decoder: 64 prompt steps, then 2 more decode
       steps; each step is one graph of 292 kernel launches)
+  python -m sharpinference_b200.profile_case prefill mini 512
+      (Phi-4-mini random-init decoder: one batched prefill of 512 prompt
+      tokens, two chunks of 256 rows)
   python -m sharpinference_b200.profile_case decode-trace mini 512
       (the persistent decode step: one step at position 512 with its
       per-phase trace, averaged per phase kind over the layers, CTA 0)
@@ -33,6 +36,16 @@ def decode(preset: str, prompt_tokens: int, steps: int) -> None:
         toks = dec.generate(prompt, steps)
         print(f"decode {preset} prompt={prompt_tokens} steps={steps}: last tokens {toks[-3:].tolist()} "
               f"device_error={native.device_error_take(0)}")
+
+
+def prefill(preset: str, prompt_tokens: int) -> None:
+    from . import phi4
+    cfg = dict(phi4.PHI4_MINI if preset == "mini" else phi4.PHI4_14B)
+    cfg["context"] = prompt_tokens + 1
+    with native.Decoder(cfg) as dec:
+        phi4.load_synthetic(dec, cfg, seed=7)
+        nxt = dec.prefill(phi4.random_prompt(7, prompt_tokens, cfg["vocab"]))
+        print(f"prefill {preset} prompt={prompt_tokens}: next token {nxt} device_error={native.device_error_take(0)}")
 
 
 def decode_trace(preset: str, position: int) -> None:
@@ -69,6 +82,9 @@ def decode_trace(preset: str, position: int) -> None:
 def main(argv: list[str]) -> None:
     if argv[0] == "decode":
         decode(argv[1], int(argv[2]), int(argv[3]))
+        return
+    if argv[0] == "prefill":
+        prefill(argv[1], int(argv[2]))
         return
     if argv[0] == "decode-trace":
         decode_trace(argv[1], int(argv[2]))
