@@ -503,6 +503,9 @@ def run_ours(args) -> None:
             g.close()
             for Wc in copies + [Xb, Yb, Cb]:
                 Wc.free()
+    gemm = None
+    if world == 1 and not args.no_gemm:
+        gemm = gemm_block(native, ctx, timed)
     decode = None
     if world == 1 and not args.no_decode:
         decode = decode_block(native, torch, local, peak, not args.no_cpu_baseline)
@@ -539,6 +542,7 @@ def run_ours(args) -> None:
             "q8_0_gemv": q8 and {"workload": "Q8_0 GEMV, config 1 and the Phi-4-14B decode shapes of config 5 "
                                              "(1 GPU; back-to-back launches cycling through weight copies > L2)",
                                  "per_shape": q8},
+            "prefill_gemm": gemm,
             "decode": decode,
             "clocks": clocks,
             "device_error_word": err,
@@ -557,6 +561,60 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+        except Exception:
+            pass
+    return 1590.0, "fallback 1.59 PFLOP/s"
+
+
+def gemm_block(native, ctx, timed) -> dict:
+    """Config 3: Y = X W^T with X [M, 3072 or 8192] fp32 N(0,1), M = 512 and
+    2048, over the five config-2 Q4_K weights (seeds 0-4), through
+    core.matrix-multiply (si_ctx_matrix_multiply: X split into BF16 hi/lo,
+    then the tcgen05 GEMM with Q4_K tiles dequantised into shared memory;
+    three BF16 products per FP32 product). Weight copies rotate through
+    > L2 per shape; each call's time includes the X split."""
+    import numpy as np
+    peak, src = bf16_peak()
+    out = {"workload": "config3: prefill GEMM Y = X W^T over the config-2 Q4_K shapes, M in {512, 2048}",
+           "tensor_products_per_product": 3, "peak_tflops": peak, "peak_source": src, "per_m": {}}
+    for m in (512, 2048):
+        rows, flops_total, ms_total = {}, 0.0, 0.0
+        for name, n, k, seed in SHAPES:
+            blob = native.synth_weights(WTYPE, seed, n, k, 0.02)
+            copies = []
+            for _ in range(min(8, max(1, -(-L2_ROTATE_BYTES // blob.nbytes)))):
+                Wc = ctx.buffer(blob.nbytes)
+                Wc.upload(blob)
+                copies.append(Wc)
+            x = native.synth_normal(3000 + seed, m * k, 1.0)
+            X, Y = ctx.buffer(x.nbytes), ctx.buffer(4 * m * n)
+            X.upload(x)
+            ctx.matrix_multiply(WTYPE, X, copies[0], Y, m, n, k)  # warm-up (workspace, attributes)
+            reps = max(3, len(copies))
+            it = iter(range(1 << 30))
+            ms = timed(lambda: ctx.matrix_multiply(WTYPE, X, copies[next(it) % len(copies)], Y, m, n, k), reps) / reps
+            flops = 2.0 * m * n * k
+            tf = flops / (ms * 1e-3) / 1e12
+            rows[name] = {"n": n, "k": k, "us": round(ms * 1e3, 1), "TFLOP/s": round(tf, 1),
+                          "tensor_frac": round(3 * tf / peak, 3)}
+            flops_total += flops
+            ms_total += ms
+            for b in copies + [X, Y]:
+                b.free()
+        tf = flops_total / (ms_total * 1e-3) / 1e12
+        out["per_m"][str(m)] = {"TFLOP/s": round(tf, 1), "tensor_frac": round(3 * tf / peak, 3),
+                                "ms_all_shapes": round(ms_total, 3), "per_shape": rows}
+    out["roofline"] = {"bound": "tensor", "achieved": out["per_m"]["2048"]["TFLOP/s"], "unit": "TFLOP/s",
+                       "peak": peak, "frac": round(3 * out["per_m"]["2048"]["TFLOP/s"] / peak, 4),
+                       "note": "achieved = algorithmic 2MNK/t; frac counts the three BF16 tensor products"}
+    return out
 
 
 def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> dict:
@@ -660,6 +718,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-q8", action="store_true", help="skip the secondary Q8_0 GEMV measurements")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-4 Phi-4-mini decoder measurement")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 prefill GEMM measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -396,6 +396,22 @@ typedef struct si_decoder_config {
 typedef struct si_decoder si_decoder;
 si_status si_decoder_create(int device, const si_decoder_config *config, si_decoder **out);
 si_status si_decoder_destroy(si_decoder *decoder);
+/* Row-sharded session on one rank of a peer group (config 5: Phi-4-14B
+ * weights row-sharded over 2/4/8 GPUs with the outputs all-gathered). Each
+ * projection slot (qkv, attn_output, ffn_up, ffn_down) holds only this
+ * rank's rows (si_rowshard_plan; upload those rows), and runs as
+ * si_rowshard_matvec_peer, whose kernel stores the rank's output rows into
+ * every rank's arena over NVLink; the vocabulary projection uses this
+ * rank's rows of token_embedding (uploaded whole: gather-row reads any
+ * row). Norms, rope, attention, swiglu, argmax and the KV cache are
+ * replicated, so every rank computes the same tokens. The group's arenas
+ * need si_decoder_arena_bytes(config) bytes; every rank must make the same
+ * session calls in the same order. Q4_K or Q8_0 weights; the persistent
+ * step and the batched prefill are not used (prefill runs the decode
+ * program per token). */
+si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *bytes);
+si_status si_decoder_create_sharded(int device, const si_decoder_config *config, si_peer_group *group,
+                                    si_decoder **out);
 /* Slots by the reference's names (Phi4D3D12TextSession.cs:391-425, 427-446):
  * token_embedding, output_norm, attn_norm_L, ffn_norm_L, qkv_weight_L,
  * attn_output_weight_L, ffn_up_weight_L, ffn_down_weight_L, rope_frequencies

@@ -56,6 +56,12 @@ struct si_decoder {
     // graph and are issued per token instead.
     k::DecodeStep *step = nullptr;
     bool direct = false;
+    // Row-sharded session (si_decoder_create_sharded): the peer group, this
+    // rank's arena (the five projection outputs live there, gathered by the
+    // peer GEMV) and the vocabulary projection's rows of token_embedding.
+    si_peer_group *group = nullptr;
+    uint8_t *arena = nullptr;
+    const void *w_vocab = nullptr;
     // Prompt prefill in chunks of up to kPrefillRows rows (buffers allocated
     // by the first prefill call): the chunk's activations, one (start,
     // count) control pair per chunk, the split-operand GEMM workspace.
@@ -127,6 +133,37 @@ si_status project(uint32_t type, const void *w, const float *x, float *y, int64_
     return k::matvec_dense(type, w, SI_TYPE_F32, x, SI_TYPE_F32, y, rows, cols, s);
 }
 
+// A projection of the session: the whole mat-vec, or in a row-sharded
+// session this rank's rows with the output stored into every rank's arena
+// (y lies in the arena; its offset is the same on every rank).
+si_status project_rows(si_decoder *d, uint32_t type, const void *w, const float *x, float *y, int64_t rows,
+                       int64_t cols) {
+    if (!d->group) return project(type, w, x, y, rows, cols, d->stream);
+    const uint64_t offset = uint64_t(reinterpret_cast<uint8_t *>(y) - d->arena);
+    return si_rowshard_matvec_peer(d->group, type, w, x, offset, rows, cols, d->stream);
+}
+
+// Arena layout of a row-sharded session: the qkv, attention-output,
+// gate_up, down and logits vectors, each 256-byte aligned. Consecutive
+// projections always use different regions, as the peer GEMV requires.
+struct ArenaLayout {
+    uint64_t qkv, out, up, down, logits, data_bytes;
+};
+
+ArenaLayout arena_layout(const si_decoder_config &c) {
+    const uint64_t H = uint64_t(c.hidden), QKV = H + 2 * uint64_t(c.kv_heads) * uint64_t(c.head_size);
+    auto al = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    ArenaLayout a{};
+    uint64_t o = 0;
+    a.qkv = o, o += al(QKV * 4);
+    a.out = o, o += al(H * 4);
+    a.up = o, o += al(2 * uint64_t(c.intermediate) * 4);
+    a.down = o, o += al(H * 4);
+    a.logits = o, o += al(uint64_t(c.vocab) * 4);
+    a.data_bytes = o;
+    return a;
+}
+
 // The decode program one instruction per launch (Phi4D3D12TextSession.cs:866-920).
 // Fusing rope-kv-write into the attention launch measured slower (1.69 vs
 // 1.59 ms per token): the one-wave rope kernel is another window in which
@@ -146,7 +183,7 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
                                       c.epsilon, s))
         return st;
     for (int l = 0; l < c.layers; ++l) {
-        if (si_status st = project(c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H, s)) return st;
+        if (si_status st = project_rows(d, c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
         if (si_status st = k::tr_rope_kv_write(d->qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
                                                d->value_cache[l], 1, H, KV, c.head_size, c.rotary_size, c.context,
                                                c.rope_scale, s))
@@ -154,19 +191,19 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
         if (si_status st = k::tr_attention_decode(d->query, d->key_cache[l], d->value_cache[l], position, d->attention,
                                                   c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
-        if (si_status st = project(c.weight_type, d->w_out[l], d->attention, d->projected, H, H, s)) return st;
+        if (si_status st = project_rows(d, c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
         if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = project(c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H, s)) return st;
+        if (si_status st = project_rows(d, c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
         if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, 1, F, s)) return st;
-        if (si_status st = project(c.weight_type, d->w_down[l], d->activated, d->down, H, F, s)) return st;
+        if (si_status st = project_rows(d, c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
         if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
                                           c.epsilon, s))
             return st;
     }
-    if (si_status st = project(c.embedding_type, d->embedding, d->normalized, d->logits, c.vocab, H, s)) return st;
+    if (si_status st = project_rows(d, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
     return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
 }
 
@@ -285,7 +322,7 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
     }
     if (!last) return SI_OK;
     if (si_status st = k::tr_select_last(P.normalized, control, d->normalized, rows, H, s)) return st;
-    if (si_status st = project(c.embedding_type, d->embedding, d->normalized, d->logits, c.vocab, H, s)) return st;
+    if (si_status st = project_rows(d, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
     return k::tr_argmax(d->logits, c.vocab, d->next_token, nullptr, s);
 }
 
@@ -358,7 +395,7 @@ si_status validate(const si_decoder_config *c) {
 
 si_status create_step(si_decoder *d);
 
-si_status create(int device, const si_decoder_config *c, si_decoder **out) {
+si_status create(int device, const si_decoder_config *c, si_peer_group *group, si_decoder **out) {
     auto *d = new si_decoder();
     d->device = device;
     d->cfg = *c;
@@ -373,9 +410,28 @@ si_status create(int device, const si_decoder_config *c, si_decoder **out) {
     si::byte_length(c->weight_type, uint64_t(H), &rb_h);
     si::byte_length(c->weight_type, uint64_t(F), &rb_f);
     si::byte_length(c->embedding_type, uint64_t(H), &rb_e);
+    int nranks = 1, rank = 0;
+    uint64_t data_bytes = 0;
+    if (group) {
+        d->group = group;
+        d->arena = si::peer_group_arena(group, &nranks, &rank, &data_bytes);
+    }
+    // Rows of a projection held by this rank (all of them unless sharded).
+    auto shard = [&](int64_t rows, int64_t *begin) {
+        int64_t b = 0, n = rows, per = rows;
+        if (group) si_rowshard_plan(rows, nranks, rank, &b, &n, &per);
+        if (begin) *begin = b;
+        return n;
+    };
     void *p = nullptr;
+    // The whole table on every rank: gather-row reads any token's row.
     if (si_status st = alloc_slot(d, "token_embedding", rb_e * uint64_t(c->vocab), &p)) return cleanup(st);
     d->embedding = p;
+    {
+        int64_t vocab_begin = 0;
+        shard(c->vocab, &vocab_begin);
+        d->w_vocab = static_cast<const uint8_t *>(p) + uint64_t(vocab_begin) * rb_e;
+    }
 
     float *f = nullptr;
     if (si_status st = alloc_typed(d, "output_norm", H * 4, &f)) return cleanup(st);
@@ -389,13 +445,17 @@ si_status create(int device, const si_decoder_config *c, si_decoder **out) {
         if (si_status st = alloc_typed(d, "ffn_norm_" + L, H * 4, &f)) return cleanup(st);
         if (si_status st = fill_ones(f, H)) return cleanup(st);
         d->ffn_norm.push_back(f);
-        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(QKV), &p)) return cleanup(st);
+        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(shard(QKV, nullptr)), &p))
+            return cleanup(st);
         d->w_qkv.push_back(p);
-        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(H), &p)) return cleanup(st);
+        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(shard(H, nullptr)), &p))
+            return cleanup(st);
         d->w_out.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(2 * F), &p)) return cleanup(st);
+        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(shard(2 * F, nullptr)), &p))
+            return cleanup(st);
         d->w_up.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(H), &p)) return cleanup(st);
+        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(shard(H, nullptr)), &p))
+            return cleanup(st);
         d->w_down.push_back(p);
         if (si_status st = alloc_typed(d, "key_cache_" + L, uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
         d->key_cache.push_back(f);
@@ -421,8 +481,25 @@ si_status create(int device, const si_decoder_config *c, si_decoder **out) {
                 {"projected", &d->projected, H},   {"gate_up", &d->gate_up, 2 * F},
                 {"activated", &d->activated, F},   {"down", &d->down, H},
                 {"logits", &d->logits, c->vocab}};
-    for (const A &a : acts)
-        if (si_status st = alloc_typed(d, a.name, uint64_t(a.n) * 4, a.dst)) return cleanup(st);
+    const ArenaLayout lay = arena_layout(*c);
+    for (const A &a : acts) {
+        // Row-sharded: the projection outputs are the arena's vectors.
+        const std::string name = a.name;
+        uint64_t off = UINT64_MAX;
+        if (group) {
+            if (name == "qkv") off = lay.qkv;
+            else if (name == "projected") off = lay.out;
+            else if (name == "gate_up") off = lay.up;
+            else if (name == "down") off = lay.down;
+            else if (name == "logits") off = lay.logits;
+        }
+        if (off != UINT64_MAX) {
+            *a.dst = reinterpret_cast<float *>(d->arena + off);
+            d->slots[name] = {d->arena + off, uint64_t(a.n) * 4};
+        } else if (si_status st = alloc_typed(d, a.name, uint64_t(a.n) * 4, a.dst)) {
+            return cleanup(st);
+        }
+    }
     if (si_status st = alloc_typed(d, "control", 8, &d->control)) return cleanup(st);
     if (si_status st = alloc_typed(d, "next_token", 4, &d->next_token)) return cleanup(st);
     if (si_status st = alloc_typed(d, "prompt", uint64_t(c->context) * 4, &d->prompt)) return cleanup(st);
@@ -434,7 +511,8 @@ si_status create(int device, const si_decoder_config *c, si_decoder **out) {
     d->pinned_feed = reinterpret_cast<k::DecodeFeed *>(reinterpret_cast<uint8_t *>(d->pinned) + 64);
     d->pinned_prompt = reinterpret_cast<int32_t *>(d->pinned_feed + 1);
     d->pinned_history = d->pinned_prompt + c->context;
-    if (si_status st = create_step(d)) return cleanup(st);
+    if (!group)
+        if (si_status st = create_step(d)) return cleanup(st);
     if (si_status st = cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return cleanup(st);
     *out = d;
     return SI_OK;
@@ -515,7 +593,47 @@ si_status si_decoder_create(int device, const si_decoder_config *config, si_deco
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, out);
+    return create(device, config, nullptr, out);
+}
+
+si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *bytes) {
+    if (!bytes) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    if (si_status st = validate(config)) return st;
+    *bytes = arena_layout(*config).data_bytes + 4096;
+    return SI_OK;
+}
+
+si_status si_decoder_create_sharded(int device, const si_decoder_config *config, si_peer_group *group,
+                                    si_decoder **out) {
+    if (!out || !group) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (si_status st = validate(config)) return st;
+    const si_decoder_config &c = *config;
+    for (uint32_t t : {c.weight_type, c.embedding_type})
+        if (t != SI_TYPE_Q4_K && t != SI_TYPE_Q8_0)
+            return fail(SI_ERR_UNSUPPORTED, "a row-sharded session takes Q4_K or Q8_0 weights");
+    int nranks = 1, rank = 0;
+    uint64_t data_bytes = 0;
+    si::peer_group_arena(group, &nranks, &rank, &data_bytes);
+    const ArenaLayout lay = arena_layout(c);
+    if (data_bytes < lay.data_bytes)
+        return fail(SI_ERR_INVALID_ARGUMENT, "the peer group's arenas hold %llu data bytes, the session needs %llu",
+                    (unsigned long long)data_bytes, (unsigned long long)lay.data_bytes);
+    const int64_t H = c.hidden, QKV = H + 2 * int64_t(c.kv_heads) * c.head_size;
+    for (int64_t rows : {QKV, H, 2 * int64_t(c.intermediate), int64_t(c.vocab)}) {
+        int64_t b, n, per;
+        if (si_status st = si_rowshard_plan(rows, nranks, rank, &b, &n, &per)) return st;
+        if (per * (nranks - 1) >= rows)
+            return fail(SI_ERR_UNSUPPORTED, "%lld rows leave a rank of %d without rows", (long long)rows, nranks);
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SI_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
+    DeviceScope scope(device);
+    return create(device, config, group, out);
 }
 
 si_status si_decoder_destroy(si_decoder *decoder) {
@@ -632,13 +750,13 @@ si_status si_decoder_prefill(si_decoder *d, const int32_t *prompt, int32_t promp
         for (int32_t i = 0; i < prompt_tokens; ++i)
             if (prompt[i] < 0 || prompt[i] >= d->cfg.vocab)
                 return fail(SI_ERR_INVALID_ARGUMENT, "prompt token %d (%d) outside the vocabulary", i, prompt[i]);
-        if (k::tr_prefill_attention_supported(d->cfg.head_size)) {
+        if (!d->group && k::tr_prefill_attention_supported(d->cfg.head_size)) {
             DeviceScope scope(d->device);
             return prefill(d, prompt, nullptr, prompt_tokens, next_token);
         }
     }
-    // Head sizes the fused prefill attention does not cover: the decode
-    // program once per prompt token.
+    // Head sizes the fused prefill attention does not cover, and row-sharded
+    // sessions: the decode program once per prompt token.
     std::vector<int32_t> history(static_cast<size_t>(prompt_tokens));
     if (si_status st = si_decoder_generate(d, prompt, prompt_tokens, 0, history.data())) return st;
     *next_token = history.back();
@@ -654,6 +772,7 @@ si_status si_decoder_prefill_embeddings(si_decoder *d, const float *embeddings, 
                     (long long)d->cfg.context);
     if (!k::tr_prefill_attention_supported(d->cfg.head_size))
         return fail(SI_ERR_UNSUPPORTED, "prefill attention supports head sizes 64, 128, 192 and 256");
+    if (d->group) return fail(SI_ERR_UNSUPPORTED, "embedding prefill is not available in a row-sharded session");
     DeviceScope scope(d->device);
     return prefill(d, nullptr, embeddings, rows, next_token);
 }

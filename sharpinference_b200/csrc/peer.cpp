@@ -118,6 +118,19 @@ si_status si_peer_group_create(int device, int nranks, int rank, const uint64_t 
     return SI_OK;
 }
 
+}  // extern "C"
+
+namespace si {
+uint8_t *peer_group_arena(si_peer_group *g, int *nranks, int *rank, uint64_t *data_bytes) {
+    *nranks = g->nranks;
+    *rank = g->rank;
+    *data_bytes = g->data_bytes;
+    return g->arenas[g->rank];
+}
+}  // namespace si
+
+extern "C" {
+
 si_status si_peer_group_destroy(si_peer_group *group) {
     delete group;
     return SI_OK;

@@ -51,6 +51,10 @@ bool ranges_overlap(const void *a, uint64_t an, const void *b, uint64_t bn);
 // Maps a cudaError_t onto si_status with the runtime's message.
 si_status cuda_error(int error, const char *what);
 
+// This rank's arena of a peer group (si_peer_group_create), the group's
+// size and rank, and the arena's data bytes (before the 4 KB of state).
+uint8_t *peer_group_arena(si_peer_group *g, int *nranks, int *rank, uint64_t *data_bytes);
+
 }  // namespace si
 
 // Launch wrappers implemented in the .cu files (host side of each kernel).

@@ -148,6 +148,8 @@ SIGNATURES = {
     "si_batch_gather_rows": [_vp, _i64, _vp, _vp, _i64, _i64, _vp],
     # decoder session
     "si_decoder_create": [_i32, _vp, C.POINTER(_vp)],
+    "si_decoder_arena_bytes": [_vp, _pu64],
+    "si_decoder_create_sharded": [_i32, _vp, _vp, C.POINTER(_vp)],
     "si_decoder_destroy": [_vp],
     "si_decoder_slot": [_vp, C.c_char_p, C.POINTER(_vp), _pu64],
     "si_decoder_upload": [_vp, C.c_char_p, _u64, _vp, _u64],
@@ -501,14 +503,25 @@ def decoder_slot_names(layers: int) -> list[str]:
     return names
 
 
+def decoder_arena_bytes(cfg: dict) -> int:
+    """Arena bytes a row-sharded session needs (si_decoder_arena_bytes)."""
+    c, v = DecoderConfig(**cfg), C.c_uint64()
+    call("si_decoder_arena_bytes", C.byref(c), C.byref(v))
+    return v.value
+
+
 class Decoder:
     """Phi4D3D12TextSession on CUDA: ForwardToken, Reset, Position, plus a
-    device-resident greedy loop (generate)."""
+    device-resident greedy loop (generate). With a PeerGroup, the row-sharded
+    session of that rank (si_decoder_create_sharded)."""
 
-    def __init__(self, cfg: dict, device: int = 0):
+    def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None):
         self.cfg = DecoderConfig(**cfg)
         h = C.c_void_p()
-        call("si_decoder_create", device, C.byref(self.cfg), C.byref(h))
+        if group is None:
+            call("si_decoder_create", device, C.byref(self.cfg), C.byref(h))
+        else:
+            call("si_decoder_create_sharded", device, C.byref(self.cfg), group.handle, C.byref(h))
         self.handle = h
         s = C.c_void_p()
         call("si_decoder_stream", h, C.byref(s))
