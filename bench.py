@@ -509,6 +509,9 @@ def run_ours(args) -> None:
     decode = None
     if world == 1 and not args.no_decode:
         decode = decode_block(native, torch, local, peak, not args.no_cpu_baseline)
+    decode14b = None
+    if not args.no_decode:
+        decode14b = decode14b_block(native, torch, ctx, world, rank, local, peak, barrier, max_over_ranks)
     err = native.device_error_take(local)
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
@@ -544,6 +547,7 @@ def run_ours(args) -> None:
                                  "per_shape": q8},
             "prefill_gemm": gemm,
             "decode": decode,
+            "decode_14b": decode14b,
             "clocks": clocks,
             "device_error_word": err,
         }
@@ -614,6 +618,104 @@ def gemm_block(native, ctx, timed) -> dict:
     out["roofline"] = {"bound": "tensor", "achieved": out["per_m"]["2048"]["TFLOP/s"], "unit": "TFLOP/s",
                        "peak": peak, "frac": round(3 * out["per_m"]["2048"]["TFLOP/s"] / peak, 4),
                        "note": "achieved = algorithmic 2MNK/t; frac counts the three BF16 tensor products"}
+    return out
+
+
+def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak: float, barrier,
+                    max_over_ranks) -> dict:
+    """Config 5 at batch 1: the Phi-4-14B-shaped Q8_0 decoder (40 layers,
+    hidden 5120, 40/10 heads of 128, FFN 17920, vocab 100352, seed 11),
+    a 1024-token random prompt, then 128 greedy steps timed on the device
+    (max over ranks). One GPU: the whole session. N GPUs: the row-sharded
+    session, every projection split by rows over the ranks with its output
+    gathered into every rank's arena by the GEMV kernel itself (NVLink peer
+    stores), the rest of the program replicated. Weights are generated on
+    the device (si_synth_weight_rows_device, slot ordinal i -> seed
+    11 * 1000003 + i, each rank its own rows)."""
+    import numpy as np
+
+    from sharpinference_b200 import phi4
+    cfg = dict(phi4.PHI4_14B)
+    prompt_len, steps = 1024, 128
+    cfg["context"] = prompt_len + steps + 1
+    group, arena, addrs = None, None, []
+    if world > 1:
+        import torch.distributed as dist
+        ab = (native.decoder_arena_bytes(cfg) + 255) // 256 * 256
+        arena = ctx.buffer(ab)
+        handles = [None] * world
+        dist.all_gather_object(handles, native.ipc_export(arena.device_pointer))
+        addrs = [arena.device_pointer if q == rank else native.ipc_open(local, handles[q]) for q in range(world)]
+        group = native.PeerGroup(local, world, rank, addrs, ab)
+    shapes = phi4.linear_shapes(cfg)
+    out = {"workload": "config5 batch 1: Phi-4-14B-shaped Q8_0 decoder (40 layers, hidden 5120, 40/10 heads of "
+                       "128, FFN 17920, vocab 100352), N(0,0.02) seed 11, 1024-token random prompt, 128 greedy steps",
+           "parallelism": "single GPU" if world == 1 else
+           f"{world} GPUs: every projection row-sharded, outputs gathered by the GEMV kernel over NVLink; "
+           "norms, rope, attention, argmax and the KV cache replicated"}
+    try:
+        with native.Decoder(cfg, local, group) as dec:
+            for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
+                if name not in shapes:
+                    continue
+                rows, cols = shapes[name]
+                begin, count = 0, rows
+                if world > 1 and name != "token_embedding":
+                    begin, count, _ = native.rowshard_plan(rows, world, rank)
+                ptr, nbytes = dec.slot(name)
+                assert nbytes == count * native.row_bytes(native.Q8_0, cols)
+                native.synth_weight_rows_device(native.Q8_0, 11 * 1_000_003 + i, begin, count, cols, 0.02, ptr,
+                                                dec.stream)
+            prompt = phi4.random_prompt(11, prompt_len, cfg["vocab"])
+            stream = torch.cuda.ExternalStream(dec.stream, device=torch.device("cuda", local))
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            barrier()
+            e[0].record(stream)
+            nxt = dec.prefill(prompt)
+            e[1].record(stream)
+            e[1].synchronize()
+            barrier()
+            with ClockSampler(local) as clk:
+                e[2].record(stream)
+                t0 = time.perf_counter()
+                toks = dec.generate([nxt], steps - 1)
+                wall = time.perf_counter() - t0
+                e[3].record(stream)
+                e[3].synchronize()
+            prefill_ms = max_over_ranks(e[0].elapsed_time(e[1]))
+            decode_ms = max_over_ranks(e[2].elapsed_time(e[3]))
+            wall = max_over_ranks(wall)
+            barrier()
+            wbytes = sum(r * native.row_bytes(native.Q8_0, c) for r, c in shapes.values())
+            kv_row = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_size"] * 4
+            kv_bytes = sum(kv_row * (p + 1) for p in range(prompt_len, prompt_len + steps)) / steps
+            tok_s = steps / (decode_ms * 1e-3)
+            # weights are read once per token across the ranks; the KV cache once per rank
+            bytes_token = wbytes + world * kv_bytes
+            out.update({
+                "decode_tok_s": round(tok_s, 1), "decode_ms_per_token": round(decode_ms / steps, 4),
+                "e2e_decode_tok_s": round(steps / wall, 1),
+                "prompt_ms": round(prefill_ms, 1),
+                "prompt_path": "batched prefill" if world == 1 else "the decode program per prompt token",
+                "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_token),
+                             "bytes": "Q8_0 weight bytes once per token (split over the ranks) + the KV-cache rows "
+                                      "attended on every rank",
+                             "achieved_aggregate": round(bytes_token * tok_s / 1e9, 1),
+                             "peak_aggregate": round(peak * world, 1), "unit": "GB/s",
+                             "frac": round(bytes_token * tok_s / 1e9 / (peak * world), 4)},
+                "clocks": clk.summary(),
+                "first_tokens": [int(t) for t in toks[:8]],
+                "batch32": "not measured: the session decodes one stream",
+                "device_error_word": native.device_error_take(local),
+            })
+    finally:
+        if group is not None:
+            barrier()  # no rank unmaps an arena another rank may still store into
+            group.close()
+            for q, a in enumerate(addrs):
+                if q != rank:
+                    native.ipc_close(local, a)
+            arena.free()
     return out
 
 

@@ -82,6 +82,7 @@ SIGNATURES = {
     "si_synth_normal": [_u64, _u64, _i64, C.c_float, _vp, _i32],
     "si_synth_weights": [_u32, _u64, _i64, _i64, C.c_float, _vp, _i32],
     "si_synth_weight_rows": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _i32],
+    "si_synth_weight_rows_device": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _vp],
     "si_matvec": [_u32, _vp, _u32, _vp, _u32, _vp, _i64, _i64, _u32, _vp],
     "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "si_matrix_multiply_workspace_bytes": [_u32, _i64, _i64, _i64, _pu64],
@@ -329,6 +330,12 @@ def synth_weight_rows(wtype: int, seed: int, row_begin: int, rows: int, cols: in
     out = np.empty(row_bytes(wtype, cols) * rows, dtype=np.uint8)
     call("si_synth_weight_rows", wtype, seed, row_begin, rows, cols, sigma, out.ctypes.data, threads)
     return out
+
+
+def synth_weight_rows_device(wtype: int, seed: int, row_begin: int, rows: int, cols: int, sigma: float, dst: int,
+                             stream=None) -> None:
+    """si_synth_weight_rows_device: the seeded rows generated in device memory."""
+    call("si_synth_weight_rows_device", wtype, seed, row_begin, rows, cols, sigma, dst, stream)
 
 
 def quantize(wtype: int, values):
