@@ -1,0 +1,376 @@
+// Few-row GEMM on the tensor cores: Y[m, n] = X[m, k] W[n, k]^T for a
+// handful of input rows (transformer.batch-shared-matvec at the reference's
+// 16 rows and config 5's 32 streams, GpuBatchTransformerInstructions.cs:
+// 224-279; a prefill chunk's tail). Same arithmetic as the prefill GEMM
+// (gemm.cu): X and the dequantised weights are split into BF16 hi/lo pairs
+// and Xhi Whi + Xlo Whi + Xhi Wlo accumulate in FP32 in tensor memory.
+//
+// What differs from the prefill GEMM, for m of 2..64 rows per tile:
+//   * The MMA is M = 128 weight rows x N = BN input rows (16, 32 or 64), so
+//     the tensor work follows the rows that exist, and the kernel is bound
+//     by the weight stream rather than by the MMA.
+//   * No workspace: warp 0 loads the FP32 X tile of each stage itself,
+//     splits it into hi/lo and stores both in the swizzled layout the MMA
+//     reads (X is a few hundred KB and stays in L2).
+//   * K is split over the CTAs of a thread-block cluster (z), so a narrow
+//     weight matrix still spreads over the SMs; the partial accumulators
+//     are summed through distributed shared memory by the cluster's first
+//     CTA in rank order (deterministic), no partial sums in global memory.
+//   * Rows t >= control[1] are not written (the batch-shared instruction's
+//     validCount, read on the device).
+//   * Programmatic dependent launch: the weight producers start streaming
+//     before the dependency wait; only the X loads and the stores wait.
+// Every mbarrier wait is bounded (device error word, no trap, no hang).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "device_common.cuh"
+#include "gemm_core.cuh"
+#include "si_internal.h"
+
+namespace si::dev {
+namespace {
+
+constexpr int kSkThreads = 192;  // 6 warps
+constexpr int kSkStages = 4;
+
+template <int BN>
+struct SkinnyCfg {
+    static constexpr uint32_t kATile = kGemmBM * kGemmBK * 2;  // 16 KB (one of hi / lo)
+    static constexpr uint32_t kBTile = BN * kGemmBK * 2;       // BN rows of 128 B
+    static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr uint32_t kIdesc = mma_idesc(BN);
+    static constexpr int kRedStride = BN + 1;  // padded row of the split-K exchange buffer
+    static constexpr size_t kSmem = size_t(kSkStages) * kStageBytes + 1024 + 256;
+    static_assert(size_t(kGemmBM) * kRedStride * 4 <= size_t(kSkStages) * kStageBytes, "exchange buffer");
+};
+
+struct SkinnyParams {
+    const uint8_t *w;
+    const float *x;
+    float *y;
+    const int32_t *control;  // null: every row; else rows t < control[1]
+    uint64_t row_bytes;
+    int m, n, k;
+    int splits;  // K split over the cluster (gridDim.z == cluster size)
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+template <int FMT, int BN>
+__global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const SkinnyParams p) {
+    using Cfg = SkinnyCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-byte aligned tiles
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kSkStages * Cfg::kStageBytes);
+    uint64_t *empty = full + kSkStages;
+    uint64_t *accum = empty + kSkStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kGemmBM, t0 = blockIdx.y * BN;
+    const int total_iters = p.k / kGemmBK;
+    const int it0 = int(int64_t(total_iters) * blockIdx.z / p.splits);
+    const int iters = int(int64_t(total_iters) * (blockIdx.z + 1) / p.splits) - it0;
+
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSkStages; ++s) {
+            mbar_init(&full[s], 128 + 32);  // weight producers + the X warp
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(Cfg::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    float acc[BN < 32 ? 32 : BN];  // epilogue warps: this thread's weight row, BN input rows
+    if (warp == 0) {
+        // X producer: FP32 rows of the stage -> BF16 hi / lo, swizzled.
+        pdl_wait();
+        for (int it = 0; it < iters; ++it) {
+            const int s = it % kSkStages;
+            if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
+            uint8_t *hi_tile = smem + s * Cfg::kStageBytes + 2 * Cfg::kATile;
+            uint8_t *lo_tile = hi_tile + Cfg::kBTile;
+            for (int r = lane; r < BN; r += 32) {
+                const int t = t0 + r;
+                const float4 *src = reinterpret_cast<const float4 *>(p.x + size_t(t) * p.k + size_t(it0 + it) * kGemmBK);
+                uint8_t *hi_row = hi_tile + (r >> 3) * 1024 + (r & 7) * 128;
+                uint8_t *lo_row = lo_tile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+                    if (t < p.m) a = __ldg(src + 2 * c), b = __ldg(src + 2 * c + 1);
+                    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                    uint32_t hv[4], lv[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t hb = pack_bf16(v[2 * q], v[2 * q + 1]);
+                        hv[q] = hb;
+                        lv[q] = pack_bf16(v[2 * q] - __uint_as_float(hb << 16),
+                                          v[2 * q + 1] - __uint_as_float(hb & 0xffff0000u));
+                    }
+                    const int pc = c ^ (r & 7);
+                    *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                    *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+                }
+            }
+            fence_proxy_async();
+            mbar_arrive(&full[s]);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int it = 0; it < iters; ++it) {
+                const int s = it % kSkStages;
+                mbar_wait(&full[s], (it / kSkStages) & 1, kErrFullBarrierTimeout);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t base = smem_u32(smem + s * Cfg::kStageBytes);
+                const uint32_t a_hi = base, a_lo = base + Cfg::kATile, b_hi = base + 2 * Cfg::kATile,
+                               b_lo = b_hi + Cfg::kBTile;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint32_t off = kk * 32;  // 16 BF16 along K within the 128-byte row
+                    mma_bf16(tmem, smem_desc(a_hi + off), smem_desc(b_hi + off), Cfg::kIdesc, (it | kk) != 0);
+                    mma_bf16(tmem, smem_desc(a_hi + off), smem_desc(b_lo + off), Cfg::kIdesc, 1);
+                    mma_bf16(tmem, smem_desc(a_lo + off), smem_desc(b_hi + off), Cfg::kIdesc, 1);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(accum);
+        }
+        __syncwarp();
+    } else {
+        // warps 2..5: weight producers (no dependency wait: weights are
+        // read-only), then the accumulator drain.
+        const int r = threadIdx.x - 64;  // weight row within the tile, 0..127
+        const bool valid_row = n0 + r < p.n;
+        const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
+        RawWeights<FMT> raw, next;
+        if (valid_row && iters > 0) fetch_weights64<FMT>(wrow, it0 * kGemmBK, raw);
+        for (int it = 0; it < iters; ++it) {
+            const int s = it % kSkStages;
+            if (valid_row && it + 1 < iters) fetch_weights64<FMT>(wrow, (it0 + it + 1) * kGemmBK, next);
+            float w[64];
+            if (valid_row) {
+                decode_weights64<FMT>(raw, w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) w[i] = 0.0f;
+            }
+            raw = next;
+            if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
+            uint8_t *hi_row = smem + s * Cfg::kStageBytes + (r >> 3) * 1024 + (r & 7) * 128;
+            uint8_t *lo_row = hi_row + Cfg::kATile;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t hv[4], lv[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float v0 = w[8 * c + 2 * t], v1 = w[8 * c + 2 * t + 1];
+                    const uint32_t hb = pack_bf16(v0, v1);
+                    hv[t] = hb;
+                    lv[t] = pack_bf16(v0 - __uint_as_float(hb << 16), v1 - __uint_as_float(hb & 0xffff0000u));
+                }
+                const int pc = c ^ (r & 7);
+                *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
+            fence_proxy_async();
+            mbar_arrive(&full[s]);
+        }
+        // TMEM lane quarter (warp % 4) holds weight rows 32 * (warp % 4) ..
+        mbar_wait(accum, 0, kErrMmaBarrierTimeout);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int quarter = warp & 3;
+#pragma unroll
+        for (int c0 = 0; c0 < (BN < 32 ? 32 : BN); c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c0 + j] = __uint_as_float(v[j]);
+        }
+    }
+
+    // Split-K: every CTA but the cluster's first leaves its partial sums in
+    // its shared memory (the stage ring is idle: the accumulator barrier
+    // completed after the last MMA read it); the first adds them in rank order.
+    const bool drain = warp >= 2;
+    const int row_local = (warp & 3) * 32 + lane;
+    float *red = reinterpret_cast<float *>(smem);
+    const uint32_t crank = p.splits > 1 ? cluster_rank() : 0;
+    if (p.splits > 1) {
+        if (drain && crank != 0) {
+#pragma unroll
+            for (int j = 0; j < BN; ++j) red[row_local * Cfg::kRedStride + j] = acc[j];
+        }
+        cluster_barrier();
+        if (drain && crank == 0) {
+            for (int q = 1; q < p.splits; ++q) {
+                const uint32_t peer = map_to_rank(smem_u32(red + row_local * Cfg::kRedStride), uint32_t(q));
+#pragma unroll
+                for (int j = 0; j < BN; ++j) acc[j] += ld_cluster_f32(peer + 4u * uint32_t(j));
+            }
+        }
+    }
+    if (drain && crank == 0) {
+        pdl_wait();  // the previous kernel may still read Y
+        const int row = n0 + row_local;
+        int valid = p.m;
+        if (p.control) valid = min(valid, p.control[1]);
+        if (row < p.n) {
+#pragma unroll
+            for (int j = 0; j < BN; ++j) {
+                const int t = t0 + j;
+                if (t < valid) p.y[size_t(t) * p.n + row] = acc[j];
+            }
+        }
+    }
+    if (p.splits > 1) cluster_barrier();  // peers keep their shared memory until the first CTA has read it
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols)
+                     : "memory");
+    }
+}
+
+int sm_count() {
+    static const int sms = [] {
+        int dev = 0, v = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v;
+    }();
+    return sms;
+}
+
+template <int FMT, int BN>
+si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
+    using Cfg = SkinnyCfg<BN>;
+    auto kernel = gemm_skinny_kernel<FMT, BN>;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmem));
+        attr = true;
+    }
+    SkinnyParams p = p0;
+    const int64_t tiles = ((p.n + kGemmBM - 1) / kGemmBM) * ((p.m + BN - 1) / BN);
+    const int iters = p.k / kGemmBK;
+    // K split over a cluster of 1, 2 or 4 CTAs: the fewest that come close
+    // to one CTA per SM, keeping at least four stages per CTA.
+    int splits = 1;
+    while (splits < 4 && tiles * splits * 2 <= sm_count() && iters / (splits * 2) >= 4) splits *= 2;
+    p.splits = splits;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned((p.n + kGemmBM - 1) / kGemmBM), unsigned((p.m + BN - 1) / BN), unsigned(splits));
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 1;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = unsigned(splits);
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SI_ERR_CUDA, "tcgen05 few-row GEMM launch failed: %s", cudaGetErrorString(e));
+    }
+    return SI_OK;
+}
+
+template <int BN>
+si_status dispatch_type(uint32_t wtype, const SkinnyParams &p, cudaStream_t st) {
+    switch (wtype) {
+    case SI_TYPE_Q4_K: return launch_skinny<SI_TYPE_Q4_K, BN>(p, st);
+    case SI_TYPE_Q8_0: return launch_skinny<SI_TYPE_Q8_0, BN>(p, st);
+    case SI_TYPE_F16: return launch_skinny<SI_TYPE_F16, BN>(p, st);
+    default: return launch_skinny<SI_TYPE_F32, BN>(p, st);
+    }
+}
+
+}  // namespace
+}  // namespace si::dev
+
+namespace si::kernels {
+using namespace si::dev;
+
+bool gemm_skinny_supported(uint32_t wtype, const void *w, const float *x, int64_t m, int64_t n, int64_t k) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0 && wtype != SI_TYPE_F16 && wtype != SI_TYPE_F32) return false;
+    if (m < 1 || n < 1 || k % kGemmBK != 0 || k > (int64_t(1) << 30) || n > (int64_t(1) << 30) ||
+        m > (int64_t(1) << 24))
+        return false;
+    if (wtype == SI_TYPE_Q4_K && k % 256 != 0) return false;
+    // 16-byte weight and input loads
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) return false;
+    uint64_t rb = 0;
+    if (byte_length(wtype, uint64_t(k), &rb) != SI_OK) return false;
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+    if (wtype == SI_TYPE_Q8_0) return wa % 4 == 0 && rb % 4 == 0;
+    return wa % 16 == 0 && rb % 16 == 0;
+}
+
+si_status gemm_skinny(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y, int64_t m,
+                      int64_t n, int64_t k, void *stream) {
+    if (!gemm_skinny_supported(wtype, w, x, m, n, k))
+        return fail(SI_ERR_UNSUPPORTED, "few-row GEMM: unsupported type, shape or alignment");
+    uint64_t rb = 0;
+    byte_length(wtype, uint64_t(k), &rb);
+    SkinnyParams p{static_cast<const uint8_t *>(w), x, y, control, rb, int(m), int(n), int(k), 1};
+    auto st = static_cast<cudaStream_t>(stream);
+    if (m <= 16) return dispatch_type<16>(wtype, p, st);
+    if (m <= 32) return dispatch_type<32>(wtype, p, st);
+    return dispatch_type<64>(wtype, p, st);
+}
+
+si_status take_error_gemm_skinny(int device, uint32_t *code) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return fail(SI_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    uint32_t v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_error_word, sizeof v);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof zero);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return fail(SI_ERR_CUDA, "device error word: %s", cudaGetErrorString(e));
+    *code |= v;
+    return SI_OK;
+}
+
+}  // namespace si::kernels

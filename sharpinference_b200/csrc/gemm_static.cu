@@ -12,12 +12,14 @@
 // Cost and limits: every GPU that loads this library reserves the array
 // (kStaticWorkspaceBytes = 64 MiB) until the process exits. A call whose
 // workspace requirement (si_matrix_multiply_workspace_bytes: 4 * m * k bytes
-// on the tensor-core path) exceeds it is refused. All calls share the one
+// of BF16 split on the tensor-core path, plus the K-split partial sums when
+// the GEMM splits K) exceeds it is refused. All calls share the one
 // array, so two calls whose executions overlap on the GPU (different
 // streams, or different host threads) race on it; serialise them. The
 // contents left by the previous call are never read: the split kernel
-// rewrites every element the GEMM reads and rows past m come from the TMA's
-// zero fill, so nothing has to be cleared first.
+// rewrites every element the GEMM reads, rows past m come from the TMA's
+// zero fill and every partial sum is written before the reduction reads it,
+// so nothing has to be cleared first.
 #include <cuda_runtime.h>
 
 #include <mutex>

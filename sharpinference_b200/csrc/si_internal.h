@@ -71,6 +71,14 @@ si_status batch_shared_matvec(uint32_t wtype, const void *w, const float *in,
 si_status gemm_workspace_bytes(uint32_t wtype, int64_t m, int64_t n, int64_t k, uint64_t *bytes);
 si_status gemm_tn(uint32_t wtype, const float *x, const void *w, float *y, int64_t m, int64_t n,
                   int64_t k, void *workspace, uint64_t workspace_bytes, void *stream);
+// Few-row tcgen05 GEMM (gemm_skinny.cu): Y = X W^T for any m with BN = 16,
+// 32 or 64 input rows per tile, no workspace; rows t >= control[1] are not
+// written when control is non-null. SI_ERR_UNSUPPORTED (nothing launched)
+// when gemm_skinny_supported is false.
+bool gemm_skinny_supported(uint32_t wtype, const void *w, const float *x, int64_t m, int64_t n, int64_t k);
+si_status gemm_skinny(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y, int64_t m,
+                      int64_t n, int64_t k, void *stream);
+si_status take_error_gemm_skinny(int device, uint32_t *code);
 si_status take_error_gemv(int device, uint32_t *code);
 si_status take_error_gemm(int device, uint32_t *code);
 si_status take_error_gemv_mma(int device, uint32_t *code);

@@ -164,6 +164,10 @@ using namespace si::dev;
 si_status shared_weight_matvec(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y,
                                int64_t m, int64_t n, int64_t k, void *stream) {
     auto st = static_cast<cudaStream_t>(stream);
+    // Two or more rows: the few-row tcgen05 GEMM (weights read once per 16,
+    // 32 or 64 rows, no workspace).
+    if (m >= 2 && gemm_skinny_supported(wtype, w, x, m, n, k))
+        return gemm_skinny(wtype, w, x, control, y, m, n, k, stream);
     // Q4_K: the batched tensor-core GEMV (eight input rows per weight pass).
     // Otherwise quantised weights: one tensor-core GEMV per input row (the weights are
     // re-read per row, from L2 when they fit, which still beats the SIMT

@@ -125,3 +125,21 @@ def test_prefill_gemm_q4_k_config3_shape(ctx, m):
         ref = oracle.matvec_f64(N.Q4_K, blob, x[r * k:(r + 1) * k], n, k)
         north_star_gate(y[r], ref, x[r * k:(r + 1) * k], rn, k)
     assert native.device_error_take(0) == 0
+
+
+@pytest.mark.parametrize("wtype", [N.Q4_K, N.Q8_0, N.F16, N.F32])
+@pytest.mark.parametrize("batch,valid,n,k", [(2, 2, 256, 8192), (16, 15, 130, 4096), (24, 24, 640, 17920),
+                                             (64, 60, 384, 2048), (100, 100, 200, 1024)])
+def test_few_row_gemm_split_k_row_tiles_deterministic(ctx, wtype, batch, valid, n, k):
+    """The few-row tcgen05 GEMM behind batch-shared-matvec: narrow weights
+    with long rows split K over a cluster (2 or 4 CTAs, partials summed
+    through distributed shared memory), 16/32/64-row tiles, more than one
+    row tile (100 rows); two runs give identical bits."""
+    blob, x, y = _shared_case(ctx, wtype, batch, n, k, valid, seed=batch * 3 + k)
+    _, _, y2 = _shared_case(ctx, wtype, batch, n, k, valid, seed=batch * 3 + k)
+    np.testing.assert_array_equal(y, y2)
+    assert np.all(y[valid:] == -31.0), "rows at or beyond validCount were written"
+    rn = row_norm_max(wtype, blob, n, k)
+    for b in range(valid):
+        north_star_gate(y[b], oracle.matvec_f64(wtype, blob, x[b], n, k), x[b], rn, k)
+    assert native.device_error_take(0) == 0
