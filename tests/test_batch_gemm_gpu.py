@@ -127,7 +127,7 @@ def test_prefill_gemm_q4_k_config3_shape(ctx, m):
     assert native.device_error_take(0) == 0
 
 
-@pytest.mark.parametrize("wtype", [N.Q4_K, N.Q8_0, N.F16, N.F32])
+@pytest.mark.parametrize("wtype", [N.Q4_K, N.Q8_0, N.F16])
 @pytest.mark.parametrize("batch,valid,n,k", [(2, 2, 256, 8192), (16, 15, 130, 4096), (24, 24, 640, 17920),
                                              (64, 60, 384, 2048), (100, 100, 200, 1024)])
 def test_few_row_gemm_split_k_row_tiles_deterministic(ctx, wtype, batch, valid, n, k):
