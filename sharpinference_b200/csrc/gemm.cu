@@ -14,7 +14,7 @@
 //   warp 1      allocates 256 TMEM columns; one thread issues
 //               tcgen05.mma (M=128, N=256, K=16, BF16 -> FP32) x 3 products,
 //               then tcgen05.commit frees the stage
-//   warps 2..5  dequantise this stage's 128x64 weight block (GGUF Q8_0 /
+//   warps 2..9  dequantise this stage's 128x64 weight block (GGUF Q8_0 /
 //               Q4_K / F16 / F32) in registers, split hi/lo and store both in
 //               the canonical K-major 128B-swizzled layout; after the last
 //               stage they drain the accumulator (tcgen05.ld) to Y
@@ -37,7 +37,7 @@ constexpr int kBM = kGemmBM;                     // weight rows per CTA (MMA M)
 constexpr int kBN = 256;                         // input rows per CTA (MMA N)
 constexpr int kBK = kGemmBK;                     // K per stage (128 B of BF16)
 constexpr int kStages = 2;
-constexpr int kThreads = 192;                    // 6 warps
+constexpr int kThreads = 64 + kProducers;       // 10 warps
 constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB (one of hi / lo)
 constexpr uint32_t kBTile = kBN * kBK * 2;       // 32 KB
 constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;  // 96 KB
@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 128 + 1);
+            mbar_init(&full[s], kProducers + 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
@@ -125,53 +125,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // warps 2..5: weight producers, then epilogue.
-        const int r = threadIdx.x - 64;  // weight row within the tile, 0..127
+        // warps 2..9: weight producers, then epilogue.
+        // Two threads per weight row, each fetching and decoding 32 of the
+        // stage's 64 columns (the dequantisation is the per-stage bound).
+        const int pt = threadIdx.x - 64, r = pt >> 1, h = pt & 1;  // row 0..127, half 0..1
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
-        RawWeights<FMT> raw, next;
-        if (valid_row && iters > 0) fetch_weights64<FMT>(wrow, it0 * kBK, raw);
+        RawHalf<FMT> raw, next;
+        if (valid_row && iters > 0) fetch_weights32<FMT>(wrow, it0 * kBK, h, raw);
         for (int it = 0; it < iters; ++it) {
             const int s = it % kStages;
             // the next stage's bytes are in flight while this one is decoded
-            if (valid_row && it + 1 < iters) fetch_weights64<FMT>(wrow, (it0 + it + 1) * kBK, next);
-            float w[64];
+            if (valid_row && it + 1 < iters) fetch_weights32<FMT>(wrow, (it0 + it + 1) * kBK, h, next);
+            float w[32];
             if (valid_row) {
-                decode_weights64<FMT>(raw, w);
+                decode_weights32<FMT>(raw, h, w);
             } else {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) w[i] = 0.0f;
+                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
             }
             raw = next;
             if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
             uint8_t *st = smem + s * kStageBytes;
-            uint8_t *hi_row = st + (r >> 3) * 1024 + (r & 7) * 128;
-            uint8_t *lo_row = hi_row + kATile;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t hv[4], lv[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float v0 = w[8 * c + 2 * t], v1 = w[8 * c + 2 * t + 1];
-                    const uint32_t hb = pack_bf16(v0, v1);
-                    const float h0 = __uint_as_float(hb << 16), h1 = __uint_as_float(hb & 0xffff0000u);
-                    hv[t] = hb;
-                    lv[t] = pack_bf16(v0 - h0, v1 - h1);
-                }
-                const int pc = c ^ (r & 7);
-                *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-            }
+            store_split_half(w, r, h, st, st + kATile);
             fence_proxy_async();
             mbar_arrive(&full[s]);
         }
-        // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32*(warp%4) ..
+        // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32*(warp%4) ..;
+        // warps 2..5 drain the first half of the columns, warps 6..9 the second.
         mbar_wait(accum, 0, kErrMmaBarrierTimeout);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int quarter = warp & 3;
         const int row = n0 + quarter * 32 + lane;
+        const int c_begin = warp >= 6 ? kBN / 2 : 0;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
+        for (int c0 = c_begin; c0 < c_begin + kBN / 2; c0 += 32) {
             uint32_t v[32];
             tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
             if (row < p.n) {

@@ -6,6 +6,8 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "device_common.cuh"
@@ -15,6 +17,7 @@ namespace si::dev {
 
 constexpr int kGemmBM = 128;  // weight rows per CTA (MMA M)
 constexpr int kGemmBK = 64;   // K per stage (128 B of BF16)
+constexpr int kProducers = 256;  // weight-producer threads: two per weight row
 
 // Instruction descriptor, kind::f16: D F32, A/B BF16, both K-major,
 // N (bits 17-22: N>>3), M = 128 (bits 24-28: M>>4).
@@ -168,6 +171,127 @@ __device__ __forceinline__ void decode_weights64(const RawWeights<FMT> &r, float
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Half of a stage's 64 columns of one row (columns 32h .. 32h+31): the
+// weight producers run two threads per row, each fetching and decoding its
+// half, so twice the warps share the dequantisation work.
+template <int FMT>
+struct RawHalf {
+    uint4 v[FMT == SI_TYPE_Q4_K ? 3 : FMT == SI_TYPE_Q8_0 ? 3 : FMT == SI_TYPE_F16 ? 4 : 8];
+    uint32_t extra;  // Q8_0: the ninth 32-bit word of the block window
+    int j;           // Q4_K: 64-column group within the super-block
+};
+
+template <int FMT>
+__device__ __forceinline__ void fetch_weights32(const uint8_t *row, int k0, int h, RawHalf<FMT> &r) {
+    if constexpr (FMT == SI_TYPE_Q4_K) {
+        // both halves need the group's 32 quant bytes (low / high nibbles)
+        const uint8_t *sb = row + (k0 >> 8) * 144;
+        r.j = (k0 >> 6) & 3;
+        r.v[0] = __ldg(reinterpret_cast<const uint4 *>(sb));
+        r.v[1] = __ldg(reinterpret_cast<const uint4 *>(sb + 16 + 32 * r.j));
+        r.v[2] = __ldg(reinterpret_cast<const uint4 *>(sb + 32 + 32 * r.j));
+    } else if constexpr (FMT == SI_TYPE_Q8_0) {
+        // blocks 2m (4-byte aligned) and 2m+1 (2 bytes past a 4-byte
+        // boundary): 36 bytes from word 0, or from word 8, of the pair
+        const uint32_t *u = reinterpret_cast<const uint32_t *>(row + (k0 >> 5) * 34) + 8 * h;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            r.v[i].x = __ldg(u + 4 * i), r.v[i].y = __ldg(u + 4 * i + 1);
+            r.v[i].z = __ldg(u + 4 * i + 2), r.v[i].w = __ldg(u + 4 * i + 3);
+        }
+        r.extra = __ldg(u + 8);
+        r.j = h;
+    } else if constexpr (FMT == SI_TYPE_F16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0 + 32 * h) * 2);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r.v[i] = __ldg(p + i);
+    } else {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + size_t(k0 + 32 * h) * 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r.v[i] = __ldg(p + i);
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, float (&w)[32]) {
+    if constexpr (FMT == SI_TYPE_Q4_K) {
+        const uint4 hd = r.v[0];
+        const uint32_t q[8] = {r.v[1].x, r.v[1].y, r.v[1].z, r.v[1].w, r.v[2].x, r.v[2].y, r.v[2].z, r.v[2].w};
+        const int j = r.j;
+        const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, mn_lo = hd.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+        const uint32_t mn_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+        const uint32_t scw = j >= 2 ? sc_hi : sc_lo, mnw = j >= 2 ? mn_hi : mn_lo;
+        const int b = ((2 * j) & 3) + h;  // sub-block byte of this half
+        const float a = h16(hd.x) * float((scw >> (8 * b)) & 0xffu);
+        const float c = h16(hd.x >> 16) * float((mnw >> (8 * b)) & 0xffu);
+        const int shift = 4 * h;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int t = 0; t < 4; ++t) w[4 * i + t] = a * float((q[i] >> (8 * t + shift)) & 15u) - c;
+    } else if constexpr (FMT == SI_TYPE_Q8_0) {
+        uint32_t wv[9];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            wv[4 * i] = r.v[i].x, wv[4 * i + 1] = r.v[i].y, wv[4 * i + 2] = r.v[i].z, wv[4 * i + 3] = r.v[i].w;
+        }
+        wv[8] = r.extra;
+        // the block starts at byte 0 (h = 0) or 2 (h = 1) of the window;
+        // two unrolled copies keep every word index a constant
+        auto decode = [&](auto offset) {
+            constexpr int o = decltype(offset)::value;
+            const float d = h16(o == 0 ? (wv[0] & 0xffffu) : (wv[0] >> 16));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                constexpr int base = o + 2;
+                const int byte = base + e;
+                w[e] = d * float(int8_t((wv[byte >> 2] >> (8 * (byte & 3))) & 0xffu));
+            }
+        };
+        if (r.j == 0) decode(std::integral_constant<int, 0>{});
+        else decode(std::integral_constant<int, 2>{});
+    } else if constexpr (FMT == SI_TYPE_F16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t vv[4] = {r.v[i].x, r.v[i].y, r.v[i].z, r.v[i].w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                w[8 * i + 2 * t] = h16(vv[t]);
+                w[8 * i + 2 * t + 1] = h16(vv[t] >> 16);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            w[4 * i] = __uint_as_float(r.v[i].x), w[4 * i + 1] = __uint_as_float(r.v[i].y);
+            w[4 * i + 2] = __uint_as_float(r.v[i].z), w[4 * i + 3] = __uint_as_float(r.v[i].w);
+        }
+    }
+}
+
+// Splits 32 decoded weights (columns 32h ..) into BF16 hi / lo and stores
+// them as 16-byte chunks 4h .. 4h+3 of row r in the canonical K-major
+// 128-byte-swizzled layout (hi tile at `hi`, lo tile at `lo`).
+__device__ __forceinline__ void store_split_half(const float (&w)[32], int r, int h, uint8_t *hi, uint8_t *lo) {
+    uint8_t *hi_row = hi + (r >> 3) * 1024 + (r & 7) * 128;
+    uint8_t *lo_row = lo + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float v0 = w[8 * c + 2 * t], v1 = w[8 * c + 2 * t + 1];
+            const uint32_t hb = pack_bf16(v0, v1);
+            hv[t] = hb;
+            lv[t] = pack_bf16(v0 - __uint_as_float(hb << 16), v1 - __uint_as_float(hb & 0xffff0000u));
+        }
+        const int pc = (4 * h + c) ^ (r & 7);
+        *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
 }
 
 

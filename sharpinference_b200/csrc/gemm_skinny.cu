@@ -34,7 +34,7 @@
 namespace si::dev {
 namespace {
 
-constexpr int kSkThreads = 192;  // 6 warps
+constexpr int kSkThreads = 64 + kProducers;  // 10 warps
 constexpr int kSkStages = 4;
 
 template <int BN>
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const Skinny
     pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSkStages; ++s) {
-            mbar_init(&full[s], 128 + 32);  // weight producers + the X warp
+            mbar_init(&full[s], kProducers + 32);  // weight producers + the X warp
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
@@ -172,61 +172,53 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const Skinny
         }
         __syncwarp();
     } else {
-        // warps 2..5: weight producers (no dependency wait: weights are
+        // warps 2..9: weight producers (no dependency wait: weights are
         // read-only), then the accumulator drain.
-        const int r = threadIdx.x - 64;  // weight row within the tile, 0..127
+        // Two threads per weight row, each fetching and decoding 32 of the
+        // stage's 64 columns (the dequantisation is the per-stage bound).
+        const int pt = threadIdx.x - 64, r = pt >> 1, h = pt & 1;  // row 0..127, half 0..1
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
-        RawWeights<FMT> raw, next;
-        if (valid_row && iters > 0) fetch_weights64<FMT>(wrow, it0 * kGemmBK, raw);
+        RawHalf<FMT> raw, next;
+        if (valid_row && iters > 0) fetch_weights32<FMT>(wrow, it0 * kGemmBK, h, raw);
         for (int it = 0; it < iters; ++it) {
             const int s = it % kSkStages;
-            if (valid_row && it + 1 < iters) fetch_weights64<FMT>(wrow, (it0 + it + 1) * kGemmBK, next);
-            float w[64];
+            // the next stage's bytes are in flight while this one is decoded
+            if (valid_row && it + 1 < iters) fetch_weights32<FMT>(wrow, (it0 + it + 1) * kGemmBK, h, next);
+            float w[32];
             if (valid_row) {
-                decode_weights64<FMT>(raw, w);
+                decode_weights32<FMT>(raw, h, w);
             } else {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) w[i] = 0.0f;
+                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
             }
             raw = next;
             if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
-            uint8_t *hi_row = smem + s * Cfg::kStageBytes + (r >> 3) * 1024 + (r & 7) * 128;
-            uint8_t *lo_row = hi_row + Cfg::kATile;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t hv[4], lv[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float v0 = w[8 * c + 2 * t], v1 = w[8 * c + 2 * t + 1];
-                    const uint32_t hb = pack_bf16(v0, v1);
-                    hv[t] = hb;
-                    lv[t] = pack_bf16(v0 - __uint_as_float(hb << 16), v1 - __uint_as_float(hb & 0xffff0000u));
-                }
-                const int pc = c ^ (r & 7);
-                *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-            }
+            uint8_t *st = smem + s * Cfg::kStageBytes;
+            store_split_half(w, r, h, st, st + Cfg::kATile);
             fence_proxy_async();
             mbar_arrive(&full[s]);
         }
-        // TMEM lane quarter (warp % 4) holds weight rows 32 * (warp % 4) ..
-        mbar_wait(accum, 0, kErrMmaBarrierTimeout);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int quarter = warp & 3;
+        // TMEM lane quarter (warp % 4) holds weight rows 32 * (warp % 4) ..;
+        // warps 2..5 drain it.
+        if (warp < 6) {
+            mbar_wait(accum, 0, kErrMmaBarrierTimeout);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int quarter = warp & 3;
 #pragma unroll
-        for (int c0 = 0; c0 < (BN < 32 ? 32 : BN); c0 += 32) {
-            uint32_t v[32];
-            tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
+            for (int c0 = 0; c0 < (BN < 32 ? 32 : BN); c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[c0 + j] = __uint_as_float(v[j]);
+                for (int j = 0; j < 32; ++j) acc[c0 + j] = __uint_as_float(v[j]);
+            }
         }
     }
 
     // Split-K: every CTA but the cluster's first leaves its partial sums in
     // its shared memory (the stage ring is idle: the accumulator barrier
     // completed after the last MMA read it); the first adds them in rank order.
-    const bool drain = warp >= 2;
+    const bool drain = warp >= 2 && warp < 6;
     const int row_local = (warp & 3) * 32 + lane;
     float *red = reinterpret_cast<float *>(smem);
     const uint32_t crank = p.splits > 1 ? cluster_rank() : 0;
