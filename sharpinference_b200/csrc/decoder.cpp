@@ -62,6 +62,15 @@ struct si_decoder {
     si_peer_group *group = nullptr;
     uint8_t *arena = nullptr;
     const void *w_vocab = nullptr;
+    // Multi-stream session (si_decoder_create_streams): `streams` rows per
+    // step, stream b's caches at rows b * context of each layer's cache;
+    // per-stream tokens / positions / greedy-loop state on the device.
+    int32_t streams = 1;
+    int32_t *st_tokens = nullptr, *st_positions = nullptr, *st_start = nullptr, *st_next = nullptr,
+            *st_history = nullptr;
+    k::StreamsFeed *st_feed = nullptr;
+    int32_t *pinned_st = nullptr;  // host staging: tokens, positions, next, history
+    cudaGraphExec_t streams_exec = nullptr, streams_feed_exec = nullptr;
     // Prompt prefill in chunks of up to kPrefillRows rows (buffers allocated
     // by the first prefill call): the chunk's activations, one (start,
     // count) control pair per chunk, the split-operand GEMM workspace.
@@ -120,6 +129,9 @@ void destroy(si_decoder *d) {
     if (d->stream) cudaStreamSynchronize(d->stream);
     if (d->step_exec) cudaGraphExecDestroy(d->step_exec);
     if (d->feed_exec) cudaGraphExecDestroy(d->feed_exec);
+    if (d->streams_exec) cudaGraphExecDestroy(d->streams_exec);
+    if (d->streams_feed_exec) cudaGraphExecDestroy(d->streams_feed_exec);
+    if (d->pinned_st) cudaFreeHost(d->pinned_st);
     if (d->step) k::decode_step_destroy(d->step);
     for (void *p : d->allocations) cudaFree(p);
     if (d->pinned) cudaFreeHost(d->pinned);
@@ -291,7 +303,8 @@ si_status batch_project(si_decoder *d, const void *w, const float *x, float *y, 
 // batch instructions with control = (start, rows), the three attention
 // instructions fused, and after the last chunk select-last -> vocabulary
 // projection -> argmax into next_token.
-si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, int32_t rows, bool last) {
+si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, int32_t rows, bool last,
+                        int64_t cache_offset) {
     const si_decoder_config &c = d->cfg;
     const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
     auto &P = d->pf;
@@ -301,11 +314,12 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
         return st;
     for (int l = 0; l < c.layers; ++l) {
         if (si_status st = batch_project(d, d->w_qkv[l], P.normalized, P.qkv, rows, QKV, H)) return st;
-        if (si_status st = k::tr_rope_kv_write(P.qkv, nullptr, control, d->freq, P.query, d->key_cache[l],
-                                               d->value_cache[l], rows, H, KV, c.head_size, c.rotary_size, c.context,
+        float *kc = d->key_cache[l] + cache_offset, *vc = d->value_cache[l] + cache_offset;
+        if (si_status st = k::tr_rope_kv_write(P.qkv, nullptr, control, d->freq, P.query, kc, vc, rows, H, KV,
+                                               c.head_size, c.rotary_size, c.context,
                                                c.rope_scale, s))
             return st;
-        if (si_status st = k::tr_prefill_attention(P.query, d->key_cache[l], d->value_cache[l], start, rows,
+        if (si_status st = k::tr_prefill_attention(P.query, kc, vc, start, rows,
                                                    P.attention, c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
         if (si_status st = batch_project(d, d->w_out[l], P.attention, P.projected, rows, H, H)) return st;
@@ -328,7 +342,10 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
 
 // Prefill of `count` rows from the session position: token ids (gathered
 // from token_embedding) or ready embedding rows from the host.
-si_status prefill(si_decoder *d, const int32_t *tokens, const float *embeddings, int32_t count, int32_t *next_token) {
+// `start0`: the first row's position; `cache_offset`: floats from each
+// layer's cache base to the stream's cache (0 for a single-stream session).
+si_status prefill(si_decoder *d, const int32_t *tokens, const float *embeddings, int32_t count, int32_t start0,
+                  int64_t cache_offset, int32_t *next_token) {
     const si_decoder_config &c = d->cfg;
     const int64_t H = c.hidden;
     if (si_status st = ensure_prefill(d)) return st;
@@ -336,7 +353,7 @@ si_status prefill(si_decoder *d, const int32_t *tokens, const float *embeddings,
     const int32_t chunks = int32_t((count + kPrefillRows - 1) / kPrefillRows);
     std::vector<int32_t> pairs(size_t(chunks) * 2);
     for (int32_t i = 0; i < chunks; ++i) {
-        pairs[size_t(2 * i)] = d->position + int32_t(i * kPrefillRows);
+        pairs[size_t(2 * i)] = start0 + int32_t(i * kPrefillRows);
         pairs[size_t(2 * i + 1)] = int32_t(std::min<int64_t>(kPrefillRows, count - i * kPrefillRows));
     }
     if (si_status st = cuda(cudaMemcpyAsync(d->pf.control, pairs.data(), pairs.size() * 4, cudaMemcpyHostToDevice, s),
@@ -359,13 +376,104 @@ si_status prefill(si_decoder *d, const int32_t *tokens, const float *embeddings,
                                                        cudaMemcpyHostToDevice, s), "upload")) {
             return st;
         }
-        if (si_status st = prefill_chunk(d, d->pf.control + 2 * i, start, rows, i + 1 == chunks)) return st;
+        if (si_status st = prefill_chunk(d, d->pf.control + 2 * i, start, rows, i + 1 == chunks, cache_offset))
+            return st;
     }
     if (si_status st = cuda(cudaMemcpyAsync(d->pinned + 2, d->next_token, 4, cudaMemcpyDeviceToHost, s), "readback"))
         return st;
     if (si_status st = cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return st;
-    d->position += count;
     *next_token = d->pinned[2];
+    return SI_OK;
+}
+
+// One decode step of every stream of a multi-stream session: the decode
+// program with each instruction over `streams` rows -- the projections as
+// the few-row tcgen05 GEMM (each weight read once per step for all
+// streams), rope-kv-write and attention at each stream's own position and
+// cache, argmax per row.
+si_status record_step_streams(si_decoder *d, k::StreamsFeed *sfeed) {
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
+    const int64_t B = d->streams, stride = c.context * KV;
+    cudaStream_t s = d->stream;
+    auto proj = [&](uint32_t type, const void *w, const float *x, float *y, int64_t rows, int64_t cols) {
+        return k::shared_weight_matvec(type, w, x, nullptr, y, B, rows, cols, s);
+    };
+    if (si_status st = k::tr_gather_rows_quant(c.embedding_type, d->embedding, c.vocab, H, d->st_tokens, B, d->hidden,
+                                               s))
+        return st;
+    if (si_status st = k::tr_rms_norm(d->hidden, nullptr, d->attn_norm[0], nullptr, nullptr, d->normalized, B, H,
+                                      c.epsilon, s))
+        return st;
+    for (int l = 0; l < c.layers; ++l) {
+        if (si_status st = proj(c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
+        if (si_status st = k::tr_rope_kv_write_streams(d->qkv, d->st_positions, d->freq, d->query, d->key_cache[l],
+                                                       d->value_cache[l], B, H, KV, c.head_size, c.rotary_size,
+                                                       c.context, stride, c.rope_scale, s))
+            return st;
+        if (si_status st = k::tr_attention_decode_streams(d->query, d->key_cache[l], d->value_cache[l],
+                                                          d->st_positions, d->attention, int(B), c.query_heads,
+                                                          c.kv_heads, c.head_size, c.context, stride, s))
+            return st;
+        if (si_status st = proj(c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
+        if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, B,
+                                          H, c.epsilon, s))
+            return st;
+        if (si_status st = proj(c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
+        if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, B, F, s)) return st;
+        if (si_status st = proj(c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
+        const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
+        if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, B, H,
+                                          c.epsilon, s))
+            return st;
+    }
+    if (si_status st = proj(c.embedding_type, d->embedding, d->normalized, d->logits, c.vocab, H)) return st;
+    return k::tr_argmax_rows(d->logits, B, c.vocab, d->st_next, sfeed, s);
+}
+
+si_status build_streams_graph(si_decoder *d, k::StreamsFeed *sfeed, cudaGraphExec_t *out) {
+    if (si_status st = cuda(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture"))
+        return st;
+    const si_status rec = record_step_streams(d, sfeed);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(d->stream, &g);
+    if (rec != SI_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rec;
+    }
+    if (e != cudaSuccess) return cuda(e, "cudaStreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return cuda(ie, "cudaGraphInstantiate");
+}
+
+// Host-side checks of a multi-stream call: every stream's token in the
+// vocabulary and positions [p, p + steps) inside the context.
+si_status check_streams(si_decoder *d, const int32_t *tokens, const int32_t *positions, int32_t steps) {
+    if (d->streams < 2) return fail(SI_ERR_INVALID_ARGUMENT, "not a multi-stream session");
+    for (int32_t b = 0; b < d->streams; ++b) {
+        if (tokens[b] < 0 || tokens[b] >= d->cfg.vocab)
+            return fail(SI_ERR_INVALID_ARGUMENT, "stream %d: token %d outside the vocabulary", b, tokens[b]);
+        if (positions[b] < 0 || int64_t(positions[b]) + steps > d->cfg.context)
+            return fail(SI_ERR_INVALID_ARGUMENT,
+                        "stream %d: positions %d..%d exceed the GPU KV cache capacity of %lld tokens", b,
+                        positions[b], positions[b] + steps - 1, (long long)d->cfg.context);
+    }
+    return SI_OK;
+}
+
+si_status upload_streams(si_decoder *d, const int32_t *tokens, const int32_t *positions, bool start) {
+    const size_t B = size_t(d->streams);
+    cudaStream_t s = d->stream;
+    std::memcpy(d->pinned_st, tokens, B * 4);
+    std::memcpy(d->pinned_st + B, positions, B * 4);
+    if (si_status st = cuda(cudaMemcpyAsync(d->st_tokens, d->pinned_st, B * 4, cudaMemcpyHostToDevice, s), "upload"))
+        return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->st_positions, d->pinned_st + B, B * 4, cudaMemcpyHostToDevice, s),
+                            "upload"))
+        return st;
+    if (start)
+        return cuda(cudaMemcpyAsync(d->st_start, d->pinned_st + B, B * 4, cudaMemcpyHostToDevice, s), "upload");
     return SI_OK;
 }
 
@@ -395,10 +503,12 @@ si_status validate(const si_decoder_config *c) {
 
 si_status create_step(si_decoder *d);
 
-si_status create(int device, const si_decoder_config *c, si_peer_group *group, si_decoder **out) {
+si_status create(int device, const si_decoder_config *c, si_peer_group *group, int32_t streams, si_decoder **out) {
     auto *d = new si_decoder();
     d->device = device;
     d->cfg = *c;
+    d->streams = streams;
+    const uint64_t B = uint64_t(streams);
     auto cleanup = [&](si_status st) {
         destroy(d);
         return st;
@@ -457,9 +567,10 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, s
         if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(shard(H, nullptr)), &p))
             return cleanup(st);
         d->w_down.push_back(p);
-        if (si_status st = alloc_typed(d, "key_cache_" + L, uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "key_cache_" + L, B * uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
         d->key_cache.push_back(f);
-        if (si_status st = alloc_typed(d, "value_cache_" + L, uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "value_cache_" + L, B * uint64_t(c->context) * KV * 4, &f))
+            return cleanup(st);
         d->value_cache.push_back(f);
     }
     // rope_frequencies initializer (Phi4D3D12TextSession.cs:394-398).
@@ -496,9 +607,24 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, s
         if (off != UINT64_MAX) {
             *a.dst = reinterpret_cast<float *>(d->arena + off);
             d->slots[name] = {d->arena + off, uint64_t(a.n) * 4};
-        } else if (si_status st = alloc_typed(d, a.name, uint64_t(a.n) * 4, a.dst)) {
+        } else if (si_status st = alloc_typed(d, a.name, B * uint64_t(a.n) * 4, a.dst)) {
             return cleanup(st);
         }
+    }
+    if (streams > 1) {
+        const uint64_t cap = uint64_t(c->context);
+        if (si_status st = alloc_typed(d, "stream_tokens", B * 4, &d->st_tokens)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "stream_positions", B * 4, &d->st_positions)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "stream_start", B * 4, &d->st_start)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "stream_next", B * 4, &d->st_next)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "stream_history", B * cap * 4, &d->st_history)) return cleanup(st);
+        if (si_status st = alloc_typed(d, "stream_feed", sizeof(k::StreamsFeed), &d->st_feed)) return cleanup(st);
+        const k::StreamsFeed feed{d->st_tokens, d->st_positions, d->st_start, d->st_history, int32_t(cap), streams};
+        if (si_status st = cuda(cudaMemcpy(d->st_feed, &feed, sizeof feed, cudaMemcpyHostToDevice), "cudaMemcpy"))
+            return cleanup(st);
+        if (si_status st = cuda(cudaMallocHost(reinterpret_cast<void **>(&d->pinned_st), (3 * B + B * cap) * 4),
+                                "cudaMallocHost"))
+            return cleanup(st);
     }
     if (si_status st = alloc_typed(d, "control", 8, &d->control)) return cleanup(st);
     if (si_status st = alloc_typed(d, "next_token", 4, &d->next_token)) return cleanup(st);
@@ -511,7 +637,7 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, s
     d->pinned_feed = reinterpret_cast<k::DecodeFeed *>(reinterpret_cast<uint8_t *>(d->pinned) + 64);
     d->pinned_prompt = reinterpret_cast<int32_t *>(d->pinned_feed + 1);
     d->pinned_history = d->pinned_prompt + c->context;
-    if (!group)
+    if (!group && streams == 1)
         if (si_status st = create_step(d)) return cleanup(st);
     if (si_status st = cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return cleanup(st);
     *out = d;
@@ -593,7 +719,7 @@ si_status si_decoder_create(int device, const si_decoder_config *config, si_deco
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, nullptr, out);
+    return create(device, config, nullptr, 1, out);
 }
 
 si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *bytes) {
@@ -633,7 +759,7 @@ si_status si_decoder_create_sharded(int device, const si_decoder_config *config,
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, group, out);
+    return create(device, config, group, 1, out);
 }
 
 si_status si_decoder_destroy(si_decoder *decoder) {
@@ -752,7 +878,9 @@ si_status si_decoder_prefill(si_decoder *d, const int32_t *prompt, int32_t promp
                 return fail(SI_ERR_INVALID_ARGUMENT, "prompt token %d (%d) outside the vocabulary", i, prompt[i]);
         if (!d->group && k::tr_prefill_attention_supported(d->cfg.head_size)) {
             DeviceScope scope(d->device);
-            return prefill(d, prompt, nullptr, prompt_tokens, next_token);
+            if (si_status st = prefill(d, prompt, nullptr, prompt_tokens, d->position, 0, next_token)) return st;
+            d->position += prompt_tokens;
+            return SI_OK;
         }
     }
     // Head sizes the fused prefill attention does not cover, and row-sharded
@@ -774,7 +902,90 @@ si_status si_decoder_prefill_embeddings(si_decoder *d, const float *embeddings, 
         return fail(SI_ERR_UNSUPPORTED, "prefill attention supports head sizes 64, 128, 192 and 256");
     if (d->group) return fail(SI_ERR_UNSUPPORTED, "embedding prefill is not available in a row-sharded session");
     DeviceScope scope(d->device);
-    return prefill(d, nullptr, embeddings, rows, next_token);
+    if (si_status st = prefill(d, nullptr, embeddings, rows, d->position, 0, next_token)) return st;
+    d->position += rows;
+    return SI_OK;
+}
+
+si_status si_decoder_create_streams(int device, const si_decoder_config *config, int32_t streams,
+                                    si_decoder **out) {
+    if (!out) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (streams < 1 || streams > 1024) return fail(SI_ERR_INVALID_ARGUMENT, "streams must be 1..1024");
+    if (si_status st = validate(config)) return st;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SI_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
+    DeviceScope scope(device);
+    return create(device, config, nullptr, streams, out);
+}
+
+
+si_status si_decoder_step_streams(si_decoder *d, const int32_t *tokens, const int32_t *positions,
+                                  int32_t *next_tokens) {
+    if (!d || !tokens || !positions || !next_tokens) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (si_status st = check_streams(d, tokens, positions, 1)) return st;
+    DeviceScope scope(d->device);
+    if (!d->streams_exec)
+        if (si_status st = build_streams_graph(d, nullptr, &d->streams_exec)) return st;
+    const size_t B = size_t(d->streams);
+    cudaStream_t s = d->stream;
+    if (si_status st = upload_streams(d, tokens, positions, false)) return st;
+    if (si_status st = cuda(cudaGraphLaunch(d->streams_exec, s), "cudaGraphLaunch")) return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->pinned_st + 2 * B, d->st_next, B * 4, cudaMemcpyDeviceToHost, s),
+                            "readback"))
+        return st;
+    if (si_status st = cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return st;
+    std::memcpy(next_tokens, d->pinned_st + 2 * B, B * 4);
+    return SI_OK;
+}
+
+si_status si_decoder_generate_streams(si_decoder *d, const int32_t *tokens, const int32_t *positions, int32_t steps,
+                                      int32_t *out) {
+    if (!d || !tokens || !positions || !out) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    if (steps < 1) return fail(SI_ERR_INVALID_ARGUMENT, "steps must be positive");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (si_status st = check_streams(d, tokens, positions, steps)) return st;
+    DeviceScope scope(d->device);
+    if (!d->streams_feed_exec)
+        if (si_status st = build_streams_graph(d, d->st_feed, &d->streams_feed_exec)) return st;
+    const size_t B = size_t(d->streams);
+    cudaStream_t s = d->stream;
+    if (si_status st = upload_streams(d, tokens, positions, true)) return st;
+    for (int32_t i = 0; i < steps; ++i)
+        if (si_status st = cuda(cudaGraphLaunch(d->streams_feed_exec, s), "cudaGraphLaunch")) return st;
+    if (si_status st = cuda(cudaMemcpyAsync(d->pinned_st + 3 * B, d->st_history, size_t(steps) * B * 4,
+                                            cudaMemcpyDeviceToHost, s),
+                            "readback"))
+        return st;
+    if (si_status st = cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return st;
+    std::memcpy(out, d->pinned_st + 3 * B, size_t(steps) * B * 4);
+    return SI_OK;
+}
+
+si_status si_decoder_prefill_stream(si_decoder *d, int32_t stream, const int32_t *prompt, int32_t prompt_tokens,
+                                    int32_t start, int32_t *next_token) {
+    if (!d || !prompt || !next_token) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(d->lock);
+    if (stream < 0 || stream >= d->streams)
+        return fail(SI_ERR_INVALID_ARGUMENT, "stream %d outside [0, %d)", stream, d->streams);
+    if (prompt_tokens <= 0 || start < 0)
+        return fail(SI_ERR_INVALID_ARGUMENT, "prompt_tokens must be positive and start >= 0");
+    if (int64_t(start) + prompt_tokens > d->cfg.context)
+        return fail(SI_ERR_INVALID_ARGUMENT, "The GPU KV cache capacity of %lld tokens has been reached.",
+                    (long long)d->cfg.context);
+    for (int32_t i = 0; i < prompt_tokens; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->cfg.vocab)
+            return fail(SI_ERR_INVALID_ARGUMENT, "prompt token %d (%d) outside the vocabulary", i, prompt[i]);
+    if (d->group || !k::tr_prefill_attention_supported(d->cfg.head_size))
+        return fail(SI_ERR_UNSUPPORTED, "stream prefill needs the fused prefill attention (head size 64/128/192/256)");
+    DeviceScope scope(d->device);
+    const int64_t offset = int64_t(stream) * d->cfg.context * int64_t(d->cfg.kv_heads) * d->cfg.head_size;
+    return prefill(d, prompt, nullptr, prompt_tokens, start, offset, next_token);
 }
 
 si_status si_decoder_reset(si_decoder *d) {

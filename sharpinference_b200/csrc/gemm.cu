@@ -131,26 +131,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int pt = threadIdx.x - 64, r = pt >> 1, h = pt & 1;  // row 0..127, half 0..1
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
-        RawHalf<FMT> raw, next;
-        if (valid_row && iters > 0) fetch_weights32<FMT>(wrow, it0 * kBK, h, raw);
-        for (int it = 0; it < iters; ++it) {
+        produce_weights<FMT>(wrow, valid_row, it0, iters, h, [&](int it, const float(&w)[32]) {
             const int s = it % kStages;
-            // the next stage's bytes are in flight while this one is decoded
-            if (valid_row && it + 1 < iters) fetch_weights32<FMT>(wrow, (it0 + it + 1) * kBK, h, next);
-            float w[32];
-            if (valid_row) {
-                decode_weights32<FMT>(raw, h, w);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
-            }
-            raw = next;
             if (it >= kStages) mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kErrEmptyBarrierTimeout);
             uint8_t *st = smem + s * kStageBytes;
             store_split_half(w, r, h, st, st + kATile);
             fence_proxy_async();
             mbar_arrive(&full[s]);
-        }
+        });
         // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32*(warp%4) ..;
         // warps 2..5 drain the first half of the columns, warps 6..9 the second.
         mbar_wait(accum, 0, kErrMmaBarrierTimeout);

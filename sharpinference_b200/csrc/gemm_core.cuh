@@ -227,11 +227,18 @@ __device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, f
         const int b = ((2 * j) & 3) + h;  // sub-block byte of this half
         const float a = h16(hd.x) * float((scw >> (8 * b)) & 0xffu);
         const float c = h16(hd.x >> 16) * float((mnw >> (8 * b)) & 0xffu);
+        // nibble -> float without the conversion pipe: the byte placed under
+        // the exponent of 2^23 (byte permute) gives 2^23 + q exactly.
         const int shift = 4 * h;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t nib = (q[i] >> shift) & 0x0F0F0F0Fu;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) w[4 * i + t] = a * float((q[i] >> (8 * t + shift)) & 15u) - c;
+            for (int t = 0; t < 4; ++t) {
+                const float f = __uint_as_float(__byte_perm(nib, 0x4B000000u, uint32_t(t) | 0x7650u)) - 8388608.0f;
+                w[4 * i + t] = a * f - c;
+            }
+        }
     } else if constexpr (FMT == SI_TYPE_Q8_0) {
         uint32_t wv[9];
 #pragma unroll
@@ -241,6 +248,8 @@ __device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, f
         wv[8] = r.extra;
         // the block starts at byte 0 (h = 0) or 2 (h = 1) of the window;
         // two unrolled copies keep every word index a constant
+        // int8 -> float without the conversion pipe: with the sign bit
+        // flipped the byte is q + 128, placed under the exponent of 2^23.
         auto decode = [&](auto offset) {
             constexpr int o = decltype(offset)::value;
             const float d = h16(o == 0 ? (wv[0] & 0xffffu) : (wv[0] >> 16));
@@ -248,7 +257,10 @@ __device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, f
             for (int e = 0; e < 32; ++e) {
                 constexpr int base = o + 2;
                 const int byte = base + e;
-                w[e] = d * float(int8_t((wv[byte >> 2] >> (8 * (byte & 3))) & 0xffu));
+                const uint32_t biased = wv[byte >> 2] ^ 0x80808080u;
+                const float f = __uint_as_float(__byte_perm(biased, 0x4B000000u, uint32_t(byte & 3) | 0x7650u)) -
+                                8388736.0f;  // 2^23 + 128
+                w[e] = d * f;
             }
         };
         if (r.j == 0) decode(std::integral_constant<int, 0>{});
@@ -268,6 +280,45 @@ __device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, f
         for (int i = 0; i < 8; ++i) {
             w[4 * i] = __uint_as_float(r.v[i].x), w[4 * i + 1] = __uint_as_float(r.v[i].y);
             w[4 * i + 2] = __uint_as_float(r.v[i].z), w[4 * i + 3] = __uint_as_float(r.v[i].w);
+        }
+    }
+}
+
+// Stages of raw weight bytes a producer thread keeps in flight (deeper
+// rings measured slower: the producers are bound by instruction issue, and
+// the ring costs registers).
+template <int FMT>
+struct PrefetchDepth {
+    static constexpr int value = 2;
+};
+
+// A producer thread's loop over its K stages: decodes stage it's 32 weights
+// (fetched PrefetchDepth stages earlier into a register ring), refills the
+// ring slot with stage it + depth, then hands the weights to emit(it, w),
+// which waits for the shared-memory slot, stores and arrives. The loop is
+// unrolled by the depth so every ring index is a constant.
+template <int FMT, class Emit>
+__device__ __forceinline__ void produce_weights(const uint8_t *wrow, bool valid, int it0, int iters, int h,
+                                                Emit &&emit) {
+    constexpr int D = PrefetchDepth<FMT>::value;
+    RawHalf<FMT> ring[D];
+#pragma unroll
+    for (int u = 0; u < D; ++u)
+        if (valid && u < iters) fetch_weights32<FMT>(wrow, (it0 + u) * kGemmBK, h, ring[u]);
+    for (int base = 0; base < iters; base += D) {
+#pragma unroll
+        for (int u = 0; u < D; ++u) {
+            const int it = base + u;
+            if (it >= iters) break;
+            float w[32];
+            if (valid) {
+                decode_weights32<FMT>(ring[u], h, w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
+            }
+            if (valid && it + D < iters) fetch_weights32<FMT>(wrow, (it0 + it + D) * kGemmBK, h, ring[u]);
+            emit(it, w);
         }
     }
 }

@@ -9,9 +9,10 @@
 //   * The MMA is M = 128 weight rows x N = BN input rows (16, 32 or 64), so
 //     the tensor work follows the rows that exist, and the kernel is bound
 //     by the weight stream rather than by the MMA.
-//   * No workspace: warp 0 loads the FP32 X tile of each stage itself,
-//     splits it into hi/lo and stores both in the swizzled layout the MMA
-//     reads (X is a few hundred KB and stays in L2).
+//   * No workspace: the TMA lands each stage's FP32 X tile in shared
+//     memory a few stages ahead (a 2-D tensor map over X, no multicast) and
+//     the weight producers split it into hi/lo in the swizzled layout the
+//     MMA reads, a few 8-column units each.
 //   * K is split over the CTAs of a thread-block cluster (z), so a narrow
 //     weight matrix still spreads over the SMs; the partial accumulators
 //     are summed through distributed shared memory by the cluster's first
@@ -35,18 +36,23 @@ namespace si::dev {
 namespace {
 
 constexpr int kSkThreads = 64 + kProducers;  // 10 warps
-constexpr int kSkStages = 4;
 
+// Stage = weight hi / lo tiles (128 x 64 BF16 each), X hi / lo tiles
+// (BN x 64 BF16 each) and the FP32 X tile the TMA lands (BN x 64, row-major,
+// converted by warp 0 into the X hi / lo tiles).
 template <int BN>
 struct SkinnyCfg {
+    static constexpr int kStages = BN >= 64 ? 3 : 4;
     static constexpr uint32_t kATile = kGemmBM * kGemmBK * 2;  // 16 KB (one of hi / lo)
     static constexpr uint32_t kBTile = BN * kGemmBK * 2;       // BN rows of 128 B
-    static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+    static constexpr uint32_t kXTile = BN * kGemmBK * 4;       // FP32 X as loaded
+    static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile + kXTile;
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     static constexpr uint32_t kIdesc = mma_idesc(BN);
     static constexpr int kRedStride = BN + 1;  // padded row of the split-K exchange buffer
-    static constexpr size_t kSmem = size_t(kSkStages) * kStageBytes + 1024 + 256;
-    static_assert(size_t(kGemmBM) * kRedStride * 4 <= size_t(kSkStages) * kStageBytes, "exchange buffer");
+    static constexpr size_t kSmem = size_t(kStages) * kStageBytes + 1024 + 256;
+    static_assert(size_t(kGemmBM) * kRedStride * 4 <= size_t(kStages) * kStageBytes, "exchange buffer");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct SkinnyParams {
@@ -79,14 +85,17 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
 }
 
 template <int FMT, int BN>
-__global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const SkinnyParams p) {
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap xmap, const SkinnyParams p) {
     using Cfg = SkinnyCfg<BN>;
+    constexpr int kSkStages = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-byte aligned tiles
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kSkStages * Cfg::kStageBytes);
     uint64_t *empty = full + kSkStages;
-    uint64_t *accum = empty + kSkStages;
+    uint64_t *xfull = empty + kSkStages;  // the FP32 X tile of the stage has landed
+    uint64_t *accum = xfull + kSkStages;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,8 +107,9 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const Skinny
     pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSkStages; ++s) {
-            mbar_init(&full[s], kProducers + 32);  // weight producers + the X warp
+            mbar_init(&full[s], kProducers);  // weight producers (they also convert X)
             mbar_init(&empty[s], 1);
+            mbar_init(&xfull[s], 1);
         }
         mbar_init(accum, 1);
         fence_barrier_init();
@@ -117,39 +127,20 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const Skinny
 
     float acc[BN < 32 ? 32 : BN];  // epilogue warps: this thread's weight row, BN input rows
     if (warp == 0) {
-        // X producer: FP32 rows of the stage -> BF16 hi / lo, swizzled.
+        // X: the TMA brings each stage's FP32 tile (rows past m read as
+        // zeros) into the stage's staging area as soon as the stage slot is
+        // free, up to kSkStages stages ahead; the producers convert it.
         pdl_wait();
-        for (int it = 0; it < iters; ++it) {
-            const int s = it % kSkStages;
-            if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
-            uint8_t *hi_tile = smem + s * Cfg::kStageBytes + 2 * Cfg::kATile;
-            uint8_t *lo_tile = hi_tile + Cfg::kBTile;
-            for (int r = lane; r < BN; r += 32) {
-                const int t = t0 + r;
-                const float4 *src = reinterpret_cast<const float4 *>(p.x + size_t(t) * p.k + size_t(it0 + it) * kGemmBK);
-                uint8_t *hi_row = hi_tile + (r >> 3) * 1024 + (r & 7) * 128;
-                uint8_t *lo_row = lo_tile + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-                    if (t < p.m) a = __ldg(src + 2 * c), b = __ldg(src + 2 * c + 1);
-                    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                    uint32_t hv[4], lv[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t hb = pack_bf16(v[2 * q], v[2 * q + 1]);
-                        hv[q] = hb;
-                        lv[q] = pack_bf16(v[2 * q] - __uint_as_float(hb << 16),
-                                          v[2 * q + 1] - __uint_as_float(hb & 0xffff0000u));
-                    }
-                    const int pc = c ^ (r & 7);
-                    *reinterpret_cast<uint4 *>(hi_row + pc * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                    *reinterpret_cast<uint4 *>(lo_row + pc * 16) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-                }
+        if (lane == 0) {
+            for (int q = 0; q < iters; ++q) {
+                const int sq = q % kSkStages;
+                if (q >= kSkStages) mbar_wait(&empty[sq], ((q / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
+                uint8_t *xs = smem + sq * Cfg::kStageBytes + 2 * Cfg::kATile + 2 * Cfg::kBTile;
+                mbar_arrive_expect_tx(&xfull[sq], Cfg::kXTile);
+                tma_load_2d(xs, &xmap, (it0 + q) * kGemmBK, t0, &xfull[sq]);
             }
-            fence_proxy_async();
-            mbar_arrive(&full[s]);
         }
+        __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             for (int it = 0; it < iters; ++it) {
@@ -179,26 +170,40 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_skinny_kernel(const Skinny
         const int pt = threadIdx.x - 64, r = pt >> 1, h = pt & 1;  // row 0..127, half 0..1
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
-        RawHalf<FMT> raw, next;
-        if (valid_row && iters > 0) fetch_weights32<FMT>(wrow, it0 * kGemmBK, h, raw);
-        for (int it = 0; it < iters; ++it) {
+        produce_weights<FMT>(wrow, valid_row, it0, iters, h, [&](int it, const float(&w)[32]) {
             const int s = it % kSkStages;
-            // the next stage's bytes are in flight while this one is decoded
-            if (valid_row && it + 1 < iters) fetch_weights32<FMT>(wrow, (it0 + it + 1) * kGemmBK, h, next);
-            float w[32];
-            if (valid_row) {
-                decode_weights32<FMT>(raw, h, w);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
-            }
-            raw = next;
             if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
             uint8_t *st = smem + s * Cfg::kStageBytes;
             store_split_half(w, r, h, st, st + Cfg::kATile);
+            // this thread's share of the stage's X tile: units of 8 columns
+            // of one row, FP32 staging -> BF16 hi / lo, swizzled
+            mbar_wait(&xfull[s], (it / kSkStages) & 1, kErrFullBarrierTimeout);
+            uint8_t *hi_tile = st + 2 * Cfg::kATile;
+            uint8_t *lo_tile = hi_tile + Cfg::kBTile;
+            const float *xs = reinterpret_cast<const float *>(hi_tile + 2 * Cfg::kBTile);
+#pragma unroll
+            for (int u = pt; u < BN * 8; u += kProducers) {
+                const int xr = u >> 3, c = u & 7;
+                const float4 a = *reinterpret_cast<const float4 *>(xs + xr * kGemmBK + 8 * c);
+                const float4 b = *reinterpret_cast<const float4 *>(xs + xr * kGemmBK + 8 * c + 4);
+                const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                uint32_t hv[4], lv[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t hb = pack_bf16(v[2 * q], v[2 * q + 1]);
+                    hv[q] = hb;
+                    lv[q] = pack_bf16(v[2 * q] - __uint_as_float(hb << 16),
+                                      v[2 * q + 1] - __uint_as_float(hb & 0xffff0000u));
+                }
+                const int pc = c ^ (xr & 7);
+                *reinterpret_cast<uint4 *>(hi_tile + (xr >> 3) * 1024 + (xr & 7) * 128 + pc * 16) =
+                    make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4 *>(lo_tile + (xr >> 3) * 1024 + (xr & 7) * 128 + pc * 16) =
+                    make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
             fence_proxy_async();
             mbar_arrive(&full[s]);
-        }
+        });
         // TMEM lane quarter (warp % 4) holds weight rows 32 * (warp % 4) ..;
         // warps 2..5 drain it.
         if (warp < 6) {
@@ -269,6 +274,33 @@ int sm_count() {
     return sms;
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// FP32 X [m, k] as a 2-D tensor map with a 64-column x BN-row box, no
+// swizzle; rows past m read as zeros.
+si_status make_x_map_f32(CUtensorMap *map, const float *x, int m, int k, int bn) {
+    static EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    if (!fn) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
+    const cuuint64_t strides[1] = {cuuint64_t(k) * 4};
+    const cuuint32_t box[2] = {cuuint32_t(kGemmBK), cuuint32_t(bn)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled (X) failed (%d)", int(r));
+    return SI_OK;
+}
+
 template <int FMT, int BN>
 si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
     using Cfg = SkinnyCfg<BN>;
@@ -300,7 +332,9 @@ si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
     attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+    CUtensorMap xmap;
+    if (si_status ms = make_x_map_f32(&xmap, p.x, p.m, p.k, BN)) return ms;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, xmap, p);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(SI_ERR_CUDA, "tcgen05 few-row GEMM launch failed: %s", cudaGetErrorString(e));

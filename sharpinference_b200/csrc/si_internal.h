@@ -115,6 +115,18 @@ struct DecodeFeed {
     int32_t capacity;
     int32_t pad;
 };
+// Multi-stream greedy loop state read by the per-row argmax: row b stores
+// its token in history[(positions[b] - start[b]) * streams + b] (when
+// within `capacity` steps), then sets tokens[b] = the token and
+// positions[b] += 1 for the next step.
+struct StreamsFeed {
+    int32_t *tokens;
+    int32_t *positions;
+    const int32_t *start;
+    int32_t *history;
+    int32_t capacity;
+    int32_t streams;
+};
 si_status tr_gather_row(uint32_t type, const void *table, int64_t rows, int64_t cols, const int32_t *index, float *out,
                         void *stream);
 // core.gather-row for `count` indices at once (rows of a prefill chunk).
@@ -152,6 +164,17 @@ si_status tr_prefill_attention(const float *query, const float *kc, const float 
                                float *out, int query_heads, int kv_heads, int head_size, int64_t context,
                                void *stream);
 si_status tr_argmax(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, void *stream);
+// argmax of each of `rows` rows of n floats into out[row].
+si_status tr_argmax_rows(const float *in, int64_t rows, int64_t n, int32_t *out, StreamsFeed *sfeed, void *stream);
+// Multi-stream decode forms: row b is stream b's token at positions[b];
+// stream b's caches start cache_stride floats after stream b - 1's.
+si_status tr_rope_kv_write_streams(const float *qkv, const int32_t *positions, const float *freq, float *query,
+                                   float *key_cache, float *value_cache, int64_t streams, int64_t qsize,
+                                   int64_t kvsize, int head_size, int rotary, int64_t context, int64_t cache_stride,
+                                   float rope_scale, void *stream);
+si_status tr_attention_decode_streams(const float *query, const float *kc, const float *vc, const int32_t *positions,
+                                      float *out, int streams, int query_heads, int kv_heads, int head_size,
+                                      int64_t context, int64_t cache_stride, void *stream);
 si_status tr_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width,
                          void *stream);
 si_status tr_gather_rows(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,

@@ -255,9 +255,12 @@ __global__ void scaled_add_kernel(const float *in, const float *update, float *o
 // position is *position and there is one row; batch form: row b is the
 // token at control[0] + b, rows b >= control[1] are skipped. Rows whose
 // position is outside [0, context) write nothing.
+// Multi-stream form (positions non-null): row b is stream b's token at
+// positions[b], written into stream b's caches (cache_stride floats apart).
 __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const int32_t *control, const float *freq,
                                float *query, float *key_cache, float *value_cache, int64_t batch, int64_t qsize,
-                               int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale) {
+                               int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale,
+                               const int32_t *positions, int64_t cache_stride) {
     pdl_trigger();
     pdl_wait();
     const int64_t width = qsize + 2 * kvsize, count = batch * width;
@@ -265,7 +268,11 @@ __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const 
     for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < count; e += int64_t(gridDim.x) * blockDim.x) {
         const int64_t row = e / width, local = e - row * width;
         int32_t pos;
-        if (control) {
+        int64_t cache_row = 0;
+        if (positions) {
+            pos = positions[row];
+            cache_row = row * cache_stride;
+        } else if (control) {
             if (row >= control[1]) continue;
             pos = control[0] + int32_t(row);
         } else {
@@ -285,9 +292,9 @@ __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const 
                              : __fadd_rn(__fmul_rn(v, c), __fmul_rn(other, s));
             }
             if (is_query) query[row * qsize + local] = v;
-            else key_cache[int64_t(pos) * kvsize + (local - qsize)] = v;
+            else key_cache[cache_row + int64_t(pos) * kvsize + (local - qsize)] = v;
         } else {
-            value_cache[int64_t(pos) * kvsize + (local - qsize - kvsize)] = v;
+            value_cache[cache_row + int64_t(pos) * kvsize + (local - qsize - kvsize)] = v;
         }
     }
 }
@@ -303,10 +310,15 @@ constexpr int kAttnWarps = 8;
 // for the G query heads of the group. Lane j holds channels j + 32 i.
 
 
+// Several streams (a multi-stream session): cluster u serves key/value head
+// u % kv_heads of stream u / kv_heads, whose query / output rows are
+// q_stride floats apart, caches cache_stride floats apart and whose
+// position is position[stream].
 template <int NPL, int MAXG, int kTile>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
     gqa_decode_kernel(const float *query, const float *key_cache, const float *value_cache, const int32_t *position,
-                      float *out, int group, int kv_heads, int head_size, int64_t context, float scale) {
+                      float *out, int group, int kv_heads, int head_size, int64_t context, float scale,
+                      int64_t q_stride, int64_t cache_stride) {
     extern __shared__ float smem[];
     const int G = group, hs = head_size;
     float *w_acc = smem;                                 // [warps][G][hs]
@@ -316,11 +328,15 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
     float *c_m = c_acc + G * hs;                         // [G]
     float *c_l = c_m + G;                                // [G]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kvh = blockIdx.x / kAttnCluster;
+    const int unit = blockIdx.x / kAttnCluster, kvh = unit % kv_heads, strm = unit / kv_heads;
+    query += strm * q_stride;
+    out += strm * q_stride;
+    key_cache += strm * cache_stride;
+    value_cache += strm * cache_stride;
     const uint32_t rank = cta_rank_in_cluster();
     pdl_trigger();
     pdl_wait();
-    int64_t active = *position;
+    int64_t active = position[strm];
     active = active < 0 ? 0 : (active > context - 1 ? context - 1 : active);
     const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
@@ -749,19 +765,24 @@ __device__ __forceinline__ void argmax_merge(float &b, uint32_t &bi, float o, ui
     }
 }
 
-// transformer.argmax over one 8-CTA cluster. With `feed` set (device-side
-// greedy loop) it also records the token and prepares the next step's
-// control: position + 1 and the next prompt token or the argmax.
+// transformer.argmax over one 8-CTA cluster per row (rows n floats apart;
+// one row unless a multi-stream session runs one per stream). With `feed`
+// set (device-side greedy loop) it also records the token and prepares the
+// next step's control: position + 1 and the next prompt token or the
+// argmax. With `sfeed` (multi-stream greedy loop) row b records its token
+// in stream b's history, and sets stream b's next token and position.
 __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
-    argmax_kernel(const float *in, int64_t n, int32_t *out, DecodeFeed *feed) {
+    argmax_kernel(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, StreamsFeed *sfeed) {
     __shared__ float sb[32];
     __shared__ uint32_t si[32];
     pdl_trigger();
     pdl_wait();
+    const int64_t row = blockIdx.x / kArgmaxCluster;
+    in += row * n;
     float b = kNegMax;
     uint32_t bi = 0;
-    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-    for (int64_t j = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; j < n; j += stride)
+    const int64_t stride = int64_t(kArgmaxCluster) * blockDim.x;
+    for (int64_t j = (blockIdx.x % kArgmaxCluster) * int64_t(blockDim.x) + threadIdx.x; j < n; j += stride)
         argmax_merge(b, bi, in[j], uint32_t(j));
     for (int o = 16; o > 0; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, b, o);
@@ -794,12 +815,18 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
         uint32_t idx = si[0];
         for (uint32_t r = 1; r < kArgmaxCluster; ++r)
             argmax_merge(best, idx, dsmem_f32(dsmem_addr(sb, r)), dsmem_u32(dsmem_addr(si, r)));
-        *out = int32_t(idx);
+        out[row] = int32_t(idx);
         if (feed) {
             const int32_t pos = feed->control[1], k = pos - feed->base;
             if (k >= 0 && k < feed->capacity) feed->history[k] = int32_t(idx);
             feed->control[1] = pos + 1;
             feed->control[0] = k + 1 < feed->prompt_tokens ? feed->prompt[k + 1] : int32_t(idx);
+        }
+        if (sfeed) {
+            const int32_t pos = sfeed->positions[row], k = pos - sfeed->start[row];
+            if (k >= 0 && k < sfeed->capacity) sfeed->history[int64_t(k) * sfeed->streams + row] = int32_t(idx);
+            sfeed->positions[row] = pos + 1;
+            sfeed->tokens[row] = int32_t(idx);
         }
     }
     cluster_sync();  // rank 0 has read every CTA's candidate
@@ -922,13 +949,25 @@ si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int3
     const int64_t count = batch * (qsize + 2 * kvsize);
     return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
                   stream, qkv, position, control, freq, query, key_cache, value_cache, batch, qsize, kvsize, head_size,
-                  rotary, context, rope_scale);
+                  rotary, context, rope_scale, static_cast<const int32_t *>(nullptr), int64_t(0));
+}
+
+si_status tr_rope_kv_write_streams(const float *qkv, const int32_t *positions, const float *freq, float *query,
+                                   float *key_cache, float *value_cache, int64_t streams, int64_t qsize,
+                                   int64_t kvsize, int head_size, int rotary, int64_t context, int64_t cache_stride,
+                                   float rope_scale, void *stream) {
+    const int64_t count = streams * (qsize + 2 * kvsize);
+    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+                  stream, qkv, static_cast<const int32_t *>(nullptr), static_cast<const int32_t *>(nullptr), freq,
+                  query, key_cache, value_cache, streams, qsize, kvsize, head_size, rotary, context, rope_scale,
+                  positions, cache_stride);
 }
 
 namespace {
 template <int NPL, int MAXG, int kTile>
 si_status launch_gqa(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
-                     int group, int kv_heads, int head_size, int64_t context, float scale, void *stream) {
+                     int group, int kv_heads, int head_size, int64_t context, float scale, int streams,
+                     int64_t q_stride, int64_t cache_stride, void *stream) {
     auto kernel = gqa_decode_kernel<NPL, MAXG, kTile>;
     const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
                                2 * group) * sizeof(float);
@@ -939,19 +978,28 @@ si_status launch_gqa(const float *query, const float *kc, const float *vc, const
             raised = true;
         }
     }
-    return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(kv_heads * kAttnCluster)),
+    return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(streams * kv_heads * kAttnCluster)),
                   dim3(kAttnWarps * 32), smem, stream, query, kc, vc, position, out, group, kv_heads, head_size,
-                  context, scale);
+                  context, scale, q_stride, cache_stride);
 }
 }  // namespace
 
 si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                               int query_heads, int kv_heads, int head_size, int64_t context, void *stream) {
+    return tr_attention_decode_streams(query, kc, vc, position, out, 1, query_heads, kv_heads, head_size, context, 0,
+                                       stream);
+}
+
+si_status tr_attention_decode_streams(const float *query, const float *kc, const float *vc, const int32_t *position,
+                                      float *out, int streams, int query_heads, int kv_heads, int head_size,
+                                      int64_t context, int64_t cache_stride, void *stream) {
     const int group = query_heads / kv_heads;
     const float scale = 1.0f / sqrtf(float(head_size));
     const int npl = (head_size + 31) / 32;
-#define SI_GQA(NPL, MAXG, TILE) \
-    launch_gqa<NPL, MAXG, TILE>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, stream)
+    const int64_t q_stride = int64_t(query_heads) * head_size;
+#define SI_GQA(NPL, MAXG, TILE)                                                                                   \
+    launch_gqa<NPL, MAXG, TILE>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, streams, \
+                                q_stride, cache_stride, stream)
     if (group <= 4) {
         if (npl <= 1) return SI_GQA(1, 4, 8);
         if (npl <= 2) return SI_GQA(2, 4, 8);
@@ -1035,7 +1083,12 @@ si_status tr_gqa_values(const float *probs, const float *vc, const int32_t *posi
 
 si_status tr_argmax(const float *in, int64_t n, int32_t *out, DecodeFeed *feed, void *stream) {
     return launch("transformer.argmax", argmax_kernel, dim3(kArgmaxCluster), dim3(kArgmaxThreads), 0, stream, in, n,
-                  out, feed);
+                  out, feed, static_cast<StreamsFeed *>(nullptr));
+}
+
+si_status tr_argmax_rows(const float *in, int64_t rows, int64_t n, int32_t *out, StreamsFeed *sfeed, void *stream) {
+    return launch("transformer.argmax", argmax_kernel, dim3(unsigned(rows * kArgmaxCluster)), dim3(kArgmaxThreads), 0,
+                  stream, in, n, out, static_cast<DecodeFeed *>(nullptr), sfeed);
 }
 
 si_status tr_select_last(const float *in, const int32_t *control, float *out, int64_t batch, int64_t width,

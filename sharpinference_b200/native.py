@@ -150,6 +150,10 @@ SIGNATURES = {
     # decoder session
     "si_decoder_create": [_i32, _vp, C.POINTER(_vp)],
     "si_decoder_arena_bytes": [_vp, _pu64],
+    "si_decoder_create_streams": [_i32, _vp, _i32, C.POINTER(_vp)],
+    "si_decoder_step_streams": [_vp, _vp, _vp, _vp],
+    "si_decoder_generate_streams": [_vp, _vp, _vp, _i32, _vp],
+    "si_decoder_prefill_stream": [_vp, _i32, _vp, _i32, _i32, _vp],
     "si_decoder_create_sharded": [_i32, _vp, _vp, C.POINTER(_vp)],
     "si_decoder_destroy": [_vp],
     "si_decoder_slot": [_vp, C.c_char_p, C.POINTER(_vp), _pu64],
@@ -522,13 +526,16 @@ class Decoder:
     device-resident greedy loop (generate). With a PeerGroup, the row-sharded
     session of that rank (si_decoder_create_sharded)."""
 
-    def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None):
+    def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None, streams: int = 1):
         self.cfg = DecoderConfig(**cfg)
+        self.streams = streams
         h = C.c_void_p()
-        if group is None:
-            call("si_decoder_create", device, C.byref(self.cfg), C.byref(h))
-        else:
+        if group is not None:
             call("si_decoder_create_sharded", device, C.byref(self.cfg), group.handle, C.byref(h))
+        elif streams != 1:
+            call("si_decoder_create_streams", device, C.byref(self.cfg), streams, C.byref(h))
+        else:
+            call("si_decoder_create", device, C.byref(self.cfg), C.byref(h))
         self.handle = h
         s = C.c_void_p()
         call("si_decoder_stream", h, C.byref(s))
@@ -581,6 +588,38 @@ class Decoder:
             raise ArgumentError(f"embedding rows must be [n, {self.cfg.hidden}], got {r.shape}")
         v = C.c_int32()
         call("si_decoder_prefill_embeddings", self.handle, r.ctypes.data, r.shape[0], C.byref(v))
+        return v.value
+
+    def _stream_args(self, tokens, positions):
+        np = _np()
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        if t.size != self.streams or p.size != self.streams:
+            raise ArgumentError(f"need {self.streams} tokens and positions")
+        return t, p
+
+    def step_streams(self, tokens, positions):
+        """One step of every stream; returns each stream's argmax."""
+        np = _np()
+        t, p = self._stream_args(tokens, positions)
+        out = np.empty(self.streams, dtype=np.int32)
+        call("si_decoder_step_streams", self.handle, t.ctypes.data, p.ctypes.data, out.ctypes.data)
+        return out
+
+    def generate_streams(self, tokens, positions, steps: int):
+        """`steps` greedy steps of every stream: [steps, streams] argmax ids."""
+        np = _np()
+        t, p = self._stream_args(tokens, positions)
+        out = np.empty((max(steps, 0), self.streams), dtype=np.int32)
+        call("si_decoder_generate_streams", self.handle, t.ctypes.data, p.ctypes.data, steps, out.ctypes.data)
+        return out
+
+    def prefill_stream(self, stream: int, prompt, start: int = 0) -> int:
+        """Batched prefill of one stream's prompt from position `start`."""
+        np = _np()
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        v = C.c_int32()
+        call("si_decoder_prefill_stream", self.handle, stream, pr.ctypes.data, pr.size, start, C.byref(v))
         return v.value
 
     def reset(self) -> None:
