@@ -512,6 +512,11 @@ def run_ours(args) -> None:
     decode14b = None
     if not args.no_decode:
         decode14b = decode14b_block(native, torch, ctx, world, rank, local, peak, barrier, max_over_ranks)
+        if world == 1:
+            b32 = decode14b_streams_block(native, torch, local, peak)
+            # stream 0's prompt is the batch-1 run's prompt: same greedy ids
+            b32["stream0_equals_batch1"] = b32["first_tokens_stream0"] == decode14b["first_tokens"]
+            decode14b["batch32"] = b32
     err = native.device_error_take(local)
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
@@ -705,7 +710,6 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
                              "frac": round(bytes_token * tok_s / 1e9 / (peak * world), 4)},
                 "clocks": clk.summary(),
                 "first_tokens": [int(t) for t in toks[:8]],
-                "batch32": "not measured: the session decodes one stream",
                 "device_error_word": native.device_error_take(local),
             })
     finally:
@@ -716,6 +720,60 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
                 if q != rank:
                     native.ipc_close(local, a)
             arena.free()
+    return out
+
+
+def decode14b_streams_block(native, torch, local: int, peak: float, streams: int = 32) -> dict:
+    """Config 5 at 32 concurrent streams on one GPU: the multi-stream
+    session (si_decoder_create_streams) over the same Phi-4-14B-shaped Q8_0
+    weights; every stream prefilled with its own 1024-token random prompt,
+    then 128 greedy steps of all streams timed on the device. tok/s =
+    streams * steps / time; per step the weights are read once for all
+    streams and every stream's attended KV rows once."""
+    from sharpinference_b200 import phi4
+    cfg = dict(phi4.PHI4_14B)
+    prompt_len, steps = 1024, 128
+    cfg["context"] = prompt_len + steps + 1
+    shapes = phi4.linear_shapes(cfg)
+    out = {"workload": f"config5 batch {streams}: Phi-4-14B-shaped Q8_0 decoder, {streams} concurrent streams, each "
+                       "a 1024-token random prompt then 128 greedy steps", "streams": streams}
+    with native.Decoder(cfg, local, streams=streams) as dec:
+        for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
+            if name in shapes:
+                rows, cols = shapes[name]
+                ptr, _ = dec.slot(name)
+                native.synth_weight_rows_device(native.Q8_0, 11 * 1_000_003 + i, 0, rows, cols, 0.02, ptr,
+                                                dec.stream)
+        stream = torch.cuda.ExternalStream(dec.stream, device=torch.device("cuda", local))
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record(stream)
+        first = [dec.prefill_stream(b, phi4.random_prompt(11 + b, prompt_len, cfg["vocab"])) for b in range(streams)]
+        e[1].record(stream)
+        with ClockSampler(local) as clk:
+            e[2].record(stream)
+            t0 = time.perf_counter()
+            toks = dec.generate_streams(first, [prompt_len] * streams, steps)
+            wall = time.perf_counter() - t0
+            e[3].record(stream)
+            e[3].synchronize()
+        decode_ms = e[2].elapsed_time(e[3])
+        wbytes = sum(r * native.row_bytes(native.Q8_0, c) for r, c in shapes.values())
+        kv_row = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_size"] * 4
+        kv_step = streams * sum(kv_row * (p + 1) for p in range(prompt_len, prompt_len + steps)) / steps
+        bytes_step = wbytes + kv_step
+        tok_s = streams * steps / (decode_ms * 1e-3)
+        out.update({
+            "decode_tok_s": round(tok_s, 1), "ms_per_step": round(decode_ms / steps, 4),
+            "e2e_decode_tok_s": round(streams * steps / wall, 1),
+            "prefill_ms_all_streams": round(e[0].elapsed_time(e[1]), 1),
+            "roofline": {"bound": "hbm", "bytes_per_step": int(bytes_step),
+                         "bytes": "Q8_0 weight bytes once per step + every stream's attended KV rows",
+                         "achieved": round(bytes_step / (decode_ms / steps * 1e-3) / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(bytes_step / (decode_ms / steps * 1e-3) / 1e9 / peak, 4)},
+            "clocks": clk.summary(),
+            "first_tokens_stream0": [int(t) for t in toks[:8, 0]],
+            "device_error_word": native.device_error_take(local),
+        })
     return out
 
 
