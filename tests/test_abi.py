@@ -194,6 +194,34 @@ def test_decoder_config_is_validated_before_any_device_call():
             native.Decoder(cfg)
 
 
+def test_session_variants_and_fused_attention_validate_on_the_host():
+    """The multi-stream and row-sharded sessions and the fused batch
+    attention check their arguments before touching a device."""
+    lib = native.lib
+    base = dict(layers=2, hidden=256, query_heads=2, kv_heads=1, head_size=128, rotary_size=96, intermediate=512,
+                vocab=640, context=64, epsilon=1e-5, rope_base=10000.0, rope_scale=1.0, weight_type=N.Q4_K,
+                embedding_type=N.Q4_K)
+    with pytest.raises(native.ArgumentError):
+        native.Decoder(base, streams=0)
+    with pytest.raises(native.InstructionAdaptationError):
+        native.Decoder(dict(base, query_heads=3), streams=4)
+    # arena bytes: the five projection outputs (256-byte aligned) + 4 KB of state
+    qkv = 256 + 2 * 128
+    want = sum((n * 4 + 255) // 256 * 256 for n in (qkv, 256, 2 * 512, 256, 640)) + 4096
+    assert native.decoder_arena_bytes(base) == want
+    with pytest.raises(native.InstructionAdaptationError):
+        native.decoder_arena_bytes(dict(base, rotary_size=97))
+    h = C.c_void_p()
+    cfg = native.DecoderConfig(**base)
+    assert lib.si_decoder_create_sharded(0, C.byref(cfg), None, C.byref(h)) == N.SI_ERR_INVALID_ARGUMENT
+    f = FAKE
+    assert lib.si_batch_grouped_query_attention(f, f, f, 0, 0, f, 2, 1, 128, 64, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_batch_grouped_query_attention(f, f, f, 0, 4, f, 3, 2, 128, 64, None) == N.SI_ERR_ADAPTATION
+    assert lib.si_batch_grouped_query_attention(f, f, f, 0, 4, f, 2, 1, 96, 64, None) == N.SI_ERR_UNSUPPORTED
+    assert lib.si_synth_weight_rows_device(N.Q4_K, 1, 0, 1, 256, 0.02, f, None) == N.SI_ERR_UNSUPPORTED
+    assert lib.si_synth_weight_rows_device(N.Q8_0, 1, 0, 1, 48, 0.02, f, None) == N.SI_ERR_INVALID_ARGUMENT
+
+
 def test_registry_signatures_and_configurations():
     mv = native.resolve(native.TIER_ZERO_FLOAT32, "core.mat-vec")
     for wt in (N.F32, N.F16, N.Q8_0, N.Q4_K):
