@@ -214,6 +214,26 @@ __device__ __forceinline__ void fetch_weights32(const uint8_t *row, int k0, int 
     }
 }
 
+// The same half-row bytes from a super-stage in shared memory: row_ss is
+// the row's 256 columns (Q4_K: one super-block, 144 bytes; Q8_0: eight
+// blocks, 272 bytes), `sub` the 64-column stage within it.
+template <int FMT>
+__device__ __forceinline__ void fetch_weights32_smem(const uint8_t *row_ss, int sub, int h, RawHalf<FMT> &r) {
+    static_assert(FMT == SI_TYPE_Q4_K || FMT == SI_TYPE_Q8_0, "super-stages hold Q4_K or Q8_0 rows");
+    if constexpr (FMT == SI_TYPE_Q4_K) {
+        r.j = sub;
+        r.v[0] = *reinterpret_cast<const uint4 *>(row_ss);
+        r.v[1] = *reinterpret_cast<const uint4 *>(row_ss + 16 + 32 * sub);
+        r.v[2] = *reinterpret_cast<const uint4 *>(row_ss + 32 + 32 * sub);
+    } else {
+        const uint32_t *u = reinterpret_cast<const uint32_t *>(row_ss + 68 * sub) + 8 * h;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) r.v[i] = make_uint4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
+        r.extra = u[8];
+        r.j = h;
+    }
+}
+
 template <int FMT>
 __device__ __forceinline__ void decode_weights32(const RawHalf<FMT> &r, int h, float (&w)[32]) {
     if constexpr (FMT == SI_TYPE_Q4_K) {

@@ -40,9 +40,15 @@ constexpr int kSkThreads = 64 + kProducers;  // 10 warps
 // Stage = weight hi / lo tiles (128 x 64 BF16 each), X hi / lo tiles
 // (BN x 64 BF16 each) and the FP32 X tile the TMA lands (BN x 64, row-major,
 // converted by warp 0 into the X hi / lo tiles).
-template <int BN>
+// TMAW: Q4_K / Q8_0 weights arrive by TMA, 128 rows x 256 columns of raw
+// GGUF bytes per transfer ("super-stage": four K stages), into a ring of
+// their own; the producers decode them from shared memory.
+template <int BN, int FMT, bool TMAW>
 struct SkinnyCfg {
-    static constexpr int kStages = BN >= 64 ? 3 : 4;
+    static constexpr uint32_t kSS = FMT == SI_TYPE_Q4_K ? 144 : 272;  // bytes of 256 columns of one row
+    static constexpr int kRawStages = TMAW ? (FMT == SI_TYPE_Q4_K ? 3 : 2) : 0;
+    static constexpr uint32_t kRawBytes = kGemmBM * kSS;
+    static constexpr int kStages = TMAW ? (BN >= 64 ? 2 : 3) : (BN >= 64 ? 3 : 4);
     static constexpr uint32_t kATile = kGemmBM * kGemmBK * 2;  // 16 KB (one of hi / lo)
     static constexpr uint32_t kBTile = BN * kGemmBK * 2;       // BN rows of 128 B
     static constexpr uint32_t kXTile = BN * kGemmBK * 4;       // FP32 X as loaded
@@ -50,7 +56,7 @@ struct SkinnyCfg {
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     static constexpr uint32_t kIdesc = mma_idesc(BN);
     static constexpr int kRedStride = BN + 1;  // padded row of the split-K exchange buffer
-    static constexpr size_t kSmem = size_t(kStages) * kStageBytes + 1024 + 256;
+    static constexpr size_t kSmem = size_t(kStages) * kStageBytes + size_t(kRawStages) * kRawBytes + 1024 + 256;
     static_assert(size_t(kGemmBM) * kRedStride * 4 <= size_t(kStages) * kStageBytes, "exchange buffer");
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
@@ -84,25 +90,39 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     return v;
 }
 
-template <int FMT, int BN>
+template <int FMT, int BN, bool TMAW>
 __global__ void __launch_bounds__(kSkThreads, 1)
-    gemm_skinny_kernel(const __grid_constant__ CUtensorMap xmap, const SkinnyParams p) {
-    using Cfg = SkinnyCfg<BN>;
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                       const SkinnyParams p) {
+    using Cfg = SkinnyCfg<BN, FMT, TMAW>;
     constexpr int kSkStages = Cfg::kStages;
+    constexpr int kRaw = Cfg::kRawStages > 0 ? Cfg::kRawStages : 1;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-byte aligned tiles
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kSkStages * Cfg::kStageBytes);
+    uint8_t *wraw = smem + kSkStages * Cfg::kStageBytes;                 // raw weight super-stages
+    uint64_t *full = reinterpret_cast<uint64_t *>(wraw + Cfg::kRawStages * Cfg::kRawBytes);
     uint64_t *empty = full + kSkStages;
-    uint64_t *xfull = empty + kSkStages;  // the FP32 X tile of the stage has landed
-    uint64_t *accum = xfull + kSkStages;
+    uint64_t *xfull = empty + kSkStages;   // the FP32 X tile of the stage has landed
+    uint64_t *xempty = xfull + kSkStages;  // the producers have converted it: the staging can refill
+    uint64_t *wfull = xempty + kSkStages;  // a raw weight super-stage has landed
+    uint64_t *wempty = wfull + kRaw;       // every producer has decoded its rows of it
+    uint64_t *accum = wempty + kRaw;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kGemmBM, t0 = blockIdx.y * BN;
-    const int total_iters = p.k / kGemmBK;
-    const int it0 = int(int64_t(total_iters) * blockIdx.z / p.splits);
-    const int iters = int(int64_t(total_iters) * (blockIdx.z + 1) / p.splits) - it0;
+    int it0, iters;
+    if constexpr (TMAW) {  // splits on super-stage boundaries
+        const int total_ss = p.k / 256;
+        const int ss0 = int(int64_t(total_ss) * blockIdx.z / p.splits);
+        it0 = 4 * ss0;
+        iters = 4 * (int(int64_t(total_ss) * (blockIdx.z + 1) / p.splits) - ss0);
+    } else {
+        const int total_iters = p.k / kGemmBK;
+        it0 = int(int64_t(total_iters) * blockIdx.z / p.splits);
+        iters = int(int64_t(total_iters) * (blockIdx.z + 1) / p.splits) - it0;
+    }
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -110,6 +130,11 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             mbar_init(&full[s], kProducers);  // weight producers (they also convert X)
             mbar_init(&empty[s], 1);
             mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], kProducers);
+        }
+        for (int s = 0; s < kRaw; ++s) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], kProducers);
         }
         mbar_init(accum, 1);
         fence_barrier_init();
@@ -128,16 +153,30 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     float acc[BN < 32 ? 32 : BN];  // epilogue warps: this thread's weight row, BN input rows
     if (warp == 0) {
         // X: the TMA brings each stage's FP32 tile (rows past m read as
-        // zeros) into the stage's staging area as soon as the stage slot is
-        // free, up to kSkStages stages ahead; the producers convert it.
-        pdl_wait();
+        // zeros) into the stage's staging area as soon as the producers have
+        // converted the tile it held, so it runs up to kSkStages stages
+        // ahead of them, independently of the MMA.
         if (lane == 0) {
+            pdl_wait();  // X may come from the previous kernel; the weights never do
             for (int q = 0; q < iters; ++q) {
                 const int sq = q % kSkStages;
-                if (q >= kSkStages) mbar_wait(&empty[sq], ((q / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
+                if (q >= kSkStages) mbar_wait(&xempty[sq], ((q / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
                 uint8_t *xs = smem + sq * Cfg::kStageBytes + 2 * Cfg::kATile + 2 * Cfg::kBTile;
                 mbar_arrive_expect_tx(&xfull[sq], Cfg::kXTile);
                 tma_load_2d(xs, &xmap, (it0 + q) * kGemmBK, t0, &xfull[sq]);
+            }
+        }
+        if constexpr (TMAW) {
+            // Weights: read-only, so no dependency wait is needed for them;
+            // one super-stage (128 rows x 256 columns) per transfer, rows
+            // past n read as zeros. Coordinates in 16-bit units.
+            if (lane == 1) {
+                for (int q = 0; q < iters / 4; ++q) {
+                    const int sq = q % kRaw;
+                    if (q >= kRaw) mbar_wait(&wempty[sq], ((q / kRaw) - 1) & 1, kErrEmptyBarrierTimeout);
+                    mbar_arrive_expect_tx(&wfull[sq], Cfg::kRawBytes);
+                    tma_load_2d(wraw + sq * Cfg::kRawBytes, &wmap, (it0 / 4 + q) * int(Cfg::kSS / 2), n0, &wfull[sq]);
+                }
             }
         }
         __syncwarp();
@@ -170,7 +209,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int pt = threadIdx.x - 64, r = pt >> 1, h = pt & 1;  // row 0..127, half 0..1
         const bool valid_row = n0 + r < p.n;
         const uint8_t *wrow = p.w + size_t(n0 + r) * p.row_bytes;
-        produce_weights<FMT>(wrow, valid_row, it0, iters, h, [&](int it, const float(&w)[32]) {
+        auto emit = [&](int it, const float(&w)[32]) {
             const int s = it % kSkStages;
             if (it >= kSkStages) mbar_wait(&empty[s], ((it / kSkStages) - 1) & 1, kErrEmptyBarrierTimeout);
             uint8_t *st = smem + s * Cfg::kStageBytes;
@@ -201,9 +240,27 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                 *reinterpret_cast<uint4 *>(lo_tile + (xr >> 3) * 1024 + (xr & 7) * 128 + pc * 16) =
                     make_uint4(lv[0], lv[1], lv[2], lv[3]);
             }
-            fence_proxy_async();
+            fence_proxy_async();  // generic reads of the staging before the next TMA write to it
+            mbar_arrive(&xempty[s]);
             mbar_arrive(&full[s]);
-        });
+        };
+        if constexpr (TMAW) {
+            for (int it = 0; it < iters; ++it) {
+                const int sub = it & 3, q = it >> 2, rs = q % kRaw;
+                if (sub == 0) mbar_wait(&wfull[rs], (q / kRaw) & 1, kErrFullBarrierTimeout);
+                RawHalf<FMT> rh;
+                fetch_weights32_smem<FMT>(wraw + rs * Cfg::kRawBytes + r * Cfg::kSS, sub, h, rh);
+                float w[32];
+                decode_weights32<FMT>(rh, h, w);
+                if (sub == 3) {
+                    fence_proxy_async();  // reads of the super-stage before the TMA refills it
+                    mbar_arrive(&wempty[rs]);
+                }
+                emit(it, w);
+            }
+        } else {
+            produce_weights<FMT>(wrow, valid_row, it0, iters, h, emit);
+        }
         // TMEM lane quarter (warp % 4) holds weight rows 32 * (warp % 4) ..;
         // warps 2..5 drain it.
         if (warp < 6) {
@@ -278,9 +335,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// FP32 X [m, k] as a 2-D tensor map with a 64-column x BN-row box, no
-// swizzle; rows past m read as zeros.
-si_status make_x_map_f32(CUtensorMap *map, const float *x, int m, int k, int bn) {
+EncodeTiledFn encoder() {
     static EncodeTiledFn fn = [] {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -289,6 +344,13 @@ si_status make_x_map_f32(CUtensorMap *map, const float *x, int m, int k, int bn)
             ptr = nullptr;
         return reinterpret_cast<EncodeTiledFn>(ptr);
     }();
+    return fn;
+}
+
+// FP32 X [m, k] as a 2-D tensor map with a 64-column x BN-row box, no
+// swizzle; rows past m read as zeros.
+si_status make_x_map_f32(CUtensorMap *map, const float *x, int m, int k, int bn) {
+    EncodeTiledFn fn = encoder();
     if (!fn) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
     const cuuint64_t strides[1] = {cuuint64_t(k) * 4};
@@ -301,10 +363,26 @@ si_status make_x_map_f32(CUtensorMap *map, const float *x, int m, int k, int bn)
     return SI_OK;
 }
 
-template <int FMT, int BN>
+// Raw GGUF weight rows as a 2-D tensor map of 16-bit units: 256 columns
+// (144 or 272 bytes) x 128 rows per box, rows past n read as zeros.
+si_status make_w_map(CUtensorMap *map, const void *w, uint64_t row_bytes, int n, uint32_t ss_bytes) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {cuuint64_t(row_bytes / 2), cuuint64_t(n)};
+    const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+    const cuuint32_t box[2] = {cuuint32_t(ss_bytes / 2), cuuint32_t(kGemmBM)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(w), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SI_ERR_CUDA, "cuTensorMapEncodeTiled (W) failed (%d)", int(r));
+    return SI_OK;
+}
+
+template <int FMT, int BN, bool TMAW>
 si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
-    using Cfg = SkinnyCfg<BN>;
-    auto kernel = gemm_skinny_kernel<FMT, BN>;
+    using Cfg = SkinnyCfg<BN, FMT, TMAW>;
+    auto kernel = gemm_skinny_kernel<FMT, BN, TMAW>;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmem));
@@ -332,9 +410,14 @@ si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
     attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 2;
-    CUtensorMap xmap;
+    CUtensorMap xmap, wmap;
     if (si_status ms = make_x_map_f32(&xmap, p.x, p.m, p.k, BN)) return ms;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, xmap, p);
+    if constexpr (TMAW) {
+        if (si_status ms = make_w_map(&wmap, p.w, p.row_bytes, p.n, Cfg::kSS)) return ms;
+    } else {
+        wmap = xmap;  // unused
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, xmap, wmap, p);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return fail(SI_ERR_CUDA, "tcgen05 few-row GEMM launch failed: %s", cudaGetErrorString(e));
@@ -344,11 +427,15 @@ si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
 
 template <int BN>
 si_status dispatch_type(uint32_t wtype, const SkinnyParams &p, cudaStream_t st) {
+    // TMA weight rows: 256-column super-stages, 16-byte aligned rows and base
+    const bool tmaw = p.k % 256 == 0 && p.row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0;
     switch (wtype) {
-    case SI_TYPE_Q4_K: return launch_skinny<SI_TYPE_Q4_K, BN>(p, st);
-    case SI_TYPE_Q8_0: return launch_skinny<SI_TYPE_Q8_0, BN>(p, st);
-    case SI_TYPE_F16: return launch_skinny<SI_TYPE_F16, BN>(p, st);
-    default: return launch_skinny<SI_TYPE_F32, BN>(p, st);
+    case SI_TYPE_Q4_K:
+        return tmaw ? launch_skinny<SI_TYPE_Q4_K, BN, true>(p, st) : launch_skinny<SI_TYPE_Q4_K, BN, false>(p, st);
+    case SI_TYPE_Q8_0:
+        return tmaw ? launch_skinny<SI_TYPE_Q8_0, BN, true>(p, st) : launch_skinny<SI_TYPE_Q8_0, BN, false>(p, st);
+    case SI_TYPE_F16: return launch_skinny<SI_TYPE_F16, BN, false>(p, st);
+    default: return launch_skinny<SI_TYPE_F32, BN, false>(p, st);
     }
 }
 
