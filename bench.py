@@ -656,18 +656,26 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
     out = {"workload": "config5 batch 1: Phi-4-14B-shaped Q8_0 decoder (40 layers, hidden 5120, 40/10 heads of "
                        "128, FFN 17920, vocab 100352), N(0,0.02) seed 11, 1024-token random prompt, 128 greedy steps",
            "parallelism": "single GPU" if world == 1 else
-           f"{world} GPUs: every projection row-sharded, outputs gathered by the GEMV kernel over NVLink; "
-           "norms, rope, attention, argmax and the KV cache replicated"}
+           f"{world} GPUs: the large projections row-sharded, outputs gathered by the GEMV kernel over NVLink; "
+           "small projections, norms, rope, attention, argmax and the KV cache replicated"}
+    # Split a projection only when its exchange (~7 us) costs less than the
+    # weight time it saves: (1 - 1/N) * bytes / HBM > 8 us.
+    shard_min = int(52e6 * world / (world - 1)) if world > 1 else 0
     try:
-        with native.Decoder(cfg, local, group) as dec:
+        with native.Decoder(cfg, local, group, shard_min_bytes=shard_min) as dec:
+            split, rep_bytes = [], 0
             for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
                 if name not in shapes:
                     continue
                 rows, cols = shapes[name]
-                begin, count = 0, rows
-                if world > 1 and name != "token_embedding":
-                    begin, count, _ = native.rowshard_plan(rows, world, rank)
                 ptr, nbytes = dec.slot(name)
+                begin, count = 0, rows
+                if nbytes < rows * native.row_bytes(native.Q8_0, cols):  # this slot holds the rank's rows
+                    begin, count, _ = native.rowshard_plan(rows, world, rank)
+                    if name.endswith("_0"):
+                        split.append(name[:-2])
+                elif world > 1:
+                    rep_bytes += nbytes
                 assert nbytes == count * native.row_bytes(native.Q8_0, cols)
                 native.synth_weight_rows_device(native.Q8_0, 11 * 1_000_003 + i, begin, count, cols, 0.02, ptr,
                                                 dec.stream)
@@ -696,15 +704,18 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
             kv_bytes = sum(kv_row * (p + 1) for p in range(prompt_len, prompt_len + steps)) / steps
             tok_s = steps / (decode_ms * 1e-3)
             # weights are read once per token across the ranks; the KV cache once per rank
-            bytes_token = wbytes + world * kv_bytes
+            bytes_token = wbytes + (world - 1) * rep_bytes + world * kv_bytes
+            if world > 1:
+                out["split_projections"] = split + ["vocabulary (token_embedding rows)"]
+                out["shard_min_bytes"] = shard_min
             out.update({
                 "decode_tok_s": round(tok_s, 1), "decode_ms_per_token": round(decode_ms / steps, 4),
                 "e2e_decode_tok_s": round(steps / wall, 1),
                 "prompt_ms": round(prefill_ms, 1),
                 "prompt_path": "batched prefill" if world == 1 else "the decode program per prompt token",
                 "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_token),
-                             "bytes": "Q8_0 weight bytes once per token (split over the ranks) + the KV-cache rows "
-                                      "attended on every rank",
+                             "bytes": "Q8_0 weight bytes per token over all ranks (split projections once, "
+                                      "replicated ones on every rank) + the KV-cache rows attended on every rank",
                              "achieved_aggregate": round(bytes_token * tok_s / 1e9, 1),
                              "peak_aggregate": round(peak * world, 1), "unit": "GB/s",
                              "frac": round(bytes_token * tok_s / 1e9 / (peak * world), 4)},

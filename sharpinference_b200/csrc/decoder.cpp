@@ -62,6 +62,11 @@ struct si_decoder {
     si_peer_group *group = nullptr;
     uint8_t *arena = nullptr;
     const void *w_vocab = nullptr;
+    // Which projections are split by rows (qkv, attn_output, ffn_up,
+    // ffn_down, vocabulary); the others are replicated and run whole on
+    // every rank, their outputs written into the rank's own arena.
+    enum { kQkv, kOut, kUp, kDown, kVocab };
+    bool sharded[5] = {false, false, false, false, false};
     // Multi-stream session (si_decoder_create_streams): `streams` rows per
     // step, stream b's caches at rows b * context of each layer's cache;
     // per-stream tokens / positions / greedy-loop state on the device.
@@ -148,9 +153,9 @@ si_status project(uint32_t type, const void *w, const float *x, float *y, int64_
 // A projection of the session: the whole mat-vec, or in a row-sharded
 // session this rank's rows with the output stored into every rank's arena
 // (y lies in the arena; its offset is the same on every rank).
-si_status project_rows(si_decoder *d, uint32_t type, const void *w, const float *x, float *y, int64_t rows,
+si_status project_rows(si_decoder *d, int kind, uint32_t type, const void *w, const float *x, float *y, int64_t rows,
                        int64_t cols) {
-    if (!d->group) return project(type, w, x, y, rows, cols, d->stream);
+    if (!d->group || !d->sharded[kind]) return project(type, w, x, y, rows, cols, d->stream);
     const uint64_t offset = uint64_t(reinterpret_cast<uint8_t *>(y) - d->arena);
     return si_rowshard_matvec_peer(d->group, type, w, x, offset, rows, cols, d->stream);
 }
@@ -195,7 +200,7 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
                                       c.epsilon, s))
         return st;
     for (int l = 0; l < c.layers; ++l) {
-        if (si_status st = project_rows(d, c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kQkv, c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
         if (si_status st = k::tr_rope_kv_write(d->qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
                                                d->value_cache[l], 1, H, KV, c.head_size, c.rotary_size, c.context,
                                                c.rope_scale, s))
@@ -203,19 +208,19 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
         if (si_status st = k::tr_attention_decode(d->query, d->key_cache[l], d->value_cache[l], position, d->attention,
                                                   c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
-        if (si_status st = project_rows(d, c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kOut, c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
         if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = project_rows(d, c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kUp, c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
         if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, 1, F, s)) return st;
-        if (si_status st = project_rows(d, c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
+        if (si_status st = project_rows(d, si_decoder::kDown, c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
         if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
                                           c.epsilon, s))
             return st;
     }
-    if (si_status st = project_rows(d, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
+    if (si_status st = project_rows(d, si_decoder::kVocab, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
     return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
 }
 
@@ -336,7 +341,7 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
     }
     if (!last) return SI_OK;
     if (si_status st = k::tr_select_last(P.normalized, control, d->normalized, rows, H, s)) return st;
-    if (si_status st = project_rows(d, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
+    if (si_status st = project_rows(d, si_decoder::kVocab, c.embedding_type, d->w_vocab, d->normalized, d->logits, c.vocab, H)) return st;
     return k::tr_argmax(d->logits, c.vocab, d->next_token, nullptr, s);
 }
 
@@ -503,7 +508,8 @@ si_status validate(const si_decoder_config *c) {
 
 si_status create_step(si_decoder *d);
 
-si_status create(int device, const si_decoder_config *c, si_peer_group *group, int32_t streams, si_decoder **out) {
+si_status create(int device, const si_decoder_config *c, si_peer_group *group, int32_t streams,
+                 uint64_t shard_min_bytes, si_decoder **out) {
     auto *d = new si_decoder();
     d->device = device;
     d->cfg = *c;
@@ -526,10 +532,16 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
         d->group = group;
         d->arena = si::peer_group_arena(group, &nranks, &rank, &data_bytes);
     }
-    // Rows of a projection held by this rank (all of them unless sharded).
-    auto shard = [&](int64_t rows, int64_t *begin) {
+    // A projection is split by rows when its weight bytes reach
+    // shard_min_bytes; rows of it held by this rank (all of them otherwise).
+    if (group) {
+        const uint64_t bytes[5] = {rb_h * uint64_t(QKV), rb_h * uint64_t(H), rb_h * uint64_t(2 * F),
+                                   rb_f * uint64_t(H), rb_e * uint64_t(c->vocab)};
+        for (int kind = 0; kind < 5; ++kind) d->sharded[kind] = bytes[kind] >= shard_min_bytes;
+    }
+    auto shard = [&](int kind, int64_t rows, int64_t *begin) {
         int64_t b = 0, n = rows, per = rows;
-        if (group) si_rowshard_plan(rows, nranks, rank, &b, &n, &per);
+        if (group && d->sharded[kind]) si_rowshard_plan(rows, nranks, rank, &b, &n, &per);
         if (begin) *begin = b;
         return n;
     };
@@ -539,7 +551,7 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
     d->embedding = p;
     {
         int64_t vocab_begin = 0;
-        shard(c->vocab, &vocab_begin);
+        shard(si_decoder::kVocab, c->vocab, &vocab_begin);
         d->w_vocab = static_cast<const uint8_t *>(p) + uint64_t(vocab_begin) * rb_e;
     }
 
@@ -555,16 +567,16 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
         if (si_status st = alloc_typed(d, "ffn_norm_" + L, H * 4, &f)) return cleanup(st);
         if (si_status st = fill_ones(f, H)) return cleanup(st);
         d->ffn_norm.push_back(f);
-        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(shard(QKV, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(shard(si_decoder::kQkv, QKV, nullptr)), &p))
             return cleanup(st);
         d->w_qkv.push_back(p);
-        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(shard(H, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(shard(si_decoder::kOut, H, nullptr)), &p))
             return cleanup(st);
         d->w_out.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(shard(2 * F, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(shard(si_decoder::kUp, 2 * F, nullptr)), &p))
             return cleanup(st);
         d->w_up.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(shard(H, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(shard(si_decoder::kDown, H, nullptr)), &p))
             return cleanup(st);
         d->w_down.push_back(p);
         if (si_status st = alloc_typed(d, "key_cache_" + L, B * uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
@@ -719,7 +731,7 @@ si_status si_decoder_create(int device, const si_decoder_config *config, si_deco
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, nullptr, 1, out);
+    return create(device, config, nullptr, 1, 0, out);
 }
 
 si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *bytes) {
@@ -730,7 +742,7 @@ si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *byte
 }
 
 si_status si_decoder_create_sharded(int device, const si_decoder_config *config, si_peer_group *group,
-                                    si_decoder **out) {
+                                    uint64_t shard_min_bytes, si_decoder **out) {
     if (!out || !group) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
     if (si_status st = validate(config)) return st;
@@ -759,7 +771,7 @@ si_status si_decoder_create_sharded(int device, const si_decoder_config *config,
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, group, 1, out);
+    return create(device, config, group, 1, shard_min_bytes, out);
 }
 
 si_status si_decoder_destroy(si_decoder *decoder) {
@@ -920,7 +932,7 @@ si_status si_decoder_create_streams(int device, const si_decoder_config *config,
     }
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
-    return create(device, config, nullptr, streams, out);
+    return create(device, config, nullptr, streams, 0, out);
 }
 
 

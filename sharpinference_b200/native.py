@@ -154,7 +154,7 @@ SIGNATURES = {
     "si_decoder_step_streams": [_vp, _vp, _vp, _vp],
     "si_decoder_generate_streams": [_vp, _vp, _vp, _i32, _vp],
     "si_decoder_prefill_stream": [_vp, _i32, _vp, _i32, _i32, _vp],
-    "si_decoder_create_sharded": [_i32, _vp, _vp, C.POINTER(_vp)],
+    "si_decoder_create_sharded": [_i32, _vp, _vp, _u64, C.POINTER(_vp)],
     "si_decoder_destroy": [_vp],
     "si_decoder_slot": [_vp, C.c_char_p, C.POINTER(_vp), _pu64],
     "si_decoder_upload": [_vp, C.c_char_p, _u64, _vp, _u64],
@@ -526,12 +526,13 @@ class Decoder:
     device-resident greedy loop (generate). With a PeerGroup, the row-sharded
     session of that rank (si_decoder_create_sharded)."""
 
-    def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None, streams: int = 1):
+    def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None, streams: int = 1,
+                 shard_min_bytes: int = 0):
         self.cfg = DecoderConfig(**cfg)
         self.streams = streams
         h = C.c_void_p()
         if group is not None:
-            call("si_decoder_create_sharded", device, C.byref(self.cfg), group.handle, C.byref(h))
+            call("si_decoder_create_sharded", device, C.byref(self.cfg), group.handle, shard_min_bytes, C.byref(h))
         elif streams != 1:
             call("si_decoder_create_streams", device, C.byref(self.cfg), streams, C.byref(h))
         else:

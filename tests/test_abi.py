@@ -213,7 +213,7 @@ def test_session_variants_and_fused_attention_validate_on_the_host():
         native.decoder_arena_bytes(dict(base, rotary_size=97))
     h = C.c_void_p()
     cfg = native.DecoderConfig(**base)
-    assert lib.si_decoder_create_sharded(0, C.byref(cfg), None, C.byref(h)) == N.SI_ERR_INVALID_ARGUMENT
+    assert lib.si_decoder_create_sharded(0, C.byref(cfg), None, 0, C.byref(h)) == N.SI_ERR_INVALID_ARGUMENT
     f = FAKE
     assert lib.si_batch_grouped_query_attention(f, f, f, 0, 0, f, 2, 1, 128, 64, None) == N.SI_ERR_ADAPTATION
     assert lib.si_batch_grouped_query_attention(f, f, f, 0, 4, f, 3, 2, 128, 64, None) == N.SI_ERR_ADAPTATION

@@ -22,9 +22,10 @@ def _row_bytes(wt, cols):
     return N.row_bytes(wt, cols)
 
 
-def _shard_weights(cfg, weights, world, rank):
-    """This rank's rows of every projection slot; token_embedding and the
-    norms whole."""
+def _shard_weights(cfg, weights, world, rank, dec=None):
+    """This rank's rows of every split projection slot (all of them, or
+    those the session split: a slot smaller than the whole matrix);
+    token_embedding, the norms and replicated projections whole."""
     h, f = cfg["hidden"], cfg["intermediate"]
     qkv = h + 2 * cfg["kv_heads"] * cfg["head_size"]
     out = {}
@@ -36,6 +37,9 @@ def _shard_weights(cfg, weights, world, rank):
             continue
         cols = f if base == "ffn_down_weight" else h
         rb = _row_bytes(cfg["weight_type"], cols)
+        if dec is not None and dec.slot(name)[1] == rows * rb:
+            out[name] = arr  # replicated
+            continue
         b, cnt, _ = N.rowshard_plan(rows, world, rank)
         out[name] = np.ascontiguousarray(arr.reshape(rows, rb)[b:b + cnt]).reshape(-1)
     return out
@@ -102,7 +106,7 @@ MID_CFG = dict(layers=2, hidden=1024, query_heads=8, kv_heads=2, head_size=128, 
                embedding_type=N.Q8_0)
 
 
-def _worker(rank, world, port, prompt, steps, result_path):
+def _worker(rank, world, port, prompt, steps, result_path, shard_min_bytes=0):
     import datetime
 
     import torch
@@ -123,8 +127,8 @@ def _worker(rank, world, port, prompt, steps, result_path):
         addrs = [arena.device_pointer if q == rank else nv.ipc_open(rank, handles[q]) for q in range(world)]
         g = nv.PeerGroup(rank, world, rank, addrs, ab)
         try:
-            with nv.Decoder(cfg, rank, g) as dec:
-                for name, arr in _shard_weights(cfg, weights, world, rank).items():
+            with nv.Decoder(cfg, rank, g, shard_min_bytes=shard_min_bytes) as dec:
+                for name, arr in _shard_weights(cfg, weights, world, rank, dec).items():
                     dec.upload(name, arr)
                 dist.barrier()  # every arena mapped and every session built before the first step
                 toks = [int(t) for t in dec.generate(prompt, steps)]
@@ -143,7 +147,10 @@ def _worker(rank, world, port, prompt, steps, result_path):
     dist.destroy_process_group()
 
 
-def test_two_rank_sharded_session_matches_oracle(tmp_path):
+# 0: every projection split; 2 MB: qkv and o replicated (1.7 and 1.1 MB of
+# Q8_0), ffn_up, ffn_down and the vocabulary projection split.
+@pytest.mark.parametrize("shard_min_bytes", [0, 2 << 20])
+def test_two_rank_sharded_session_matches_oracle(tmp_path, shard_min_bytes):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -153,7 +160,8 @@ def test_two_rank_sharded_session_matches_oracle(tmp_path):
     prompt = [int(t) for t in np.random.default_rng(83).integers(0, cfg["vocab"], 12)]
     want = oracle.Decoder(cfg, weights).generate(prompt, 12)
     res = str(tmp_path / "res")
-    mp.start_processes(_worker, args=(2, _free_port(), prompt, 12, res), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), prompt, 12, res, shard_min_bytes), nprocs=2, join=True,
+                       start_method="spawn")
     for r in range(2):
         got = open(f"{res}.{r}").read()
         assert got == " ".join(map(str, want)), f"rank {r}: {got}"
