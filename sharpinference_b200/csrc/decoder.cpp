@@ -67,6 +67,8 @@ struct si_decoder {
     // every rank, their outputs written into the rank's own arena.
     enum { kQkv, kOut, kUp, kDown, kVocab };
     bool sharded[5] = {false, false, false, false, false};
+    // The projection outputs of even / odd layers (arena regions).
+    float *par_qkv[2] = {}, *par_out[2] = {}, *par_up[2] = {}, *par_down[2] = {};
     // Multi-stream session (si_decoder_create_streams): `streams` rows per
     // step, stream b's caches at rows b * context of each layer's cache;
     // per-stream tokens / positions / greedy-loop state on the device.
@@ -161,10 +163,14 @@ si_status project_rows(si_decoder *d, int kind, uint32_t type, const void *w, co
 }
 
 // Arena layout of a row-sharded session: the qkv, attention-output,
-// gate_up, down and logits vectors, each 256-byte aligned. Consecutive
-// projections always use different regions, as the peer GEMV requires.
+// gate_up and down vectors twice (even and odd layers) and the logits, each
+// 256-byte aligned. A rank enters a peer GEMV only after every rank has
+// finished its previous peer GEMV, i.e. after every rank has consumed what
+// it read before that call; with two copies per layer-repeated region (and
+// gate_up split whenever anything is), a region is overwritten only after
+// its previous content has been consumed on every rank.
 struct ArenaLayout {
-    uint64_t qkv, out, up, down, logits, data_bytes;
+    uint64_t qkv[2], out[2], up[2], down[2], logits, data_bytes;
 };
 
 ArenaLayout arena_layout(const si_decoder_config &c) {
@@ -172,10 +178,12 @@ ArenaLayout arena_layout(const si_decoder_config &c) {
     auto al = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
     ArenaLayout a{};
     uint64_t o = 0;
-    a.qkv = o, o += al(QKV * 4);
-    a.out = o, o += al(H * 4);
-    a.up = o, o += al(2 * uint64_t(c.intermediate) * 4);
-    a.down = o, o += al(H * 4);
+    for (int par = 0; par < 2; ++par) {
+        a.qkv[par] = o, o += al(QKV * 4);
+        a.out[par] = o, o += al(H * 4);
+        a.up[par] = o, o += al(2 * uint64_t(c.intermediate) * 4);
+        a.down[par] = o, o += al(H * 4);
+    }
     a.logits = o, o += al(uint64_t(c.vocab) * 4);
     a.data_bytes = o;
     return a;
@@ -200,23 +208,26 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
                                       c.epsilon, s))
         return st;
     for (int l = 0; l < c.layers; ++l) {
-        if (si_status st = project_rows(d, si_decoder::kQkv, c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
-        if (si_status st = k::tr_rope_kv_write(d->qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
+        // row-sharded: this layer's copy of the projection outputs
+        float *qkv = d->group ? d->par_qkv[l & 1] : d->qkv, *projected = d->group ? d->par_out[l & 1] : d->projected;
+        float *gate_up = d->group ? d->par_up[l & 1] : d->gate_up, *down = d->group ? d->par_down[l & 1] : d->down;
+        if (si_status st = project_rows(d, si_decoder::kQkv, c.weight_type, d->w_qkv[l], d->normalized, qkv, QKV, H)) return st;
+        if (si_status st = k::tr_rope_kv_write(qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
                                                d->value_cache[l], 1, H, KV, c.head_size, c.rotary_size, c.context,
                                                c.rope_scale, s))
             return st;
         if (si_status st = k::tr_attention_decode(d->query, d->key_cache[l], d->value_cache[l], position, d->attention,
                                                   c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
-        if (si_status st = project_rows(d, si_decoder::kOut, c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
-        if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
+        if (si_status st = project_rows(d, si_decoder::kOut, c.weight_type, d->w_out[l], d->attention, projected, H, H)) return st;
+        if (si_status st = k::tr_rms_norm(d->hidden, projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = project_rows(d, si_decoder::kUp, c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
-        if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, 1, F, s)) return st;
-        if (si_status st = project_rows(d, si_decoder::kDown, c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
+        if (si_status st = project_rows(d, si_decoder::kUp, c.weight_type, d->w_up[l], d->normalized, gate_up, 2 * F, H)) return st;
+        if (si_status st = k::tr_swiglu(gate_up, nullptr, d->activated, 1, F, s)) return st;
+        if (si_status st = project_rows(d, si_decoder::kDown, c.weight_type, d->w_down[l], d->activated, down, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
-        if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
+        if (si_status st = k::tr_rms_norm(d->after, down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
                                           c.epsilon, s))
             return st;
     }
@@ -537,7 +548,11 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
     if (group) {
         const uint64_t bytes[5] = {rb_h * uint64_t(QKV), rb_h * uint64_t(H), rb_h * uint64_t(2 * F),
                                    rb_f * uint64_t(H), rb_e * uint64_t(c->vocab)};
-        for (int kind = 0; kind < 5; ++kind) d->sharded[kind] = bytes[kind] >= shard_min_bytes;
+        bool any = false;
+        for (int kind = 0; kind < 5; ++kind) any |= d->sharded[kind] = bytes[kind] >= shard_min_bytes;
+        // a layer-repeated peer call in every layer, so that the vocabulary
+        // projection is never the only one (its logits region has one copy)
+        if (any) d->sharded[si_decoder::kUp] = true;
     }
     auto shard = [&](int kind, int64_t rows, int64_t *begin) {
         int64_t b = 0, n = rows, per = rows;
@@ -610,10 +625,10 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
         const std::string name = a.name;
         uint64_t off = UINT64_MAX;
         if (group) {
-            if (name == "qkv") off = lay.qkv;
-            else if (name == "projected") off = lay.out;
-            else if (name == "gate_up") off = lay.up;
-            else if (name == "down") off = lay.down;
+            if (name == "qkv") off = lay.qkv[0];
+            else if (name == "projected") off = lay.out[0];
+            else if (name == "gate_up") off = lay.up[0];
+            else if (name == "down") off = lay.down[0];
             else if (name == "logits") off = lay.logits;
         }
         if (off != UINT64_MAX) {
@@ -621,6 +636,14 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
             d->slots[name] = {d->arena + off, uint64_t(a.n) * 4};
         } else if (si_status st = alloc_typed(d, a.name, B * uint64_t(a.n) * 4, a.dst)) {
             return cleanup(st);
+        }
+    }
+    if (group) {
+        for (int par = 0; par < 2; ++par) {
+            d->par_qkv[par] = reinterpret_cast<float *>(d->arena + lay.qkv[par]);
+            d->par_out[par] = reinterpret_cast<float *>(d->arena + lay.out[par]);
+            d->par_up[par] = reinterpret_cast<float *>(d->arena + lay.up[par]);
+            d->par_down[par] = reinterpret_cast<float *>(d->arena + lay.down[par]);
         }
     }
     if (streams > 1) {

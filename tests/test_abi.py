@@ -205,9 +205,11 @@ def test_session_variants_and_fused_attention_validate_on_the_host():
         native.Decoder(base, streams=0)
     with pytest.raises(native.InstructionAdaptationError):
         native.Decoder(dict(base, query_heads=3), streams=4)
-    # arena bytes: the five projection outputs (256-byte aligned) + 4 KB of state
+    # arena bytes: the four per-layer projection outputs twice (even / odd
+    # layers) and the logits, each 256-byte aligned, + 4 KB of state
     qkv = 256 + 2 * 128
-    want = sum((n * 4 + 255) // 256 * 256 for n in (qkv, 256, 2 * 512, 256, 640)) + 4096
+    al = lambda n: (n * 4 + 255) // 256 * 256  # noqa: E731
+    want = 2 * sum(al(n) for n in (qkv, 256, 2 * 512, 256)) + al(640) + 4096
     assert native.decoder_arena_bytes(base) == want
     with pytest.raises(native.InstructionAdaptationError):
         native.decoder_arena_bytes(dict(base, rotary_size=97))
