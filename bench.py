@@ -826,7 +826,7 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
             dec.reset()
             e[4].record(stream)
             t0 = time.perf_counter()
-            nxt = dec.prefill(prompt)  # batched prefill (two chunks of 256 rows)
+            nxt = dec.prefill(prompt)  # batched prefill (one chunk of 512 rows)
             prefill_wall = time.perf_counter() - t0
             e[5].record(stream)
             e[2].record(stream)

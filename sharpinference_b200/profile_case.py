@@ -10,7 +10,7 @@ launch with `-s 1 -c 1`): synthetic seeded weights and inputs, device-resident.
       steps; each step is one graph of 292 kernel launches)
   python -m sharpinference_b200.profile_case prefill mini 512
       (Phi-4-mini random-init decoder: one batched prefill of 512 prompt
-      tokens, two chunks of 256 rows)
+      tokens, one chunk of 512 rows)
   python -m sharpinference_b200.profile_case decode-trace mini 512
       (the persistent decode step: one step at position 512 with its
       per-phase trace, averaged per phase kind over the layers, CTA 0)

@@ -54,11 +54,12 @@ def _prefill_cfg(wtype=native.Q4_K, context=640):
     return cfg
 
 
-@pytest.mark.parametrize("wtype,tokens", [(native.Q4_K, 300), (native.Q4_K, 40), (native.Q8_0, 257),
-                                          (native.F16, 96)])
+@pytest.mark.parametrize("wtype,tokens", [(native.Q4_K, 600), (native.Q4_K, 40), (native.Q8_0, 257),
+                                          (native.F16, 96), (native.Q8_0, 513)])
 def test_prefill_matches_oracle(wtype, tokens):
-    """Chunks of 256 rows (300 = 256 + 44), GEMMs on the tensor cores from
-    64 rows and the batch mat-vec below, then greedy decode from there."""
+    """Chunks of 512 rows (600 = 512 + 88, 513 = 512 + 1), GEMMs on the
+    tensor cores from 64 rows and the few-row paths below, then greedy
+    decode from there."""
     cfg = _prefill_cfg(wtype)
     weights = tiny_decoder_weights(cfg, seed=50 + wtype)
     prompt = np.random.default_rng(tokens).integers(0, cfg["vocab"], tokens)
