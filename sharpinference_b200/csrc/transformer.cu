@@ -301,7 +301,10 @@ __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const 
 
 // ---- decode attention --------------------------------------------------------
 constexpr int kAttnCluster = 8;
-constexpr int kAttnWarps = 8;
+// Warps per CTA: 8 for one stream; 4 for several (more clusters fill the
+// GPU; measured at 32 Phi-4-14B streams 1198 vs 1025 tok/s, while one
+// stream loses with 4: 597 vs 648 tok/s on Phi-4-mini).
+constexpr int kAttnWarpsOne = 8, kAttnWarpsMany = 4;
 
 // One cluster of kAttnCluster CTAs per key/value head. Tokens 0..active,
 // active = min(max(0, *position), context - 1), are split into contiguous
@@ -314,7 +317,7 @@ constexpr int kAttnWarps = 8;
 // u % kv_heads of stream u / kv_heads, whose query / output rows are
 // q_stride floats apart, caches cache_stride floats apart and whose
 // position is position[stream].
-template <int NPL, int MAXG, int kTile>
+template <int NPL, int MAXG, int kTile, int kAttnWarps>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
     gqa_decode_kernel(const float *query, const float *key_cache, const float *value_cache, const int32_t *position,
                       float *out, int group, int kv_heads, int head_size, int64_t context, float scale,
@@ -972,11 +975,11 @@ si_status tr_rope_kv_write_streams(const float *qkv, const int32_t *positions, c
 }
 
 namespace {
-template <int NPL, int MAXG, int kTile>
+template <int NPL, int MAXG, int kTile, int kAttnWarps>
 si_status launch_gqa(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                      int group, int kv_heads, int head_size, int64_t context, float scale, int streams,
                      int64_t q_stride, int64_t cache_stride, void *stream) {
-    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile>;
+    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile, kAttnWarps>;
     const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
                                2 * group) * sizeof(float);
     if (smem > 48 * 1024) {
@@ -1005,9 +1008,13 @@ si_status tr_attention_decode_streams(const float *query, const float *kc, const
     const float scale = 1.0f / sqrtf(float(head_size));
     const int npl = (head_size + 31) / 32;
     const int64_t q_stride = int64_t(query_heads) * head_size;
-#define SI_GQA(NPL, MAXG, TILE)                                                                                   \
-    launch_gqa<NPL, MAXG, TILE>(query, kc, vc, position, out, group, kv_heads, head_size, context, scale, streams, \
-                                q_stride, cache_stride, stream)
+#define SI_GQA(NPL, MAXG, TILE)                                                                                \
+    (streams > 1 ? launch_gqa<NPL, MAXG, TILE, kAttnWarpsMany>(query, kc, vc, position, out, group, kv_heads,      \
+                                                               head_size, context, scale, streams, q_stride,      \
+                                                               cache_stride, stream)                              \
+                 : launch_gqa<NPL, MAXG, TILE, kAttnWarpsOne>(query, kc, vc, position, out, group, kv_heads,       \
+                                                              head_size, context, scale, streams, q_stride,       \
+                                                              cache_stride, stream))
     if (group <= 4) {
         if (npl <= 1) return SI_GQA(1, 4, 8);
         if (npl <= 2) return SI_GQA(2, 4, 8);
