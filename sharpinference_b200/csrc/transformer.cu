@@ -944,7 +944,9 @@ si_status tr_rms_norm(const float *in, const float *residual, const float *weigh
 
 si_status tr_swiglu(const float *gate_up, const int32_t *control, float *out, int64_t batch, int64_t width,
                     void *stream) {
-    return launch("transformer.swiglu", swiglu_kernel, dim3(elementwise_grid(batch * width, 256)), dim3(256), 0,
+    // 128-thread CTAs: twice the CTAs of 256 for a decode row (more loads in
+    // flight); Phi-4-mini decode 659 vs 648 tok/s with rope-kv-write alike
+    return launch("transformer.swiglu", swiglu_kernel, dim3(elementwise_grid(batch * width, 128)), dim3(128), 0,
                   stream, gate_up, control, out, batch, width);
 }
 
@@ -958,7 +960,7 @@ si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int3
                            int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale,
                            void *stream) {
     const int64_t count = batch * (qsize + 2 * kvsize);
-    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 128)), dim3(128), 0,
                   stream, qkv, position, control, freq, query, key_cache, value_cache, batch, qsize, kvsize, head_size,
                   rotary, context, rope_scale, static_cast<const int32_t *>(nullptr), int64_t(0));
 }
@@ -968,7 +970,7 @@ si_status tr_rope_kv_write_streams(const float *qkv, const int32_t *positions, c
                                    int64_t kvsize, int head_size, int rotary, int64_t context, int64_t cache_stride,
                                    float rope_scale, void *stream) {
     const int64_t count = streams * (qsize + 2 * kvsize);
-    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 256)), dim3(256), 0,
+    return launch("transformer.rope-kv-write", rope_kv_kernel, dim3(elementwise_grid(count, 128)), dim3(128), 0,
                   stream, qkv, static_cast<const int32_t *>(nullptr), static_cast<const int32_t *>(nullptr), freq,
                   query, key_cache, value_cache, streams, qsize, kvsize, head_size, rotary, context, rope_scale,
                   positions, cache_stride);
