@@ -148,10 +148,21 @@ def cpu_reference_sweep(shapes, weights, xs, threads: int) -> float:
 
 
 def make_inputs(shapes):
-    from sharpinference_b200 import native
-    weights = [native.synth_weights(WTYPE, seed, n, k, 0.02) for _, n, k, seed in shapes]
-    xs = [native.synth_normal(1000 + seed, k, 1.0) for _, n, k, seed in shapes]
+    """The sweep's weights and inputs, made by the oracle's generator and
+    quantiser (bit-identical to the library's, which the CPU tests check), so
+    a CPU-only process never loads the CUDA library."""
+    import oracle
+    weights = [oracle.quantize(WTYPE, oracle.normal(seed, n * k, 0.02)) for _, n, k, seed in shapes]
+    xs = [oracle.normal(1000 + seed, k, 1.0) for _, n, k, seed in shapes]
     return weights, xs
+
+
+def line_config(world: int) -> dict:
+    """`config` of both arms' JSON lines: the workload only (how each arm runs
+    it is described outside `config`)."""
+    return {"workload": WORKLOAD, "shapes_nk": [[n, k] for _, n, k, _ in SHAPES], "bytes_per_step": step_bytes(SHAPES),
+            "l2": "inputs larger than L2 (402 MB of weights streamed per step)",
+            "parallelism": "single GPU" if world == 1 else f"{world} GPUs (row-shard or replicate per shape)"}
 
 
 def cpu_baseline_sample(budget_s: float = 10.0) -> dict:
@@ -185,9 +196,8 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,0.02) Q4_K weights, N(0,1) x)",
-        "config": {"workload": WORKLOAD, "shapes_nk": [[n, k] for _, n, k, _ in SHAPES],
-                   "bytes_per_step": step_bytes(SHAPES)},
+        "data": "synthetic (seeded N(0,0.02) weights quantized to Q4_K; x ~ N(0,1))",
+        "config": line_config(world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"full sweep x {args.steps} steps; C restatement of CpuHalfMatrixOperators.MatVec "
                                    "(per-row dequantise + FP32 dot, rows parallel)"},
@@ -529,10 +539,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantized to Q4_K; x ~ N(0,1))",
-            "config": {"workload": WORKLOAD, "shapes_nk": [[n, k] for _, n, k, _ in SHAPES],
-                       "bytes_per_step": bytes_step,
-                       "l2": "inputs larger than L2 (402 MB of weights streamed per step)",
-                       "parallelism": par, "shard_policy": policy or None,
+            "config": line_config(world),
+            "method": {"parallelism": par, "shard_policy": policy or None,
                        "per_shape": "back-to-back launches of one shape cycling through weight copies > L2",
                        "submission": "one recorded graph per step (PDL edges between the launches)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

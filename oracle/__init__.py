@@ -96,19 +96,43 @@ def byte_length(wtype: int, elements: int) -> int:
     return b.value
 
 
+_PAR_MIN = 1 << 22  # elements: below this one call, above it chunks over host threads
+
+
+def _chunks(count: int, align: int):
+    """[begin, end) ranges covering count elements in multiples of align, one per host thread."""
+    threads = max(1, int(lib.or_online_cores()))
+    step = max(align, -(-count // threads) // align * align)
+    return [(b, min(count, b + step)) for b in range(0, count, step)]
+
+
+def _parallel(fn, ranges) -> None:
+    # ctypes releases the GIL inside the C calls, so the chunks run in parallel
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(len(ranges)) as ex:
+        list(ex.map(lambda r: fn(*r), ranges))
+
+
 def normal(seed: int, count: int, sigma: float = 1.0, offset: int = 0) -> np.ndarray:
     out = np.empty(count, dtype=np.float32)
-    lib.or_normal_fill(seed, offset, count, sigma, _ptr(out))
+    if count < _PAR_MIN:
+        lib.or_normal_fill(seed, offset, count, sigma, _ptr(out))
+    else:  # element i depends on (seed, offset + i) only: chunks give the same values
+        _parallel(lambda b, e: lib.or_normal_fill(seed, offset + b, e - b, sigma, _ptr(out) + 4 * b),
+                  _chunks(count, 2))
     return out
 
 
 def quantize(wtype: int, values: np.ndarray) -> np.ndarray:
     values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
     out = np.empty(byte_length(wtype, values.size), dtype=np.uint8)
-    if wtype == Q8_0:
-        lib.or_quantize_q8_0(_ptr(values), values.size, _ptr(out))
-    elif wtype == Q4_K:
-        lib.or_quantize_q4_k(_ptr(values), values.size, _ptr(out))
+    if wtype in (Q8_0, Q4_K):
+        fn, per, nb = (lib.or_quantize_q8_0, 32, 34) if wtype == Q8_0 else (lib.or_quantize_q4_k, 256, 144)
+        if values.size < _PAR_MIN or values.size % per:
+            fn(_ptr(values), values.size, _ptr(out))
+        else:  # blocks are independent
+            _parallel(lambda b, e: fn(_ptr(values) + 4 * b, e - b, _ptr(out) + b // per * nb),
+                      _chunks(values.size, per))
     elif wtype == F16:
         out = np.array([lib.or_f32_to_f16(float(v)) for v in values], dtype=np.uint16).view(np.uint8)
     else:

@@ -273,6 +273,27 @@ si_status si_matvec(uint32_t weight_type, const void *weight, uint32_t input_typ
     return run_matvec(weight_type, weight, input_type, input, output_type, output, rows, cols, stream);
 }
 
+si_status si_gemv_default_plan(uint32_t weight_type, int64_t rows, int64_t cols, si_gemv_plan *plan) {
+    if (!plan) return fail(SI_ERR_INVALID_ARGUMENT, "null plan");
+    if (rows <= 0 || cols <= 0) return fail(SI_ERR_INVALID_ARGUMENT, "rows and cols must be positive");
+    const si_status st = kernels::gemv_default_plan(weight_type, rows, cols, plan);
+    if (st == SI_ERR_UNSUPPORTED)
+        return fail(SI_ERR_UNSUPPORTED, "no tensor-core GEMV shape for %s [%lld, %lld]", type_name(weight_type),
+                    (long long)rows, (long long)cols);
+    return st;
+}
+
+si_status si_matvec_quant_planned(uint32_t weight_type, const void *weight, const float *input, float *output,
+                                  int64_t rows, int64_t cols, const si_gemv_plan *plan, void *stream) {
+    if (!plan) return fail(SI_ERR_INVALID_ARGUMENT, "null plan");
+    if (weight_type != SI_TYPE_Q8_0 && weight_type != SI_TYPE_Q4_K)
+        return fail(SI_ERR_ADAPTATION, "planned GEMV: weight must be Q8_0 or Q4_K.");
+    if (si_status st = validate_matvec(weight_type, weight, SI_TYPE_F32, input, SI_TYPE_F32, output, rows, cols,
+                                       SI_MATVEC_DEFAULT, true))
+        return st;
+    return kernels::matvec_quant_planned(weight_type, weight, input, output, rows, cols, *plan, stream);
+}
+
 si_status si_batch_shared_matvec(uint32_t weight_type, const void *weight, const float *input, const int32_t *control,
                                  float *output, int64_t batch, int64_t out_features, int64_t in_features,
                                  void *stream) {

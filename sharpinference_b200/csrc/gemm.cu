@@ -246,12 +246,7 @@ uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 // minimises waves x (stages per CTA + a fixed cost of about four stages
 // for the TMEM drain and pipeline fill), keeping at least two stages per CTA.
 int gemm_splits(int64_t m, int64_t n, int64_t k) {
-    static const int sms = [] {
-        int dev = 0, v = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        return v;
-    }();
+    const int sms = device_sm_count();
     const int64_t tiles = ((n + kBM - 1) / kBM) * ((m + kBN - 1) / kBN);
     const int64_t iters = k / kBK;
     int best = 1;
@@ -267,11 +262,9 @@ int gemm_splits(int64_t m, int64_t n, int64_t k) {
 template <int FMT>
 si_status launch_gemm(const void *w, float *y, uint64_t rb, int m, int n, int k, int splits, const CUtensorMap &hi,
                       const CUtensorMap &lo, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gemm_tcgen05_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem));
-        attr = true;
-    }
+    if (const int ae = opt_in_smem(reinterpret_cast<const void *>(gemm_tcgen05_kernel<FMT>), int(kGemmSmem)))
+        return fail(SI_ERR_CUDA, "tcgen05 GEMM shared-memory opt-in failed: %s",
+                    cudaGetErrorString(cudaError_t(ae)));
     GemmParams p{static_cast<const uint8_t *>(w), y, rb, m, n, k, splits};
     const dim3 grid(unsigned((n + kBM - 1) / kBM), unsigned((m + kBN - 1) / kBN), unsigned(splits));
     gemm_tcgen05_kernel<FMT><<<grid, kThreads, kGemmSmem, st>>>(hi, lo, p);

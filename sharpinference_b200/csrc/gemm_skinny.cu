@@ -321,15 +321,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
 }
 
-int sm_count() {
-    static const int sms = [] {
-        int dev = 0, v = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        return v;
-    }();
-    return sms;
-}
+int sm_count() { return device_sm_count(); }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -383,11 +375,8 @@ template <int FMT, int BN, bool TMAW>
 si_status launch_skinny(const SkinnyParams &p0, cudaStream_t st) {
     using Cfg = SkinnyCfg<BN, FMT, TMAW>;
     auto kernel = gemm_skinny_kernel<FMT, BN, TMAW>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmem));
-        attr = true;
-    }
+    if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), int(Cfg::kSmem)))
+        return fail(SI_ERR_CUDA, "few-row GEMM shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
     SkinnyParams p = p0;
     const int64_t tiles = ((p.n + kGemmBM - 1) / kGemmBM) * ((p.m + BN - 1) / BN);
     const int iters = p.k / kGemmBK;

@@ -34,29 +34,30 @@ static __device__ __align__(256) uint8_t g_static_workspace[kStaticWorkspaceByte
 
 // Device address of g_static_workspace per device. In host code the symbol
 // is only a stand-in; the real address comes from cudaGetSymbolAddress with
-// the device current (done once per device, on its first call).
-struct WorkspaceSlot {
-    std::once_flag once;
-    void *ptr = nullptr;
-    cudaError_t status = cudaSuccess;
-};
-WorkspaceSlot g_slots[64];
+// the device current, on the device's first successful call. Only a
+// successful lookup is kept: a failed one (for example a first call made
+// while the stream is being captured) clears the runtime's error state and
+// is tried again on the next call.
+std::mutex g_slots_mu;
+void *g_slots[si::kMaxDevices];
 
 si_status workspace_for_current_device(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return si::fail(SI_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= 64) return si::fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
-    WorkspaceSlot &slot = g_slots[dev];
-    std::call_once(slot.once, [&slot] {
+    if (dev < 0 || dev >= si::kMaxDevices) return si::fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+    std::lock_guard<std::mutex> g(g_slots_mu);
+    if (!g_slots[dev]) {
         void *p = nullptr;
-        slot.status = cudaGetSymbolAddress(&p, g_static_workspace);
-        slot.ptr = slot.status == cudaSuccess ? p : nullptr;
-    });
-    if (slot.status != cudaSuccess || !slot.ptr)
-        return si::fail(SI_ERR_CUDA, "cudaGetSymbolAddress(static workspace) failed on device %d: %s", dev,
-                        cudaGetErrorString(slot.status));
-    *out = slot.ptr;
+        e = cudaGetSymbolAddress(&p, g_static_workspace);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return si::fail(SI_ERR_CUDA, "cudaGetSymbolAddress(static workspace) failed on device %d: %s", dev,
+                            cudaGetErrorString(e));
+        }
+        g_slots[dev] = p;
+    }
+    *out = g_slots[dev];
     return SI_OK;
 }
 

@@ -340,19 +340,7 @@ __global__ void __launch_bounds__(256) gemv_rowwarp_kernel(const uint8_t *__rest
     }
 }
 
-int g_sm_count[64];
-
-int sm_count() {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (!g_sm_count[dev]) {
-        int n = 0;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        g_sm_count[dev] = n > 0 ? n : 148;
-    }
-    return g_sm_count[dev];
-}
+int sm_count() { return device_sm_count(); }
 
 si_status launch_status(const char *what) {
     const cudaError_t e = cudaGetLastError();
@@ -444,20 +432,14 @@ si_status matvec_quant(uint32_t wtype, const void *w, const float *x, float *y, 
         const int grid = std::min(p.num_tiles, sm_count());
         const int threads = p.consumer_threads + 32;
         if (wtype == SI_TYPE_Q4_K) {
-            static bool attr4 = false;
-            if (!attr4) {
-                cudaFuncSetAttribute(gemv_staged_kernel<SI_TYPE_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     227 * 1024);
-                attr4 = true;
-            }
+            if (const int ae = opt_in_smem(reinterpret_cast<const void *>(gemv_staged_kernel<SI_TYPE_Q4_K>), 227 * 1024))
+                return fail(SI_ERR_CUDA, "staged GEMV shared-memory opt-in failed: %s",
+                            cudaGetErrorString(cudaError_t(ae)));
             gemv_staged_kernel<SI_TYPE_Q4_K><<<grid, threads, smem, st>>>(p);
         } else {
-            static bool attr8 = false;
-            if (!attr8) {
-                cudaFuncSetAttribute(gemv_staged_kernel<SI_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     227 * 1024);
-                attr8 = true;
-            }
+            if (const int ae = opt_in_smem(reinterpret_cast<const void *>(gemv_staged_kernel<SI_TYPE_Q8_0>), 227 * 1024))
+                return fail(SI_ERR_CUDA, "staged GEMV shared-memory opt-in failed: %s",
+                            cudaGetErrorString(cudaError_t(ae)));
             gemv_staged_kernel<SI_TYPE_Q8_0><<<grid, threads, smem, st>>>(p);
         }
         return launch_status("staged quantized GEMV");

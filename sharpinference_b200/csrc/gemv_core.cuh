@@ -353,6 +353,14 @@ struct I8State {
 __device__ __forceinline__ uint32_t digit_byte(int v, int add, uint32_t shift) {
     return uint32_t((v + add) >> shift);
 }
+// rint(v) for |v| < 2^22 on the FMA pipe instead of the conversion pipe:
+// v + 1.5 * 2^23 lies in [2^23, 2^24), where the float spacing is 1, so the
+// addition rounds v to the nearest integer (ties to even, as
+// __float2int_rn) and the integer is the sum's low mantissa bits. `m` is a
+// power of two with |x * m| < 2^22, so x * m is exact and one FMA suffices.
+__device__ __forceinline__ int rint_scaled(float x, float m) {
+    return __float_as_int(fmaf(x, m, 12582912.0f)) - 0x4B400000;
+}
 // Low bytes of four words packed into one.
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
@@ -370,14 +378,40 @@ struct I8Path {
     static __device__ __forceinline__ void load(const XS &X, int sb, int lane, State &st, uint8_t *, int64_t, int) {
         const int64_t xb = int64_t(sb) * 256;
         const bool aligned = X.aligned(xb);
-        float v[8];
+        const int t = lane & 3, g = lane >> 2;
+        const int half = g >> 2, digit = g & 3;
+        // Every x value this lane needs is requested here, before any of it is
+        // used: the eight consecutive values of the amax / sub-block sums and
+        // the 32 values of its B fragments (sub-blocks 4 * half .. + 3, k =
+        // 4t..4t+3 and 16+4t..16+4t+3). One memory round trip instead of one
+        // per sub-block (with the shared-memory ring filling the SM, the L1
+        // keeps little, so each later load went back to L2).
+        float v[8], q[4][8];
         if (aligned) {
             const float4 a = X.get4(xb + 8 * lane);
             const float4 b = X.get4(xb + 8 * lane + 4);
+            float4 qa[4], qc[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t e0 = xb + 32 * (4 * half + j) + 4 * t;
+                qa[j] = X.get4(e0);
+                qc[j] = X.get4(e0 + 16);
+            }
             v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                q[j][0] = qa[j].x, q[j][1] = qa[j].y, q[j][2] = qa[j].z, q[j][3] = qa[j].w;
+                q[j][4] = qc[j].x, q[j][5] = qc[j].y, q[j][6] = qc[j].z, q[j][7] = qc[j].w;
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = X.get(xb + 8 * lane + i);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t e0 = xb + 32 * (4 * half + j) + 4 * t;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) q[j][i] = X.get(e0 + i), q[j][4 + i] = X.get(e0 + 16 + i);
+            }
         }
         float amax = 0.0f, psum = 0.0f;
 #pragma unroll
@@ -386,7 +420,6 @@ struct I8Path {
         for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
         psum += __shfl_xor_sync(0xffffffffu, psum, 1);
         psum += __shfl_xor_sync(0xffffffffu, psum, 2);  // lanes 4s..4s+3 hold the sum of sub-block s
-        const int t = lane & 3, g = lane >> 2;
         st.sx_lo_t = __shfl_sync(0xffffffffu, psum, 4 * t);
         st.sx_hi_t = __shfl_sync(0xffffffffu, psum, 4 * (t + 4));
         // scale = 2^(22 - e) with amax < 2^e: |x * scale| < 2^22.
@@ -409,26 +442,16 @@ struct I8Path {
         // B fragments: lane (g,t) holds column g = 4 * half + digit of
         // sub-blocks 4 * half .. 4 * half + 3, k = 4t..4t+3 (b0) and
         // 16+4t..16+4t+3 (b1); column digit 3 stays zero.
-        const int half = g >> 2, digit = g & 3;
         const int dadd = digit == 0 ? 0x8080 : (digit == 1 ? 0x80 : 0);
         const uint32_t dshift = digit == 0 ? 16u : (digit == 1 ? 8u : 0u);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             uint32_t b0 = 0, b1 = 0;
             if ((s >> 2) == half && digit < 3) {
-                float q[8];
-                const int64_t e0 = xb + 32 * s + 4 * t;
-                if (aligned) {
-                    const float4 a = X.get4(e0);
-                    const float4 c = X.get4(e0 + 16);
-                    q[0] = a.x, q[1] = a.y, q[2] = a.z, q[3] = a.w, q[4] = c.x, q[5] = c.y, q[6] = c.z, q[7] = c.w;
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = X.get(e0 + i), q[4 + i] = X.get(e0 + 16 + i);
-                }
+                const float *qs = q[s & 3];
                 uint32_t dg[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) dg[i] = digit_byte(__float2int_rn(q[i] * scale), dadd, dshift);
+                for (int i = 0; i < 8; ++i) dg[i] = digit_byte(rint_scaled(qs[i], scale), dadd, dshift);
                 b0 = pack_low_bytes(dg[0], dg[1], dg[2], dg[3]);
                 b1 = pack_low_bytes(dg[4], dg[5], dg[6], dg[7]);
             }
@@ -570,10 +593,10 @@ struct I8T8Path {
             if (present) {
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 4 * t));
                 const float4 c = __ldg(reinterpret_cast<const float4 *>(xs + 32 * s + 16 + 4 * t));
-                v[0] = __float2int_rn(a.x * scale), v[1] = __float2int_rn(a.y * scale);
-                v[2] = __float2int_rn(a.z * scale), v[3] = __float2int_rn(a.w * scale);
-                v[4] = __float2int_rn(c.x * scale), v[5] = __float2int_rn(c.y * scale);
-                v[6] = __float2int_rn(c.z * scale), v[7] = __float2int_rn(c.w * scale);
+                v[0] = rint_scaled(a.x, scale), v[1] = rint_scaled(a.y, scale);
+                v[2] = rint_scaled(a.z, scale), v[3] = rint_scaled(a.w, scale);
+                v[4] = rint_scaled(c.x, scale), v[5] = rint_scaled(c.y, scale);
+                v[6] = rint_scaled(c.z, scale), v[7] = rint_scaled(c.w, scale);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[i] = 0;
@@ -591,7 +614,7 @@ struct I8T8Path {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float sv = t == 0 ? ps[i] : ps[4 + i];
-            vm[i] = (present && t < 2) ? __float2int_rn(sv * scale_m) : 0;
+            vm[i] = (present && t < 2) ? rint_scaled(sv, scale_m) : 0;
         }
 #pragma unroll
         for (int d = 0; d < 3; ++d)
@@ -733,7 +756,7 @@ struct Q8Path {
         // Images: lane l owns elements 8l..8l+7 = bytes 34 * (l / 4) + 2 + 8 * (l % 4) .. + 7 of the column.
         int vi[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) vi[i] = __float2int_rn(v[i] * scale);
+        for (int i = 0; i < 8; ++i) vi[i] = rint_scaled(v[i], scale);
         const uint32_t pos = 34u * uint32_t(lane >> 2) + 2u + 8u * uint32_t(lane & 3);
 #pragma unroll
         for (int d = 0; d < 3; ++d) {

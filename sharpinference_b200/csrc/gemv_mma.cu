@@ -383,56 +383,30 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     }
 }
 
-int g_sms[64];
+int num_sms() { return device_sm_count(); }
 
-int num_sms() {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (!g_sms[dev]) {
-        int n = 0;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        g_sms[dev] = n > 0 ? n : 148;
-    }
-    return g_sms[dev];
-}
-
-// Launch shape of one GEMV: cluster size (K split), row-tile height and the
-// shared-memory budget of one CTA.
+// Launch shape of one GEMV: cluster size (K split), row-tile height, the
+// shared-memory budget of one CTA, superblocks per compute warp and CTAs
+// per SM (si_gemv_plan carries the same fields across the C ABI).
 struct Shape {
     int cluster;
     int rt;
     int budget_kb;
-    int path;  // 0: FP16 MMA, 1: INT8 MMA
-    int wps;   // compute warps per superblock column (1, or 2 on the INT8 path with 32-row tiles)
-    int max_groups;  // 0: one CTA (cluster) per SM; else at most this many
+    int path;        // 0: FP16 MMA, 1: INT8 MMA
+    int wps;         // compute warps per superblock column (1, or 2 on the INT8 path with 32-row tiles)
+    int max_groups;  // 0: ctas_per_sm CTAs (clusters of CTAs) per SM; else at most this many
+    int spw;         // 0: one superblock per warp while that fits, else 2; or forced 1 / 2
+    int per_sm;      // CTAs resident per SM the grid is sized for (1 or 2)
 };
-
-// Optional override for tuning sweeps:
-// SI_Q4K_GEMV_PLAN="cluster,rows_per_tile,budget_kb[,path[,warps_per_column[,max_groups]]]"
-// (for example "2,16,100" or "1,32,226,1,2"); ignored when it does not fit.
-bool shape_override(Shape &s) {
-    static Shape o{0, 0, 0, 0, 1, 0};
-    static bool parsed = false;
-    if (!parsed) {
-        parsed = true;
-        if (const char *e = std::getenv("SI_Q4K_GEMV_PLAN")) {
-            Shape t{0, 0, 0, 0, 1, 0};
-            if (std::sscanf(e, "%d,%d,%d,%d,%d,%d", &t.cluster, &t.rt, &t.budget_kb, &t.path, &t.wps, &t.max_groups) >=
-                3)
-                o = t;
-        }
-    }
-    if (o.cluster <= 0) return false;
-    s = o;
-    return true;
-}
 
 // Largest ring budget: the 227 KB a CTA may hold, less 1 KB of headroom.
 // The bytes in flight per SM set the bandwidth (Little's law): with one
 // stage held by the compute warps, a 4 x 55.8 KB ring (K = 3072, 32-row
 // tiles) keeps ~167 KB in flight where 3 stages kept ~111 KB.
 constexpr int kMaxBudgetKb = 226;
+// Two CTAs per SM: each holds at most half of the SM's 228 KB (less the
+// 1 KB the hardware reserves per CTA).
+constexpr int kHalfBudgetKb = 112;
 
 // Default launch shape: one CTA per SM with the whole shared memory as
 // ring and 32-row tiles. K is split over a cluster only when a CTA would
@@ -440,9 +414,13 @@ constexpr int kMaxBudgetKb = 226;
 // superblock warps keep the x fragments in registers without spilling.
 // (Measured on the Phi-4-mini shapes: splitting K = 3072 halves the compute
 // warps per SM and loses; K = 8192 split in two gains about 10%.)
+// Tiles are 32 rows unless the busiest CTA would stream at least 8% fewer
+// rows with 16-row tiles, which happens when there are several tiles per CTA
+// and 32-row tiles leave a ragged last round (gate_up: 512 tiles of 32 on 148
+// CTAs = 4 rounds, 1024 tiles of 16 = 7 rounds, 112 rows instead of 128;
+// measured 7.4 us instead of 8.5 us). With one or two tiles per CTA the fixed
+// cost of a tile outweighs the balance, and 32-row tiles stay.
 Shape default_shape(int64_t rows, int nsb, int sms, int path) {
-    (void)rows;
-    (void)sms;
     int cs = 1;
     if (nsb > kMaxComputeWarps) {
         cs = 0;
@@ -450,28 +428,35 @@ Shape default_shape(int64_t rows, int nsb, int sms, int path) {
             if (nsb % c == 0 && nsb / c <= kMaxComputeWarps) cs = c;
         if (!cs) cs = 1;  // two superblocks per warp
     }
-    return {cs, 32, kMaxBudgetKb, path, 1, 0};
+    int rt = 32;
+    const int64_t groups = std::max(1, sms / cs);
+    const int64_t tiles32 = (rows + 31) / 32, tiles16 = (rows + 15) / 16;
+    if (tiles32 > 2 * groups) {
+        const int64_t busiest32 = (tiles32 + groups - 1) / groups * 32;
+        const int64_t busiest16 = (tiles16 + groups - 1) / groups * 16;
+        if (busiest16 * 100 <= busiest32 * 92) rt = 16;
+    }
+    return {cs, rt, kMaxBudgetKb, path, 1, 0, 0, 1};
+}
+
+Shape shape_from_plan(const si_gemv_plan &g) {
+    return {g.cluster, g.rows_per_tile, g.smem_kb, g.mma_path, g.warps_per_column, g.max_groups,
+            g.superblocks_per_warp, g.ctas_per_sm};
 }
 
 // path: 0 FP16 / 1 INT8 (Q4_K), 2 Q8_0. col_bytes: bytes of 256 elements;
 // scratch_bytes: per compute warp scratch of the path.
 // group_cap > 0 limits the clusters (CTAs) of the grid to what can be
 // resident at once.
+// `forced`: an explicit launch shape (si_matvec_quant_planned), else the default.
 bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint32_t col_bytes,
-              uint32_t scratch_bytes, int group_cap, MmaParams &p, size_t &smem, int &rt, int tokens = 1) {
+              uint32_t scratch_bytes, int group_cap, MmaParams &p, size_t &smem, int &rt, int tokens,
+              const Shape *forced) {
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int nsb = int(cols / 256);
-    Shape sh = default_shape(rows, nsb, sms, path);
-    Shape o;
-    if (shape_override(o) && o.cluster >= 1 && o.cluster <= 8 && (o.rt == 16 || o.rt == 32) &&
-        o.budget_kb >= 32 && o.budget_kb <= kMaxBudgetKb && (o.wps == 1 || o.wps == 2)) {
-        const int opath = path >= 2 ? path : o.path;
-        if (opath == path || (path < 2 && (opath == 0 || opath == 1))) {
-            sh = o;
-            sh.path = opath;
-        }
-    }
+    Shape sh = forced ? *forced : default_shape(rows, nsb, sms, path);
+    if (path >= 2) sh.path = path;  // Q8_0 and the batched path have one MMA path each
     if (nsb % sh.cluster != 0) sh.cluster = 1;
     const size_t budget = size_t(sh.budget_kb) * 1024;
     for (;;) {
@@ -480,7 +465,8 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint
         p.nsb = nsb;
         p.cluster = sh.cluster;
         p.nsb_cta = nsb_cta;
-        p.spw = nsb_cta > kMaxComputeWarps ? 2 : 1;
+        p.spw = (nsb_cta > kMaxComputeWarps || (sh.spw == 2 && nsb_cta >= 2)) ? 2 : 1;
+        if (sh.spw == 1 && p.spw == 2) return false;  // one superblock per warp cannot cover this K slice
         const int columns = (nsb_cta + p.spw - 1) / p.spw;
         rt = sh.rt;
         p.row_bytes = col_bytes * uint32_t(nsb);
@@ -519,7 +505,7 @@ bool plan_mma(int64_t rows, int64_t cols, const void *w, int sms, int path, uint
         }
         p.num_tiles = int((rows + rt - 1) / rt);
         // One CTA per SM at most: a cluster of CS CTAs takes CS SMs.
-        p.groups = std::max(1, std::min(p.num_tiles, sms / p.cluster));
+        p.groups = std::max(1, std::min(p.num_tiles, sh.per_sm * sms / p.cluster));
         if (sh.max_groups > 0) p.groups = std::min(p.groups, sh.max_groups);
         if (group_cap > 0) p.groups = std::min(p.groups, group_cap);
         p.max_local_tiles = (p.num_tiles + p.groups - 1) / p.groups;
@@ -597,10 +583,10 @@ int max_active_clusters(void (*kernel)(MmaParams), int cluster, int threads, siz
 namespace {
 
 // One launch of the tensor-core GEMV skeleton. path: 1 Q4_K INT8 (or FP16
-// by override), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
+// by an explicit shape), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
 si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream,
                      const PeerGather *peer, const int32_t *control, int token, int ntok, int64_t x_stride,
-                     int64_t y_stride) {
+                     int64_t y_stride, const Shape *forced = nullptr) {
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
@@ -619,16 +605,6 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
         {gemv_mma_q4k_kernel<I8T8Path, 1, 16, 1, 12>, gemv_mma_q4k_kernel<I8T8Path, 1, 32, 1, 12>},
         {gemv_mma_q4k_kernel<I8T8Path, 1, 16, 1, 16>, gemv_mma_q4k_kernel<I8T8Path, 1, 32, 1, 16>}};
     static const Kernel kernel_wps2 = gemv_mma_q4k_kernel<I8Path, 1, 32, 2, kMaxWps2Warps>;
-    static std::once_flag attr_once;
-    std::call_once(attr_once, [] {
-        for (auto &a : kernels)
-            for (auto &b : a)
-                for (auto &c : b)
-                    for (Kernel k : c) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        for (auto &a : kernels_t8)
-            for (Kernel k : a) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(kernel_wps2, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    });
     const bool q8 = path == 2, batched = path == 3;
     const uint32_t col_bytes = q8 ? Q8Path::kColBytes : I8Path::kColBytes;
     // Plan; with a K split, shrink the grid to the clusters that can be
@@ -637,7 +613,7 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
     int cap = 0;
     for (int attempt = 0; attempt < 4; ++attempt) {
         if (!plan_mma(rows, cols, w, sms, path, col_bytes, q8 ? Q8Path::kScratchBytes : 0u, cap, p, smem, rt,
-                      batched ? I8T8Path::kTokens : 1))
+                      batched ? I8T8Path::kTokens : 1, forced))
             return SI_ERR_UNSUPPORTED;
         if (batched) {
             if (p.spw != 1 || p.wps != 1) return SI_ERR_UNSUPPORTED;
@@ -646,6 +622,11 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
             kernel = p.wps == 2 ? kernel_wps2
                                 : kernels[p.path][p.spw - 1][p.compute_warps > 12 ? 1 : 0][rt == 32 ? 1 : 0];
         }
+        // The occupancy query below and the launch both need the kernel's
+        // shared-memory opt-in on this device.
+        if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), 227 * 1024))
+            return fail(SI_ERR_CUDA, "tensor-core GEMV shared-memory opt-in failed: %s",
+                        cudaGetErrorString(cudaError_t(ae)));
         if (p.cluster == 1) break;
         const int fit = max_active_clusters(kernel, p.cluster, (p.compute_warps + 2) * 32, smem);
         if (fit <= 0) return SI_ERR_UNSUPPORTED;
@@ -693,6 +674,38 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, control, token, 1, cols,
                       rows);
+}
+
+// The launch shape si_matvec picks for a Q4_K / Q8_0 GEMV on the current device.
+si_status gemv_default_plan(uint32_t wtype, int64_t rows, int64_t cols, si_gemv_plan *plan) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
+    if (cols % 256 != 0 || rows <= 0) return SI_ERR_UNSUPPORTED;
+    const Shape sh = default_shape(rows, int(cols / 256), num_sms(), wtype == SI_TYPE_Q8_0 ? 2 : 1);
+    *plan = si_gemv_plan{sh.cluster, sh.rt, sh.budget_kb, sh.path == 0 ? 0 : 1, sh.wps, sh.spw, sh.per_sm,
+                         sh.max_groups};
+    return SI_OK;
+}
+
+// One GEMV with an explicit launch shape. SI_ERR_INVALID_ARGUMENT for a
+// shape outside the documented ranges; SI_ERR_UNSUPPORTED when the shape
+// cannot cover this matrix (nothing launched).
+si_status matvec_quant_planned(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                               const si_gemv_plan &g, void *stream) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return fail(SI_ERR_UNSUPPORTED, "planned GEMV: Q8_0 or Q4_K");
+    if (g.cluster < 1 || g.cluster > 8 || (g.rows_per_tile != 16 && g.rows_per_tile != 32) || g.smem_kb < 32 ||
+        g.smem_kb > kMaxBudgetKb || (g.mma_path != 0 && g.mma_path != 1) ||
+        (g.warps_per_column != 1 && g.warps_per_column != 2) || g.superblocks_per_warp < 0 ||
+        g.superblocks_per_warp > 2 || (g.ctas_per_sm != 1 && g.ctas_per_sm != 2) || g.max_groups < 0 ||
+        (g.ctas_per_sm == 2 && g.smem_kb > kHalfBudgetKb))
+        return fail(SI_ERR_INVALID_ARGUMENT,
+                    "GEMV plan out of range (cluster 1..8, rows_per_tile 16/32, smem_kb 32..%d and <= %d at two "
+                    "CTAs per SM, mma_path 0/1, warps_per_column 1/2, superblocks_per_warp 0..2, ctas_per_sm 1/2)",
+                    kMaxBudgetKb, kHalfBudgetKb);
+    const Shape sh = shape_from_plan(g);
+    const si_status st = launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, nullptr, nullptr, 0,
+                                    1, cols, rows, &sh);
+    if (st == SI_ERR_UNSUPPORTED) return fail(SI_ERR_UNSUPPORTED, "GEMV plan does not fit this matrix");
+    return st;
 }
 
 // Q4_K batch: y[b] = W x[b] for the m input rows, eight per launch (each

@@ -55,6 +55,17 @@ si_status cuda_error(int error, const char *what);
 // size and rank, and the arena's data bytes (before the 4 KB of state).
 uint8_t *peer_group_arena(si_peer_group *g, int *nranks, int *rank, uint64_t *data_bytes);
 
+// Per-device launch state (launch_state.cpp). Kernel attributes and the SM
+// count are properties of a device; one process may drive several devices
+// from several threads, so both are kept per device behind a lock.
+constexpr int kMaxDevices = 64;
+int current_device();
+// Streaming multiprocessors of the current device.
+int device_sm_count();
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device (once per device and kernel); returns the cudaError_t value.
+int opt_in_smem(const void *kernel, int bytes);
+
 }  // namespace si
 
 // Launch wrappers implemented in the .cu files (host side of each kernel).
@@ -97,6 +108,11 @@ struct PeerGather {
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                            void *stream, const PeerGather *peer = nullptr, const int32_t *control = nullptr,
                            int token = 0);
+// The launch shape matvec_quant_mma picks, and one GEMV with an explicit shape
+// (si_gemv_default_plan / si_matvec_quant_planned).
+si_status gemv_default_plan(uint32_t wtype, int64_t rows, int64_t cols, si_gemv_plan *plan);
+si_status matvec_quant_planned(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                               const si_gemv_plan &plan, void *stream);
 // Q4_K batch on the tensor cores, eight input rows per launch; SI_ERR_UNSUPPORTED
 // when the shape or alignment needs another kernel (nothing launched then).
 si_status matvec_q4k_batched(const void *w, const float *x, float *y, int64_t m, int64_t rows, int64_t cols,

@@ -140,12 +140,9 @@ si_status launch_shared(const void *w, const float *x, float *y, const int32_t *
                         int64_t k, cudaStream_t st) {
     uint64_t rb;
     if (si_status s = byte_length(FMT, uint64_t(k), &rb)) return s;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(shared_weight_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(shared_weight_smem()));
-        attr = true;
-    }
+    if (const int ae = opt_in_smem(reinterpret_cast<const void *>(shared_weight_kernel<FMT>), int(shared_weight_smem())))
+        return fail(SI_ERR_CUDA, "shared-weight mat-vec shared-memory opt-in failed: %s",
+                    cudaGetErrorString(cudaError_t(ae)));
     const dim3 grid(unsigned((n + kRowsPerCta - 1) / kRowsPerCta), unsigned((m + kTokens - 1) / kTokens));
     if (grid.y > 65535u) return fail(SI_ERR_INVALID_ARGUMENT, "too many input rows (%lld)", (long long)m);
     shared_weight_kernel<FMT><<<grid, 256, shared_weight_smem(), st>>>(static_cast<const uint8_t *>(w), rb, x, y,

@@ -862,15 +862,7 @@ __global__ void gather_rows_kernel(const float *table, int64_t rows, const int32
 }
 
 // ---- launch helpers -----------------------------------------------------------
-int sm_count_cached() {
-    static int n = [] {
-        int dev = 0, v = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        return v;
-    }();
-    return n;
-}
+int sm_count_cached() { return device_sm_count(); }
 
 int elementwise_grid(int64_t count, int threads) {
     const int64_t blocks = (count + threads - 1) / threads;
@@ -985,11 +977,8 @@ si_status launch_gqa(const float *query, const float *kc, const float *vc, const
     const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
                                2 * group) * sizeof(float);
     if (smem > 48 * 1024) {
-        static bool raised = false;
-        if (!raised) {
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            raised = true;
-        }
+        if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), 200 * 1024))
+            return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
     }
     return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(streams * kv_heads * kAttnCluster)),
                   dim3(kAttnWarps * 32), smem, stream, query, kc, vc, position, out, group, kv_heads, head_size,
@@ -1045,11 +1034,9 @@ si_status launch_prefill_attention(const float *query, const float *kc, const fl
                                    float *out, int query_heads, int kv_heads, void *stream) {
     constexpr size_t smem = size_t(kPfRows * (HS + 4) + 2 * kPfKeys * (HS + 4) + 2 * kPfKeys * HS +
                                    kPfRows * (kPfKeys + 4)) * sizeof(float);
-    static bool raised = false;
-    if (!raised) {
-        cudaFuncSetAttribute(prefill_attention_kernel<HS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        raised = true;
-    }
+    if (const int ae = opt_in_smem(reinterpret_cast<const void *>(prefill_attention_kernel<HS>), int(smem)))
+        return fail(SI_ERR_CUDA, "prefill attention shared-memory opt-in failed: %s",
+                    cudaGetErrorString(cudaError_t(ae)));
     const dim3 grid(unsigned(query_heads), unsigned((count + kPfRows - 1) / kPfRows));
     return launch("transformer.batch-grouped-query-attention", prefill_attention_kernel<HS>, grid, dim3(kPfThreads),
                   smem, stream, query, kc, vc, start, count, out, query_heads, query_heads / kv_heads, kv_heads,

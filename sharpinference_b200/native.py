@@ -85,6 +85,8 @@ SIGNATURES = {
     "si_synth_weight_rows_device": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _vp],
     "si_matvec": [_u32, _vp, _u32, _vp, _u32, _vp, _i64, _i64, _u32, _vp],
     "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "si_gemv_default_plan": [_u32, _i64, _i64, _vp],
+    "si_matvec_quant_planned": [_u32, _vp, _vp, _vp, _i64, _i64, _vp, _vp],
     "si_matrix_multiply_workspace_bytes": [_u32, _i64, _i64, _i64, _pu64],
     "si_matrix_multiply": [_u32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _u64, _vp],
     "si_matrix_multiply_static_workspace": [_u32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -359,6 +361,29 @@ def dequantize(wtype: int, blob, count: int):
 
 
 # ---- executor ----------------------------------------------------------------------
+class GemvPlan(C.Structure):
+    """si_gemv_plan: launch shape of the tensor-core Q8_0 / Q4_K GEMV."""
+    _fields_ = [(n, C.c_int32) for n in ("cluster", "rows_per_tile", "smem_kb", "mma_path", "warps_per_column",
+                                         "superblocks_per_warp", "ctas_per_sm", "max_groups")]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def gemv_default_plan(wtype: int, rows: int, cols: int) -> GemvPlan:
+    plan = GemvPlan()
+    call("si_gemv_default_plan", wtype, rows, cols, C.byref(plan))
+    return plan
+
+
+def gemv_plan(**fields) -> GemvPlan:
+    """A plan with the default's fields for a K = 3072 matrix, overridden by `fields`."""
+    base = {"cluster": 1, "rows_per_tile": 32, "smem_kb": 226, "mma_path": 1, "warps_per_column": 1,
+            "superblocks_per_warp": 0, "ctas_per_sm": 1, "max_groups": 0}
+    base.update(fields)
+    return GemvPlan(**base)
+
+
 class Buffer:
     """A device slot owned by a Context (D3D12VmResourcePool-style ownership)."""
 
@@ -445,6 +470,11 @@ class Context:
                input_offset=0, output_offset=0, input_type=F32, output_type=F32, config=MATVEC_DEFAULT):
         call("si_ctx_matvec", self.handle, wtype, weight.handle, weight_offset, input_type, input.handle,
              input_offset, output_type, output.handle, output_offset, rows, cols, config)
+
+    def matvec_planned(self, wtype, weight: Buffer, input: Buffer, output: Buffer, rows, cols, plan: "GemvPlan"):
+        """core.mat-vec on Q8_0 / Q4_K weights with an explicit launch shape, on this context's stream."""
+        call("si_matvec_quant_planned", wtype, weight.device_pointer, input.device_pointer, output.device_pointer,
+             rows, cols, C.byref(plan), self.stream)
 
     def batch_shared_matvec(self, wtype, weight: Buffer, input: Buffer, control: Buffer, output: Buffer, batch,
                             out_features, in_features, *, weight_offset=0, input_offset=0, control_offset=0,

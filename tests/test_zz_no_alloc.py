@@ -48,6 +48,36 @@ def test_static_workspace_matches_allocating_entry_point(ctx, wtype, m, n, k):
             b.free()
 
 
+def _align256(v):
+    return (v + 255) // 256 * 256
+
+
+def test_static_workspace_call_allocates_nothing(ctx):
+    """The entry point's claim: after the first call on a device (which looks
+    up the array's address), a call takes no device memory. The shape splits
+    K, so the partial sums live in the shared array too."""
+    import torch
+    wtype, m, n, k = N.Q4_K, 512, 640, 3072
+    need = C.c_uint64()
+    native.check(native.lib.si_matrix_multiply_workspace_bytes(wtype, m, n, k, C.byref(need)))
+    assert need.value > 2 * _align256(m * k * 2), "shape must split K (partial sums in the workspace)"
+    blob = native.synth_weights(wtype, 23, n, k, 0.02)
+    W, X, Y = ctx.buffer(blob.nbytes), ctx.buffer(m * k * 4), ctx.buffer(m * n * 4)
+    try:
+        W.upload(blob)
+        X.upload(native.synth_normal(41, m * k, 1.0))
+        for _ in range(2):  # first calls: address lookup and kernel module loading
+            _static_call(ctx, wtype, X, W, Y, m, n, k)
+        free_before, _ = torch.cuda.mem_get_info(0)
+        for _ in range(3):
+            _static_call(ctx, wtype, X, W, Y, m, n, k)
+        free_after, _ = torch.cuda.mem_get_info(0)
+        assert free_after == free_before, f"device memory changed by {free_before - free_after} bytes"
+    finally:
+        for b in (W, X, Y):
+            b.free()
+
+
 def test_static_workspace_rejects_oversized_request(ctx):
     m, n, k = 4096, 128, 8192  # needs 4*m*k = 128 MiB of scratch
     W, X, Y = ctx.buffer(native.row_bytes(N.Q4_K, k) * n), ctx.buffer(m * k * 4), ctx.buffer(m * n * 4)
