@@ -864,7 +864,9 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
                          "achieved": round(bytes_per_token * tok_s / 1e9, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(bytes_per_token * tok_s / 1e9 / peak, 4),
                          "ideal_tok_s": round(peak * 1e9 / bytes_per_token, 1)},
-            "launches_per_token": 1 + 9 * cfg["layers"] + 3,
+            # gather-row, five per layer (qkv with its norm, attention with rope-kv-write, out with the
+            # residual add, gate_up with its norm, down with swiglu and the residual add), vocabulary, argmax
+            "launches_per_token": 1 + 5 * cfg["layers"] + 2,
             "clocks": clk.summary(),
             "first_tokens": [int(t) for t in toks[:8]],
         })

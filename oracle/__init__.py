@@ -14,7 +14,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "liboracle.so"
 
-F32, F16, Q8_0, Q4_K = 0, 1, 8, 12
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
 
 
 def build(force: bool = False) -> Path:
@@ -38,6 +38,8 @@ def _load() -> C.CDLL:
         "or_dequantize_q8_0": ([vp, i64, vp], None),
         "or_quantize_q4_k": ([vp, i64, vp], None),
         "or_dequantize_q4_k": ([vp, i64, vp], None),
+        "or_quantize_q6_k": ([vp, i64, vp], None),
+        "or_dequantize_q6_k": ([vp, i64, vp], None),
         "or_dequantize_row": ([u32, vp, i64, vp], i32),
         "or_matvec": ([u32, vp, vp, vp, i64, i64, i32], i32),
         "or_matvec_f64": ([u32, vp, vp, vp, i64, i64, i32], i32),
@@ -70,6 +72,7 @@ def _load() -> C.CDLL:
         "or_copy_embedding_rows": ([vp, vp, i64, i64, i64], None),
         "or_rope_frequencies": ([C.c_float, i32, vp], None),
         "or_decoder_step": ([vp, vp, vp, vp, vp, C.c_int32, C.c_int32, vp, C.POINTER(C.c_int32), i32], i32),
+        "or_decoder_step_typed": ([vp, vp, vp, vp, vp, vp, C.c_int32, C.c_int32, vp, C.POINTER(C.c_int32), i32], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -126,8 +129,9 @@ def normal(seed: int, count: int, sigma: float = 1.0, offset: int = 0) -> np.nda
 def quantize(wtype: int, values: np.ndarray) -> np.ndarray:
     values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
     out = np.empty(byte_length(wtype, values.size), dtype=np.uint8)
-    if wtype in (Q8_0, Q4_K):
-        fn, per, nb = (lib.or_quantize_q8_0, 32, 34) if wtype == Q8_0 else (lib.or_quantize_q4_k, 256, 144)
+    if wtype in (Q8_0, Q4_K, Q6_K):
+        fn, per, nb = {Q8_0: (lib.or_quantize_q8_0, 32, 34), Q4_K: (lib.or_quantize_q4_k, 256, 144),
+                       Q6_K: (lib.or_quantize_q6_k, 256, 210)}[wtype]
         if values.size < _PAR_MIN or values.size % per:
             fn(_ptr(values), values.size, _ptr(out))
         else:  # blocks are independent
@@ -391,8 +395,9 @@ class Decoder:
     """The Phi-4 decode program on the CPU (or_decoder_step). `weights` maps
     the reference's slot names to numpy arrays (raw GGUF bytes or FP32)."""
 
-    def __init__(self, cfg: dict, weights: dict, threads: int = 0):
+    def __init__(self, cfg: dict, weights: dict, threads: int = 0, slot_types=None):
         self.cfg = DecoderConfig(**cfg)
+        self._types = None if slot_types is None else (C.c_uint32 * len(slot_types))(*slot_types)
         c = self.cfg
         names = ["token_embedding", "output_norm"]
         for layer in range(c.layers):
@@ -410,9 +415,9 @@ class Decoder:
 
     def forward_token(self, token: int) -> int:
         nxt = C.c_int32()
-        _check(lib.or_decoder_step(C.byref(self.cfg), self._ptrs, _ptr(self.freq), _ptr(self.key_cache),
-                                   _ptr(self.value_cache), token, self.position, _ptr(self.logits), C.byref(nxt),
-                                   self.threads), "decoder_step")
+        _check(lib.or_decoder_step_typed(C.byref(self.cfg), self._ptrs, self._types, _ptr(self.freq),
+                                         _ptr(self.key_cache), _ptr(self.value_cache), token, self.position,
+                                         _ptr(self.logits), C.byref(nxt), self.threads), "decoder_step")
         self.position += 1
         return int(nxt.value)
 

@@ -90,6 +90,9 @@ int or_byte_length(uint32_t type, uint64_t elements, uint64_t *bytes) {
     case OR_Q4_K:
         if (elements % OR_Q4_K_BLOCK) return -2;
         *bytes = elements / OR_Q4_K_BLOCK * OR_Q4_K_BYTES; return 0;
+    case OR_Q6_K:
+        if (elements % OR_Q6_K_BLOCK) return -2;
+        *bytes = elements / OR_Q6_K_BLOCK * OR_Q6_K_BYTES; return 0;
     default: return -1;
     }
 }
@@ -204,6 +207,71 @@ void or_dequantize_q4_k(const uint8_t *blocks, int64_t n, float *out) {
     }
 }
 
+/* Q6_K superblock (GGUF layout, 210 bytes): ql[128] low four bits, qh[64] high
+ * two bits, 16 int8 sub-block scales, fp16 d. Element e = 128h + 32j + l
+ * (h < 2, j < 4, l < 32): low bits = ql[64h + l + 32(j & 1)] >> 4(j >> 1),
+ * high bits = (qh[32h + l] >> 2j) & 3, q = low | high << 4 in [0, 63];
+ * w = (d * scale[e / 16]) * (q - 32). */
+static int q6k_code(const uint8_t *o, int e) {
+    const int h = e >> 7, j = (e >> 5) & 3, l = e & 31;
+    const int low = (o[64 * h + l + 32 * (j & 1)] >> (4 * (j >> 1))) & 15;
+    const int high = (o[128 + 32 * h + l] >> (2 * j)) & 3;
+    return low | (high << 4);
+}
+
+/* Quantiser of this restatement (the format's reader is what parity needs):
+ * per 16-element group a scale s = absmax / 31; d = max s / 127 as fp16;
+ * scale = round(s / d) in [0, 127] (1 when s > 0 rounds to 0);
+ * q = round(x / (d * scale)) + 32 clamped to [0, 63]. */
+void or_quantize_q6_k(const float *x, int64_t n, uint8_t *out) {
+    for (int64_t b = 0; b < n / OR_Q6_K_BLOCK; ++b) {
+        const float *v = x + b * OR_Q6_K_BLOCK;
+        uint8_t *o = out + b * OR_Q6_K_BYTES;
+        float gs[16], smax = 0.0f;
+        for (int g = 0; g < 16; ++g) {
+            float amax = 0.0f;
+            for (int i = 0; i < 16; ++i) {
+                float t = fabsf(v[16 * g + i]);
+                if (t > amax) amax = t;
+            }
+            gs[g] = amax / 31.0f;
+            if (gs[g] > smax) smax = gs[g];
+        }
+        uint16_t dh = or_f32_to_f16(smax / 127.0f);
+        float d = or_f16_to_f32(dh);
+        int sc[16];
+        for (int g = 0; g < 16; ++g) {
+            sc[g] = d > 0.0f ? (int)clampf(roundf(gs[g] / d), 0.0f, 127.0f) : 0;
+            if (sc[g] == 0 && gs[g] > 0.0f && d > 0.0f) sc[g] = 1;
+        }
+        uint8_t q[256];
+        for (int e = 0; e < 256; ++e) {
+            float a = d * (float)sc[e / 16];
+            q[e] = a > 0.0f ? (uint8_t)(clampf(roundf(v[e] / a), -32.0f, 31.0f) + 32.0f) : 32;
+        }
+        memset(o, 0, OR_Q6_K_BYTES);
+        for (int e = 0; e < 256; ++e) {
+            const int h = e >> 7, j = (e >> 5) & 3, l = e & 31;
+            o[64 * h + l + 32 * (j & 1)] |= (uint8_t)((q[e] & 15) << (4 * (j >> 1)));
+            o[128 + 32 * h + l] |= (uint8_t)((q[e] >> 4) << (2 * j));
+        }
+        for (int g = 0; g < 16; ++g) o[192 + g] = (uint8_t)(int8_t)sc[g];
+        wr16(o + 208, dh);
+    }
+}
+
+void or_dequantize_q6_k(const uint8_t *blocks, int64_t n, float *out) {
+    for (int64_t b = 0; b < n / OR_Q6_K_BLOCK; ++b) {
+        const uint8_t *o = blocks + b * OR_Q6_K_BYTES;
+        float d = or_f16_to_f32(rd16(o + 208));
+        float *w = out + b * OR_Q6_K_BLOCK;
+        for (int e = 0; e < 256; ++e) {
+            float a = d * (float)(int8_t)o[192 + e / 16];
+            w[e] = a * (float)(q6k_code(o, e) - 32);
+        }
+    }
+}
+
 int or_dequantize_row(uint32_t type, const void *row, int64_t cols, float *out) {
     switch (type) {
     case OR_F32: memcpy(out, row, (size_t)cols * 4); return 0;
@@ -218,6 +286,9 @@ int or_dequantize_row(uint32_t type, const void *row, int64_t cols, float *out) 
     case OR_Q4_K:
         if (cols % 256) return -2;
         or_dequantize_q4_k((const uint8_t *)row, cols, out); return 0;
+    case OR_Q6_K:
+        if (cols % 256) return -2;
+        or_dequantize_q6_k((const uint8_t *)row, cols, out); return 0;
     default: return -1;
     }
 }

@@ -10,12 +10,14 @@
  *     (GpuMatVecTests.cs:13-67, CpuVmMixedWeightsTests.cs:62-104,
  *     GpuTransformerInstructionTests.cs:280-324); the fixtures live in
  *     tests/golden/ with the script that writes them.
- *   - Q8_0 / Q4_K: the reference has no quantized arithmetic
- *     (GgufModelFile.cs:314-320 throws for Q4_K). The block layouts follow the
- *     published GGUF format; dequantisation is exact FP32 arithmetic defined
- *     here. No GGUF quantized golden vector exists in the reference, so
- *     parity with externally produced GGUF files is UNPINNED. Kernel and
- *     oracle consume identical block bytes.
+ *   - Q8_0 / Q4_K / Q6_K: the reference has no quantized arithmetic
+ *     (GgufModelFile.cs:314-320 throws for the K-quants). The block layouts
+ *     follow the published GGUF format; dequantisation is exact FP32
+ *     arithmetic. The dequantisers are pinned bit for bit to an independent
+ *     implementation, gguf-py 0.19.0 (`gguf.quants.dequantize`, llama.cpp's
+ *     Python package), on the BASELINE workloads' blocks and on random valid
+ *     blocks (tests/test_gguf_reference_codecs.py); the Q8_0 quantiser is
+ *     pinned to gguf-py's too. Kernel and oracle consume identical bytes.
  *   - TensorPrimitives.Dot (System.Numerics.Tensors 10.0.0) does not specify
  *     its SIMD summation order, so bitwise parity with the CPU path is
  *     unpinned; the restatement uses an 8-lane FP32 accumulation.
@@ -31,7 +33,7 @@ extern "C" {
 #endif
 
 /* GGUF tensor type ids (GgufModelFile.cs:24-46). */
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12 };
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q6_K = 14 };
 
 /* Block geometry: Q8_0 34 B / 32 elements (GgufModelFile.cs:318),
  * Q4_K 144 B / 256 elements (absent from the reference; GGUF format). */
@@ -39,6 +41,9 @@ enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12 };
 #define OR_Q8_0_BYTES 34
 #define OR_Q4_K_BLOCK 256
 #define OR_Q4_K_BYTES 144
+/* Q6_K 210 B / 256 elements (GGUF format; the reference's table stops at Q8_1). */
+#define OR_Q6_K_BLOCK 256
+#define OR_Q6_K_BYTES 210
 
 /* ---- seeded synthetic inputs ------------------------------------------ */
 uint64_t or_splitmix64(uint64_t seed, uint64_t index);
@@ -56,6 +61,8 @@ void or_quantize_q8_0(const float *x, int64_t n, uint8_t *out);
 void or_dequantize_q8_0(const uint8_t *blocks, int64_t n, float *out);
 void or_quantize_q4_k(const float *x, int64_t n, uint8_t *out);
 void or_dequantize_q4_k(const uint8_t *blocks, int64_t n, float *out);
+void or_quantize_q6_k(const float *x, int64_t n, uint8_t *out);
+void or_dequantize_q6_k(const uint8_t *blocks, int64_t n, float *out);
 /* Dequantise one row of `cols` elements of any supported type. */
 int or_dequantize_row(uint32_t type, const void *row, int64_t cols, float *out);
 
@@ -144,6 +151,9 @@ void or_rope_frequencies(float base, int rotary_size, float *out);
 int or_decoder_step(const or_decoder_config *cfg, const void *const *w, const float *freq, float *key_cache,
                     float *value_cache, int32_t token, int32_t position, float *logits, int32_t *next_token,
                     int threads);
+int or_decoder_step_typed(const or_decoder_config *cfg, const void *const *w, const uint32_t *types,
+                          const float *freq, float *key_cache, float *value_cache, int32_t token, int32_t position,
+                          float *logits, int32_t *next_token, int threads);
 
 #ifdef __cplusplus
 }

@@ -408,6 +408,15 @@ void or_batch_gather_rows(const float *table, int64_t rows, const int32_t *contr
 int or_decoder_step(const or_decoder_config *cfg, const void *const *w, const float *freq, float *key_cache,
                     float *value_cache, int32_t token, int32_t position, float *logits, int32_t *next_token,
                     int threads) {
+    return or_decoder_step_typed(cfg, w, NULL, freq, key_cache, value_cache, token, position, logits, next_token,
+                                 threads);
+}
+
+/* The same program with a GGUF type per slot (`types` in the order of `w`,
+ * NULL: cfg's weight_type for every projection), as a mixed-type file holds. */
+int or_decoder_step_typed(const or_decoder_config *cfg, const void *const *w, const uint32_t *types,
+                          const float *freq, float *key_cache, float *value_cache, int32_t token, int32_t position,
+                          float *logits, int32_t *next_token, int threads) {
     const int64_t H = cfg->hidden, Q = (int64_t)cfg->query_heads * cfg->head_size,
                   KV = (int64_t)cfg->kv_heads * cfg->head_size, F = cfg->intermediate;
     if (Q != H) return -3;
@@ -421,17 +430,20 @@ int or_decoder_step(const or_decoder_config *cfg, const void *const *w, const fl
     const int64_t layer_cache = cfg->context * KV;
     for (int l = 0; l < cfg->layers && !rc; ++l) {
         const void *const *lw = w + 2 + 6 * l;
+        const uint32_t *lt = types ? types + 2 + 6 * l : NULL;
+        const uint32_t tq = lt ? lt[2] : cfg->weight_type, to = lt ? lt[3] : cfg->weight_type,
+                       tu = lt ? lt[4] : cfg->weight_type, td = lt ? lt[5] : cfg->weight_type;
         float *kc = key_cache + l * layer_cache, *vc = value_cache + l * layer_cache;
-        if ((rc = or_matvec(cfg->weight_type, lw[2], normalized, qkv, Q + 2 * KV, H, threads))) break;
+        if ((rc = or_matvec(tq, lw[2], normalized, qkv, Q + 2 * KV, H, threads))) break;
         or_rope_kv_write(qkv, position, freq, query, kc, vc, Q, KV, cfg->head_size, cfg->rotary_size, cfg->context,
                          cfg->rope_scale);
         or_grouped_query_attention(query, kc, vc, position, attention, cfg->query_heads, cfg->kv_heads,
                                    cfg->head_size, cfg->context);
-        if ((rc = or_matvec(cfg->weight_type, lw[3], attention, projected, H, Q, threads))) break;
+        if ((rc = or_matvec(to, lw[3], attention, projected, H, Q, threads))) break;
         or_residual_rms_norm(hidden, projected, (const float *)lw[1], after, normalized, H, cfg->epsilon);
-        if ((rc = or_matvec(cfg->weight_type, lw[4], normalized, gate_up, 2 * F, H, threads))) break;
+        if ((rc = or_matvec(tu, lw[4], normalized, gate_up, 2 * F, H, threads))) break;
         or_swiglu(gate_up, activated, F);
-        if ((rc = or_matvec(cfg->weight_type, lw[5], activated, down, H, F, threads))) break;
+        if ((rc = or_matvec(td, lw[5], activated, down, H, F, threads))) break;
         const float *next_norm = l == cfg->layers - 1 ? (const float *)w[1] : (const float *)w[2 + 6 * (l + 1)];
         or_residual_rms_norm(after, down, next_norm, hidden, normalized, H, cfg->epsilon);
     }

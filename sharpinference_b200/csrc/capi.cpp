@@ -99,7 +99,7 @@ si_status validate_matvec(uint32_t wtype, const void *w, uint32_t xtype, const v
     if (uint64_t(rows) > 0xFFFFFFFFull / 64)
         return fail(SI_ERR_INVALID_ARGUMENT, "Cooperative MatVec exceeds 32-bit thread indexing.");
     if (!known_type(wtype)) return fail(SI_ERR_UNSUPPORTED, "GGUF tensor type '%u' is not supported.", wtype);
-    const bool quant = wtype == SI_TYPE_Q8_0 || wtype == SI_TYPE_Q4_K;
+    const bool quant = wtype == SI_TYPE_Q8_0 || wtype == SI_TYPE_Q4_K || wtype == SI_TYPE_Q6_K;
     if ((xtype != SI_TYPE_F32 && xtype != SI_TYPE_F16) || (ytype != SI_TYPE_F32 && ytype != SI_TYPE_F16))
         return fail(SI_ERR_ADAPTATION, "core.mat-vec: input and output must be F32 or F16.");
     if (quant && (xtype != SI_TYPE_F32 || ytype != SI_TYPE_F32))
@@ -130,7 +130,7 @@ si_status validate_matvec(uint32_t wtype, const void *w, uint32_t xtype, const v
 
 si_status run_matvec(uint32_t wtype, const void *w, uint32_t xtype, const void *x, uint32_t ytype, void *y,
                      int64_t rows, int64_t cols, void *stream) {
-    if (wtype == SI_TYPE_Q8_0 || wtype == SI_TYPE_Q4_K)
+    if (wtype == SI_TYPE_Q8_0 || wtype == SI_TYPE_Q4_K || wtype == SI_TYPE_Q6_K)
         return kernels::matvec_quant(wtype, w, static_cast<const float *>(x), static_cast<float *>(y), rows, cols,
                                      stream);
     return kernels::matvec_dense(wtype, w, xtype, x, ytype, y, rows, cols, stream);
@@ -609,7 +609,7 @@ si_status si_instruction_resolve(const char *collection_id, const char *name, in
 si_status si_instruction_validate(int instruction_id, const uint32_t *t, int n, const char *configuration) {
     if (!t && n) return fail(SI_ERR_INVALID_ARGUMENT, "null port types");
     const char *cfg = configuration ? configuration : "";
-    auto quant = [](uint32_t v) { return v == SI_TYPE_Q8_0 || v == SI_TYPE_Q4_K; };
+    auto quant = [](uint32_t v) { return v == SI_TYPE_Q8_0 || v == SI_TYPE_Q4_K || v == SI_TYPE_Q6_K; };
     switch (instruction_id) {
     case kMatVec32:
     case kMatVec16: {

@@ -37,6 +37,9 @@ struct si_decoder {
     const float *output_norm = nullptr;
     std::vector<const float *> attn_norm, ffn_norm;
     std::vector<const void *> w_qkv, w_out, w_up, w_down;
+    // GGUF type of every layer's projection weights (one type for all of them
+    // unless the session was created with per-slot types, as a Q4_K_M file has)
+    std::vector<uint32_t> t_qkv, t_out, t_up, t_down;
     std::vector<float *> key_cache, value_cache;
     float *freq = nullptr;
     int32_t *control = nullptr, *next_token = nullptr, *prompt = nullptr, *history = nullptr;
@@ -69,6 +72,14 @@ struct si_decoder {
     bool sharded[5] = {false, false, false, false, false};
     // The projection outputs of even / odd layers (arena regions).
     float *par_qkv[2] = {}, *par_out[2] = {}, *par_up[2] = {}, *par_down[2] = {};
+    // Tensor-parallel session (si_decoder_create_tensor_parallel): this rank's
+    // partition, the residual stream in two local buffers, and the exchange
+    // descriptors of the out / down partial sums and the vocabulary rows.
+    bool tp = false;
+    si_tp_partition part{};
+    float *res_a = nullptr, *res_b = nullptr;
+    float *o_parts = nullptr, *down_parts = nullptr;  // [nranks][hidden] in this rank's arena
+    k::PeerGather pg_out{}, pg_down{}, pg_vocab{};
     // Multi-stream session (si_decoder_create_streams): `streams` rows per
     // step, stream b's caches at rows b * context of each layer's cache;
     // per-stream tokens / positions / greedy-loop state on the device.
@@ -148,7 +159,8 @@ void destroy(si_decoder *d) {
 
 si_status project(uint32_t type, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                   cudaStream_t s) {
-    if (type == SI_TYPE_Q8_0 || type == SI_TYPE_Q4_K) return k::matvec_quant(type, w, x, y, rows, cols, s);
+    if (type == SI_TYPE_Q8_0 || type == SI_TYPE_Q4_K || type == SI_TYPE_Q6_K)
+        return k::matvec_quant(type, w, x, y, rows, cols, s);
     return k::matvec_dense(type, w, SI_TYPE_F32, x, SI_TYPE_F32, y, rows, cols, s);
 }
 
@@ -211,7 +223,7 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
         // row-sharded: this layer's copy of the projection outputs
         float *qkv = d->group ? d->par_qkv[l & 1] : d->qkv, *projected = d->group ? d->par_out[l & 1] : d->projected;
         float *gate_up = d->group ? d->par_up[l & 1] : d->gate_up, *down = d->group ? d->par_down[l & 1] : d->down;
-        if (si_status st = project_rows(d, si_decoder::kQkv, c.weight_type, d->w_qkv[l], d->normalized, qkv, QKV, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kQkv, d->t_qkv[l], d->w_qkv[l], d->normalized, qkv, QKV, H)) return st;
         if (si_status st = k::tr_rope_kv_write(qkv, position, nullptr, d->freq, d->query, d->key_cache[l],
                                                d->value_cache[l], 1, H, KV, c.head_size, c.rotary_size, c.context,
                                                c.rope_scale, s))
@@ -219,13 +231,13 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
         if (si_status st = k::tr_attention_decode(d->query, d->key_cache[l], d->value_cache[l], position, d->attention,
                                                   c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
-        if (si_status st = project_rows(d, si_decoder::kOut, c.weight_type, d->w_out[l], d->attention, projected, H, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kOut, d->t_out[l], d->w_out[l], d->attention, projected, H, H)) return st;
         if (si_status st = k::tr_rms_norm(d->hidden, projected, d->ffn_norm[l], nullptr, d->after, d->normalized, 1,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = project_rows(d, si_decoder::kUp, c.weight_type, d->w_up[l], d->normalized, gate_up, 2 * F, H)) return st;
+        if (si_status st = project_rows(d, si_decoder::kUp, d->t_up[l], d->w_up[l], d->normalized, gate_up, 2 * F, H)) return st;
         if (si_status st = k::tr_swiglu(gate_up, nullptr, d->activated, 1, F, s)) return st;
-        if (si_status st = project_rows(d, si_decoder::kDown, c.weight_type, d->w_down[l], d->activated, down, H, F)) return st;
+        if (si_status st = project_rows(d, si_decoder::kDown, d->t_down[l], d->w_down[l], d->activated, down, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
         if (si_status st = k::tr_rms_norm(d->after, down, next_norm, nullptr, d->hidden, d->normalized, 1, H,
                                           c.epsilon, s))
@@ -235,11 +247,78 @@ si_status record_step_unfused(si_decoder *d, k::DecodeFeed *feed) {
     return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
 }
 
-// One decode step on d->stream: the persistent step's launch, or the
-// program instruction by instruction (nine launches per layer, each
-// programmatically dependent on the previous one).
+// The decode program with each small instruction fused into a neighbouring
+// launch, five launches per layer (one GPU, Q4_K / Q8_0 projections):
+//   qkv GEMV        rms-norm(hidden, attn_norm) fused into its input load
+//   attention       rope-kv-write fused in (q and k rotated from qkv, the
+//                   token's k / v rows stored into the caches)
+//   out GEMV        residual add in its epilogue: hidden += W_o attention
+//   gate_up GEMV    rms-norm(hidden, ffn_norm) fused into its input load
+//   down GEMV       swiglu(gate_up) fused into its input load, residual add:
+//                   hidden += W_down swiglu(gate_up)
+// then the vocabulary GEMV with rms-norm(hidden, output_norm) and argmax.
+// The residual stream lives in `hidden` (updated in place); the reference's
+// separate after / normalized / activated vectors are never materialised.
+// The arithmetic is the instructions' own except for the order of two
+// roundings: the norm scale 1/rms multiplies each output row instead of each
+// input element (W (x * s * w) = s * (W (x * w))).
+bool fused_step_supported(const si_decoder *d) {
+    const si_decoder_config &c = d->cfg;
+    const auto quant = [](uint32_t t) { return t == SI_TYPE_Q4_K || t == SI_TYPE_Q8_0; };
+    for (int l = 0; l < c.layers; ++l)
+        if (!quant(d->t_qkv[l]) || !quant(d->t_out[l]) || !quant(d->t_up[l]) || !quant(d->t_down[l])) return false;
+    return !d->group && d->streams == 1 && quant(c.embedding_type) && c.hidden % 256 == 0 &&
+           c.intermediate % 256 == 0 && c.rotary_size % 2 == 0;
+}
+
+si_status record_step_fused(si_decoder *d, k::DecodeFeed *feed) {
+    const si_decoder_config &c = d->cfg;
+    const int64_t H = c.hidden, KV = int64_t(c.kv_heads) * c.head_size, QKV = H + 2 * KV, F = c.intermediate;
+    cudaStream_t s = d->stream;
+    int32_t *position = d->control + 1;
+    auto gemv = [&](const void *w, const float *x, float *y, int64_t rows, int64_t cols, int in_mode,
+                    const float *norm, const float *resid, uint32_t type) -> si_status {
+        k::GemvFusion f;
+        f.in_mode = in_mode;
+        f.norm_w = norm;
+        f.eps = c.epsilon;
+        f.resid = resid;
+        const si_status st = k::matvec_quant_fused(type, w, x, y, rows, cols, f, s);
+        if (st == SI_ERR_UNSUPPORTED)
+            return fail(SI_ERR_UNSUPPORTED, "fused decode step: no tensor-core GEMV for [%lld, %lld]", (long long)rows,
+                        (long long)cols);
+        return st;
+    };
+    if (si_status st = k::tr_gather_row(c.embedding_type, d->embedding, c.vocab, H, d->control, d->hidden, s)) return st;
+    for (int l = 0; l < c.layers; ++l) {
+        if (si_status st = gemv(d->w_qkv[l], d->hidden, d->qkv, QKV, H, 1, d->attn_norm[l], nullptr, d->t_qkv[l]))
+            return st;
+        if (si_status st = k::tr_attention_decode_rope(d->qkv, position, d->freq, d->key_cache[l], d->value_cache[l],
+                                                       d->attention, c.query_heads, c.kv_heads, c.head_size,
+                                                       c.rotary_size, c.context, c.rope_scale, s))
+            return st;
+        if (si_status st = gemv(d->w_out[l], d->attention, d->hidden, H, H, 0, nullptr, d->hidden, d->t_out[l]))
+            return st;
+        if (si_status st = gemv(d->w_up[l], d->hidden, d->gate_up, 2 * F, H, 1, d->ffn_norm[l], nullptr, d->t_up[l]))
+            return st;
+        if (si_status st = gemv(d->w_down[l], d->gate_up, d->hidden, H, F, 2, nullptr, d->hidden, d->t_down[l]))
+            return st;
+    }
+    if (si_status st = gemv(d->w_vocab, d->hidden, d->logits, c.vocab, H, 1, d->output_norm, nullptr, c.embedding_type))
+        return st;
+    return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
+}
+
+// One decode step on d->stream: the persistent step's launch, the fused
+// program (five launches per layer) or the program instruction by
+// instruction (nine launches per layer); every launch programmatically
+// dependent on the previous one.
+si_status record_step_tp(si_decoder *d, k::DecodeFeed *feed);
+
 si_status record_step(si_decoder *d, k::DecodeFeed *feed) {
+    if (d->tp) return record_step_tp(d, feed);
     if (d->step) return k::decode_step_launch(d->step, feed, d->stream);
+    if (fused_step_supported(d)) return record_step_fused(d, feed);
     return record_step_unfused(d, feed);
 }
 
@@ -296,7 +375,11 @@ si_status ensure_prefill(si_decoder *d) {
     for (auto [n, kk] : {std::pair<int64_t, int64_t>{QKV, H}, {H, H}, {2 * F, H}, {H, F}})
         for (int64_t rows = 64; rows <= R; rows += 64) {  // the split count depends on the rows
             uint64_t b = 0;
-            k::gemm_workspace_bytes(c.weight_type, rows, n, kk, &b);
+            for (uint32_t t : {d->t_qkv[0], d->t_out[0], d->t_up[0], d->t_down[0], uint32_t(SI_TYPE_Q4_K),
+                               uint32_t(SI_TYPE_Q8_0)}) {
+                k::gemm_workspace_bytes(t, rows, n, kk, &b);
+                ws = std::max(ws, b);
+            }
             ws = std::max(ws, b);
         }
     if (ws) {
@@ -311,8 +394,9 @@ si_status ensure_prefill(si_decoder *d) {
 
 // Y[rows, n] = X[rows, k] W^T: the tcgen05 GEMM from 64 rows, the batch
 // GEMV below that.
-si_status batch_project(si_decoder *d, const void *w, const float *x, float *y, int64_t rows, int64_t n, int64_t k) {
-    return k::gemm_tn(d->cfg.weight_type, x, w, y, rows, n, k, d->pf.workspace, d->pf.workspace_bytes, d->stream);
+si_status batch_project(si_decoder *d, uint32_t type, const void *w, const float *x, float *y, int64_t rows, int64_t n,
+                        int64_t k) {
+    return k::gemm_tn(type, x, w, y, rows, n, k, d->pf.workspace, d->pf.workspace_bytes, d->stream);
 }
 
 // The prefill program of one chunk (Phi4D3D12TextSession.cs:1018-1155) on
@@ -330,7 +414,7 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
                                       c.epsilon, s))
         return st;
     for (int l = 0; l < c.layers; ++l) {
-        if (si_status st = batch_project(d, d->w_qkv[l], P.normalized, P.qkv, rows, QKV, H)) return st;
+        if (si_status st = batch_project(d, d->t_qkv[l], d->w_qkv[l], P.normalized, P.qkv, rows, QKV, H)) return st;
         float *kc = d->key_cache[l] + cache_offset, *vc = d->value_cache[l] + cache_offset;
         if (si_status st = k::tr_rope_kv_write(P.qkv, nullptr, control, d->freq, P.query, kc, vc, rows, H, KV,
                                                c.head_size, c.rotary_size, c.context,
@@ -339,13 +423,13 @@ si_status prefill_chunk(si_decoder *d, const int32_t *control, int32_t start, in
         if (si_status st = k::tr_prefill_attention(P.query, kc, vc, start, rows,
                                                    P.attention, c.query_heads, c.kv_heads, c.head_size, c.context, s))
             return st;
-        if (si_status st = batch_project(d, d->w_out[l], P.attention, P.projected, rows, H, H)) return st;
+        if (si_status st = batch_project(d, d->t_out[l], d->w_out[l], P.attention, P.projected, rows, H, H)) return st;
         if (si_status st = k::tr_rms_norm(P.hidden, P.projected, d->ffn_norm[l], control, P.after, P.normalized, rows,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = batch_project(d, d->w_up[l], P.normalized, P.gate_up, rows, 2 * F, H)) return st;
+        if (si_status st = batch_project(d, d->t_up[l], d->w_up[l], P.normalized, P.gate_up, rows, 2 * F, H)) return st;
         if (si_status st = k::tr_swiglu(P.gate_up, control, P.activated, rows, F, s)) return st;
-        if (si_status st = batch_project(d, d->w_down[l], P.activated, P.down, rows, H, F)) return st;
+        if (si_status st = batch_project(d, d->t_down[l], d->w_down[l], P.activated, P.down, rows, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
         if (si_status st = k::tr_rms_norm(P.after, P.down, next_norm, control, P.hidden, P.normalized, rows, H,
                                           c.epsilon, s))
@@ -423,7 +507,7 @@ si_status record_step_streams(si_decoder *d, k::StreamsFeed *sfeed) {
                                       c.epsilon, s))
         return st;
     for (int l = 0; l < c.layers; ++l) {
-        if (si_status st = proj(c.weight_type, d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
+        if (si_status st = proj(d->t_qkv[l], d->w_qkv[l], d->normalized, d->qkv, QKV, H)) return st;
         if (si_status st = k::tr_rope_kv_write_streams(d->qkv, d->st_positions, d->freq, d->query, d->key_cache[l],
                                                        d->value_cache[l], B, H, KV, c.head_size, c.rotary_size,
                                                        c.context, stride, c.rope_scale, s))
@@ -432,13 +516,13 @@ si_status record_step_streams(si_decoder *d, k::StreamsFeed *sfeed) {
                                                           d->st_positions, d->attention, int(B), c.query_heads,
                                                           c.kv_heads, c.head_size, c.context, stride, s))
             return st;
-        if (si_status st = proj(c.weight_type, d->w_out[l], d->attention, d->projected, H, H)) return st;
+        if (si_status st = proj(d->t_out[l], d->w_out[l], d->attention, d->projected, H, H)) return st;
         if (si_status st = k::tr_rms_norm(d->hidden, d->projected, d->ffn_norm[l], nullptr, d->after, d->normalized, B,
                                           H, c.epsilon, s))
             return st;
-        if (si_status st = proj(c.weight_type, d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
+        if (si_status st = proj(d->t_up[l], d->w_up[l], d->normalized, d->gate_up, 2 * F, H)) return st;
         if (si_status st = k::tr_swiglu(d->gate_up, nullptr, d->activated, B, F, s)) return st;
-        if (si_status st = proj(c.weight_type, d->w_down[l], d->activated, d->down, H, F)) return st;
+        if (si_status st = proj(d->t_down[l], d->w_down[l], d->activated, d->down, H, F)) return st;
         const float *next_norm = l + 1 < c.layers ? d->attn_norm[l + 1] : d->output_norm;
         if (si_status st = k::tr_rms_norm(d->after, d->down, next_norm, nullptr, d->hidden, d->normalized, B, H,
                                           c.epsilon, s))
@@ -520,8 +604,11 @@ si_status validate(const si_decoder_config *c) {
 
 si_status create_step(si_decoder *d);
 
+// slot_types: null, or one GGUF type per slot of si_decoder_slot order
+// (token_embedding, output_norm, then per layer attn_norm, ffn_norm, qkv,
+// attn_output, ffn_up, ffn_down): the projections' own types.
 si_status create(int device, const si_decoder_config *c, si_peer_group *group, int32_t streams,
-                 uint64_t shard_min_bytes, si_decoder **out) {
+                 uint64_t shard_min_bytes, si_decoder **out, const uint32_t *slot_types = nullptr) {
     auto *d = new si_decoder();
     d->device = device;
     d->cfg = *c;
@@ -583,16 +670,25 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
         if (si_status st = alloc_typed(d, "ffn_norm_" + L, H * 4, &f)) return cleanup(st);
         if (si_status st = fill_ones(f, H)) return cleanup(st);
         d->ffn_norm.push_back(f);
-        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb_h * uint64_t(shard(si_decoder::kQkv, QKV, nullptr)), &p))
+        const uint32_t *lt = slot_types ? slot_types + 2 + 6 * l : nullptr;
+        const uint32_t tq = lt ? lt[2] : c->weight_type, to = lt ? lt[3] : c->weight_type,
+                       tu = lt ? lt[4] : c->weight_type, td = lt ? lt[5] : c->weight_type;
+        d->t_qkv.push_back(tq), d->t_out.push_back(to), d->t_up.push_back(tu), d->t_down.push_back(td);
+        auto rb = [](uint32_t t, int64_t cols) {
+            uint64_t b = 0;
+            si::byte_length(t, uint64_t(cols), &b);
+            return b;
+        };
+        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb(tq, H) * uint64_t(shard(si_decoder::kQkv, QKV, nullptr)), &p))
             return cleanup(st);
         d->w_qkv.push_back(p);
-        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb_h * uint64_t(shard(si_decoder::kOut, H, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb(to, H) * uint64_t(shard(si_decoder::kOut, H, nullptr)), &p))
             return cleanup(st);
         d->w_out.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb_h * uint64_t(shard(si_decoder::kUp, 2 * F, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb(tu, H) * uint64_t(shard(si_decoder::kUp, 2 * F, nullptr)), &p))
             return cleanup(st);
         d->w_up.push_back(p);
-        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb_f * uint64_t(shard(si_decoder::kDown, H, nullptr)), &p))
+        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb(td, F) * uint64_t(shard(si_decoder::kDown, H, nullptr)), &p))
             return cleanup(st);
         d->w_down.push_back(p);
         if (si_status st = alloc_typed(d, "key_cache_" + L, B * uint64_t(c->context) * KV * 4, &f)) return cleanup(st);
@@ -680,6 +776,240 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
     return SI_OK;
 }
 
+// ---- tensor-parallel session ------------------------------------------------
+// Megatron-style pairing of the decode program over the ranks of a peer
+// group, one GPU each:
+//   qkv       rows of this rank's key/value heads (their query, key and value
+//             rows), input = rms-norm of the residual stream
+//   attention this rank's heads only (rope-kv-write fused, local caches)
+//   out       K-parallel: W_o[:, this rank's query-head columns] times the
+//             local attention output; the partial vector goes to every
+//             rank's arena (the exchange is fused into the GEMV)
+//   gate_up   rows of this rank's slice of the intermediate (its gate rows
+//             and the matching up rows), input = rms-norm of (residual +
+//             the out partials of every rank, in rank order)
+//   down      K-parallel over the same slice, swiglu fused into its input,
+//             partial vector exchanged like out's
+// and the vocabulary projection row-sharded over the ranks (rows gathered
+// into every arena) after the final norm, then argmax on every rank. Two
+// exchanges per layer; every rank sums the partials in the same order, so
+// every rank holds bit-identical residual streams and picks the same token.
+// Region reuse: a rank enters the down exchange of layer l only after every
+// rank finished its out exchange of layer l, hence its gate_up of layer l
+// (the reader of the out partials) completes before any rank's out exchange
+// of layer l + 1 can start overwriting them; likewise for the down partials
+// and the next layer's qkv GEMV.
+struct TpLayout {
+    uint64_t o_parts, down_parts, logits, data_bytes;
+};
+
+TpLayout tp_layout(const si_decoder_config &c, int nranks) {
+    auto al = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    TpLayout t{};
+    uint64_t o = 0;
+    t.o_parts = o, o += al(uint64_t(nranks) * uint64_t(c.hidden) * 4);
+    t.down_parts = o, o += al(uint64_t(nranks) * uint64_t(c.hidden) * 4);
+    t.logits = o, o += al(uint64_t(c.vocab) * 4);
+    t.data_bytes = o;
+    return t;
+}
+
+// Contiguous split of `units` over n ranks, the first units % n ranks one more.
+void split_units(int64_t units, int n, int r, int64_t *begin, int64_t *count) {
+    const int64_t base = units / n, extra = units % n;
+    *count = base + (r < extra ? 1 : 0);
+    *begin = r * base + std::min<int64_t>(r, extra);
+}
+
+si_status tp_plan(const si_decoder_config &c, int n, int r, si_tp_partition *p) {
+    if (n < 1 || r < 0 || r >= n) return fail(SI_ERR_INVALID_ARGUMENT, "rank %d of %d ranks", r, n);
+    if (c.kv_heads < n)
+        return fail(SI_ERR_UNSUPPORTED, "%d key/value heads cannot be split over %d ranks", c.kv_heads, n);
+    const int G = c.query_heads / c.kv_heads;
+    int64_t b = 0, cnt = 0;
+    split_units(c.kv_heads, n, r, &b, &cnt);
+    p->kv_head_begin = int32_t(b), p->kv_heads = int32_t(cnt);
+    p->query_head_begin = int32_t(b * G), p->query_heads = int32_t(cnt * G);
+    // the intermediate in 256-element units: the down GEMV's K slice is whole superblocks
+    if (c.intermediate % 256) return fail(SI_ERR_UNSUPPORTED, "intermediate %d is not a multiple of 256", c.intermediate);
+    split_units(c.intermediate / 256, n, r, &b, &cnt);
+    if (cnt == 0) return fail(SI_ERR_UNSUPPORTED, "intermediate %d leaves rank %d without rows", c.intermediate, r);
+    p->ffn_begin = b * 256, p->ffn_rows = cnt * 256;
+    int64_t per = 0;
+    if (si_status st = si_rowshard_plan(c.vocab, n, r, &b, &cnt, &per)) return st;
+    if (per * (n - 1) >= c.vocab) return fail(SI_ERR_UNSUPPORTED, "vocabulary %d leaves a rank without rows", c.vocab);
+    p->vocab_begin = b, p->vocab_rows = cnt;
+    // the out projection's K slice (this rank's query-head columns) is whole superblocks too
+    for (int q = 0; q < n; ++q) {
+        int64_t kb, kc;
+        split_units(c.kv_heads, n, q, &kb, &kc);
+        if ((kb * G * c.head_size) % 256 || (kc * G * c.head_size) % 256)
+            return fail(SI_ERR_UNSUPPORTED,
+                        "the out projection's column slice of rank %d (%lld query heads of %d) is not a multiple of "
+                        "256 columns", q, (long long)(kc * G), c.head_size);
+    }
+    return SI_OK;
+}
+
+si_status record_step_tp(si_decoder *d, k::DecodeFeed *feed) {
+    const si_decoder_config &c = d->cfg;
+    const si_tp_partition &P = d->part;
+    const int64_t H = c.hidden, hs = c.head_size;
+    const int64_t qkv_local = int64_t(P.query_heads + 2 * P.kv_heads) * hs, q_cols = int64_t(P.query_heads) * hs;
+    const int nranks = d->pg_out.nranks;
+    cudaStream_t s = d->stream;
+    int32_t *position = d->control + 1;
+    auto gemv = [&](uint32_t type, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                    const k::GemvFusion &f, const k::PeerGather *peer) -> si_status {
+        const si_status st = k::matvec_quant_fused(type, w, x, y, rows, cols, f, s, peer);
+        if (st == SI_ERR_UNSUPPORTED)
+            return fail(SI_ERR_UNSUPPORTED, "tensor-parallel step: no tensor-core GEMV for [%lld, %lld]",
+                        (long long)rows, (long long)cols);
+        return st;
+    };
+    // the GEMV input: rms-norm of (x + parts[0] + ... + parts[nparts-1]), that sum stored to h_out
+    auto norm_of = [&](const float *parts, int nparts, const float *norm, float *h_out) {
+        k::GemvFusion f;
+        f.in_mode = 3;
+        f.norm_w = norm;
+        f.eps = c.epsilon;
+        f.parts = parts;
+        f.nparts = nparts;
+        f.part_stride = H;
+        f.h_out = h_out;
+        return f;
+    };
+    if (si_status st = k::tr_gather_row(c.embedding_type, d->embedding, c.vocab, H, d->control, d->res_b, s)) return st;
+    for (int l = 0; l < c.layers; ++l) {
+        // residual stream: res_b (+ the previous layer's down partials) -> res_a
+        if (si_status st = gemv(d->t_qkv[l], d->w_qkv[l], d->res_b, d->qkv, qkv_local, H,
+                                norm_of(d->down_parts, l ? nranks : 0, d->attn_norm[l], d->res_a), nullptr))
+            return st;
+        if (si_status st = k::tr_attention_decode_rope(d->qkv, position, d->freq, d->key_cache[l], d->value_cache[l],
+                                                       d->attention, P.query_heads, P.kv_heads, c.head_size,
+                                                       c.rotary_size, c.context, c.rope_scale, s))
+            return st;
+        if (si_status st = gemv(d->t_out[l], d->w_out[l], d->attention, nullptr, H, q_cols, k::GemvFusion{}, &d->pg_out))
+            return st;
+        // residual stream: res_a + the out partials -> res_b
+        if (si_status st = gemv(d->t_up[l], d->w_up[l], d->res_a, d->gate_up, 2 * P.ffn_rows, H,
+                                norm_of(d->o_parts, nranks, d->ffn_norm[l], d->res_b), nullptr))
+            return st;
+        k::GemvFusion sw;
+        sw.in_mode = 2;
+        if (si_status st = gemv(d->t_down[l], d->w_down[l], d->gate_up, nullptr, H, P.ffn_rows, sw, &d->pg_down))
+            return st;
+    }
+    if (si_status st = gemv(c.embedding_type, d->w_vocab, d->res_b, nullptr, P.vocab_rows, H,
+                            norm_of(d->down_parts, nranks, d->output_norm, nullptr), &d->pg_vocab))
+        return st;
+    return k::tr_argmax(d->logits, c.vocab, d->next_token, feed, s);
+}
+
+si_status create_tp(int device, const si_decoder_config *c, si_peer_group *group, si_decoder **out) {
+    auto *d = new si_decoder();
+    d->device = device;
+    d->cfg = *c;
+    d->tp = true;
+    d->group = group;
+    auto cleanup = [&](si_status st) {
+        destroy(d);
+        return st;
+    };
+    int nranks = 1, rank = 0;
+    uint64_t data_bytes = 0;
+    d->arena = si::peer_group_arena(group, &nranks, &rank, &data_bytes);
+    if (si_status st = tp_plan(*c, nranks, rank, &d->part)) return cleanup(st);
+    const si_tp_partition &P = d->part;
+    const TpLayout lay = tp_layout(*c, nranks);
+    if (data_bytes < lay.data_bytes)
+        return cleanup(fail(SI_ERR_INVALID_ARGUMENT, "the peer group's arenas hold %llu data bytes, the session needs %llu",
+                            (unsigned long long)data_bytes, (unsigned long long)lay.data_bytes));
+    if (si_status st = cuda(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreate"))
+        return cleanup(st);
+    const int64_t H = c->hidden, hs = c->head_size, F = P.ffn_rows;
+    const int64_t qkv_local = int64_t(P.query_heads + 2 * P.kv_heads) * hs, q_cols = int64_t(P.query_heads) * hs;
+    const int64_t kv_local = int64_t(P.kv_heads) * hs;
+    auto rb = [](uint32_t t, int64_t cols) {
+        uint64_t b = 0;
+        si::byte_length(t, uint64_t(cols), &b);
+        return b;
+    };
+    void *p = nullptr;
+    if (si_status st = alloc_slot(d, "token_embedding", rb(c->embedding_type, H) * uint64_t(c->vocab), &p))
+        return cleanup(st);
+    d->embedding = p;
+    d->w_vocab = static_cast<const uint8_t *>(p) + uint64_t(P.vocab_begin) * rb(c->embedding_type, H);
+    float *f = nullptr;
+    if (si_status st = alloc_typed(d, "output_norm", H * 4, &f)) return cleanup(st);
+    if (si_status st = fill_ones(f, H)) return cleanup(st);
+    d->output_norm = f;
+    const uint32_t t = c->weight_type;
+    for (int l = 0; l < c->layers; ++l) {
+        const std::string L = std::to_string(l);
+        if (si_status st = alloc_typed(d, "attn_norm_" + L, H * 4, &f)) return cleanup(st);
+        if (si_status st = fill_ones(f, H)) return cleanup(st);
+        d->attn_norm.push_back(f);
+        if (si_status st = alloc_typed(d, "ffn_norm_" + L, H * 4, &f)) return cleanup(st);
+        if (si_status st = fill_ones(f, H)) return cleanup(st);
+        d->ffn_norm.push_back(f);
+        d->t_qkv.push_back(t), d->t_out.push_back(t), d->t_up.push_back(t), d->t_down.push_back(t);
+        // this rank's rows: its query heads, then its key heads, then its value heads
+        if (si_status st = alloc_slot(d, "qkv_weight_" + L, rb(t, H) * uint64_t(qkv_local), &p)) return cleanup(st);
+        d->w_qkv.push_back(p);
+        // every row, this rank's query-head columns
+        if (si_status st = alloc_slot(d, "attn_output_weight_" + L, rb(t, q_cols) * uint64_t(H), &p)) return cleanup(st);
+        d->w_out.push_back(p);
+        // this rank's gate rows, then the matching up rows
+        if (si_status st = alloc_slot(d, "ffn_up_weight_" + L, rb(t, H) * uint64_t(2 * F), &p)) return cleanup(st);
+        d->w_up.push_back(p);
+        // every row, this rank's intermediate columns
+        if (si_status st = alloc_slot(d, "ffn_down_weight_" + L, rb(t, F) * uint64_t(H), &p)) return cleanup(st);
+        d->w_down.push_back(p);
+        if (si_status st = alloc_typed(d, "key_cache_" + L, uint64_t(c->context) * kv_local * 4, &f)) return cleanup(st);
+        d->key_cache.push_back(f);
+        if (si_status st = alloc_typed(d, "value_cache_" + L, uint64_t(c->context) * kv_local * 4, &f))
+            return cleanup(st);
+        d->value_cache.push_back(f);
+    }
+    if (si_status st = alloc_typed(d, "rope_frequencies", uint64_t(c->rotary_size / 2) * 4, &d->freq)) return cleanup(st);
+    {
+        std::vector<float> fr(size_t(c->rotary_size / 2));
+        for (int i = 0; i < c->rotary_size / 2; ++i)
+            fr[size_t(i)] = 1.0f / std::pow(c->rope_base, 2.0f * float(i) / float(c->rotary_size));
+        if (si_status st = cuda(cudaMemcpy(d->freq, fr.data(), fr.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy"))
+            return cleanup(st);
+    }
+    if (si_status st = alloc_typed(d, "hidden", H * 4, &d->res_b)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "hidden_after_attention", H * 4, &d->res_a)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "qkv", uint64_t(qkv_local) * 4, &d->qkv)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "attention", uint64_t(q_cols) * 4, &d->attention)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "gate_up", uint64_t(2 * F) * 4, &d->gate_up)) return cleanup(st);
+    d->o_parts = reinterpret_cast<float *>(d->arena + lay.o_parts);
+    d->down_parts = reinterpret_cast<float *>(d->arena + lay.down_parts);
+    d->logits = reinterpret_cast<float *>(d->arena + lay.logits);
+    d->slots["logits"] = {d->logits, uint64_t(c->vocab) * 4};
+    if (si_status st = si::peer_gather_desc(group, lay.o_parts, int64_t(rank) * H, H, &d->pg_out)) return cleanup(st);
+    if (si_status st = si::peer_gather_desc(group, lay.down_parts, int64_t(rank) * H, H, &d->pg_down))
+        return cleanup(st);
+    if (si_status st = si::peer_gather_desc(group, lay.logits, P.vocab_begin, P.vocab_rows, &d->pg_vocab))
+        return cleanup(st);
+    if (si_status st = alloc_typed(d, "control", 8, &d->control)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "next_token", 4, &d->next_token)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "prompt", uint64_t(c->context) * 4, &d->prompt)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "history", uint64_t(c->context) * 4, &d->history)) return cleanup(st);
+    if (si_status st = alloc_typed(d, "feed", sizeof(k::DecodeFeed), &d->feed)) return cleanup(st);
+    const size_t pinned_bytes = 64 + sizeof(k::DecodeFeed) + 2 * size_t(c->context) * 4;
+    if (si_status st = cuda(cudaMallocHost(reinterpret_cast<void **>(&d->pinned), pinned_bytes), "cudaMallocHost"))
+        return cleanup(st);
+    d->pinned_feed = reinterpret_cast<k::DecodeFeed *>(reinterpret_cast<uint8_t *>(d->pinned) + 64);
+    d->pinned_prompt = reinterpret_cast<int32_t *>(d->pinned_feed + 1);
+    d->pinned_history = d->pinned_prompt + c->context;
+    if (si_status st = cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return cleanup(st);
+    *out = d;
+    return SI_OK;
+}
+
 si_status ensure_graphs(si_decoder *d) {
     if (!d->direct && !d->step_exec)
         if (si_status st = build_graph(d, nullptr, &d->step_exec)) return st;
@@ -758,6 +1088,41 @@ si_status si_decoder_create(int device, const si_decoder_config *config, si_deco
     return create(device, config, nullptr, 1, 0, out);
 }
 
+si_status si_decoder_create_typed(int device, const si_decoder_config *config, const uint32_t *slot_types,
+                                  int32_t slot_count, si_decoder **out) {
+    if (!out || !slot_types) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (si_status st = validate(config)) return st;
+    const si_decoder_config &c = *config;
+    if (slot_count != 2 + 6 * c.layers)
+        return fail(SI_ERR_INVALID_ARGUMENT, "%d slot types given, the session has %d slots", slot_count,
+                    2 + 6 * c.layers);
+    if (slot_types[0] != c.embedding_type)
+        return fail(SI_ERR_INVALID_ARGUMENT, "token_embedding type %u differs from the configuration's %u",
+                    slot_types[0], c.embedding_type);
+    for (int i = 0; i < slot_count; ++i) {
+        const int r = i < 2 ? i : (i - 2) % 6;  // 1, 0, 1 = norms
+        const bool norm = i == 1 || (i >= 2 && r < 2);
+        if (norm && slot_types[i] != SI_TYPE_F32)
+            return fail(SI_ERR_UNSUPPORTED, "norm slot %d must be F32 (GGUF type 0), got %u", i, slot_types[i]);
+        if (!norm && !si::known_type(slot_types[i]))
+            return fail(SI_ERR_UNSUPPORTED, "slot %d: GGUF tensor type '%u' is not supported.", i, slot_types[i]);
+        if (!norm && i >= 2) {
+            uint64_t b;
+            if (si_status st = si::byte_length(slot_types[i], uint64_t(r == 5 ? c.intermediate : c.hidden), &b))
+                return st;
+        }
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SI_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
+    DeviceScope scope(device);
+    return create(device, config, nullptr, 1, 0, out, slot_types);
+}
+
 si_status si_decoder_arena_bytes(const si_decoder_config *config, uint64_t *bytes) {
     if (!bytes) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
     if (si_status st = validate(config)) return st;
@@ -796,6 +1161,39 @@ si_status si_decoder_create_sharded(int device, const si_decoder_config *config,
     if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
     DeviceScope scope(device);
     return create(device, config, group, 1, shard_min_bytes, out);
+}
+
+si_status si_tp_partition_plan(const si_decoder_config *config, int32_t nranks, int32_t rank, si_tp_partition *out) {
+    if (!out) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    if (si_status st = validate(config)) return st;
+    return tp_plan(*config, nranks, rank, out);
+}
+
+si_status si_decoder_tp_arena_bytes(const si_decoder_config *config, int32_t nranks, uint64_t *bytes) {
+    if (!bytes || nranks < 1) return fail(SI_ERR_INVALID_ARGUMENT, "null argument or no ranks");
+    if (si_status st = validate(config)) return st;
+    *bytes = tp_layout(*config, nranks).data_bytes + 4096;  // + the peer group's state
+    return SI_OK;
+}
+
+si_status si_decoder_create_tensor_parallel(int device, const si_decoder_config *config, si_peer_group *group,
+                                            si_decoder **out) {
+    if (!out || !group) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (si_status st = validate(config)) return st;
+    const si_decoder_config &c = *config;
+    for (uint32_t t : {c.weight_type, c.embedding_type})
+        if (t != SI_TYPE_Q4_K && t != SI_TYPE_Q8_0)
+            return fail(SI_ERR_UNSUPPORTED, "a tensor-parallel session takes Q4_K or Q8_0 weights");
+    if (c.hidden % 256) return fail(SI_ERR_UNSUPPORTED, "hidden %d is not a multiple of 256", c.hidden);
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SI_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= n) return fail(SI_ERR_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, n);
+    DeviceScope scope(device);
+    return create_tp(device, config, group, out);
 }
 
 si_status si_decoder_destroy(si_decoder *decoder) {

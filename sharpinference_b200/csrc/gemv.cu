@@ -299,7 +299,32 @@ __global__ void __launch_bounds__(256) gemv_rowwarp_kernel(const uint8_t *__rest
     for (int64_t row = warp; row < rows; row += nwarps) {
         const uint8_t *wr = w + row * row_bytes;
         float acc = 0.0f;
-        if constexpr (FMT == SI_TYPE_Q8_0) {
+        if constexpr (FMT == SI_TYPE_Q6_K) {
+            // lane l takes 16-element groups l, l + 32, ... of the row; group g of
+            // superblock b is elements e = 16 (g % 16) .. + 15 of the GGUF block:
+            // low bits ql[64h + l0 + 32(j & 1) + i] nibble j >> 1, high bits
+            // (qh[32h + l0 + i] >> 2j) & 3, w = (d * scale[g % 16]) * (q - 32).
+            // Superblocks are 210 bytes, so reads are 16-bit.
+            for (int64_t g = lane; g < cols / 16; g += 32) {
+                const uint8_t *blk = wr + (g >> 4) * kQ6KBytes;
+                const int e0 = int(g & 15) * 16, h = e0 >> 7, j = (e0 >> 5) & 3, l0 = e0 & 31;
+                const uint16_t *ql = reinterpret_cast<const uint16_t *>(blk + 64 * h + l0 + 32 * (j & 1));
+                const uint16_t *qh = reinterpret_cast<const uint16_t *>(blk + 128 + 32 * h + l0);
+                const float *xe = x + g * 16;
+                const int lshift = 4 * (j >> 1), hshift = 2 * j;
+                float sq = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t lw = ql[i], hw = qh[i];
+                    const int q0 = int(((lw >> lshift) & 15u) | (((hw >> hshift) & 3u) << 4)) - 32;
+                    const int q1 = int(((lw >> (8 + lshift)) & 15u) | (((hw >> (8 + hshift)) & 3u) << 4)) - 32;
+                    sq = fmaf(float(q0), xe[2 * i], sq);
+                    sq = fmaf(float(q1), xe[2 * i + 1], sq);
+                }
+                const float d = __half2float(*reinterpret_cast<const __half *>(blk + 208));
+                acc = fmaf(d * float(int8_t(blk[192 + (g & 15)])), sq, acc);
+            }
+        } else if constexpr (FMT == SI_TYPE_Q8_0) {
             for (int64_t b = lane; b < cols / 32; b += 32) {
                 const uint8_t *blk = wr + b * 34;
                 const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
@@ -359,6 +384,7 @@ si_status launch_coop(const void *w, const void *x, void *y, int64_t rows, int64
 
 // Shape plan of the staged kernel; false when the shape needs the fallback.
 bool plan_staged(uint32_t wtype, int64_t rows, int64_t cols, const void *w, StagedParams &p, size_t &smem) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return false;
     if (cols % 256 != 0 || rows <= 0 || rows > (int64_t(1) << 30)) return false;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const int64_t units = cols / 64;
@@ -447,7 +473,10 @@ si_status matvec_quant(uint32_t wtype, const void *w, const float *x, float *y, 
     uint64_t rb;
     if (si_status s = byte_length(wtype, uint64_t(cols), &rb)) return s;
     const int64_t blocks = std::min<int64_t>((rows + 7) / 8, int64_t(sm_count()) * 8);
-    if (wtype == SI_TYPE_Q4_K)
+    if (wtype == SI_TYPE_Q6_K)
+        gemv_rowwarp_kernel<SI_TYPE_Q6_K><<<unsigned(blocks), 256, 0, st>>>(static_cast<const uint8_t *>(w), x, y,
+                                                                            rows, cols, rb);
+    else if (wtype == SI_TYPE_Q4_K)
         gemv_rowwarp_kernel<SI_TYPE_Q4_K><<<unsigned(blocks), 256, 0, st>>>(static_cast<const uint8_t *>(w), x, y,
                                                                             rows, cols, rb);
     else

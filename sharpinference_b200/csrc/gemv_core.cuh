@@ -36,13 +36,18 @@ __device__ __forceinline__ float4 ldx4(const float *p) {
     else return __ldg(reinterpret_cast<const float4 *>(p));
 }
 
+// Modes: 0 x as is; 1 (x (+ res)) * scale * w (rms-norm with the scale given
+// or applied later); 2 swiglu of [gate | up] (u at offset `up`); 3 the
+// residual stream after a K-split exchange: (x + res[0] + ... + res[nparts-1])
+// * scale * w, partial vectors `up` floats apart, summed in rank order.
 template <int M, int kL2 = 0>
 struct XSrc {
     const float *x;
     const float *res;
     const float *w;
     float scale;
-    int64_t up;  // mode 2: offset of u
+    int64_t up;  // mode 2: offset of u; mode 3: floats between partial vectors
+    int nparts = 0;  // mode 3
     __device__ __forceinline__ bool aligned(int64_t i) const {
         return M != 0 || (reinterpret_cast<uintptr_t>(x + i) & 15u) == 0;
     }
@@ -56,6 +61,10 @@ struct XSrc {
         } else if constexpr (M == 1) {
             const float v = res ? __fadd_rn(a, ldx<kL2>(res + i)) : a;
             return __fmul_rn(__fmul_rn(v, scale), ldx<kL2>(w + i));
+        } else if constexpr (M == 3) {
+            float v = a;
+            for (int r = 0; r < nparts; ++r) v = __fadd_rn(v, ldx<kL2>(res + r * up + i));
+            return __fmul_rn(__fmul_rn(v, scale), ldx<kL2>(w + i));
         } else {
             return swish_mul(a, ldx<kL2>(x + up + i));
         }
@@ -64,6 +73,14 @@ struct XSrc {
         float4 a = ldx4<kL2>(x + i);
         if constexpr (M == 0) {
             return a;
+        } else if constexpr (M == 3) {
+            for (int r = 0; r < nparts; ++r) {
+                const float4 p = ldx4<kL2>(res + r * up + i);
+                a = make_float4(__fadd_rn(a.x, p.x), __fadd_rn(a.y, p.y), __fadd_rn(a.z, p.z), __fadd_rn(a.w, p.w));
+            }
+            const float4 m = ldx4<kL2>(w + i);
+            return make_float4(__fmul_rn(__fmul_rn(a.x, scale), m.x), __fmul_rn(__fmul_rn(a.y, scale), m.y),
+                               __fmul_rn(__fmul_rn(a.z, scale), m.z), __fmul_rn(__fmul_rn(a.w, scale), m.w));
         } else if constexpr (M == 1) {
             if (res) {
                 const float4 r = ldx4<kL2>(res + i);
@@ -380,37 +397,33 @@ struct I8Path {
         const bool aligned = X.aligned(xb);
         const int t = lane & 3, g = lane >> 2;
         const int half = g >> 2, digit = g & 3;
-        // Every x value this lane needs is requested here, before any of it is
-        // used: the eight consecutive values of the amax / sub-block sums and
-        // the 32 values of its B fragments (sub-blocks 4 * half .. + 3, k =
-        // 4t..4t+3 and 16+4t..16+4t+3). One memory round trip instead of one
-        // per sub-block (with the shared-memory ring filling the SM, the L1
-        // keeps little, so each later load went back to L2).
+        // Each lane loads (and transforms) eight consecutive values, lane l
+        // elements 8l .. 8l+7 of the superblock: one memory round trip, every
+        // input transform computed once. The 32 values of the lane's B
+        // fragments (sub-blocks 4 * half .. + 3, k = 4t..4t+3 and
+        // 16+4t..16+4t+3) are then gathered from the lanes holding them.
         float v[8], q[4][8];
         if (aligned) {
             const float4 a = X.get4(xb + 8 * lane);
             const float4 b = X.get4(xb + 8 * lane + 4);
-            float4 qa[4], qc[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int64_t e0 = xb + 32 * (4 * half + j) + 4 * t;
-                qa[j] = X.get4(e0);
-                qc[j] = X.get4(e0 + 16);
-            }
             v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                q[j][0] = qa[j].x, q[j][1] = qa[j].y, q[j][2] = qa[j].z, q[j][3] = qa[j].w;
-                q[j][4] = qc[j].x, q[j][5] = qc[j].y, q[j][6] = qc[j].z, q[j][7] = qc[j].w;
-            }
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = X.get(xb + 8 * lane + i);
+        }
+        // element 32 s + 4t + i (i < 4) sits in lane 4s + t/2, slot 4(t%2) + i;
+        // element 32 s + 16 + 4t + i in lane 4s + 2 + t/2, same slot
+        const bool odd_t = (t & 1) != 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int64_t e0 = xb + 32 * (4 * half + j) + 4 * t;
+        for (int j = 0; j < 4; ++j) {
+            const int s0 = 4 * (4 * half + j) + (t >> 1);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) q[j][i] = X.get(e0 + i), q[j][4 + i] = X.get(e0 + 16 + i);
+            for (int i = 0; i < 4; ++i) {
+                const float lo_a = __shfl_sync(0xffffffffu, v[i], s0), lo_b = __shfl_sync(0xffffffffu, v[4 + i], s0);
+                const float hi_a = __shfl_sync(0xffffffffu, v[i], s0 + 2),
+                            hi_b = __shfl_sync(0xffffffffu, v[4 + i], s0 + 2);
+                q[j][i] = odd_t ? lo_b : lo_a;
+                q[j][4 + i] = odd_t ? hi_b : hi_a;
             }
         }
         float amax = 0.0f, psum = 0.0f;

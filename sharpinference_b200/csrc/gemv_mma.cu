@@ -80,6 +80,16 @@ struct MmaParams {
     int path;             // host side: 0 FP16 MMA, 1 INT8 MMA
     int groups;           // clusters (or CTAs when cluster == 1) in the grid
     int max_local_tiles;  // ceil(num_tiles / groups): row-sum slots per CTA when cluster > 1
+    // Fused neighbours of the decode program (kernels::GemvFusion):
+    int in_mode;          // 0: x as is; 1: rms-norm of x (x * norm_w, rows * 1/rms); 2: swiglu of [gate | up]
+    const float *norm_w;  // in_mode 1: the norm weight (K floats)
+    float eps;            // in_mode 1
+    const float *resid;   // non-null: y[r] = resid[r] + (W x)[r] (resid may equal y)
+    // in_mode 3: x + the partial vectors of a K-split exchange, rms-normed
+    const float *parts;   // nparts vectors of K floats, part_stride apart
+    int nparts;
+    int64_t part_stride;
+    float *h_out;         // non-null: CTA 0 stores x + the partials (the residual stream) here
 };
 
 // --- thread-block cluster helpers (distributed shared memory) ---
@@ -111,9 +121,11 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
 }
 // Output row store: into y, or (row-sharded GEMV) into every rank's output
 // vector at this rank's row offset, over NVLink for the peers.
-__device__ __forceinline__ void store_y(const MmaParams &p, int row, float v, int tok = 0) {
+// `res`: resid[row] when p.resid is set, loaded ahead by the caller.
+__device__ __forceinline__ void store_y(const MmaParams &p, int row, float v, int tok = 0, float res = 0.0f) {
     if (p.control && p.token + tok >= p.control[1]) return;  // read after the dependency wait
     if (p.peer.nranks == 0) {
+        if (p.resid) v = __fadd_rn(res, v);  // residual add of the decode program (batch 1)
         p.y[tok * p.y_stride + row] = v;
         return;
     }
@@ -161,6 +173,46 @@ __device__ __forceinline__ void peer_handshake(const MmaParams &p) {
         }
     }
     *reinterpret_cast<volatile uint32_t *>(g.epoch) = e;
+}
+
+// 1 / rms of the input vector (transformer.rms-norm, GpuTransformerInstructionCollection.cs:323-368):
+// sum of squares over all K elements by one warp (lane-strided partial sums,
+// fixed shuffle tree), then 1 / sqrt(sum / K + eps). Called by the reducer
+// warp after the dependency wait; the rows it stores are scaled by it.
+__device__ __forceinline__ float inv_rms_warp(const float *x, int64_t k, float eps, int lane) {
+    float s = 0.0f;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && k % 128 == 0) {
+        for (int64_t i = int64_t(lane) * 4; i < k; i += 128) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + i));
+            s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                                       __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+        }
+    } else {
+        for (int64_t i = lane; i < k; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, float(k)), eps)));
+}
+
+// Mode 3: the residual stream after a K-split exchange, x + parts[0] + ...
+// (rank order, as the compute warps form it), stored to h_out when given;
+// returns 1 / rms of it with the reference's arithmetic.
+__device__ __forceinline__ float inv_rms_parts_warp(const MmaParams &p, int64_t k, int lane, float *h_out) {
+    float s = 0.0f;
+    for (int64_t i = int64_t(lane) * 4; i < k; i += 128) {
+        float4 v = __ldg(reinterpret_cast<const float4 *>(p.x + i));
+        for (int r = 0; r < p.nparts; ++r) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(p.parts + r * p.part_stride + i));
+            v = make_float4(__fadd_rn(v.x, q.x), __fadd_rn(v.y, q.y), __fadd_rn(v.z, q.z), __fadd_rn(v.w, q.w));
+        }
+        if (h_out) *reinterpret_cast<float4 *>(h_out + i) = v;
+        s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                                   __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, float(k)), p.eps)));
 }
 
 // Every thread of every CTA of the cluster (hardware barrier).
@@ -250,12 +302,19 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         // Reducer: fixed-order sum of the C0 per-column partials of each
         // output (row r, input row u) = index r * TK + u of the tile.
         if (CS == 1) pdl_wait();  // y may still be read by the previous kernel
+        const float row_scale =
+            CS != 1 ? 1.0f
+            : p.in_mode == 1 ? inv_rms_warp(p.x, int64_t(p.nsb) * 256, p.eps, lane)
+            : p.in_mode == 3 ? inv_rms_parts_warp(p, int64_t(p.nsb) * 256, lane, blockIdx.x == 0 ? p.h_out : nullptr)
+                             : 1.0f;
         int it = 0;
         for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
             const int b = it & 1;
-            mbar_wait(&pfull[b], (it >> 1) & 1, kErrEpilogueTimeout);
             const int r0 = tile * RT;
             const int nrows = min(RT, p.rows - r0);
+            // the residual of this lane's row, loaded while the tile is computed
+            const float res = (CS == 1 && TK == 1 && p.resid && lane < nrows) ? p.resid[r0 + lane] : 0.0f;
+            mbar_wait(&pfull[b], (it >> 1) & 1, kErrEpilogueTimeout);
             const float *pb = part + size_t(b) * C0 * RTK;
 #pragma unroll
             for (int o0 = 0; o0 < RTK; o0 += 32) {
@@ -265,7 +324,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                 if (r < nrows)
                     for (int c = 0; c < C0; ++c) a += pb[c * RTK + o];
                 if (CS == 1) {
-                    if (r < nrows && (TK == 1 || u < p.ntok)) store_y(p, r0 + r, a, u);
+                    if (r < nrows && (TK == 1 || u < p.ntok)) store_y(p, r0 + r, __fmul_rn(a, row_scale), u, res);
                 } else {
                     rowsum[it * RTK + o] = a;
                 }
@@ -290,7 +349,14 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                 if (has1) Path::load(X, gsb + sb1, lane, st1, my_scratch, p.x_stride, p.ntok);
             }
         };
-        load_x(XSrc<0>{p.x, nullptr, nullptr, 1.0f, int64_t(p.nsb) * 256});
+        if (p.in_mode == 1)
+            load_x(XSrc<1>{p.x, nullptr, p.norm_w, 1.0f, 0});
+        else if (p.in_mode == 3)
+            load_x(XSrc<3>{p.x, p.parts, p.norm_w, 1.0f, p.part_stride, p.nparts});
+        else if (p.in_mode == 2)
+            load_x(XSrc<2>{p.x, nullptr, nullptr, 1.0f, int64_t(p.nsb) * 256});
+        else
+            load_x(XSrc<0>{p.x, nullptr, nullptr, 1.0f, int64_t(p.nsb) * 256});
 
         const int g = lane >> 2, t = lane & 3;
         constexpr int kUnits = RT / 16 / WPS;  // 16-row groups per warp per tile
@@ -359,19 +425,48 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     }
     if (CS > 1) {
         pdl_wait();          // y may still be read by the previous kernel
-        cluster_sync_all();  // every CTA's row sums are complete and visible to the cluster
+        const float row_scale =
+            warp != C + 1 ? 1.0f
+            : p.in_mode == 1 ? inv_rms_warp(p.x, int64_t(p.nsb) * 256, p.eps, lane)
+            : p.in_mode == 3 ? inv_rms_parts_warp(p, int64_t(p.nsb) * 256, lane, blockIdx.x == 0 ? p.h_out : nullptr)
+                             : 1.0f;
         const int local_tiles = first_tile < p.num_tiles ? (p.num_tiles - 1 - first_tile) / tile_step + 1 : 0;
+        // residuals of this lane's first rows, loaded before the cluster barrier
+        constexpr int kResAhead = 4;
+        float res_ahead[kResAhead];
+#pragma unroll
+        for (int j = 0; j < kResAhead; ++j) {
+            res_ahead[j] = 0.0f;
+            const int i = int(crank) * 32 + lane + j * CS * 32;
+            if (warp == C + 1 && TK == 1 && p.resid && i < local_tiles * RTK) {
+                const int li = i / RTK, r = i - li * RTK;
+                const int row = (first_tile + li * tile_step) * RT + r;
+                if (row < p.rows) res_ahead[j] = p.resid[row];
+            }
+        }
+        cluster_sync_all();  // every CTA's row sums are complete and visible to the cluster
         const uint32_t base = smem_u32(rowsum);
         // The reducer warps of the cluster finish the rows (one warp per CTA
         // stores, so only it has output stores to fence on a sharded call).
+        int j = 0;
         for (int i = warp == C + 1 ? int(crank) * 32 + lane : local_tiles * RTK; i < local_tiles * RTK;
-             i += CS * 32) {
+             i += CS * 32, ++j) {
             const int li = i / RTK, rem = i - li * RTK, r = rem / TK, u = rem % TK;
             const int row = (first_tile + li * tile_step) * RT + r;
             if (row < p.rows && (TK == 1 || u < p.ntok)) {
                 float a = 0.0f;
                 for (int k = 0; k < CS; ++k) a += ld_cluster_f32(mapa_shared(base + 4u * uint32_t(i), uint32_t(k)));
-                store_y(p, row, a, u);
+                float res = 0.0f;
+                if (p.resid) {
+                    if (j < kResAhead) {
+#pragma unroll
+                        for (int q = 0; q < kResAhead; ++q)
+                            if (q == j) res = res_ahead[q];
+                    } else {
+                        res = p.resid[row];
+                    }
+                }
+                store_y(p, row, __fmul_rn(a, row_scale), u, res);
             }
         }
         cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
@@ -586,7 +681,7 @@ namespace {
 // by an explicit shape), 2 Q8_0, 3 Q4_K batched (up to 8 input rows).
 si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t rows, int64_t cols, void *stream,
                      const PeerGather *peer, const int32_t *control, int token, int ntok, int64_t x_stride,
-                     int64_t y_stride, const Shape *forced = nullptr) {
+                     int64_t y_stride, const Shape *forced = nullptr, const GemvFusion *fusion = nullptr) {
     MmaParams p{};
     size_t smem = 0;
     int rt = 0;
@@ -638,6 +733,16 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
     p.y = y;
     if (peer) p.peer = *peer;
     p.control = control;
+    if (fusion) {
+        p.in_mode = fusion->in_mode;
+        p.norm_w = fusion->norm_w;
+        p.eps = fusion->eps;
+        p.resid = fusion->resid;
+        p.parts = fusion->parts;
+        p.nparts = fusion->nparts;
+        p.part_stride = fusion->part_stride;
+        p.h_out = fusion->h_out;
+    }
     p.token = token;
     p.ntok = ntok;
     p.x_stride = x_stride;
@@ -674,6 +779,22 @@ si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float 
     if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
     return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, control, token, 1, cols,
                       rows);
+}
+
+// The decode program's GEMV with its neighbours fused (see GemvFusion).
+// SI_ERR_UNSUPPORTED (nothing launched, no error string) when the tensor-core
+// GEMV does not take the shape; the caller then runs the instructions apart.
+si_status matvec_quant_fused(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                             const GemvFusion &f, void *stream, const PeerGather *peer) {
+    if (wtype != SI_TYPE_Q4_K && wtype != SI_TYPE_Q8_0) return SI_ERR_UNSUPPORTED;
+    const auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if ((f.in_mode != 0 && !a16(x)) || ((f.in_mode == 1 || f.in_mode == 3) && (!f.norm_w || !a16(f.norm_w))) ||
+        (f.in_mode == 3 && ((f.nparts > 0 && (!f.parts || !a16(f.parts) || f.part_stride % 4)) ||
+                            (f.h_out && !a16(f.h_out)))) ||
+        (peer && f.resid))
+        return SI_ERR_UNSUPPORTED;
+    return launch_mma(wtype == SI_TYPE_Q8_0 ? 2 : 1, w, x, y, rows, cols, stream, peer, nullptr, 0, 1, cols, rows,
+                      nullptr, &f);
 }
 
 // The launch shape si_matvec picks for a Q4_K / Q8_0 GEMV on the current device.

@@ -188,6 +188,50 @@ void scale_min_q4_k(const uint8_t *packed, int s, int *sc, int *m) {
     }
 }
 
+// Q6_K superblock (GGUF layout, 210 bytes): ql[128] low four bits, qh[64]
+// high two bits, 16 int8 sub-block scales, binary16 d. Element e = 128h +
+// 32j + l: low bits in ql[64h + l + 32(j & 1)] (nibble j >> 1), high bits
+// (qh[32h + l] >> 2j) & 3; w = (d * scale[e / 16]) * (q - 32).
+// Quantiser: per 16 elements s = absmax / 31, d = max s / 127 (binary16),
+// scale = round(s / d) in [0, 127] (1 when a non-zero s rounds to 0),
+// q = round(x / (d * scale)) + 32 in [0, 63].
+void quantize_q6_k_block(const float *v, uint8_t *o) {
+    float gs[16], smax = 0.0f;
+    for (int g = 0; g < 16; ++g) {
+        float amax = 0.0f;
+        for (int i = 0; i < 16; ++i) amax = std::max(amax, std::fabs(v[16 * g + i]));
+        gs[g] = amax / 31.0f;
+        smax = std::max(smax, gs[g]);
+    }
+    const uint16_t dh = float_to_half(smax / 127.0f);
+    const float d = half_to_float(dh);
+    int sc[16];
+    for (int g = 0; g < 16; ++g) {
+        sc[g] = d > 0.0f ? int(clampf(std::round(gs[g] / d), 0.0f, 127.0f)) : 0;
+        if (sc[g] == 0 && gs[g] > 0.0f && d > 0.0f) sc[g] = 1;
+    }
+    std::memset(o, 0, kQ6KBytes);
+    for (int e = 0; e < 256; ++e) {
+        const float a = d * float(sc[e / 16]);
+        const int q = a > 0.0f ? int(clampf(std::round(v[e] / a), -32.0f, 31.0f) + 32.0f) : 32;
+        const int h = e >> 7, j = (e >> 5) & 3, l = e & 31;
+        o[64 * h + l + 32 * (j & 1)] |= uint8_t((q & 15) << (4 * (j >> 1)));
+        o[128 + 32 * h + l] |= uint8_t((q >> 4) << (2 * j));
+    }
+    for (int g = 0; g < 16; ++g) o[192 + g] = uint8_t(int8_t(sc[g]));
+    put16(o + 208, dh);
+}
+
+void dequantize_q6_k_block(const uint8_t *o, float *w) {
+    const float d = half_to_float(get16(o + 208));
+    for (int e = 0; e < 256; ++e) {
+        const int h = e >> 7, j = (e >> 5) & 3, l = e & 31;
+        const int low = (o[64 * h + l + 32 * (j & 1)] >> (4 * (j >> 1))) & 15;
+        const int high = (o[128 + 32 * h + l] >> (2 * j)) & 3;
+        w[e] = (d * float(int8_t(o[192 + e / 16]))) * float((low | (high << 4)) - 32);
+    }
+}
+
 template <class F>
 void parallel_for(int64_t n, int threads, F &&body, int64_t grain = 1024) {
     if (threads <= 0) threads = int(std::max(1u, std::thread::hardware_concurrency()));
@@ -256,6 +300,11 @@ si_status si_quantize(uint32_t type, const float *src, int64_t count, void *dst)
             for (int64_t b = b0; b < b1; ++b) quantize_q4_k_block(src + 256 * b, o + 144 * b);
         });
         return SI_OK;
+    case SI_TYPE_Q6_K:
+        parallel_for(count / 256, 0, [&](int64_t b0, int64_t b1) {
+            for (int64_t b = b0; b < b1; ++b) quantize_q6_k_block(src + 256 * b, o + kQ6KBytes * b);
+        });
+        return SI_OK;
     }
     return fail(SI_ERR_UNSUPPORTED, "unsupported type");
 }
@@ -292,6 +341,9 @@ si_status si_dequantize(uint32_t type, const void *src, int64_t count, float *ds
             }
         }
         return SI_OK;
+    case SI_TYPE_Q6_K:
+        for (int64_t b = 0; b < count / 256; ++b) dequantize_q6_k_block(p + kQ6KBytes * b, dst + 256 * b);
+        return SI_OK;
     }
     return fail(SI_ERR_UNSUPPORTED, "unsupported type");
 }
@@ -313,6 +365,7 @@ si_status si_synth_weights(uint32_t type, uint64_t seed, int64_t rows, int64_t c
 si_status si_synth_weight_rows(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows, int64_t cols,
                                float sigma, void *dst, int threads) {
     if (!dst || rows <= 0 || cols <= 0 || row_begin < 0) return fail(SI_ERR_INVALID_ARGUMENT, "invalid shape");
+    if (!known_type(type)) return fail(SI_ERR_UNSUPPORTED, "GGUF tensor type '%u' is not supported.", type);
     uint64_t rb;
     if (si_status st = byte_length(type, uint64_t(cols), &rb)) return st;
     auto *o = static_cast<uint8_t *>(dst);
@@ -325,6 +378,7 @@ si_status si_synth_weight_rows(uint32_t type, uint64_t seed, int64_t row_begin, 
             if (type == SI_TYPE_F32) std::memcpy(dr, row.data(), rb);
             else if (type == SI_TYPE_F16) for (int64_t c = 0; c < cols; ++c) put16(dr + 2 * c, float_to_half(row[size_t(c)]));
             else if (type == SI_TYPE_Q8_0) for (int64_t b = 0; b < cols / 32; ++b) quantize_q8_0_block(row.data() + 32 * b, dr + 34 * b);
+            else if (type == SI_TYPE_Q6_K) for (int64_t b = 0; b < cols / 256; ++b) quantize_q6_k_block(row.data() + 256 * b, dr + kQ6KBytes * b);
             else for (int64_t b = 0; b < cols / 256; ++b) quantize_q4_k_block(row.data() + 256 * b, dr + 144 * b);
         }
     }, 8);

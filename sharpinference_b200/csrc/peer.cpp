@@ -127,6 +127,26 @@ uint8_t *peer_group_arena(si_peer_group *g, int *nranks, int *rank, uint64_t *da
     *data_bytes = g->data_bytes;
     return g->arenas[g->rank];
 }
+
+si_status peer_gather_desc(si_peer_group *g, uint64_t output_offset, int64_t row_base, int64_t rows,
+                           kernels::PeerGather *out) {
+    if (output_offset % 16 != 0 || row_base < 0 ||
+        output_offset + uint64_t(row_base + rows) * 4 > g->data_bytes)
+        return fail(SI_ERR_INVALID_ARGUMENT, "peer output rows [%lld, +%lld) at offset %llu leave the arena",
+                    (long long)row_base, (long long)rows, (unsigned long long)output_offset);
+    kernels::PeerGather pg{};
+    for (int q = 0; q < g->nranks; ++q) {
+        pg.ys[q] = reinterpret_cast<float *>(g->arenas[q] + output_offset);
+        pg.flags[q] = reinterpret_cast<uint32_t *>(g->arenas[q] + g->data_bytes);
+    }
+    pg.ticket = reinterpret_cast<uint32_t *>(g->arenas[g->rank] + g->data_bytes + 256);
+    pg.epoch = reinterpret_cast<uint32_t *>(g->arenas[g->rank] + g->data_bytes + 512);
+    pg.nranks = g->nranks;
+    pg.rank = g->rank;
+    pg.row_base = row_base;
+    *out = pg;
+    return SI_OK;
+}
 }  // namespace si
 
 extern "C" {

@@ -20,9 +20,10 @@ constexpr int kQ8_0Block = 32;
 constexpr int kQ8_0Bytes = 34;
 constexpr int kQ4KBlock = 256;
 constexpr int kQ4KBytes = 144;
+constexpr int kQ6KBytes = 210;
 
 inline bool known_type(uint32_t t) {
-    return t == SI_TYPE_F32 || t == SI_TYPE_F16 || t == SI_TYPE_Q8_0 || t == SI_TYPE_Q4_K;
+    return t == SI_TYPE_F32 || t == SI_TYPE_F16 || t == SI_TYPE_Q8_0 || t == SI_TYPE_Q4_K || t == SI_TYPE_Q6_K;
 }
 
 inline const char *type_name(uint32_t t) {
@@ -31,6 +32,7 @@ inline const char *type_name(uint32_t t) {
     case SI_TYPE_F16: return "F16";
     case SI_TYPE_Q8_0: return "Q8_0";
     case SI_TYPE_Q4_K: return "Q4_K";
+    case SI_TYPE_Q6_K: return "Q6_K";
     default: return "unknown";
     }
 }
@@ -54,6 +56,11 @@ si_status cuda_error(int error, const char *what);
 // This rank's arena of a peer group (si_peer_group_create), the group's
 // size and rank, and the arena's data bytes (before the 4 KB of state).
 uint8_t *peer_group_arena(si_peer_group *g, int *nranks, int *rank, uint64_t *data_bytes);
+namespace kernels { struct PeerGather; }
+// The exchange descriptor of a peer GEMV whose output rows land at row
+// row_base of the float vector at output_offset in every rank's arena.
+si_status peer_gather_desc(si_peer_group *g, uint64_t output_offset, int64_t row_base, int64_t rows,
+                           kernels::PeerGather *out);
 
 // Per-device launch state (launch_state.cpp). Kernel attributes and the SM
 // count are properties of a device; one process may drive several devices
@@ -108,6 +115,28 @@ struct PeerGather {
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                            void *stream, const PeerGather *peer = nullptr, const int32_t *control = nullptr,
                            int token = 0);
+// Neighbours of a decode-program GEMV fused into it (batch 1, one GPU):
+//  in_mode 1: the input is rms-normed on the fly (transformer.rms-norm with
+//             weight norm_w and epsilon eps: rows = (W (x * norm_w)) / rms(x));
+//  in_mode 2: the input is transformer.swiglu of x = [gate | up] (K floats each);
+//  in_mode 3: the input is the residual stream after a K-split exchange,
+//             x + parts[0] + ... + parts[nparts-1] (rank order, part_stride
+//             floats apart), rms-normed as in mode 1; CTA 0 stores that sum
+//             to h_out when h_out is given;
+//  resid:     y[r] = resid[r] + (W x)[r] (the residual add; resid may be y).
+// peer: the output rows go to every rank's arena (PeerGather) instead of y.
+struct GemvFusion {
+    int in_mode = 0;
+    const float *norm_w = nullptr;
+    float eps = 0.0f;
+    const float *resid = nullptr;
+    const float *parts = nullptr;
+    int nparts = 0;
+    int64_t part_stride = 0;
+    float *h_out = nullptr;
+};
+si_status matvec_quant_fused(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
+                             const GemvFusion &f, void *stream, const PeerGather *peer = nullptr);
 // The launch shape matvec_quant_mma picks, and one GEMV with an explicit shape
 // (si_gemv_default_plan / si_matvec_quant_planned).
 si_status gemv_default_plan(uint32_t wtype, int64_t rows, int64_t cols, si_gemv_plan *plan);
@@ -164,6 +193,12 @@ si_status tr_rope_kv_write(const float *qkv, const int32_t *position, const int3
                            int64_t kvsize, int head_size, int rotary, int64_t context, float rope_scale, void *stream);
 si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                               int query_heads, int kv_heads, int head_size, int64_t context, void *stream);
+// transformer.rope-kv-write followed by transformer.grouped-query-attention
+// (one stream), as one kernel: q and the token's k rotated from qkv, the k / v
+// rows stored into the caches at *position, then the attention.
+si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, const float *freq, float *kc, float *vc,
+                                   float *out, int query_heads, int kv_heads, int head_size, int rotary,
+                                   int64_t context, float rope_scale, void *stream);
 si_status tr_gqa_scores(const float *query, const float *kc, const int32_t *position, const int32_t *control,
                         float *scores, int64_t batch, int query_heads, int kv_heads, int head_size, int64_t context,
                         void *stream);

@@ -41,6 +41,17 @@ __device__ __forceinline__ void dequant8(const uint8_t *row, int64_t c, int64_t 
         const __half *r = reinterpret_cast<const __half *>(row);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = c + i < cols ? __half2float(r[c + i]) : 0.0f;
+    } else if constexpr (FMT == SI_TYPE_Q6_K) {
+        // eight elements of one 16-element group: same nibble / 2-bit fields
+        const uint8_t *blk = row + (c >> 8) * 210;
+        const int e0 = int(c & 255), h = e0 >> 7, j = (e0 >> 5) & 3, l0 = e0 & 31;
+        const float a = h2f(blk + 208) * float(int8_t(blk[192 + (e0 >> 4)]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int low = (blk[64 * h + l0 + i + 32 * (j & 1)] >> (4 * (j >> 1))) & 15;
+            const int high = (blk[128 + 32 * h + l0 + i] >> (2 * j)) & 3;
+            v[i] = a * float((low | (high << 4)) - 32);
+        }
     } else if constexpr (FMT == SI_TYPE_Q8_0) {
         const uint8_t *blk = row + (c >> 5) * 34;
         const float d = h2f(blk);
@@ -188,6 +199,7 @@ si_status shared_weight_matvec(uint32_t wtype, const void *w, const float *x, co
     case SI_TYPE_F16: return launch_shared<SI_TYPE_F16>(w, x, y, control, m, n, k, st);
     case SI_TYPE_Q8_0: return launch_shared<SI_TYPE_Q8_0>(w, x, y, control, m, n, k, st);
     case SI_TYPE_Q4_K: return launch_shared<SI_TYPE_Q4_K>(w, x, y, control, m, n, k, st);
+    case SI_TYPE_Q6_K: return launch_shared<SI_TYPE_Q6_K>(w, x, y, control, m, n, k, st);
     default: return fail(SI_ERR_UNSUPPORTED, "unsupported weight type %u", wtype);
     }
 }

@@ -84,9 +84,17 @@ __device__ float block_sum(float v, float *red) {
 
 // ---- element access of a table row ----------------------------------------
 // Element c of a row in GGUF layout, dequantised exactly as the CPU codecs
-// do it: Q8_0 d*q; Q4_K (d*sc)*q - (dmin*m).
+// do it: Q8_0 d*q; Q4_K (d*sc)*q - (dmin*m); Q6_K (d*scale)*(q-32).
 __device__ __forceinline__ float row_element(uint32_t type, const uint8_t *row, int64_t c) {
     switch (type) {
+    case SI_TYPE_Q6_K: {
+        const uint8_t *b = row + (c >> 8) * kQ6KBytes;
+        const int e = int(c & 255), h = e >> 7, j = (e >> 5) & 3, l = e & 31;
+        const int low = (b[64 * h + l + 32 * (j & 1)] >> (4 * (j >> 1))) & 15;
+        const int high = (b[128 + 32 * h + l] >> (2 * j)) & 3;
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(b[208] | (b[209] << 8))));
+        return __fmul_rn(__fmul_rn(d, float(int8_t(b[192 + (e >> 4)]))), float((low | (high << 4)) - 32));
+    }
     case SI_TYPE_F32: return reinterpret_cast<const float *>(row)[c];
     case SI_TYPE_F16: return __half2float(reinterpret_cast<const __half *>(row)[c]);
     case SI_TYPE_Q8_0: {
@@ -301,6 +309,33 @@ __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const 
 
 // ---- decode attention --------------------------------------------------------
 constexpr int kAttnCluster = 8;
+
+// transformer.rope-kv-write fused into the decode attention (one stream): the
+// query and the token's key come from the qkv projection and are rotated on
+// the fly with the rope-kv-write arithmetic above; the key and value rows of
+// the token are stored into the caches by the CTA whose token range holds the
+// position, before it reads them.
+struct RopeFuse {
+    const float *qkv;   // [query | key | value] of the token
+    const float *freq;  // rotary / 2 frequencies
+    float *key_cache;   // the caches as written (same buffers the attention reads)
+    float *value_cache;
+    int64_t qsize, kvsize;
+    int rotary;
+    float rope_scale;
+};
+
+// Element d of one head of qkv after rope (rope_kv_kernel's arithmetic), with
+// the scaled cosines / sines of the position's angles in cs[ri], cs[half + ri].
+__device__ __forceinline__ float rope_element(const float *head, int d, const float *cs, const RopeFuse &r) {
+    const float v = head[d];
+    if (d >= r.rotary) return v;
+    const int half = r.rotary / 2;
+    const int ri = d < half ? d : d - half;
+    const float other = head[d < half ? d + half : d - half];
+    const float c = cs[ri], sn = cs[half + ri];
+    return d < half ? __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, sn)) : __fadd_rn(__fmul_rn(v, c), __fmul_rn(other, sn));
+}
 // Warps per CTA: 8 for one stream; 4 for several (more clusters fill the
 // GPU; measured at 32 Phi-4-14B streams 1198 vs 1025 tok/s, while one
 // stream loses with 4: 597 vs 648 tok/s on Phi-4-mini).
@@ -317,11 +352,11 @@ constexpr int kAttnWarpsOne = 8, kAttnWarpsMany = 4;
 // u % kv_heads of stream u / kv_heads, whose query / output rows are
 // q_stride floats apart, caches cache_stride floats apart and whose
 // position is position[stream].
-template <int NPL, int MAXG, int kTile, int kAttnWarps>
+template <int NPL, int MAXG, int kTile, int kAttnWarps, bool ROPE>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarps * 32)
     gqa_decode_kernel(const float *query, const float *key_cache, const float *value_cache, const int32_t *position,
                       float *out, int group, int kv_heads, int head_size, int64_t context, float scale,
-                      int64_t q_stride, int64_t cache_stride) {
+                      int64_t q_stride, int64_t cache_stride, RopeFuse rf) {
     extern __shared__ float smem[];
     const int G = group, hs = head_size;
     float *w_acc = smem;                                 // [warps][G][hs]
@@ -338,13 +373,72 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
     value_cache += strm * cache_stride;
     const uint32_t rank = cta_rank_in_cluster();
     pdl_trigger();
-    pdl_wait();
-    int64_t active = position[strm];
+    // Read before the dependency wait: the position (written by an earlier
+    // step or a host copy) and every cache row of an earlier token. Only the
+    // row at the position is new in this step: written by the preceding
+    // rope-kv-write, or (ROPE) taken from this step's qkv.
+    const int32_t pos = position[strm];
+    int64_t active = pos;
     active = active < 0 ? 0 : (active > context - 1 ? context - 1 : active);
+    const int64_t fresh = (pos >= 0 && pos < context) ? int64_t(pos) : -1;
     const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
-
     const int64_t stride = int64_t(kv_heads) * hs;
+    float *rope_cs = c_l + G;  // [rotary]: scaled cos of the half's angles, then scaled sin
+    if constexpr (ROPE) {
+        const int half = rf.rotary / 2;
+        for (int ri = threadIdx.x; ri < half; ri += blockDim.x) {
+            const float angle = __fmul_rn(float(pos), rf.freq[ri]);
+            rope_cs[ri] = __fmul_rn(cosf(angle), rf.rope_scale);
+            rope_cs[half + ri] = __fmul_rn(sinf(angle), rf.rope_scale);
+        }
+    }
+    auto load_tile = [&](int64_t tb, float (&kr)[kTile][NPL], float (&vr)[kTile][NPL], bool skip_fresh) {
+#pragma unroll
+        for (int u = 0; u < kTile; ++u) {
+            const int64_t t = tb + u;
+            const bool row_ok = t < t1 && !(skip_fresh && t == fresh);
+            const float *kp = key_cache + t * stride + int64_t(kvh) * hs;
+            const float *vp = value_cache + t * stride + int64_t(kvh) * hs;
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                const int d = lane + 32 * i;
+                const bool ok = row_ok && d < hs;
+                kr[u][i] = ok ? kp[d] : 0.0f;
+                vr[u][i] = ok ? vp[d] : 0.0f;
+            }
+        }
+    };
+    const int64_t tb0 = t0 + int64_t(warp) * kTile;
+    float kr[kTile][NPL], vr[kTile][NPL];
+    if (tb0 < t1) load_tile(tb0, kr, vr, true);
+    pdl_wait();
+    // The new row of this step, in registers: lane channels d = lane + 32 i.
+    float kf[NPL], vf[NPL];
+    if constexpr (ROPE) {
+        __syncthreads();  // the rope table
+        const float *kh = rf.qkv + rf.qsize + int64_t(kvh) * hs;
+        const float *vh = rf.qkv + rf.qsize + rf.kvsize + int64_t(kvh) * hs;
+        const bool mine = fresh >= t0 && fresh < t1;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int d = lane + 32 * i;
+            kf[i] = (mine && d < hs) ? rope_element(kh, d, rope_cs, rf) : 0.0f;
+            vf[i] = (mine && d < hs) ? vh[d] : 0.0f;
+        }
+        // the caches keep it for later steps (rope-kv-write writes nothing
+        // for a position outside the cache)
+        if (mine && warp == 0) {
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < hs) {
+                    rf.key_cache[fresh * stride + int64_t(kvh) * hs + d] = kf[i];
+                    rf.value_cache[fresh * stride + int64_t(kvh) * hs + d] = vf[i];
+                }
+            }
+        }
+    }
     float q[MAXG][NPL], acc[MAXG][NPL], m[MAXG], l[MAXG];
 #pragma unroll
     for (int g = 0; g < MAXG; ++g) {
@@ -353,23 +447,31 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 #pragma unroll
         for (int i = 0; i < NPL; ++i) {
             const int d = lane + 32 * i;
-            q[g][i] = (g < G && d < hs) ? query[(int64_t(kvh) * G + g) * hs + d] : 0.0f;
+            if constexpr (ROPE)
+                q[g][i] = (g < G && d < hs) ? rope_element(rf.qkv + (int64_t(kvh) * G + g) * hs, d, rope_cs, rf)
+                                            : 0.0f;
+            else
+                q[g][i] = (g < G && d < hs) ? query[(int64_t(kvh) * G + g) * hs + d] : 0.0f;
             acc[g][i] = 0.0f;
         }
     }
-    for (int64_t tb = t0 + int64_t(warp) * kTile; tb < t1; tb += int64_t(kAttnWarps) * kTile) {
-        float kr[kTile][NPL], vr[kTile][NPL];
+    for (int64_t tb = tb0; tb < t1; tb += int64_t(kAttnWarps) * kTile) {
+        if (tb != tb0) load_tile(tb, kr, vr, false);
+        if (fresh >= tb && fresh < tb + kTile && fresh < t1) {
 #pragma unroll
-        for (int u = 0; u < kTile; ++u) {
-            const int64_t t = tb + u;
-            const float *kp = key_cache + t * stride + int64_t(kvh) * hs;
-            const float *vp = value_cache + t * stride + int64_t(kvh) * hs;
+            for (int u = 0; u < kTile; ++u) {
+                if (tb + u != fresh) continue;
 #pragma unroll
-            for (int i = 0; i < NPL; ++i) {
-                const int d = lane + 32 * i;
-                const bool ok = t < t1 && d < hs;
-                kr[u][i] = ok ? kp[d] : 0.0f;
-                vr[u][i] = ok ? vp[d] : 0.0f;
+                for (int i = 0; i < NPL; ++i) {
+                    const int d = lane + 32 * i;
+                    if constexpr (ROPE) {
+                        kr[u][i] = kf[i];
+                        vr[u][i] = vf[i];
+                    } else {
+                        kr[u][i] = d < hs ? key_cache[fresh * stride + int64_t(kvh) * hs + d] : 0.0f;
+                        vr[u][i] = d < hs ? value_cache[fresh * stride + int64_t(kvh) * hs + d] : 0.0f;
+                    }
+                }
             }
         }
 #pragma unroll
@@ -969,22 +1071,46 @@ si_status tr_rope_kv_write_streams(const float *qkv, const int32_t *positions, c
 }
 
 namespace {
-template <int NPL, int MAXG, int kTile, int kAttnWarps>
+template <int NPL, int MAXG, int kTile, int kAttnWarps, bool ROPE = false>
 si_status launch_gqa(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                      int group, int kv_heads, int head_size, int64_t context, float scale, int streams,
-                     int64_t q_stride, int64_t cache_stride, void *stream) {
-    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile, kAttnWarps>;
+                     int64_t q_stride, int64_t cache_stride, void *stream, const RopeFuse &rf = RopeFuse{}) {
+    auto kernel = gqa_decode_kernel<NPL, MAXG, kTile, kAttnWarps, ROPE>;
     const size_t smem = size_t(kAttnWarps * group * head_size + 2 * kAttnWarps * group + group * head_size +
-                               2 * group) * sizeof(float);
+                               2 * group + (ROPE ? rf.rotary : 0)) * sizeof(float);
     if (smem > 48 * 1024) {
         if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), 200 * 1024))
             return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
     }
     return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(streams * kv_heads * kAttnCluster)),
                   dim3(kAttnWarps * 32), smem, stream, query, kc, vc, position, out, group, kv_heads, head_size,
-                  context, scale, q_stride, cache_stride);
+                  context, scale, q_stride, cache_stride, rf);
 }
 }  // namespace
+
+si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, const float *freq, float *kc, float *vc,
+                                   float *out, int query_heads, int kv_heads, int head_size, int rotary,
+                                   int64_t context, float rope_scale, void *stream) {
+    const int group = query_heads / kv_heads;
+    const float scale = 1.0f / sqrtf(float(head_size));
+    const int npl = (head_size + 31) / 32;
+    const int64_t qsize = int64_t(query_heads) * head_size, kvsize = int64_t(kv_heads) * head_size;
+    const RopeFuse rf{qkv, freq, kc, vc, qsize, kvsize, rotary, rope_scale};
+#define SI_GQA_R(NPL, MAXG, TILE)                                                                               \
+    launch_gqa<NPL, MAXG, TILE, kAttnWarpsOne, true>(qkv, kc, vc, position, out, group, kv_heads, head_size,      \
+                                                     context, scale, 1, qsize, 0, stream, rf)
+    if (group <= 4) {
+        if (npl <= 1) return SI_GQA_R(1, 4, 8);
+        if (npl <= 2) return SI_GQA_R(2, 4, 8);
+        if (npl <= 4) return SI_GQA_R(4, 4, 8);
+        return SI_GQA_R(8, 4, 4);
+    }
+    if (npl <= 1) return SI_GQA_R(1, 8, 8);
+    if (npl <= 2) return SI_GQA_R(2, 8, 4);
+    if (npl <= 4) return SI_GQA_R(4, 8, 4);
+    return SI_GQA_R(8, 8, 2);
+#undef SI_GQA_R
+}
 
 si_status tr_attention_decode(const float *query, const float *kc, const float *vc, const int32_t *position, float *out,
                               int query_heads, int kv_heads, int head_size, int64_t context, void *stream) {

@@ -15,8 +15,8 @@ _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "libsharpinfer_cuda.so"
 
 # GGUF tensor type ids (GgufModelFile.cs:24-46)
-F32, F16, Q8_0, Q4_K, I32 = 0, 1, 8, 12, 26
-TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", I32: "I32"}
+F32, F16, Q8_0, Q4_K, Q6_K, I32 = 0, 1, 8, 12, 14, 26
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", I32: "I32"}
 
 MATVEC_DEFAULT, MATVEC_COOPERATIVE, MATVEC_QUANT_STAGED = 0, 1, 2
 
@@ -151,12 +151,16 @@ SIGNATURES = {
     "si_batch_gather_rows": [_vp, _i64, _vp, _vp, _i64, _i64, _vp],
     # decoder session
     "si_decoder_create": [_i32, _vp, C.POINTER(_vp)],
+    "si_decoder_create_typed": [_i32, _vp, _vp, _i32, C.POINTER(_vp)],
     "si_decoder_arena_bytes": [_vp, _pu64],
     "si_decoder_create_streams": [_i32, _vp, _i32, C.POINTER(_vp)],
     "si_decoder_step_streams": [_vp, _vp, _vp, _vp],
     "si_decoder_generate_streams": [_vp, _vp, _vp, _i32, _vp],
     "si_decoder_prefill_stream": [_vp, _i32, _vp, _i32, _i32, _vp],
     "si_decoder_create_sharded": [_i32, _vp, _vp, _u64, C.POINTER(_vp)],
+    "si_tp_partition_plan": [_vp, _i32, _i32, _vp],
+    "si_decoder_tp_arena_bytes": [_vp, _i32, _pu64],
+    "si_decoder_create_tensor_parallel": [_i32, _vp, _vp, C.POINTER(_vp)],
     "si_decoder_destroy": [_vp],
     "si_decoder_slot": [_vp, C.c_char_p, C.POINTER(_vp), _pu64],
     "si_decoder_upload": [_vp, C.c_char_p, _u64, _vp, _u64],
@@ -544,6 +548,25 @@ def decoder_slot_names(layers: int) -> list[str]:
     return names
 
 
+class TpPartition(C.Structure):
+    """si_tp_partition: one rank's slices of a tensor-parallel session."""
+    _fields_ = [("kv_head_begin", C.c_int32), ("kv_heads", C.c_int32), ("query_head_begin", C.c_int32),
+                ("query_heads", C.c_int32), ("ffn_begin", C.c_int64), ("ffn_rows", C.c_int64),
+                ("vocab_begin", C.c_int64), ("vocab_rows", C.c_int64)]
+
+
+def tp_partition(cfg: dict, nranks: int, rank: int) -> TpPartition:
+    part = TpPartition()
+    call("si_tp_partition_plan", C.byref(DecoderConfig(**cfg)), nranks, rank, C.byref(part))
+    return part
+
+
+def tp_arena_bytes(cfg: dict, nranks: int) -> int:
+    v = C.c_uint64()
+    call("si_decoder_tp_arena_bytes", C.byref(DecoderConfig(**cfg)), nranks, C.byref(v))
+    return v.value
+
+
 def decoder_arena_bytes(cfg: dict) -> int:
     """Arena bytes a row-sharded session needs (si_decoder_arena_bytes)."""
     c, v = DecoderConfig(**cfg), C.c_uint64()
@@ -557,11 +580,16 @@ class Decoder:
     session of that rank (si_decoder_create_sharded)."""
 
     def __init__(self, cfg: dict, device: int = 0, group: "PeerGroup | None" = None, streams: int = 1,
-                 shard_min_bytes: int = 0):
+                 shard_min_bytes: int = 0, slot_types: "list[int] | None" = None, tensor_parallel: bool = False):
         self.cfg = DecoderConfig(**cfg)
         self.streams = streams
         h = C.c_void_p()
-        if group is not None:
+        if tensor_parallel:  # si_decoder_create_tensor_parallel on the group's rank
+            call("si_decoder_create_tensor_parallel", device, C.byref(self.cfg), group.handle, C.byref(h))
+        elif slot_types is not None:  # one GGUF type per slot (decoder_slot_names order)
+            t = (C.c_uint32 * len(slot_types))(*slot_types)
+            call("si_decoder_create_typed", device, C.byref(self.cfg), t, len(slot_types), C.byref(h))
+        elif group is not None:
             call("si_decoder_create_sharded", device, C.byref(self.cfg), group.handle, shard_min_bytes, C.byref(h))
         elif streams != 1:
             call("si_decoder_create_streams", device, C.byref(self.cfg), streams, C.byref(h))

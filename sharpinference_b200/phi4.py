@@ -111,6 +111,25 @@ def config_from_gguf(f: "native.GgufFile", context: int = 4096) -> dict:
     return cfg
 
 
+def slot_types_from_gguf(f: "native.GgufFile", layers: int) -> list[int]:
+    """The GGUF type of every session slot's tensor (decoder_slot_names
+    order), for si_decoder_create_typed: mixed-type files such as Q4_K_M keep
+    some projections and the embedding in Q6_K."""
+    return [f.tensors[gguf_tensor_name(slot)].type for slot in native.decoder_slot_names(layers)]
+
+
+def open_session_gguf(f: "native.GgufFile", context: int = 4096, device: int = 0) -> "native.Decoder":
+    """A decoder session for a phi3 GGUF file: per-slot types when the file
+    mixes weight types, every tensor uploaded unchanged."""
+    cfg = config_from_gguf(f, context)
+    types = slot_types_from_gguf(f, cfg["layers"])
+    names = native.decoder_slot_names(cfg["layers"])
+    mixed = any(t != cfg["weight_type"] for t, slot in zip(types, names) if "_weight_" in slot)
+    dec = native.Decoder(cfg, device, slot_types=types if mixed else None)
+    load_gguf(dec, f)
+    return dec
+
+
 def load_gguf(decoder: "native.Decoder", f: "native.GgufFile") -> None:
     """Uploads every slot's GGUF tensor unchanged (Phi4D3D12TextSession.cs:56-57)."""
     for slot in native.decoder_slot_names(decoder.cfg.layers):
@@ -143,3 +162,45 @@ def save_gguf(path, cfg: dict, weights: dict) -> None:
         else:
             tensors.append((gguf_tensor_name(slot), 0, [h], np.asarray(weights[slot], dtype=np.float32)))
     gguf.write(path, meta, tensors)
+
+
+def _col_slice(blob: np.ndarray, wtype: int, rows: int, cols: int, c0: int, c1: int) -> np.ndarray:
+    """Columns [c0, c1) of a [rows, cols] matrix in GGUF bytes (c0, c1 on block boundaries)."""
+    rb = native.row_bytes(wtype, cols)
+    b0 = native.row_bytes(wtype, c0) if c0 else 0
+    b1 = native.row_bytes(wtype, c1)
+    return np.ascontiguousarray(np.asarray(blob).view(np.uint8).reshape(rows, rb)[:, b0:b1]).reshape(-1)
+
+
+def _row_slice(blob: np.ndarray, wtype: int, cols: int, ranges) -> np.ndarray:
+    rb = native.row_bytes(wtype, cols)
+    m = np.asarray(blob).view(np.uint8).reshape(-1, rb)
+    return np.ascontiguousarray(np.concatenate([m[a:b] for a, b in ranges])).reshape(-1)
+
+
+def tp_slice_weights(cfg: dict, weights: dict, part) -> dict:
+    """One rank's slots of a tensor-parallel session (si_tp_partition_plan),
+    cut from the whole model's GGUF bytes: qkv rows of the rank's heads, the
+    out projection's columns of its query heads, its gate / up rows and down
+    columns of the intermediate; token_embedding and the norms whole."""
+    h, f, hs = cfg["hidden"], cfg["intermediate"], cfg["head_size"]
+    kv = cfg["kv_heads"] * hs
+    wt = cfg["weight_type"]
+    q0, q1 = part.query_head_begin * hs, (part.query_head_begin + part.query_heads) * hs
+    k0, k1 = part.kv_head_begin * hs, (part.kv_head_begin + part.kv_heads) * hs
+    f0, f1 = part.ffn_begin, part.ffn_begin + part.ffn_rows
+    out = {}
+    for name, arr in weights.items():
+        base = name.rsplit("_", 1)[0]
+        if base == "qkv_weight":
+            out[name] = _row_slice(arr, wt, h, [(q0, q1), (h + k0, h + k1), (h + kv + k0, h + kv + k1)])
+        elif base == "attn_output_weight":
+            out[name] = _col_slice(arr, wt, h, h, q0, q1)
+        elif base == "ffn_up_weight":
+            out[name] = _row_slice(arr, wt, h, [(f0, f1), (f + f0, f + f1)])
+        elif base == "ffn_down_weight":
+            out[name] = _col_slice(arr, wt, h, f, f0, f1)
+        else:
+            out[name] = arr
+    return out
+

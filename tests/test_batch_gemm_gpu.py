@@ -55,7 +55,7 @@ def _shared_case(ctx, wtype, batch, n, k, valid, seed):
     return blob, x.reshape(batch, k), y
 
 
-@pytest.mark.parametrize("wtype", [N.F16, N.Q8_0, N.Q4_K])
+@pytest.mark.parametrize("wtype", [N.F16, N.Q8_0, N.Q4_K, N.Q6_K])
 @pytest.mark.parametrize("batch,valid", [(16, 16), (16, 11), (32, 32), (5, 0), (3, 7)])
 def test_batch_shared_quant_parity_and_valid_mask(ctx, wtype, batch, valid):
     n, k = 300, 512
@@ -83,7 +83,7 @@ def test_batch_shared_tensor_core_shapes(ctx, wtype, batch, valid, n, k):
     assert native.device_error_take(0) == 0
 
 
-@pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K])
+@pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K, N.Q6_K])
 @pytest.mark.parametrize("m,n,k", [(1, 64, 256), (33, 129, 512), (64, 1000, 768), (300, 200, 256), (257, 128, 1024),
                                    (64, 7, 256)])
 def test_matrix_multiply_parity(ctx, wtype, m, n, k):

@@ -25,7 +25,7 @@ def _logit_gate(gpu, ref):
     assert rel_l2 <= 1e-4, rel_l2
 
 
-@pytest.mark.parametrize("wtype", [native.Q4_K, native.Q8_0, native.F16])
+@pytest.mark.parametrize("wtype", [native.Q4_K, native.Q8_0, native.F16, native.Q6_K])
 def test_forward_token_matches_oracle(wtype):
     cfg = tiny_decoder_config(wtype)
     weights = tiny_decoder_weights(cfg, seed=7 + wtype)

@@ -28,7 +28,7 @@ def test_normal_generator_matches_oracle(seed):
     assert abs(float(big.mean())) < 0.02 and abs(float(big.std()) - 1.0) < 0.02
 
 
-@pytest.mark.parametrize("wtype", [native.Q8_0, native.Q4_K])
+@pytest.mark.parametrize("wtype", [native.Q8_0, native.Q4_K, native.Q6_K])
 @pytest.mark.parametrize("sigma", [0.02, 1.0, 300.0])
 def test_quantizer_bit_exact_with_oracle(wtype, sigma):
     x = oracle.normal(3, 256 * 37, sigma)
@@ -38,7 +38,7 @@ def test_quantizer_bit_exact_with_oracle(wtype, sigma):
     assert np.array_equal(native.quantize(wtype, x), oracle.quantize(wtype, x))
 
 
-@pytest.mark.parametrize("wtype", [native.Q8_0, native.Q4_K])
+@pytest.mark.parametrize("wtype", [native.Q8_0, native.Q4_K, native.Q6_K])
 def test_dequantize_bit_exact_with_oracle(wtype):
     x = oracle.normal(5, 256 * 19, 0.02)
     blob = oracle.quantize(wtype, x)
@@ -49,7 +49,7 @@ def test_dequantize_bit_exact_with_oracle(wtype):
 
 def test_synth_weights_equals_generate_then_quantize():
     rows, cols = 33, 512
-    for wtype in (native.Q8_0, native.Q4_K, native.F16, native.F32):
+    for wtype in (native.Q8_0, native.Q4_K, native.Q6_K, native.F16, native.F32):
         blob = native.synth_weights(wtype, 9, rows, cols, 0.02)
         ref = native.quantize(wtype, oracle.normal(9, rows * cols, 0.02)) if wtype != native.F16 else \
             oracle.normal(9, rows * cols, 0.02).astype(np.float16).view(np.uint8)
@@ -90,3 +90,17 @@ def test_round_trip_is_idempotent():
     blob = native.quantize(native.Q8_0, x)
     w = native.dequantize(native.Q8_0, blob, x.size)
     assert np.array_equal(native.quantize(native.Q8_0, w), blob)
+
+
+def test_q6_k_block_layout_and_error_bound():
+    """Q6_K round trip: |w - x| <= half a step of each 16-element group
+    (d * scale / 2, plus the binary16 rounding of d), codes inside [0, 63]."""
+    x = oracle.normal(4, 256 * 32, 0.02)
+    blob = native.quantize(native.Q6_K, x)
+    assert blob.size == 32 * 210
+    w = native.dequantize(native.Q6_K, blob, x.size)
+    blocks = blob.reshape(32, 210)
+    d = blocks[:, 208:210].copy().view(np.float16).astype(np.float32).reshape(32, 1)
+    sc = blocks[:, 192:208].view(np.int8).astype(np.float32)
+    step = np.repeat(d * sc, 16, axis=1).reshape(-1)
+    assert np.all(np.abs(w - x) <= 0.5 * step * 1.001 + 1e-12)

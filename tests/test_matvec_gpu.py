@@ -152,7 +152,16 @@ def test_q8_0_shapes_and_tails(ctx, rows, cols):
     check_quant(N.Q8_0, blob, x, outs, rows, cols)
 
 
-@pytest.mark.parametrize("wtype", [N.Q8_0, N.Q4_K])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (7, 512), (300, 3072), (29, 5120), (3, 8192), (5, 17920),
+                                       (40, 1024)])
+def test_q6_k_shapes(ctx, rows, cols):
+    """Q6_K (210-byte superblocks: 16-bit aligned, 16-element int8-scaled
+    groups) against the oracle, odd superblock counts included."""
+    blob, x, outs = quant_case(ctx, N.Q6_K, rows, cols, seed=rows + cols)
+    check_quant(N.Q6_K, blob, x, outs, rows, cols)
+
+
+@pytest.mark.parametrize("wtype", [N.Q8_0, N.Q4_K, N.Q6_K])
 def test_quant_unaligned_weight_view_uses_row_warp_path(ctx, wtype):
     rows, cols = 77, 1024
     blob, x, outs = quant_case(ctx, wtype, rows, cols, seed=5, offset=2)

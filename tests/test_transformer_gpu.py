@@ -289,7 +289,7 @@ def test_argmax_matches_oracle_and_tie_rules(ctx, dev):
         assert int(dev.get(out)[0]) == oracle.argmax(x)
 
 
-@pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K])
+@pytest.mark.parametrize("wtype", [N.F32, N.F16, N.Q8_0, N.Q4_K, N.Q6_K])
 def test_gather_row_is_exact(ctx, dev, wtype):
     rows, cols = 37, 3072
     rng = np.random.default_rng(wtype)
