@@ -639,23 +639,25 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
     """Config 5 at batch 1: the Phi-4-14B-shaped Q8_0 decoder (40 layers,
     hidden 5120, 40/10 heads of 128, FFN 17920, vocab 100352, seed 11),
     a 1024-token random prompt, then 128 greedy steps timed on the device
-    (max over ranks). One GPU: the whole session. N GPUs: the row-sharded
-    session, every projection split by rows over the ranks with its output
-    gathered into every rank's arena by the GEMV kernel itself (NVLink peer
-    stores), the rest of the program replicated. Weights are generated on
-    the device (si_synth_weight_rows_device, slot ordinal i -> seed
-    11 * 1000003 + i, each rank its own rows)."""
-    import numpy as np
-
+    (max over ranks). One GPU: the whole session. N GPUs: the
+    tensor-parallel session (Megatron pairing: qkv and gate_up by rows of
+    the rank's heads and intermediate slice, out and down by columns with
+    their partial vectors exchanged through the NVLink peer arenas inside the
+    GEMV, heads-local attention, the vocabulary projection by rows). Weights
+    are generated on the device (slot ordinal i -> seed 11 * 1000003 + i),
+    each rank only its slices."""
     from sharpinference_b200 import phi4
     cfg = dict(phi4.PHI4_14B)
     prompt_len, steps = 1024, 128
     cfg["context"] = prompt_len + steps + 1
     group, arena, addrs = None, None, []
-    if world > 1:
+    tp = world > 1
+    if tp:
         import torch.distributed as dist
-        ab = (native.decoder_arena_bytes(cfg) + 255) // 256 * 256
+        ab = (native.tp_arena_bytes(cfg, world) + 255) // 256 * 256
         arena = ctx.buffer(ab)
+        import numpy as np
+        arena.upload(np.zeros(ab, np.uint8))
         handles = [None] * world
         dist.all_gather_object(handles, native.ipc_export(arena.device_pointer))
         addrs = [arena.device_pointer if q == rank else native.ipc_open(local, handles[q]) for q in range(world)]
@@ -664,29 +666,45 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
     out = {"workload": "config5 batch 1: Phi-4-14B-shaped Q8_0 decoder (40 layers, hidden 5120, 40/10 heads of "
                        "128, FFN 17920, vocab 100352), N(0,0.02) seed 11, 1024-token random prompt, 128 greedy steps",
            "parallelism": "single GPU" if world == 1 else
-           f"{world} GPUs: the large projections row-sharded, outputs gathered by the GEMV kernel over NVLink; "
-           "small projections, norms, rope, attention, argmax and the KV cache replicated"}
-    # Split a projection only when its exchange (~7 us) costs less than the
-    # weight time it saves: (1 - 1/N) * bytes / HBM > 8 us.
-    shard_min = int(52e6 * world / (world - 1)) if world > 1 else 0
+           f"{world} GPUs, tensor parallel: qkv / gate_up by rows of the rank's heads and intermediate slice, "
+           "out / down by columns with partial sums exchanged inside the GEMV over NVLink (two exchanges per "
+           "layer), heads-local attention, vocabulary rows split"}
+    q8, H, hs, F = native.Q8_0, cfg["hidden"], cfg["head_size"], cfg["intermediate"]
+    KV = cfg["kv_heads"] * hs
     try:
-        with native.Decoder(cfg, local, group, shard_min_bytes=shard_min) as dec:
-            split, rep_bytes = [], 0
+        with native.Decoder(cfg, local, group, tensor_parallel=tp) as dec:
+            part = native.tp_partition(cfg, world, rank) if tp else None
             for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
                 if name not in shapes:
                     continue
                 rows, cols = shapes[name]
                 ptr, nbytes = dec.slot(name)
-                begin, count = 0, rows
-                if nbytes < rows * native.row_bytes(native.Q8_0, cols):  # this slot holds the rank's rows
-                    begin, count, _ = native.rowshard_plan(rows, world, rank)
-                    if name.endswith("_0"):
-                        split.append(name[:-2])
-                elif world > 1:
-                    rep_bytes += nbytes
-                assert nbytes == count * native.row_bytes(native.Q8_0, cols)
-                native.synth_weight_rows_device(native.Q8_0, 11 * 1_000_003 + i, begin, count, cols, 0.02, ptr,
-                                                dec.stream)
+                seed = 11 * 1_000_003 + i
+                base = name.rsplit("_", 1)[0]
+                if not tp or base == "token_embedding":
+                    native.synth_weight_rows_device(q8, seed, 0, rows, cols, 0.02, ptr, dec.stream)
+                    continue
+                rb = native.row_bytes(q8, cols)
+                if base in ("qkv_weight", "ffn_up_weight"):
+                    if base == "qkv_weight":
+                        q0, q1 = part.query_head_begin * hs, (part.query_head_begin + part.query_heads) * hs
+                        k0, k1 = part.kv_head_begin * hs, (part.kv_head_begin + part.kv_heads) * hs
+                        ranges = [(q0, q1), (H + k0, H + k1), (H + KV + k0, H + KV + k1)]
+                    else:
+                        f0, f1 = part.ffn_begin, part.ffn_begin + part.ffn_rows
+                        ranges = [(f0, f1), (F + f0, F + f1)]
+                    off = 0
+                    for r0, r1 in ranges:
+                        native.synth_weight_rows_device(q8, seed, r0, r1 - r0, cols, 0.02, ptr + off, dec.stream)
+                        off += (r1 - r0) * rb
+                    assert off == nbytes, name
+                else:  # column slices: attn_output (query-head columns), ffn_down (intermediate columns)
+                    if base == "attn_output_weight":
+                        c0, cn = part.query_head_begin * hs, part.query_heads * hs
+                    else:
+                        c0, cn = part.ffn_begin, part.ffn_rows
+                    assert nbytes == rows * native.row_bytes(q8, cn), name
+                    native.synth_weight_block_device(q8, seed, 0, rows, c0, cn, cols, 0.02, ptr, dec.stream)
             prompt = phi4.random_prompt(11, prompt_len, cfg["vocab"])
             stream = torch.cuda.ExternalStream(dec.stream, device=torch.device("cuda", local))
             e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -707,23 +725,23 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
             decode_ms = max_over_ranks(e[2].elapsed_time(e[3]))
             wall = max_over_ranks(wall)
             barrier()
-            wbytes = sum(r * native.row_bytes(native.Q8_0, c) for r, c in shapes.values())
+            wbytes = sum(r * native.row_bytes(q8, c) for r, c in shapes.values())
             kv_row = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_size"] * 4
             kv_bytes = sum(kv_row * (p + 1) for p in range(prompt_len, prompt_len + steps)) / steps
             tok_s = steps / (decode_ms * 1e-3)
-            # weights are read once per token across the ranks; the KV cache once per rank
-            bytes_token = wbytes + (world - 1) * rep_bytes + world * kv_bytes
-            if world > 1:
-                out["split_projections"] = split + ["vocabulary (token_embedding rows)"]
-                out["shard_min_bytes"] = shard_min
+            # every weight byte and every KV row is read by one rank per token
+            bytes_token = wbytes + kv_bytes
+            if tp:
+                out["partition_rank0"] = {n: getattr(native.tp_partition(cfg, world, 0), n)
+                                          for n, _ in native.TpPartition._fields_}
             out.update({
                 "decode_tok_s": round(tok_s, 1), "decode_ms_per_token": round(decode_ms / steps, 4),
                 "e2e_decode_tok_s": round(steps / wall, 1),
                 "prompt_ms": round(prefill_ms, 1),
                 "prompt_path": "batched prefill" if world == 1 else "the decode program per prompt token",
                 "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_token),
-                             "bytes": "Q8_0 weight bytes per token over all ranks (split projections once, "
-                                      "replicated ones on every rank) + the KV-cache rows attended on every rank",
+                             "bytes": "Q8_0 weight bytes per token (each read by one rank) + the KV-cache rows "
+                                      "attended (each by one rank)",
                              "achieved_aggregate": round(bytes_token * tok_s / 1e9, 1),
                              "peak_aggregate": round(peak * world, 1), "unit": "GB/s",
                              "frac": round(bytes_token * tok_s / 1e9 / (peak * world), 4)},
@@ -890,6 +908,60 @@ def decode_block(native, torch, local: int, peak: float, cpu_sample: bool) -> di
     return out
 
 
+def run_case(case: list[str]) -> None:
+    """One hot-path case run twice on GPU 0, for an ncu capture of a single
+    launch (`-k <kernel> -s 1 -c 1`): seeded weights and inputs in device memory.
+
+      --case gemv Q4_K 200064 3072      (also Q8_0 / Q6_K, any N K)
+      --case batch Q4_K 200064 3072 16  (transformer.batch-shared-matvec, 16 rows)
+      --case gemm Q4_K 200064 3072 512  (core.matrix-multiply, 512 rows)
+      --case decode mini 64 2           (Phi-4-mini decoder: 64 prompt steps, then 2 steps; one graph per step)
+      --case prefill mini 512           (Phi-4-mini decoder: one batched prefill of 512 tokens)
+    """
+    import numpy as np
+
+    from sharpinference_b200 import native, phi4
+    kind = case[0]
+    if kind in ("decode", "prefill"):
+        cfg = dict(phi4.PHI4_MINI if case[1] == "mini" else phi4.PHI4_14B)
+        prompt_tokens = int(case[2])
+        steps = int(case[3]) if kind == "decode" else 0
+        cfg["context"] = prompt_tokens + steps + 1
+        with native.Decoder(cfg) as dec:
+            phi4.load_synthetic(dec, cfg, seed=7)
+            prompt = phi4.random_prompt(7, prompt_tokens, cfg["vocab"])
+            if kind == "decode":
+                toks = dec.generate(prompt, steps)
+                print(f"decode {case[1]} prompt={prompt_tokens} steps={steps}: last tokens {toks[-3:].tolist()} "
+                      f"device_error={native.device_error_take(0)}")
+            else:
+                nxt = dec.prefill(prompt)
+                print(f"prefill {case[1]} prompt={prompt_tokens}: next token {nxt} "
+                      f"device_error={native.device_error_take(0)}")
+        return
+    types = {"Q4_K": native.Q4_K, "Q8_0": native.Q8_0, "Q6_K": native.Q6_K, "F16": native.F16, "F32": native.F32}
+    wt, n, k = types[case[1]], int(case[2]), int(case[3])
+    m = int(case[4]) if len(case) > 4 else 1
+    blob = native.synth_weights(wt, 4, n, k, 0.02)
+    x = native.synth_normal(1004, m * k, 1.0)
+    with native.Context(0) as ctx:
+        W, X, Y, Cb = ctx.buffer(blob.nbytes), ctx.buffer(x.nbytes), ctx.buffer(4 * m * n), ctx.buffer(8)
+        W.upload(blob), X.upload(x), Cb.upload(np.array([0, m], np.int32))
+        for _ in range(2):
+            if kind == "gemv":
+                ctx.matvec(wt, W, X, Y, n, k)
+            elif kind == "batch":
+                ctx.batch_shared_matvec(wt, W, X, Cb, Y, m, n, k)
+            elif kind == "gemm":
+                ctx.matrix_multiply(wt, X, W, Y, m, n, k)
+            else:
+                raise SystemExit(f"unknown case {kind}")
+        ctx.synchronize()
+        y = Y.readback().view(np.float32)
+        print(f"{kind} {case[1]} {n}x{k} m={m}: finite={bool(np.all(np.isfinite(y)))} "
+              f"device_error={native.device_error_take(0)}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -900,8 +972,11 @@ def main() -> None:
     ap.add_argument("--no-q8", action="store_true", help="skip the secondary Q8_0 GEMV measurements")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-4 Phi-4-mini decoder measurement")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 prefill GEMM measurement")
+    ap.add_argument("--case", nargs="+", help="run one hot-path case for a profiler capture (see run_case)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args.case)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

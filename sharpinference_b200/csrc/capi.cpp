@@ -335,7 +335,6 @@ si_status si_device_error_take(int device, uint32_t *code) {
     if (!code) return fail(SI_ERR_INVALID_ARGUMENT, "null argument");
     *code = 0;
     if (si_status st = kernels::take_error_gemv(device, code)) return st;
-    if (si_status st = kernels::take_error_decode_step(device, code)) return st;
     if (si_status st = kernels::take_error_gemv_mma(device, code)) return st;
     if (si_status st = kernels::take_error_gemm_skinny(device, code)) return st;
     return kernels::take_error_gemm(device, code);

@@ -54,11 +54,6 @@ struct si_decoder {
     int32_t *pinned_prompt = nullptr, *pinned_history = nullptr;
     cudaGraphExec_t step_exec = nullptr, feed_exec = nullptr;
 
-    // The persistent decode step (one cooperative launch per token) where the
-    // model allows it; `direct`: its launches could not be recorded into a
-    // graph and are issued per token instead.
-    k::DecodeStep *step = nullptr;
-    bool direct = false;
     // Row-sharded session (si_decoder_create_sharded): the peer group, this
     // rank's arena (the five projection outputs live there, gathered by the
     // peer GEMV) and the vocabulary projection's rows of token_embedding.
@@ -150,7 +145,6 @@ void destroy(si_decoder *d) {
     if (d->streams_exec) cudaGraphExecDestroy(d->streams_exec);
     if (d->streams_feed_exec) cudaGraphExecDestroy(d->streams_feed_exec);
     if (d->pinned_st) cudaFreeHost(d->pinned_st);
-    if (d->step) k::decode_step_destroy(d->step);
     for (void *p : d->allocations) cudaFree(p);
     if (d->pinned) cudaFreeHost(d->pinned);
     if (d->stream) cudaStreamDestroy(d->stream);
@@ -317,7 +311,6 @@ si_status record_step_tp(si_decoder *d, k::DecodeFeed *feed);
 
 si_status record_step(si_decoder *d, k::DecodeFeed *feed) {
     if (d->tp) return record_step_tp(d, feed);
-    if (d->step) return k::decode_step_launch(d->step, feed, d->stream);
     if (fused_step_supported(d)) return record_step_fused(d, feed);
     return record_step_unfused(d, feed);
 }
@@ -328,15 +321,6 @@ si_status build_graph(si_decoder *d, k::DecodeFeed *feed, cudaGraphExec_t *out) 
     const si_status rec = record_step(d, feed);
     cudaGraph_t g = nullptr;
     const cudaError_t e = cudaStreamEndCapture(d->stream, &g);
-    if (rec != SI_OK && d->step) {
-        // A cooperative launch that cannot be captured: issue the persistent
-        // step directly every token.
-        if (g) cudaGraphDestroy(g);
-        cudaGetLastError();
-        si::clear_error();
-        d->direct = true;
-        return SI_OK;
-    }
     if (rec != SI_OK) {
         if (g) cudaGraphDestroy(g);
         return rec;
@@ -602,7 +586,6 @@ si_status validate(const si_decoder_config *c) {
     return si::byte_length(c->embedding_type, uint64_t(c->hidden), &b);
 }
 
-si_status create_step(si_decoder *d);
 
 // slot_types: null, or one GGUF type per slot of si_decoder_slot order
 // (token_embedding, output_norm, then per layer attn_norm, ffn_norm, qkv,
@@ -769,8 +752,6 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
     d->pinned_feed = reinterpret_cast<k::DecodeFeed *>(reinterpret_cast<uint8_t *>(d->pinned) + 64);
     d->pinned_prompt = reinterpret_cast<int32_t *>(d->pinned_feed + 1);
     d->pinned_history = d->pinned_prompt + c->context;
-    if (!group && streams == 1)
-        if (si_status st = create_step(d)) return cleanup(st);
     if (si_status st = cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return cleanup(st);
     *out = d;
     return SI_OK;
@@ -1011,52 +992,16 @@ si_status create_tp(int device, const si_decoder_config *c, si_peer_group *group
 }
 
 si_status ensure_graphs(si_decoder *d) {
-    if (!d->direct && !d->step_exec)
+    if (!d->step_exec)
         if (si_status st = build_graph(d, nullptr, &d->step_exec)) return st;
-    if (!d->direct && !d->feed_exec)
+    if (!d->feed_exec)
         if (si_status st = build_graph(d, d->feed, &d->feed_exec)) return st;
     return SI_OK;
 }
 
-// One decode step on the stream: the recorded graph, or the persistent
-// step's launch when it could not be recorded.
+// One decode step on the stream: the recorded graph.
 si_status run_step(si_decoder *d, bool with_feed) {
-    if (d->direct) return record_step(d, with_feed ? d->feed : nullptr);
     return cuda(cudaGraphLaunch(with_feed ? d->feed_exec : d->step_exec, d->stream), "cudaGraphLaunch");
-}
-
-// The persistent step is opt-in (SI_DECODE_STEP=1): on B200 it measured
-// 2.09 ms per Phi-4-mini token against 1.76 ms for the recorded nine-launch
-// program. Its 195 phases each pay a grid barrier (~1 us) and 3-4 us of
-// input-load latency behind the weight stream, which the launch-per-
-// instruction program overlaps better.
-si_status create_step(si_decoder *d) {
-    const char *e = std::getenv("SI_DECODE_STEP");
-    if (!e || std::atoi(e) == 0) return SI_OK;
-    const si_decoder_config &c = d->cfg;
-    k::DecodeStepModel m{};
-    m.layers = c.layers, m.hidden = c.hidden, m.query_heads = c.query_heads, m.kv_heads = c.kv_heads;
-    m.head_size = c.head_size, m.rotary_size = c.rotary_size, m.intermediate = c.intermediate, m.vocab = c.vocab;
-    m.context = c.context, m.epsilon = c.epsilon, m.rope_scale = c.rope_scale;
-    m.weight_type = c.weight_type, m.embedding_type = c.embedding_type;
-    m.embedding = d->embedding, m.output_norm = d->output_norm;
-    m.attn_norm = d->attn_norm.data(), m.ffn_norm = d->ffn_norm.data();
-    m.w_qkv = d->w_qkv.data(), m.w_out = d->w_out.data(), m.w_up = d->w_up.data(), m.w_down = d->w_down.data();
-    m.key_cache = d->key_cache.data(), m.value_cache = d->value_cache.data(), m.freq = d->freq;
-    m.control = d->control, m.next_token = d->next_token;
-    m.act_hidden = d->hidden, m.act_after = d->after, m.act_qkv = d->qkv, m.act_attention = d->attention;
-    m.act_gate_up = d->gate_up, m.act_logits = d->logits;
-    unsigned long long *trace = nullptr;
-    uint64_t trace_entries = 0;
-    if (const char *e = std::getenv("SI_DECODE_TRACE"))
-        if (std::atoi(e) != 0) m.trace = &trace, m.trace_entries = &trace_entries;
-    const si_status st = k::decode_step_create(m, &d->step);
-    if (st == SI_OK && trace) d->slots["step_trace"] = {trace, trace_entries * 8};
-    if (st == SI_ERR_UNSUPPORTED) {
-        d->step = nullptr;
-        return SI_OK;
-    }
-    return st;
 }
 
 si_status slot_range(si_decoder *d, const char *name, uint64_t offset, uint64_t bytes, uint8_t **p) {

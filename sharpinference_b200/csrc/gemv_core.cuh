@@ -1,6 +1,5 @@
-// Device building blocks of the tensor-core quantised GEMV, shared by the
-// stand-alone GEMV kernels (gemv_mma.cu) and the persistent decode step
-// (decode_step.cu): the input source with its fused transforms, the MMA and
+// Device building blocks of the tensor-core quantised GEMV kernels
+// (gemv_mma.cu): the input source with its fused transforms, the MMA and
 // ldmatrix wrappers, and per weight format the x load (B fragments in
 // registers) and the 16-row partial product of one superblock column.
 #pragma once

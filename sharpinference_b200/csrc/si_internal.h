@@ -230,39 +230,4 @@ si_status tr_select_last(const float *in, const int32_t *control, float *out, in
                          void *stream);
 si_status tr_gather_rows(const float *table, int64_t rows, const int32_t *control, float *out, int64_t batch,
                          int64_t width, void *stream);
-// Persistent decode step (decode_step.cu): the decode program of one token
-// as one cooperative launch. decode_step_create returns SI_ERR_UNSUPPORTED
-// (nothing allocated) for a model it does not cover; the session then
-// records the per-instruction program.
-struct DecodeStepModel {
-    int layers, hidden, query_heads, kv_heads, head_size, rotary_size, intermediate, vocab;
-    int64_t context;
-    float epsilon, rope_scale;
-    uint32_t weight_type, embedding_type;
-    const void *embedding;
-    const float *output_norm;
-    const float *const *attn_norm;
-    const float *const *ffn_norm;
-    const void *const *w_qkv;
-    const void *const *w_out;
-    const void *const *w_up;
-    const void *const *w_down;
-    float *const *key_cache;
-    float *const *value_cache;
-    const float *freq;
-    int32_t *control;     // [token, position]
-    int32_t *next_token;
-    // activations (the session's slots): the two residual streams, qkv,
-    // attention output, gate_up, logits
-    float *act_hidden, *act_after, *act_qkv, *act_attention, *act_gate_up, *act_logits;
-    // Optional phase trace: when non-null, receives the device buffer of
-    // per-phase timestamps and its entry count.
-    unsigned long long **trace = nullptr;
-    uint64_t *trace_entries = nullptr;
-};
-struct DecodeStep;
-si_status decode_step_create(const DecodeStepModel &m, DecodeStep **out);
-si_status decode_step_launch(DecodeStep *st, DecodeFeed *feed, void *stream);
-void decode_step_destroy(DecodeStep *st);
-si_status take_error_decode_step(int device, uint32_t *code);
 }  // namespace si::kernels

@@ -58,13 +58,16 @@ __device__ __forceinline__ uint16_t half_bits_rne(float f) {
     return uint16_t(sign | h);
 }
 
-// One thread per 32-element block of the row range: F32, F16 or Q8_0.
+// One thread per 32-element block of the block [row_begin, + rows) x
+// [col_begin, + out_cols) of the [*, cols] matrix: F32, F16 or Q8_0; dst
+// rows are row_bytes apart and hold the out_cols columns.
 __global__ void synth_rows_kernel(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows, int64_t cols,
-                                  float sigma, uint8_t *dst, uint64_t row_bytes) {
-    const int64_t blocks_per_row = cols / 32, total = rows * blocks_per_row;
+                                  int64_t col_begin, int64_t out_cols, float sigma, uint8_t *dst, uint64_t row_bytes) {
+    const int64_t blocks_per_row = out_cols / 32, total = rows * blocks_per_row;
     for (int64_t b = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; b < total; b += int64_t(gridDim.x) * blockDim.x) {
         const int64_t r = b / blocks_per_row, c0 = (b - r * blocks_per_row) * 32;
-        const uint64_t e0 = uint64_t(row_begin + r) * uint64_t(cols) + uint64_t(c0);  // even: cols % 32 == 0
+        // even: cols, col_begin and c0 are multiples of 32
+        const uint64_t e0 = uint64_t(row_begin + r) * uint64_t(cols) + uint64_t(col_begin + c0);
         float v[32];
 #pragma unroll
         for (int i = 0; i < 16; ++i) normal_pair(seed, (e0 >> 1) + i, sigma, v[2 * i], v[2 * i + 1]);
@@ -99,21 +102,29 @@ __global__ void synth_rows_kernel(uint32_t type, uint64_t seed, int64_t row_begi
 
 }  // namespace
 
-extern "C" si_status si_synth_weight_rows_device(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows,
-                                                 int64_t cols, float sigma, void *dst, void *stream) {
-    if (!dst || rows <= 0 || cols <= 0 || row_begin < 0)
+extern "C" si_status si_synth_weight_block_device(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows,
+                                                  int64_t col_begin, int64_t col_count, int64_t cols, float sigma,
+                                                  void *dst, void *stream) {
+    if (!dst || rows <= 0 || cols <= 0 || row_begin < 0 || col_begin < 0 || col_count <= 0 ||
+        col_begin + col_count > cols)
         return si::fail(SI_ERR_INVALID_ARGUMENT, "invalid shape or null destination");
     if (type != SI_TYPE_F32 && type != SI_TYPE_F16 && type != SI_TYPE_Q8_0)
         return si::fail(SI_ERR_UNSUPPORTED, "device synthesis makes F32, F16 or Q8_0 weights");
-    if (cols % 32 != 0) return si::fail(SI_ERR_INVALID_ARGUMENT, "cols must be a multiple of 32");
+    if (cols % 32 != 0 || col_begin % 32 != 0 || col_count % 32 != 0)
+        return si::fail(SI_ERR_INVALID_ARGUMENT, "cols, col_begin and col_count must be multiples of 32");
     uint64_t rb = 0;
-    if (si_status st = si::byte_length(type, uint64_t(cols), &rb)) return st;
+    if (si_status st = si::byte_length(type, uint64_t(col_count), &rb)) return st;
     if (si_status st = si::device_range("destination", dst, rb * uint64_t(rows))) return st;
-    const int64_t total = rows * (cols / 32);
+    const int64_t total = rows * (col_count / 32);
     const int grid = int(std::min<int64_t>((total + 127) / 128, 148 * 32));
-    synth_rows_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(type, seed, row_begin, rows, cols, sigma,
-                                                                           static_cast<uint8_t *>(dst), rb);
+    synth_rows_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        type, seed, row_begin, rows, cols, col_begin, col_count, sigma, static_cast<uint8_t *>(dst), rb);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return si::fail(SI_ERR_CUDA, "synthesis launch failed: %s", cudaGetErrorString(e));
     return SI_OK;
+}
+
+extern "C" si_status si_synth_weight_rows_device(uint32_t type, uint64_t seed, int64_t row_begin, int64_t rows,
+                                                 int64_t cols, float sigma, void *dst, void *stream) {
+    return si_synth_weight_block_device(type, seed, row_begin, rows, 0, cols, cols, sigma, dst, stream);
 }

@@ -83,6 +83,7 @@ SIGNATURES = {
     "si_synth_weights": [_u32, _u64, _i64, _i64, C.c_float, _vp, _i32],
     "si_synth_weight_rows": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _i32],
     "si_synth_weight_rows_device": [_u32, _u64, _i64, _i64, _i64, C.c_float, _vp, _vp],
+    "si_synth_weight_block_device": [_u32, _u64, _i64, _i64, _i64, _i64, _i64, C.c_float, _vp, _vp],
     "si_matvec": [_u32, _vp, _u32, _vp, _u32, _vp, _i64, _i64, _u32, _vp],
     "si_batch_shared_matvec": [_u32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "si_gemv_default_plan": [_u32, _i64, _i64, _vp],
@@ -346,6 +347,11 @@ def synth_weight_rows_device(wtype: int, seed: int, row_begin: int, rows: int, c
                              stream=None) -> None:
     """si_synth_weight_rows_device: the seeded rows generated in device memory."""
     call("si_synth_weight_rows_device", wtype, seed, row_begin, rows, cols, sigma, dst, stream)
+
+
+def synth_weight_block_device(wtype: int, seed: int, row_begin: int, rows: int, col_begin: int, col_count: int,
+                              cols: int, sigma: float, dst: int, stream) -> None:
+    call("si_synth_weight_block_device", wtype, seed, row_begin, rows, col_begin, col_count, cols, sigma, dst, stream)
 
 
 def quantize(wtype: int, values):

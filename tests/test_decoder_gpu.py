@@ -114,28 +114,6 @@ def test_session_argument_errors():
     assert native.device_error_take(0) == 0
 
 
-@pytest.mark.parametrize("wtype", [native.Q4_K])
-def test_persistent_step_matches_oracle(monkeypatch, wtype):
-    """The opt-in persistent decode step (one cooperative launch per token)
-    gives the oracle's greedy tokens, through ForwardToken and the device loop."""
-    monkeypatch.setenv("SI_DECODE_STEP", "1")
-    cfg = tiny_decoder_config(wtype)
-    weights = tiny_decoder_weights(cfg, seed=21)
-    prompt = np.random.default_rng(21).integers(0, cfg["vocab"], 12)
-    ref = oracle.Decoder(cfg, weights)
-    want = ref.generate(prompt, 20)
-    with native.Decoder(cfg) as dec:
-        _load(dec, weights)
-        got, tok = [], None
-        for i in range(12):
-            tok = dec.forward_token(int(prompt[i]))
-            got.append(tok)
-        assert got == want[:12]
-        rest = dec.generate([got[-1]], 19)
-        assert got + list(rest) == want
-    assert native.device_error_take(0) == 0
-
-
 def test_session_from_gguf_file(tmp_path):
     """A model saved as a phi3 GGUF file, opened by the library's reader and
     uploaded byte-for-byte into the session, decodes the oracle's tokens."""
