@@ -337,6 +337,7 @@ si_status si_device_error_take(int device, uint32_t *code) {
     if (si_status st = kernels::take_error_gemv(device, code)) return st;
     if (si_status st = kernels::take_error_gemv_mma(device, code)) return st;
     if (si_status st = kernels::take_error_gemm_skinny(device, code)) return st;
+    if (si_status st = kernels::take_error_gemm_fewrow(device, code)) return st;
     return kernels::take_error_gemm(device, code);
 }
 

@@ -18,6 +18,9 @@ enum : uint32_t {
     kErrMmaBarrierTimeout = 4u,
     kErrEpilogueTimeout = 8u,
     kErrPeerTimeout = 16u,  // a row-sharded GEMV's rank never published its rows
+    // a Q8_0 block scale above 512 or a Q4_K minimum scale above 1024 reached the
+    // few-row GEMM's FP16 operands (gemm_fewrow.cu): those rows are not exact
+    kErrRange = 32u,
 };
 static __device__ uint32_t g_error_word;
 

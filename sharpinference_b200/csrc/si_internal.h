@@ -97,6 +97,13 @@ bool gemm_skinny_supported(uint32_t wtype, const void *w, const float *x, int64_
 si_status gemm_skinny(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y, int64_t m,
                       int64_t n, int64_t k, void *stream);
 si_status take_error_gemm_skinny(int device, uint32_t *code);
+// Few-row GEMM with the dequantised weights in tensor memory (gemm_fewrow.cu):
+// Q4_K / Q8_0, 1..32 input rows, k a multiple of 256, 16-byte aligned weight
+// rows and X; rows t >= control[1] are not written.
+bool gemm_fewrow_supported(uint32_t wtype, const void *w, const float *x, int64_t m, int64_t n, int64_t k);
+si_status gemm_fewrow(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y, int64_t m,
+                      int64_t n, int64_t k, void *stream);
+si_status take_error_gemm_fewrow(int device, uint32_t *code);
 si_status take_error_gemv(int device, uint32_t *code);
 si_status take_error_gemm(int device, uint32_t *code);
 si_status take_error_gemv_mma(int device, uint32_t *code);

@@ -172,10 +172,14 @@ using namespace si::dev;
 si_status shared_weight_matvec(uint32_t wtype, const void *w, const float *x, const int32_t *control, float *y,
                                int64_t m, int64_t n, int64_t k, void *stream) {
     auto st = static_cast<cudaStream_t>(stream);
-    // Two or more rows: the few-row tcgen05 GEMM (weights read once per 16,
-    // 32 or 64 rows, no workspace) -- except Q4_K up to 16 rows, where the
-    // batched integer GEMV below measured faster (lm_head 3072 -> 200064 at
-    // 16 rows: 255 vs 434 us; at 32 rows the GEMM wins, 468 vs 506 us).
+    // 2..32 rows of Q4_K / Q8_0: the few-row GEMM with the dequantised
+    // weights in tensor memory (no split of W; weights read once per call).
+    if (m >= 2 && gemm_fewrow_supported(wtype, w, x, m, n, k))
+        return gemm_fewrow(wtype, w, x, control, y, m, n, k, stream);
+    // Otherwise two or more rows: the few-row tcgen05 GEMM (weights read once
+    // per 16, 32 or 64 rows, no workspace) -- except Q4_K up to 16 rows, where
+    // the batched integer GEMV below measured faster (lm_head 3072 -> 200064
+    // at 16 rows: 255 vs 434 us; at 32 rows the GEMM wins, 468 vs 506 us).
     const bool q4k_small = wtype == SI_TYPE_Q4_K && m <= 16;
     if (m >= 2 && !q4k_small && gemm_skinny_supported(wtype, w, x, m, n, k))
         return gemm_skinny(wtype, w, x, control, y, m, n, k, stream);
