@@ -76,10 +76,11 @@ struct FwCfg {
     // 128-byte swizzle. One MMA with N = 2 BN covers both.
     static constexpr int kN = 2 * BN;
     static constexpr uint32_t kBHalf = uint32_t(kN) * 256u;
-    static constexpr int kBSlots = 4;                         // two stages
+    static constexpr int kBStages = 3;                        // X operand ring depth in stages
+    static constexpr int kBSlots = 2 * kBStages;
     // Q4_K: the stage's 32-column sums (rows as above, columns 0..15 of a 128-byte row)
     static constexpr uint32_t kBMin = kQ4K ? uint32_t(kN) * 128u : 0u;
-    static constexpr int kBMinSlots = kQ4K ? 2 : 0;
+    static constexpr int kBMinSlots = kQ4K ? kBStages : 0;
     static constexpr int kScaleSlots = 8;                     // per-(input row, stage) 1 / scale
     static constexpr int kRedStride = BN + 1;
     static constexpr uint32_t kRed = kFwRows * kRedStride * 4u;
@@ -140,8 +141,20 @@ __device__ __forceinline__ float fw_ld_cluster(uint32_t addr) {
 // Bounded mbarrier wait. The first wait of the CTA that runs out raises the
 // CTA's abort flag; every later wait sees it and gives up at once, so a
 // broken pipeline costs one time limit, not one per stage.
+// Non-blocking phase test (no suspend): the common case of a phase that has
+// already completed costs no sleep / wake-up.
+__device__ __forceinline__ bool fw_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ bool fw_wait(uint64_t *bar, uint32_t parity, uint32_t err, volatile uint32_t *abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 64; ++i)
+        if (fw_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0; i < kMaxPolls; ++i) {
         if (*abort) return false;
@@ -372,6 +385,7 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
     using C = FwCfg<FMT, BN>;
     constexpr int kR = C::kRaw, kA = C::kASlots, kNB = C::kBSlots, kNAcc = C::kAccSlots, kHalfBN = BN / 2;
     constexpr int kNS = C::kScaleSlots, kLag = C::kLag, kSD = 8;
+    constexpr bool kEarly = BN == 16;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -472,7 +486,7 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
                         if constexpr (C::kQ4K) {
                             if (h == 1) {  // the stage's mins term, into the same accumulator
                                 const uint32_t amin = tmem + uint32_t(C::kMinCol0) + (g % C::kAMinSlots) * 8;
-                                mma_ts(dacc, amin, smem_desc(smem_u32(bmin + (g & 1) * C::kBMin)), C::kIdesc, 1);
+                                mma_ts(dacc, amin, smem_desc(smem_u32(bmin + (g % C::kBStages) * C::kBMin)), C::kIdesc, 1);
                             }
                         }
                     }
@@ -491,19 +505,21 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
         const uint32_t tl = tmem + (uint32_t(quarter * 32) << 16);
         int valid = -1;
         uint32_t g = 0;
-        // y += c * (1 / scale) * (acc_hi + acc_lo) of stage gg
-        auto readback = [&](uint32_t gg, float c, float (&y)[kHalfBN]) {
-            const uint32_t acs = gg % kNAcc;
+        // read-back of stage gg in two parts: start the loads (issued before the next stage's
+        // dequantisation so that their latency overlaps it), then y += c / scale * (acc_hi + acc_lo)
+        uint32_t vh[kHalfBN], vl[kHalfBN];
+        auto readback_start = [&](uint32_t gg) {
             fw_wait(&stage_done[gg % kSD], (gg / kSD) & 1, kErrMmaBarrierTimeout, abort);
             fw_wait(&scale_full[gg % kNS], (gg / kNS) & 1, kErrFullBarrierTimeout, abort);
             tc_fence_after();
-            uint32_t vh[kHalfBN], vl[kHalfBN];
-            const uint32_t col = tl + uint32_t(C::kAccCol0) + acs * C::kN + uint32_t(h * kHalfBN);
+            const uint32_t col = tl + uint32_t(C::kAccCol0) + (gg % kNAcc) * C::kN + uint32_t(h * kHalfBN);
             tmem_ld_nw<kHalfBN>(col, vh);
             tmem_ld_nw<kHalfBN>(col + BN, vl);
+        };
+        auto readback_finish = [&](uint32_t gg, float c, float (&y)[kHalfBN]) {
             tc_wait_ld();
             tc_fence_before();
-            mbar_arrive(&acc_empty[acs]);
+            mbar_arrive(&acc_empty[gg % kNAcc]);
             const float *inv = scale_inv + (gg % kNS) * BN + h * kHalfBN;
 #pragma unroll
             for (int j = 0; j < kHalfBN; ++j)
@@ -516,6 +532,9 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
             for (int j = 0; j < kHalfBN; ++j) y[j] = 0.0f;
             float c1 = 1.0f, c2 = 1.0f;  // multipliers of the stages one and two behind
             for (int s = 0; s < nst; ++s, ++g) {
+                // 16 input rows: the read-back loads go out before the dequantisation; 32 rows
+                // (18 warps, 96 registers a thread) keep them after it
+                if (kEarly && s >= kLag) readback_start(g - kLag);
                 const uint32_t rs = g % kR;
                 fw_wait(&raw_full[rs], (g / kR) & 1, kErrFullBarrierTimeout, abort);
                 const uint8_t *src = raw + rs * C::kRawBytes + row * C::kSS;
@@ -535,12 +554,21 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
                 mbar_arrive(&a_full[as]);
                 fence_proxy_async();  // reads of the raw slot before the TMA refills it
                 mbar_arrive(&raw_empty[rs]);
-                if (s >= kLag) readback(g - kLag, kLag == 2 ? c2 : c1, y);
+                if (s >= kLag) {
+                    if (!kEarly) readback_start(g - kLag);
+                    readback_finish(g - kLag, kLag == 2 ? c2 : c1, y);
+                }
                 c2 = c1;
                 c1 = cur;
             }
-            if (kLag == 2 && nst >= 2) readback(g - 2, c2, y);
-            if (nst >= 1) readback(g - 1, c1, y);
+            if (kLag == 2 && nst >= 2) {
+                readback_start(g - 2);
+                readback_finish(g - 2, c2, y);
+            }
+            if (nst >= 1) {
+                readback_start(g - 1);
+                readback_finish(g - 1, c1, y);
+            }
             if (valid < 0) {
                 pdl_wait();  // control comes from the stream; the previous kernel may still read Y
                 valid = p.m;
@@ -622,8 +650,8 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
                 for (int i = 0; i < 8; ++i) cur[i].x *= sc, cur[i].y *= sc, cur[i].z *= sc, cur[i].w *= sc;
             }
             const uint32_t u0 = 2 * xg;
-            if (xg >= 2) {  // stage xg - 2, the last user of both slots and of the sums slot, completed
-                const uint32_t prev = xg - 2;
+            if (xg >= uint32_t(C::kBStages)) {  // the last user of both slots and of the sums slot completed
+                const uint32_t prev = xg - C::kBStages;
                 fw_wait(&stage_done[prev % kSD], (prev / kSD) & 1, kErrEmptyBarrierTimeout, abort);
             }
             const uint32_t hs = uint32_t(u >> 2);
@@ -654,7 +682,7 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
                 for (int i = 0; i < 32; ++i) sum += v[i];
                 const __half shi = __float2half_rn(sum);
                 const __half slo = __float2half_rn(sum - __half2float(shi));
-                uint8_t *mb = bmin + (xg & 1) * C::kBMin;
+                uint8_t *mb = bmin + (xg % C::kBStages) * C::kBMin;
                 uint8_t *mh = mb + uint32_t(r >> 3) * 1024 + sw * 128;
                 uint8_t *ml = mb + uint32_t((BN + r) >> 3) * 1024 + sw * 128;
                 *reinterpret_cast<__half *>(mh + ((0u ^ sw) << 4) + 2 * u) = shi;
