@@ -23,6 +23,7 @@ restatement in oracle/, all host threads) on the same workload.
 from __future__ import annotations
 
 import argparse
+import re
 import datetime
 import json
 import os
@@ -680,7 +681,7 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
                 rows, cols = shapes[name]
                 ptr, nbytes = dec.slot(name)
                 seed = 11 * 1_000_003 + i
-                base = name.rsplit("_", 1)[0]
+                base = re.sub(r"_\d+$", "", name)  # slot name without its layer index
                 if not tp or base == "token_embedding":
                     native.synth_weight_rows_device(q8, seed, 0, rows, cols, 0.02, ptr, dec.stream)
                     continue
