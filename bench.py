@@ -670,8 +670,7 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
            f"{world} GPUs, tensor parallel: qkv / gate_up by rows of the rank's heads and intermediate slice, "
            "out / down by columns with partial sums exchanged inside the GEMV over NVLink (two exchanges per "
            "layer), heads-local attention, vocabulary rows split"}
-    q8, H, hs, F = native.Q8_0, cfg["hidden"], cfg["head_size"], cfg["intermediate"]
-    KV = cfg["kv_heads"] * hs
+    q8 = native.Q8_0
     try:
         with native.Decoder(cfg, local, group, tensor_parallel=tp) as dec:
             part = native.tp_partition(cfg, world, rank) if tp else None
@@ -681,29 +680,17 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
                 rows, cols = shapes[name]
                 ptr, nbytes = dec.slot(name)
                 seed = 11 * 1_000_003 + i
-                base = re.sub(r"_\d+$", "", name)  # slot name without its layer index
-                if not tp or base == "token_embedding":
+                lay = phi4.tp_slot_layout(cfg, part, name) if tp else ("whole",)
+                if lay[0] == "whole":
                     native.synth_weight_rows_device(q8, seed, 0, rows, cols, 0.02, ptr, dec.stream)
-                    continue
-                rb = native.row_bytes(q8, cols)
-                if base in ("qkv_weight", "ffn_up_weight"):
-                    if base == "qkv_weight":
-                        q0, q1 = part.query_head_begin * hs, (part.query_head_begin + part.query_heads) * hs
-                        k0, k1 = part.kv_head_begin * hs, (part.kv_head_begin + part.kv_heads) * hs
-                        ranges = [(q0, q1), (H + k0, H + k1), (H + KV + k0, H + KV + k1)]
-                    else:
-                        f0, f1 = part.ffn_begin, part.ffn_begin + part.ffn_rows
-                        ranges = [(f0, f1), (F + f0, F + f1)]
+                elif lay[0] == "rows":  # qkv rows of the rank's heads, gate / up rows of its intermediate slice
                     off = 0
-                    for r0, r1 in ranges:
+                    for r0, r1 in lay[1]:
                         native.synth_weight_rows_device(q8, seed, r0, r1 - r0, cols, 0.02, ptr + off, dec.stream)
-                        off += (r1 - r0) * rb
+                        off += (r1 - r0) * native.row_bytes(q8, cols)
                     assert off == nbytes, name
                 else:  # column slices: attn_output (query-head columns), ffn_down (intermediate columns)
-                    if base == "attn_output_weight":
-                        c0, cn = part.query_head_begin * hs, part.query_heads * hs
-                    else:
-                        c0, cn = part.ffn_begin, part.ffn_rows
+                    c0, cn = lay[1], lay[2] - lay[1]
                     assert nbytes == rows * native.row_bytes(q8, cn), name
                     native.synth_weight_block_device(q8, seed, 0, rows, c0, cn, cols, 0.02, ptr, dec.stream)
             prompt = phi4.random_prompt(11, prompt_len, cfg["vocab"])

@@ -10,6 +10,8 @@ host memory stays at one slot.
 """
 from __future__ import annotations
 
+import re
+
 import numpy as np
 
 from . import native
@@ -178,28 +180,44 @@ def _row_slice(blob: np.ndarray, wtype: int, cols: int, ranges) -> np.ndarray:
     return np.ascontiguousarray(np.concatenate([m[a:b] for a, b in ranges])).reshape(-1)
 
 
-def tp_slice_weights(cfg: dict, weights: dict, part) -> dict:
-    """One rank's slots of a tensor-parallel session (si_tp_partition_plan),
-    cut from the whole model's GGUF bytes: qkv rows of the rank's heads, the
-    out projection's columns of its query heads, its gate / up rows and down
-    columns of the intermediate; token_embedding and the norms whole."""
+def tp_slot_layout(cfg: dict, part, name: str):
+    """How one rank's slot of a tensor-parallel session (si_tp_partition_plan)
+    is cut from the whole tensor: ("rows", [(r0, r1), ...]) for the qkv rows
+    of the rank's heads (query, then key, then value rows) and its gate / up
+    rows of the intermediate; ("cols", c0, c1) for the out projection's
+    columns of its query heads and down's columns of its intermediate slice;
+    ("whole",) for token_embedding (gather-row reads every row; the
+    vocabulary projection uses the rank's rows of it in place) and the norms."""
+    base = re.sub(r"_\d+$", "", name)  # slot name without its layer index
     h, f, hs = cfg["hidden"], cfg["intermediate"], cfg["head_size"]
     kv = cfg["kv_heads"] * hs
-    wt = cfg["weight_type"]
     q0, q1 = part.query_head_begin * hs, (part.query_head_begin + part.query_heads) * hs
     k0, k1 = part.kv_head_begin * hs, (part.kv_head_begin + part.kv_heads) * hs
     f0, f1 = part.ffn_begin, part.ffn_begin + part.ffn_rows
+    if base == "qkv_weight":
+        return ("rows", [(q0, q1), (h + k0, h + k1), (h + kv + k0, h + kv + k1)])
+    if base == "ffn_up_weight":
+        return ("rows", [(f0, f1), (f + f0, f + f1)])
+    if base == "attn_output_weight":
+        return ("cols", q0, q1)
+    if base == "ffn_down_weight":
+        return ("cols", f0, f1)
+    return ("whole",)
+
+
+def tp_slice_weights(cfg: dict, weights: dict, part) -> dict:
+    """One rank's slots of a tensor-parallel session (si_tp_partition_plan),
+    cut from the whole model's GGUF bytes as tp_slot_layout says."""
+    shapes = linear_shapes(cfg)
+    wt = cfg["weight_type"]
     out = {}
     for name, arr in weights.items():
-        base = name.rsplit("_", 1)[0]
-        if base == "qkv_weight":
-            out[name] = _row_slice(arr, wt, h, [(q0, q1), (h + k0, h + k1), (h + kv + k0, h + kv + k1)])
-        elif base == "attn_output_weight":
-            out[name] = _col_slice(arr, wt, h, h, q0, q1)
-        elif base == "ffn_up_weight":
-            out[name] = _row_slice(arr, wt, h, [(f0, f1), (f + f0, f + f1)])
-        elif base == "ffn_down_weight":
-            out[name] = _col_slice(arr, wt, h, f, f0, f1)
+        lay = tp_slot_layout(cfg, part, name)
+        if lay[0] == "rows":
+            out[name] = _row_slice(arr, wt, shapes[name][1], lay[1])
+        elif lay[0] == "cols":
+            rows, cols = shapes[name]
+            out[name] = _col_slice(arr, wt, rows, cols, lay[1], lay[2])
         else:
             out[name] = arr
     return out
