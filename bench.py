@@ -640,46 +640,62 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
     """Config 5 at batch 1: the Phi-4-14B-shaped Q8_0 decoder (40 layers,
     hidden 5120, 40/10 heads of 128, FFN 17920, vocab 100352, seed 11),
     a 1024-token random prompt, then 128 greedy steps timed on the device
-    (max over ranks). One GPU: the whole session. N GPUs: the
-    tensor-parallel session (Megatron pairing: qkv and gate_up by rows of
-    the rank's heads and intermediate slice, out and down by columns with
-    their partial vectors exchanged through the NVLink peer arenas inside the
-    GEMV, heads-local attention, the vocabulary projection by rows). Weights
-    are generated on the device (slot ordinal i -> seed 11 * 1000003 + i),
-    each rank only its slices."""
+    (max over ranks). One GPU: the whole session. N GPUs: both multi-GPU
+    sessions of the library, each measured, the faster reported:
+      * tensor parallel (Megatron pairing: qkv and gate_up by rows of the
+        rank's heads and intermediate slice, out and down by columns with
+        their partial vectors exchanged through the NVLink peer arenas inside
+        the GEMV, heads-local attention, the vocabulary projection by rows);
+      * row sharded (the projections whose weights reach shard_min_bytes
+        split by rows, their outputs all-gathered inside the GEMV; the rest
+        replicated).
+    Weights are generated on the device (slot ordinal i -> seed
+    11 * 1000003 + i), each rank only its part."""
     from sharpinference_b200 import phi4
     cfg = dict(phi4.PHI4_14B)
     prompt_len, steps = 1024, 128
     cfg["context"] = prompt_len + steps + 1
+    q8 = native.Q8_0
+    shapes = phi4.linear_shapes(cfg)
     group, arena, addrs = None, None, []
-    tp = world > 1
-    if tp:
-        import torch.distributed as dist
-        ab = (native.tp_arena_bytes(cfg, world) + 255) // 256 * 256
-        arena = ctx.buffer(ab)
+    if world > 1:
         import numpy as np
+        import torch.distributed as dist
+        ab = (max(native.tp_arena_bytes(cfg, world), native.decoder_arena_bytes(cfg)) + 255) // 256 * 256
+        arena = ctx.buffer(ab)
         arena.upload(np.zeros(ab, np.uint8))
         handles = [None] * world
         dist.all_gather_object(handles, native.ipc_export(arena.device_pointer))
         addrs = [arena.device_pointer if q == rank else native.ipc_open(local, handles[q]) for q in range(world)]
         group = native.PeerGroup(local, world, rank, addrs, ab)
-    shapes = phi4.linear_shapes(cfg)
-    out = {"workload": "config5 batch 1: Phi-4-14B-shaped Q8_0 decoder (40 layers, hidden 5120, 40/10 heads of "
-                       "128, FFN 17920, vocab 100352), N(0,0.02) seed 11, 1024-token random prompt, 128 greedy steps",
-           "parallelism": "single GPU" if world == 1 else
-           f"{world} GPUs, tensor parallel: qkv / gate_up by rows of the rank's heads and intermediate slice, "
-           "out / down by columns with partial sums exchanged inside the GEMV over NVLink (two exchanges per "
-           "layer), heads-local attention, vocabulary rows split"}
-    q8 = native.Q8_0
-    try:
-        with native.Decoder(cfg, local, group, tensor_parallel=tp) as dec:
+    # Split a projection only when its exchange (~7 us) costs less than the
+    # weight time it saves: (1 - 1/N) * bytes / HBM > 8 us.
+    shard_min = int(52e6 * world / (world - 1)) if world > 1 else 0
+
+    def run(kind: str) -> dict:
+        tp = kind == "tensor_parallel"
+        kw = {"tensor_parallel": True} if tp else ({"shard_min_bytes": shard_min} if kind == "row_sharded" else {})
+        res = {}
+        with native.Decoder(cfg, local, group if world > 1 else None, **kw) as dec:
             part = native.tp_partition(cfg, world, rank) if tp else None
+            split, rep_bytes = [], 0
             for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
                 if name not in shapes:
                     continue
                 rows, cols = shapes[name]
                 ptr, nbytes = dec.slot(name)
                 seed = 11 * 1_000_003 + i
+                if kind == "row_sharded":
+                    begin, count = 0, rows
+                    if nbytes < rows * native.row_bytes(q8, cols):  # this slot holds the rank's rows
+                        begin, count, _ = native.rowshard_plan(rows, world, rank)
+                        if name.endswith("_0"):
+                            split.append(name[:-2])
+                    else:
+                        rep_bytes += nbytes
+                    assert nbytes == count * native.row_bytes(q8, cols), name
+                    native.synth_weight_rows_device(q8, seed, begin, count, cols, 0.02, ptr, dec.stream)
+                    continue
                 lay = phi4.tp_slot_layout(cfg, part, name) if tp else ("whole",)
                 if lay[0] == "whole":
                     native.synth_weight_rows_device(q8, seed, 0, rows, cols, 0.02, ptr, dec.stream)
@@ -717,19 +733,23 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
             kv_row = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_size"] * 4
             kv_bytes = sum(kv_row * (p + 1) for p in range(prompt_len, prompt_len + steps)) / steps
             tok_s = steps / (decode_ms * 1e-3)
-            # every weight byte and every KV row is read by one rank per token
-            bytes_token = wbytes + kv_bytes
+            if kind == "row_sharded":  # split weights once, replicated ones and the KV cache on every rank
+                bytes_token = wbytes + (world - 1) * rep_bytes + world * kv_bytes
+                res["split_projections"] = split + ["vocabulary (token_embedding rows)"]
+                res["shard_min_bytes"] = shard_min
+            else:  # every weight byte and every KV row read by one rank
+                bytes_token = wbytes + kv_bytes
             if tp:
-                out["partition_rank0"] = {n: getattr(native.tp_partition(cfg, world, 0), n)
+                res["partition_rank0"] = {n: getattr(native.tp_partition(cfg, world, 0), n)
                                           for n, _ in native.TpPartition._fields_}
-            out.update({
+            res.update({
                 "decode_tok_s": round(tok_s, 1), "decode_ms_per_token": round(decode_ms / steps, 4),
                 "e2e_decode_tok_s": round(steps / wall, 1),
                 "prompt_ms": round(prefill_ms, 1),
                 "prompt_path": "batched prefill" if world == 1 else "the decode program per prompt token",
                 "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_token),
-                             "bytes": "Q8_0 weight bytes per token (each read by one rank) + the KV-cache rows "
-                                      "attended (each by one rank)",
+                             "bytes": "Q8_0 weight bytes per token over all ranks + the KV-cache rows attended "
+                                      "(replicated weights and caches counted once per rank)",
                              "achieved_aggregate": round(bytes_token * tok_s / 1e9, 1),
                              "peak_aggregate": round(peak * world, 1), "unit": "GB/s",
                              "frac": round(bytes_token * tok_s / 1e9 / (peak * world), 4)},
@@ -737,6 +757,27 @@ def decode14b_block(native, torch, ctx, world: int, rank: int, local: int, peak:
                 "first_tokens": [int(t) for t in toks[:8]],
                 "device_error_word": native.device_error_take(local),
             })
+        return res
+
+    out = {"workload": "config5 batch 1: Phi-4-14B-shaped Q8_0 decoder (40 layers, hidden 5120, 40/10 heads of "
+                       "128, FFN 17920, vocab 100352), N(0,0.02) seed 11, 1024-token random prompt, 128 greedy steps"}
+    try:
+        if world == 1:
+            out["parallelism"] = "single GPU"
+            out.update(run("single"))
+        else:
+            sessions = {kind: run(kind) for kind in ("tensor_parallel", "row_sharded")}
+            best = max(sessions, key=lambda k: sessions[k]["decode_tok_s"])
+            out["parallelism"] = (
+                f"{world} GPUs, the faster of two sessions: {best} "
+                + ("(qkv / gate_up by rows of the rank's heads and intermediate slice, out / down by columns with "
+                   "partial sums exchanged inside the GEMV over NVLink, heads-local attention, vocabulary rows "
+                   "split)" if best == "tensor_parallel" else
+                   "(the large projections row-sharded with their outputs all-gathered inside the GEMV over "
+                   "NVLink; the rest replicated)"))
+            out.update(sessions[best])
+            out["sessions"] = {k: {"decode_tok_s": v["decode_tok_s"], "decode_ms_per_token": v["decode_ms_per_token"],
+                                   "first_tokens": v["first_tokens"]} for k, v in sessions.items()}
     finally:
         if group is not None:
             barrier()  # no rank unmaps an arena another rank may still store into
