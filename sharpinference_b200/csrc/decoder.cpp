@@ -75,6 +75,9 @@ struct si_decoder {
     float *res_a = nullptr, *res_b = nullptr;
     float *o_parts = nullptr, *down_parts = nullptr;  // [nranks][hidden] in this rank's arena
     k::PeerGather pg_out{}, pg_down{}, pg_vocab{};
+    // this rank's counts / epochs of the publish-only out (0) and down (1) exchanges
+    const unsigned long long *o_counts = nullptr, *d_counts = nullptr;
+    const uint32_t *o_epoch = nullptr, *d_epoch = nullptr;
     // Multi-stream session (si_decoder_create_streams): `streams` rows per
     // step, stream b's caches at rows b * context of each layer's cache;
     // per-stream tokens / positions / greedy-loop state on the device.
@@ -775,11 +778,20 @@ si_status create(int device, const si_decoder_config *c, si_peer_group *group, i
 // into every arena) after the final norm, then argmax on every rank. Two
 // exchanges per layer; every rank sums the partials in the same order, so
 // every rank holds bit-identical residual streams and picks the same token.
-// Region reuse: a rank enters the down exchange of layer l only after every
-// rank finished its out exchange of layer l, hence its gate_up of layer l
-// (the reader of the out partials) completes before any rank's out exchange
-// of layer l + 1 can start overwriting them; likewise for the down partials
-// and the next layer's qkv GEMV.
+// The out and down exchanges are publish-only: the producing GEMV stores its
+// partial rows into every arena, fences, and adds its row count to every
+// rank's count of that exchange; it does not wait for the peers. The
+// consuming GEMV (gate_up after out; the next qkv, or the vocabulary GEMV,
+// after down) waits for every rank's count after its weight prefetch.
+// Region reuse: rank A writes the out partials of layer l + 1 into rank B's
+// arena only after A's qkv of layer l + 1 saw B's down count of layer l,
+// which B publishes from its down GEMV of layer l; that GEMV stores after
+// its dependency wait, i.e. after B's gate_up of layer l — the reader of the
+// out partials of layer l — completed. Likewise A writes the down partials
+// of layer l + 1 only after A's gate_up of layer l + 1 saw B's out count of
+// layer l + 1, published after B's qkv of layer l + 1, the reader of the
+// down partials of layer l, completed. The vocabulary rows keep the full
+// handshake, so every token ends with all ranks in step.
 struct TpLayout {
     uint64_t o_parts, down_parts, logits, data_bytes;
 };
@@ -848,7 +860,8 @@ si_status record_step_tp(si_decoder *d, k::DecodeFeed *feed) {
                         (long long)rows, (long long)cols);
         return st;
     };
-    // the GEMV input: rms-norm of (x + parts[0] + ... + parts[nparts-1]), that sum stored to h_out
+    // the GEMV input: rms-norm of (x + parts[0] + ... + parts[nparts-1]), that sum stored to h_out;
+    // the parts of the publish-only exchanges are read once every rank's count has arrived
     auto norm_of = [&](const float *parts, int nparts, const float *norm, float *h_out) {
         k::GemvFusion f;
         f.in_mode = 3;
@@ -858,6 +871,12 @@ si_status record_step_tp(si_decoder *d, k::DecodeFeed *feed) {
         f.nparts = nparts;
         f.part_stride = H;
         f.h_out = h_out;
+        if (nparts > 0) {
+            f.wait_counts = parts == d->o_parts ? d->o_counts : d->d_counts;
+            f.wait_epoch = parts == d->o_parts ? d->o_epoch : d->d_epoch;
+            f.wait_ranks = nparts;
+            f.wait_rows = H;
+        }
         return f;
     };
     if (si_status st = k::tr_gather_row(c.embedding_type, d->embedding, c.vocab, H, d->control, d->res_b, s)) return st;
@@ -970,8 +989,12 @@ si_status create_tp(int device, const si_decoder_config *c, si_peer_group *group
     d->down_parts = reinterpret_cast<float *>(d->arena + lay.down_parts);
     d->logits = reinterpret_cast<float *>(d->arena + lay.logits);
     d->slots["logits"] = {d->logits, uint64_t(c->vocab) * 4};
-    if (si_status st = si::peer_gather_desc(group, lay.o_parts, int64_t(rank) * H, H, &d->pg_out)) return cleanup(st);
-    if (si_status st = si::peer_gather_desc(group, lay.down_parts, int64_t(rank) * H, H, &d->pg_down))
+    // out / down: publish-only exchanges (the next GEMV waits for them); the vocabulary rows: full handshake
+    if (si_status st = si::peer_gather_desc_nowait(group, lay.o_parts, int64_t(rank) * H, H, 0, &d->pg_out))
+        return cleanup(st);
+    if (si_status st = si::peer_counts(group, 0, &d->o_counts, &d->o_epoch)) return cleanup(st);
+    if (si_status st = si::peer_counts(group, 1, &d->d_counts, &d->d_epoch)) return cleanup(st);
+    if (si_status st = si::peer_gather_desc_nowait(group, lay.down_parts, int64_t(rank) * H, H, 1, &d->pg_down))
         return cleanup(st);
     if (si_status st = si::peer_gather_desc(group, lay.logits, P.vocab_begin, P.vocab_rows, &d->pg_vocab))
         return cleanup(st);

@@ -90,6 +90,11 @@ struct MmaParams {
     int nparts;
     int64_t part_stride;
     float *h_out;         // non-null: CTA 0 stores x + the partials (the residual stream) here
+    // consumer of a publish-only exchange (see consumer_wait)
+    const unsigned long long *wait_counts;
+    const uint32_t *wait_epoch;
+    int wait_ranks;
+    int64_t wait_rows;
 };
 
 // --- thread-block cluster helpers (distributed shared memory) ---
@@ -175,17 +180,81 @@ __device__ __forceinline__ void peer_handshake(const MmaParams &p) {
     *reinterpret_cast<volatile uint32_t *>(g.epoch) = e;
 }
 
+// End of a publish-only exchange GEMV (tensor-parallel partial sums): no
+// wait for the peers here. The storing warp fenced its rows at system scope
+// before the CTA barrier; this thread fences once more (cumulative over them)
+// and adds the CTA's stored rows to its slot of every rank's count of this
+// kind; the launch's last CTA (ticket) advances this rank's epoch of the
+// kind, which the consumer GEMV on this rank reads after the dependency wait.
+__device__ __forceinline__ void peer_publish(const MmaParams &p, uint32_t rows) {
+    const kernels::PeerGather &g = p.peer;
+    __threadfence_system();
+    if (rows)
+        for (int q = 0; q < g.nranks; ++q)
+            asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(g.counts[q] + g.rank),
+                         "l"(static_cast<unsigned long long>(rows))
+                         : "memory");
+    const uint32_t t = atomicAdd(g.ticket, 1u);
+    if (t != gridDim.x - 1) return;
+    *g.ticket = 0u;
+    *reinterpret_cast<volatile uint32_t *>(g.kind_epoch) = *reinterpret_cast<volatile uint32_t *>(g.kind_epoch) + 1u;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *addr) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// Consumer of a publish-only exchange: every warp that reads x / the parts
+// waits (lane 0, bounded) until each rank's count of the exchange reached
+// epoch * rows, i.e. every rank has stored and fenced all its rows.
+__device__ __forceinline__ void consumer_wait(const MmaParams &p, int lane) {
+    if (!p.wait_counts) return;
+    if (lane == 0) {
+        const unsigned long long target =
+            static_cast<unsigned long long>(*reinterpret_cast<const volatile uint32_t *>(p.wait_epoch)) *
+            static_cast<unsigned long long>(p.wait_rows);
+        const uint64_t t0 = globaltimer_ns();
+        for (int q = 0; q < p.wait_ranks; ++q) {
+            uint32_t polls = 0;
+            while (ld_acquire_sys_u64(p.wait_counts + q) < target) {
+                if (++polls > kMaxPolls || globaltimer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(&g_error_word, kErrPeerTimeout);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+    __syncwarp();
+}
+
 // 1 / rms of the input vector (transformer.rms-norm, GpuTransformerInstructionCollection.cs:323-368):
 // sum of squares over all K elements by one warp (lane-strided partial sums,
 // fixed shuffle tree), then 1 / sqrt(sum / K + eps). Called by the reducer
 // warp after the dependency wait; the rows it stores are scaled by it.
+// The loads of 8 strides are issued before any of them is used, so the warp
+// pays one L2 round trip per 1024 elements instead of one per 128; the sums
+// keep their element order.
+constexpr int kRmsBatch = 8;
+__device__ __forceinline__ float sq4(float s, float4 v) {
+    return __fadd_rn(s, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                                  __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+}
 __device__ __forceinline__ float inv_rms_warp(const float *x, int64_t k, float eps, int lane) {
     float s = 0.0f;
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && k % 128 == 0) {
-        for (int64_t i = int64_t(lane) * 4; i < k; i += 128) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + i));
-            s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                                       __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+        for (int64_t i0 = int64_t(lane) * 4; i0 < k; i0 += 128 * kRmsBatch) {
+            float4 v[kRmsBatch];
+#pragma unroll
+            for (int j = 0; j < kRmsBatch; ++j) {
+                const int64_t i = i0 + 128 * j;
+                v[j] = i < k ? __ldg(reinterpret_cast<const float4 *>(x + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < kRmsBatch; ++j)
+                if (i0 + 128 * j < k) s = sq4(s, v[j]);
         }
     } else {
         for (int64_t i = lane; i < k; i += 32) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
@@ -200,15 +269,34 @@ __device__ __forceinline__ float inv_rms_warp(const float *x, int64_t k, float e
 // returns 1 / rms of it with the reference's arithmetic.
 __device__ __forceinline__ float inv_rms_parts_warp(const MmaParams &p, int64_t k, int lane, float *h_out) {
     float s = 0.0f;
-    for (int64_t i = int64_t(lane) * 4; i < k; i += 128) {
-        float4 v = __ldg(reinterpret_cast<const float4 *>(p.x + i));
-        for (int r = 0; r < p.nparts; ++r) {
-            const float4 q = __ldg(reinterpret_cast<const float4 *>(p.parts + r * p.part_stride + i));
-            v = make_float4(__fadd_rn(v.x, q.x), __fadd_rn(v.y, q.y), __fadd_rn(v.z, q.z), __fadd_rn(v.w, q.w));
+    for (int64_t i0 = int64_t(lane) * 4; i0 < k; i0 += 128 * kRmsBatch) {
+        float4 v[kRmsBatch];
+#pragma unroll
+        for (int j = 0; j < kRmsBatch; ++j) {
+            const int64_t i = i0 + 128 * j;
+            v[j] = i < k ? __ldg(reinterpret_cast<const float4 *>(p.x + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (h_out) *reinterpret_cast<float4 *>(h_out + i) = v;
-        s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                                   __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+        for (int r = 0; r < p.nparts; ++r) {
+            float4 q[kRmsBatch];
+#pragma unroll
+            for (int j = 0; j < kRmsBatch; ++j) {
+                const int64_t i = i0 + 128 * j;
+                q[j] = i < k ? __ldg(reinterpret_cast<const float4 *>(p.parts + r * p.part_stride + i))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < kRmsBatch; ++j)
+                v[j] = make_float4(__fadd_rn(v[j].x, q[j].x), __fadd_rn(v[j].y, q[j].y), __fadd_rn(v[j].z, q[j].z),
+                                   __fadd_rn(v[j].w, q[j].w));
+        }
+#pragma unroll
+        for (int j = 0; j < kRmsBatch; ++j) {
+            const int64_t i = i0 + 128 * j;
+            if (i < k) {
+                if (h_out) *reinterpret_cast<float4 *>(h_out + i) = v[j];
+                s = sq4(s, v[j]);
+            }
+        }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
@@ -254,6 +342,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = CS > 1 ? cluster_ctarank() : 0u;
+    uint32_t peer_rows = 0;  // output rows this thread stored (publish-only exchange count)
     const int first_tile = CS > 1 ? int(cluster_id_x()) : int(blockIdx.x);
     const int tile_step = CS > 1 ? int(cluster_count_x()) : int(gridDim.x);
     pdl_trigger();
@@ -301,7 +390,10 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     } else if (warp == C + 1) {
         // Reducer: fixed-order sum of the C0 per-column partials of each
         // output (row r, input row u) = index r * TK + u of the tile.
-        if (CS == 1) pdl_wait();  // y may still be read by the previous kernel
+        if (CS == 1) {
+            pdl_wait();  // y may still be read by the previous kernel
+            consumer_wait(p, lane);
+        }
         const float row_scale =
             CS != 1 ? 1.0f
             : p.in_mode == 1 ? inv_rms_warp(p.x, int64_t(p.nsb) * 256, p.eps, lane)
@@ -324,7 +416,10 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                 if (r < nrows)
                     for (int c = 0; c < C0; ++c) a += pb[c * RTK + o];
                 if (CS == 1) {
-                    if (r < nrows && (TK == 1 || u < p.ntok)) store_y(p, r0 + r, __fmul_rn(a, row_scale), u, res);
+                    if (r < nrows && (TK == 1 || u < p.ntok)) {
+                        store_y(p, r0 + r, __fmul_rn(a, row_scale), u, res);
+                        ++peer_rows;
+                    }
                 } else {
                     rowsum[it * RTK + o] = a;
                 }
@@ -342,6 +437,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
         const bool has1 = SPW == 2 && sb1 < p.nsb_cta;
         const int gsb = int(crank) * p.nsb_cta;
         pdl_wait();  // x is produced by the previous kernel
+        consumer_wait(p, lane);
         uint8_t *my_scratch = scratch + size_t(warp) * Path::kScratchBytes;
         auto load_x = [&](const auto &X) {
             Path::load(X, gsb + sb0, lane, st0, my_scratch, p.x_stride, p.ntok);
@@ -425,6 +521,7 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     }
     if (CS > 1) {
         pdl_wait();          // y may still be read by the previous kernel
+        if (warp == C + 1) consumer_wait(p, lane);
         const float row_scale =
             warp != C + 1 ? 1.0f
             : p.in_mode == 1 ? inv_rms_warp(p.x, int64_t(p.nsb) * 256, p.eps, lane)
@@ -467,11 +564,20 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
                     }
                 }
                 store_y(p, row, __fmul_rn(a, row_scale), u, res);
+                ++peer_rows;
             }
         }
         cluster_sync_all();  // no CTA leaves while a peer may still read its row sums
     }
-    if (p.peer.nranks > 0) {
+    if (p.peer.nranks > 0 && p.peer.nowait) {
+        // only the reducer warp stores output rows: it fences them, counts them and publishes
+        if (warp == C + 1) {
+            __threadfence_system();
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) peer_rows += __shfl_xor_sync(0xffffffffu, peer_rows, off);
+            if (lane == 0) peer_publish(p, peer_rows);
+        }
+    } else if (p.peer.nranks > 0) {
         if (warp == C + 1) __threadfence_system();  // the output stores of the reducer warp, before the ticket
         __syncthreads();
         if (threadIdx.x == 0) peer_handshake(p);
@@ -742,6 +848,10 @@ si_status launch_mma(int path, const void *w, const float *x, float *y, int64_t 
         p.nparts = fusion->nparts;
         p.part_stride = fusion->part_stride;
         p.h_out = fusion->h_out;
+        p.wait_counts = fusion->wait_counts;
+        p.wait_epoch = fusion->wait_epoch;
+        p.wait_ranks = fusion->wait_ranks;
+        p.wait_rows = fusion->wait_rows;
     }
     p.token = token;
     p.ntok = ntok;

@@ -147,6 +147,26 @@ si_status peer_gather_desc(si_peer_group *g, uint64_t output_offset, int64_t row
     *out = pg;
     return SI_OK;
 }
+
+// State area after the data bytes: flags (+0), ticket (+256), epoch (+512),
+// publish-only counts (+1024: four kinds of kMaxPeerRanks u64), kind epochs (+1536).
+si_status peer_gather_desc_nowait(si_peer_group *g, uint64_t output_offset, int64_t row_base, int64_t rows, int kind,
+                                  kernels::PeerGather *out) {
+    if (kind < 0 || kind > 3) return fail(SI_ERR_INVALID_ARGUMENT, "exchange kind %d", kind);
+    if (si_status st = peer_gather_desc(g, output_offset, row_base, rows, out)) return st;
+    for (int q = 0; q < g->nranks; ++q)
+        out->counts[q] = reinterpret_cast<unsigned long long *>(g->arenas[q] + g->data_bytes + 1024 + 64 * kind);
+    out->kind_epoch = reinterpret_cast<uint32_t *>(g->arenas[g->rank] + g->data_bytes + 1536 + 4 * kind);
+    out->nowait = 1;
+    return SI_OK;
+}
+
+si_status peer_counts(si_peer_group *g, int kind, const unsigned long long **counts, const uint32_t **epoch) {
+    if (kind < 0 || kind > 3) return fail(SI_ERR_INVALID_ARGUMENT, "exchange kind %d", kind);
+    *counts = reinterpret_cast<const unsigned long long *>(g->arenas[g->rank] + g->data_bytes + 1024 + 64 * kind);
+    *epoch = reinterpret_cast<const uint32_t *>(g->arenas[g->rank] + g->data_bytes + 1536 + 4 * kind);
+    return SI_OK;
+}
 }  // namespace si
 
 extern "C" {

@@ -61,6 +61,11 @@ namespace kernels { struct PeerGather; }
 // row_base of the float vector at output_offset in every rank's arena.
 si_status peer_gather_desc(si_peer_group *g, uint64_t output_offset, int64_t row_base, int64_t rows,
                            kernels::PeerGather *out);
+// Publish-only exchange of kind `kind` (0..3): the producer descriptor, and
+// this rank's counts / epoch of that kind for the consumer's wait.
+si_status peer_gather_desc_nowait(si_peer_group *g, uint64_t output_offset, int64_t row_base, int64_t rows, int kind,
+                                  kernels::PeerGather *out);
+si_status peer_counts(si_peer_group *g, int kind, const unsigned long long **counts, const uint32_t **epoch);
 
 // Per-device launch state (launch_state.cpp). Kernel attributes and the SM
 // count are properties of a device; one process may drive several devices
@@ -117,6 +122,13 @@ struct PeerGather {
     int nranks;                       // 0: not a sharded call
     int rank;
     int64_t row_base;                 // global index of this rank's first row
+    // Publish-only exchange (no wait at the producer): every CTA adds the rows
+    // it stored to counts[q][rank] of every rank q (after a system-scope
+    // fence), and the launch's last CTA advances this rank's kind_epoch; the
+    // consumer waits for the counts (GemvFusion::wait_*).
+    int nowait;
+    unsigned long long *counts[kMaxPeerRanks];
+    uint32_t *kind_epoch;
 };
 // control/token: batch-shared use, y is written only when token < control[1].
 si_status matvec_quant_mma(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
@@ -141,6 +153,12 @@ struct GemvFusion {
     int nparts = 0;
     int64_t part_stride = 0;
     float *h_out = nullptr;
+    // Consumer of a publish-only exchange: before reading x / parts, wait
+    // until every rank's count reached (*wait_epoch) * wait_rows.
+    const unsigned long long *wait_counts = nullptr;
+    const uint32_t *wait_epoch = nullptr;
+    int wait_ranks = 0;
+    int64_t wait_rows = 0;
 };
 si_status matvec_quant_fused(uint32_t wtype, const void *w, const float *x, float *y, int64_t rows, int64_t cols,
                              const GemvFusion &f, void *stream, const PeerGather *peer = nullptr);
