@@ -153,8 +153,7 @@ __device__ __forceinline__ bool fw_test(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 __device__ __forceinline__ bool fw_wait(uint64_t *bar, uint32_t parity, uint32_t err, volatile uint32_t *abort) {
-    for (int i = 0; i < 64; ++i)
-        if (fw_test(bar, parity)) return true;
+    if (fw_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0; i < kMaxPolls; ++i) {
         if (*abort) return false;
@@ -280,7 +279,9 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint3
     const __half2 h = __floats2half2_rn(a, b);
     const float2 hf = __half22float2(h);
     hi = h2bits(h);
-    lo = h2bits(__floats2half2_rn(a - hf.x, b - hf.y));
+    // (a, b) - hi in one packed FMA (x * -1 + y is exact)
+    const float2 r = __ffma2_rn(hf, make_float2(-1.0f, -1.0f), make_float2(a, b));
+    lo = h2bits(__floats2half2_rn(r.x, r.y));
 }
 
 // One Q4_K half stage of this thread's weight row (sub-blocks 4h .. 4h+3)
@@ -628,7 +629,9 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
         pdl_wait();  // X may come from the previous kernel
         load(0, cur);
         const uint32_t sw = uint32_t(r & 7);
-        for (uint32_t xg = 0; xg < total; ++xg) {
+        // stage xg converts from `cur` while the loads of xg + 1 land in `nxt`; the two
+        // buffers swap roles every stage (the body is instantiated for both orders)
+        auto stage = [&](uint32_t xg, float4 (&cur)[8], float4 (&nxt)[8]) {
             load(xg + 1, nxt);
             const float *v = reinterpret_cast<const float *>(cur);
             // per (row, stage) power-of-two scale: values below 2^10 (32-column sums stay inside
@@ -677,9 +680,10 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
             }
             if constexpr (C::kQ4K) {
                 // sub-block sum: columns u and 8 + u of the mins operand, hi in row r, lo in row BN + r
-                float sum = 0.0f;
+                float2 s2 = make_float2(0.0f, 0.0f);  // even / odd columns, then added
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sum += v[i];
+                for (int i = 0; i < 32; i += 2) s2 = __fadd2_rn(s2, make_float2(v[i], v[i + 1]));
+                const float sum = s2.x + s2.y;
                 const __half shi = __float2half_rn(sum);
                 const __half slo = __float2half_rn(sum - __half2float(shi));
                 uint8_t *mb = bmin + (xg % C::kBStages) * C::kBMin;
@@ -694,8 +698,10 @@ __global__ void __launch_bounds__(FwCfg<FMT, BN>::kThreads, 1)
             fence_proxy_async();  // the X tiles, written through the generic proxy, for the tensor core
             mbar_arrive(&xb_full[(u0 + hs) % kNB]);
             mbar_arrive(&scale_full[xg % kNS]);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+        };
+        for (uint32_t xg = 0; xg < total; xg += 2) {
+            stage(xg, cur, nxt);
+            if (xg + 1 < total) stage(xg + 1, nxt, cur);
         }
     }
 
