@@ -307,6 +307,18 @@ __global__ void rope_kv_kernel(const float *qkv, const int32_t *position, const 
     }
 }
 
+// 16-byte asynchronous copies global -> shared (zero-filled when !valid).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    const uint32_t dst = uint32_t(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // ---- decode attention --------------------------------------------------------
 constexpr int kAttnCluster = 8;
 
@@ -567,6 +579,311 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
     cluster_sync();  // no CTA leaves while a peer may still read its partials
 }
 
+// ---- decode attention with the key/value rows staged in shared memory -------
+// One stream. The same cluster of kAttnCluster CTAs per key/value head and the
+// same contiguous token ranges as gqa_decode_kernel, but the CTA's cache rows
+// are copied into shared memory (cp.async) before the dependency wait, and
+// after it the work is laid out so that no step waits on a chain of shuffles:
+//   scores   one thread per (query head, token): a 4-way split dot product
+//            over the staged key row (rows padded by 4 floats, so the float4
+//            loads of consecutive tokens fall in different banks);
+//   softmax  one warp per query head: running max, rescale, exp, denominator;
+//   values   warp w takes tokens w, w + 16, ...; lane j holds channel quads
+//            j and j + 32 of every query head; warp partials summed in order.
+// The CTA partials (weighted values, max, denominator) go into rank 0's shared
+// memory; one cluster-barrier phase later rank 0 merges them in rank order.
+// Tokens past the staging capacity are taken in further passes (online
+// softmax across passes).
+constexpr int kStThreads = 512, kStWarps = kStThreads / 32, kStMaxG = 8, kStSmemLimit = 227 * 1024;
+
+struct StLayout {
+    int ks, vs, hb, qs, fr, ss, st, cs, sl, slot, total;  // float offsets; total floats
+};
+// The shared-memory carve-up for G query heads per key/value head, head size
+// hs, cap staged tokens and a rope table of `rotary` floats. Every region
+// starts on a 16-byte boundary.
+__host__ __device__ inline StLayout st_layout(int G, int hs, int cap, int rotary) {
+    StLayout L{};
+    const int capp = (cap + 31) & ~31;
+    int o = 0;
+    L.ks = o;  // staged keys [cap][hs + 4]; at the end the warp partials [warps][G][hs]
+    o += cap * (hs + 4) > kStWarps * G * hs ? cap * (hs + 4) : kStWarps * G * hs;
+    L.vs = o;  // staged values [cap][hs]
+    o += cap * hs;
+    L.hb = o;  // the token's raw q heads, k head, v head
+    o += (G + 2) * hs;
+    L.qs = o;  // q after rope [G][hs]
+    o += G * hs;
+    L.fr = o;  // the token's key (after rope) and value [2][hs]
+    o += 2 * hs;
+    L.ss = o;  // scores, then probabilities [G][capp]
+    o += G * capp;
+    L.st = o;  // running max [8], denominator [8], rescale [8]
+    o += 32;
+    L.cs = o;  // rope cos / sin
+    o += (rotary + 3) & ~3;
+    L.slot = G * hs + 16;  // acc [G][hs], then max at +G*hs, denominator at +G*hs+8
+    L.sl = o;              // rank 0: one slot per CTA of the cluster
+    o += kAttnCluster * L.slot;
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+struct StagedAttn {
+    const float *query;  // without rope: the query vector
+    const float *key_cache, *value_cache;
+    const int32_t *position;
+    float *out;
+    int group, kv_heads, head_size, cap;
+    int64_t context;
+    float scale;
+};
+
+template <int MAXG, bool ROPE>
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThreads, 1)
+    gqa_decode_staged_kernel(const StagedAttn a, const RopeFuse rf) {
+    extern __shared__ __align__(16) float sm[];
+    const int G = a.group, hs = a.head_size, hs4 = hs >> 2, kst = hs + 4, cap = a.cap, capp = (cap + 31) & ~31;
+    const StLayout L = st_layout(G, hs, cap, ROPE ? rf.rotary : 0);
+    float *Ks = sm + L.ks, *Vs = sm + L.vs, *hb = sm + L.hb, *qs = sm + L.qs, *fr = sm + L.fr, *Ss = sm + L.ss,
+          *stat = sm + L.st, *cs = sm + L.cs, *slots = sm + L.sl;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kvh = blockIdx.x / kAttnCluster;
+    const uint32_t rank = cta_rank_in_cluster();
+    // First cluster-barrier phase: arrived here, waited before the first
+    // store into rank 0's shared memory (every CTA of the cluster has started).
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+    pdl_trigger();
+    // Before the dependency wait: the position and every cache row of an
+    // earlier token (written by earlier steps). The row at the position is
+    // this step's: from the qkv vector (ROPE) or from the preceding
+    // rope-kv-write.
+    const int32_t pos = *a.position;
+    int64_t active = pos;
+    active = active < 0 ? 0 : (active > a.context - 1 ? a.context - 1 : active);
+    const int64_t fresh = (pos >= 0 && pos < a.context) ? int64_t(pos) : -1;
+    const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
+    const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
+    const int64_t stride = int64_t(a.kv_heads) * hs;
+    const float *kbase = a.key_cache + int64_t(kvh) * hs, *vbase = a.value_cache + int64_t(kvh) * hs;
+    if (tid < 8) {
+        stat[tid] = -INFINITY;
+        stat[8 + tid] = 0.0f;
+        stat[16 + tid] = 0.0f;
+    }
+    if constexpr (ROPE) {
+        const int half = rf.rotary / 2;
+        for (int ri = tid; ri < half; ri += kStThreads) {
+            const float angle = __fmul_rn(float(pos), rf.freq[ri]);
+            cs[ri] = __fmul_rn(cosf(angle), rf.rope_scale);
+            cs[half + ri] = __fmul_rn(sinf(angle), rf.rope_scale);
+        }
+    }
+    // rows c0 .. c0 + n - 1 of the CTA's range into Ks / Vs (the fresh row is
+    // written from registers instead)
+    auto stage = [&](int64_t c0, int n) {
+        const int rowq = n * hs4;
+        for (int i = tid; i < 2 * rowq; i += kStThreads) {
+            const bool isv = i >= rowq;
+            const int j = isv ? i - rowq : i;
+            const int r = j / hs4, c = j - r * hs4;
+            const int64_t t = c0 + r;
+            if (t == fresh) continue;
+            const float *src = (isv ? vbase : kbase) + t * stride + 4 * c;
+            float *dst = isv ? Vs + r * hs + 4 * c : Ks + r * kst + 4 * c;
+            cp_async16(dst, src, true);
+        }
+        cp_async_commit();
+    };
+    const int n0 = t1 - t0 < int64_t(cap) ? int(t1 - t0) : cap;  // <= 0: no tokens for this CTA
+    if (n0 > 0) stage(t0, n0);
+    pdl_wait();
+    const bool mine = fresh >= t0 && fresh < t1;
+    {
+        // the token's heads, one memory round trip
+        const float *qsrc = (ROPE ? rf.qkv : a.query) + int64_t(kvh) * G * hs;
+        float4 *hb4 = reinterpret_cast<float4 *>(hb);
+        for (int i = tid; i < G * hs4; i += kStThreads) hb4[i] = *reinterpret_cast<const float4 *>(qsrc + 4 * i);
+        if (mine && tid < 2 * hs4) {
+            const bool isv = tid >= hs4;
+            const int c = isv ? tid - hs4 : tid;
+            const float *src;
+            if constexpr (ROPE) src = rf.qkv + rf.qsize + (isv ? rf.kvsize : 0) + int64_t(kvh) * hs + 4 * c;
+            else src = (isv ? vbase : kbase) + fresh * stride + 4 * c;
+            hb4[G * hs4 + tid] = *reinterpret_cast<const float4 *>(src);
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hs; i += kStThreads) {
+        if constexpr (ROPE) {
+            const int g = i / hs, d = i - g * hs;
+            qs[i] = rope_element(hb + g * hs, d, cs, rf);
+        } else {
+            qs[i] = hb[i];
+        }
+    }
+    if (mine) {
+        for (int d = tid; d < hs; d += kStThreads) {
+            float kf = hb[G * hs + d];
+            if constexpr (ROPE) kf = rope_element(hb + G * hs, d, cs, rf);
+            const float vf = hb[(G + 1) * hs + d];
+            fr[d] = kf;
+            fr[hs + d] = vf;
+            if (fresh < t0 + n0) {
+                Ks[int(fresh - t0) * kst + d] = kf;
+                Vs[int(fresh - t0) * hs + d] = vf;
+            }
+            if constexpr (ROPE) {  // rope-kv-write's stores (nothing for a position outside the cache)
+                rf.key_cache[fresh * stride + int64_t(kvh) * hs + d] = kf;
+                rf.value_cache[fresh * stride + int64_t(kvh) * hs + d] = vf;
+            }
+        }
+    }
+    float4 acc[MAXG][2];
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) acc[g][0] = acc[g][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int64_t c0 = t0; c0 < t1; c0 += cap) {
+        const int n = t1 - c0 < int64_t(cap) ? int(t1 - c0) : cap;
+        if (c0 != t0) {
+            __syncthreads();  // the previous pass is done with Ks / Vs / Ss
+            stage(c0, n);
+            if (fresh >= c0 && fresh < c0 + n)
+                for (int d = tid; d < hs; d += kStThreads) {
+                    Ks[int(fresh - c0) * kst + d] = fr[d];
+                    Vs[int(fresh - c0) * hs + d] = fr[hs + d];
+                }
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        for (int i = tid; i < G * capp; i += kStThreads) {
+            const int g = i / capp, t = i - g * capp;
+            if (t >= n) continue;
+            const float4 *kr = reinterpret_cast<const float4 *>(Ks + t * kst);
+            const float4 *qr = reinterpret_cast<const float4 *>(qs + g * hs);
+            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+#pragma unroll 4
+            for (int c = 0; c < hs4; ++c) {
+                const float4 k4 = kr[c], q4 = qr[c];
+                s0 = __fadd_rn(s0, __fmul_rn(q4.x, k4.x));
+                s1 = __fadd_rn(s1, __fmul_rn(q4.y, k4.y));
+                s2 = __fadd_rn(s2, __fmul_rn(q4.z, k4.z));
+                s3 = __fadd_rn(s3, __fmul_rn(q4.w, k4.w));
+            }
+            Ss[g * capp + t] = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), a.scale);
+        }
+        __syncthreads();
+        if (warp < G) {
+            const int g = warp;
+            float mx = -INFINITY;
+            for (int t = lane; t < n; t += 32) mx = fmaxf(mx, Ss[g * capp + t]);
+            mx = warp_max(mx);
+            const float m_old = stat[g], m_new = fmaxf(m_old, mx);
+            const float corr = m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new));
+            float ls = 0.0f;
+            for (int t = lane; t < n; t += 32) {
+                const float p = expf(__fsub_rn(Ss[g * capp + t], m_new));
+                Ss[g * capp + t] = p;
+                ls = __fadd_rn(ls, p);
+            }
+            ls = warp_sum(ls);
+            __syncwarp();
+            if (lane == 0) {
+                stat[8 + g] = __fadd_rn(__fmul_rn(stat[8 + g], corr), ls);
+                stat[g] = m_new;
+                stat[16 + g] = corr;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g) {
+            if (g >= G) break;
+            const float corr = stat[16 + g];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                acc[g][j].x = __fmul_rn(acc[g][j].x, corr);
+                acc[g][j].y = __fmul_rn(acc[g][j].y, corr);
+                acc[g][j].z = __fmul_rn(acc[g][j].z, corr);
+                acc[g][j].w = __fmul_rn(acc[g][j].w, corr);
+            }
+        }
+        for (int t = warp; t < n; t += kStWarps) {
+            float4 v4[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int c = lane + 32 * j;
+                v4[j] = c < hs4 ? reinterpret_cast<const float4 *>(Vs + t * hs)[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int g = 0; g < MAXG; ++g) {
+                if (g >= G) break;
+                const float p = Ss[g * capp + t];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    acc[g][j].x = __fadd_rn(acc[g][j].x, __fmul_rn(p, v4[j].x));
+                    acc[g][j].y = __fadd_rn(acc[g][j].y, __fmul_rn(p, v4[j].y));
+                    acc[g][j].z = __fadd_rn(acc[g][j].z, __fmul_rn(p, v4[j].z));
+                    acc[g][j].w = __fadd_rn(acc[g][j].w, __fmul_rn(p, v4[j].w));
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();  // a CTA without tokens staged nothing; one with tokens has waited already
+    __syncthreads();     // every pass done with Ks: it takes the warp partials now
+    float *red = Ks;
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) {
+        if (g >= G) break;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int c = lane + 32 * j;
+            if (c < hs4) reinterpret_cast<float4 *>(red + (warp * G + g) * hs)[c] = acc[g][j];
+        }
+    }
+    __syncthreads();
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+    const uint32_t slot0 = dsmem_addr(slots + int(rank) * L.slot, 0);
+    for (int i = tid; i < G * hs; i += kStThreads) {
+        float A = 0.0f;
+        for (int w = 0; w < kStWarps; ++w) A = __fadd_rn(A, red[w * G * hs + i]);
+        dsmem_st_f32(slot0 + 4u * uint32_t(i), A);
+    }
+    if (tid < G) {
+        dsmem_st_f32(slot0 + 4u * uint32_t(G * hs + tid), stat[tid]);
+        dsmem_st_f32(slot0 + 4u * uint32_t(G * hs + 8 + tid), stat[8 + tid]);
+    }
+    // Second phase: the partials are in rank 0. Ranks 1.. leave (only rank
+    // 0's shared memory is read remotely); rank 0 waits and merges.
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+    if (rank != 0) return;
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+    for (int i = tid; i < G * hs; i += kStThreads) {
+        const int g = i / hs;
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, slots[r * L.slot + G * hs + g]);
+        float A = 0.0f, Lsum = 0.0f;
+        if (M != -INFINITY)
+#pragma unroll
+            for (int r = 0; r < kAttnCluster; ++r) {
+                const float mr = slots[r * L.slot + G * hs + g];
+                if (mr == -INFINITY) continue;
+                const float f = expf(__fsub_rn(mr, M));
+                A = __fadd_rn(A, __fmul_rn(slots[r * L.slot + i], f));
+                Lsum = __fadd_rn(Lsum, __fmul_rn(slots[r * L.slot + G * hs + 8 + g], f));
+            }
+        a.out[int64_t(kvh) * G * hs + i] = __fdiv_rn(A, Lsum);
+    }
+}
+
 // ---- unfused attention instructions (single and batch forms) --------------
 // transformer.gqa-scores / batch-gqa-scores. Single form (control null):
 // active = *position and the token test is the instruction's unsigned
@@ -694,16 +1011,6 @@ constexpr int kPfThreads = 128;
 constexpr int kPfRowStride = kPfThreads / 16;  // rows ty, ty + stride, .. (4 per thread)
 static_assert(kPfRows == 4 * kPfRowStride, "four rows per thread");
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
-    const uint32_t dst = uint32_t(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem), "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
 
 template <int HS>
 __global__ void __launch_bounds__(kPfThreads, HS <= 128 ? 4 : 2)
@@ -1088,6 +1395,29 @@ si_status launch_gqa(const float *query, const float *kc, const float *vc, const
 }
 }  // namespace
 
+namespace {
+// Tokens per staging pass of gqa_decode_staged_kernel for this shape (the
+// most a CTA takes at the cache's last position, as far as 227 KB of shared
+// memory hold them), or 0 when the shape needs the register-tile kernel.
+int staged_cap(int group, int head_size, int64_t context, int rotary) {
+    if (group < 1 || group > kStMaxG || head_size < 4 || head_size > 256 || head_size % 4 != 0) return 0;
+    int cap = int(std::min<int64_t>((context + kAttnCluster - 1) / kAttnCluster, 1024));
+    while (cap > 0 && size_t(st_layout(group, head_size, cap, rotary).total) * sizeof(float) > size_t(kStSmemLimit))
+        cap -= cap > 64 ? 16 : 1;
+    return cap;
+}
+
+template <bool ROPE>
+si_status launch_staged(const StagedAttn &a, const RopeFuse &rf, void *stream) {
+    auto kernel = a.group <= 4 ? gqa_decode_staged_kernel<4, ROPE> : gqa_decode_staged_kernel<kStMaxG, ROPE>;
+    const int smem = st_layout(a.group, a.head_size, a.cap, ROPE ? rf.rotary : 0).total * int(sizeof(float));
+    if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), smem))
+        return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
+    return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(a.kv_heads * kAttnCluster)),
+                  dim3(kStThreads), size_t(smem), stream, a, rf);
+}
+}  // namespace
+
 si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, const float *freq, float *kc, float *vc,
                                    float *out, int query_heads, int kv_heads, int head_size, int rotary,
                                    int64_t context, float rope_scale, void *stream) {
@@ -1096,6 +1426,10 @@ si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, co
     const int npl = (head_size + 31) / 32;
     const int64_t qsize = int64_t(query_heads) * head_size, kvsize = int64_t(kv_heads) * head_size;
     const RopeFuse rf{qkv, freq, kc, vc, qsize, kvsize, rotary, rope_scale};
+    if (const int cap = staged_cap(group, head_size, context, rotary))
+        return launch_staged<true>(StagedAttn{nullptr, kc, vc, position, out, group, kv_heads, head_size, cap, context,
+                                              scale},
+                                   rf, stream);
 #define SI_GQA_R(NPL, MAXG, TILE)                                                                               \
     launch_gqa<NPL, MAXG, TILE, kAttnWarpsOne, true>(qkv, kc, vc, position, out, group, kv_heads, head_size,      \
                                                      context, scale, 1, qsize, 0, stream, rf)
@@ -1125,6 +1459,11 @@ si_status tr_attention_decode_streams(const float *query, const float *kc, const
     const float scale = 1.0f / sqrtf(float(head_size));
     const int npl = (head_size + 31) / 32;
     const int64_t q_stride = int64_t(query_heads) * head_size;
+    if (streams == 1)
+        if (const int cap = staged_cap(group, head_size, context, 0))
+            return launch_staged<false>(StagedAttn{query, kc, vc, position, out, group, kv_heads, head_size, cap,
+                                                   context, scale},
+                                        RopeFuse{}, stream);
 #define SI_GQA(NPL, MAXG, TILE)                                                                                \
     (streams > 1 ? launch_gqa<NPL, MAXG, TILE, kAttnWarpsMany>(query, kc, vc, position, out, group, kv_heads,      \
                                                                head_size, context, scale, streams, q_stride,      \

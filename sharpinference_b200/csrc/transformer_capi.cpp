@@ -126,6 +126,28 @@ si_status si_grouped_query_attention(const float *query, const float *key_cache,
                                         head_size, context, stream);
 }
 
+si_status si_rope_grouped_query_attention(const float *qkv, const int32_t *position, const float *frequencies,
+                                          float *key_cache, float *value_cache, float *output, int32_t query_heads,
+                                          int32_t kv_heads, int32_t head_size, int32_t rotary_size, int64_t context,
+                                          float rope_scale, void *stream) {
+    const char *op = "transformer.grouped-query-attention";
+    if (si_status st = attention_shape(op, query_heads, kv_heads, head_size, context)) return st;
+    const int64_t qsize = int64_t(query_heads) * head_size;
+    if (si_status st = rope_shape("transformer.rope-kv-write", qsize, kv_heads, head_size, rotary_size, context,
+                                  rope_scale))
+        return st;
+    if (head_size > 256) return fail(SI_ERR_UNSUPPORTED, "%s: head_size %d above 256.", op, head_size);
+    if (query_heads / kv_heads > 8) return fail(SI_ERR_UNSUPPORTED, "%s: more than 8 query heads per key/value head.", op);
+    const int64_t kv = int64_t(kv_heads) * head_size;
+    if (si_status st = ports({{"qkv", qkv, (qsize + 2 * kv) * F}, {"position", position, 4},
+                              {"frequencies", frequencies, uint64_t(rotary_size / 2) * F},
+                              {"key_cache", key_cache, context * kv * F}, {"value_cache", value_cache, context * kv * F},
+                              {"output", output, qsize * F}}))
+        return st;
+    return kernels::tr_attention_decode_rope(qkv, position, frequencies, key_cache, value_cache, output, query_heads,
+                                             kv_heads, head_size, rotary_size, context, rope_scale, stream);
+}
+
 si_status si_gqa_scores(const float *query, const float *key_cache, const int32_t *position, float *scores,
                         int32_t query_heads, int32_t kv_heads, int32_t head_size, int64_t context, void *stream) {
     if (si_status st = attention_shape("transformer.gqa-scores", query_heads, kv_heads, head_size, context)) return st;

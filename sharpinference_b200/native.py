@@ -134,6 +134,7 @@ SIGNATURES = {
     "si_scaled_add": [_vp, _vp, _vp, _i64, C.c_float, _vp],
     "si_rope_kv_write": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, C.c_float, _vp],
     "si_grouped_query_attention": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],
+    "si_rope_grouped_query_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i64, C.c_float, _vp],
     "si_gqa_scores": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],
     "si_causal_softmax": [_vp, _vp, _vp, _i32, _i64, _vp],
     "si_gqa_values": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _vp],

@@ -202,6 +202,38 @@ def test_grouped_query_attention_matches_oracle(ctx, dev, shape, pos):
     np.testing.assert_allclose(dev.get(out), ref, rtol=2e-5, atol=2e-6)
 
 
+ROPE_ATTN_SHAPES = [PHI4_MINI, PHI4_14B, dict(qh=16, kvh=2, hs=96, rot=64), dict(qh=4, kvh=1, hs=256, rot=128),
+                    dict(qh=8, kvh=8, hs=64, rot=64), dict(qh=6, kvh=2, hs=2, rot=2)]
+
+
+@pytest.mark.parametrize("shape", ROPE_ATTN_SHAPES, ids=lambda s: f"{s['qh']}x{s['kvh']}x{s['hs']}")
+@pytest.mark.parametrize("pos,T", [(0, 64), (9, 64), (63, 64), (64, 64), (520, 1024), (1023, 1024), (3000, 4096)])
+def test_rope_attention_matches_rope_kv_write_then_attention(ctx, dev, shape, pos, T):
+    """The fused decode step (si_rope_grouped_query_attention) equals
+    rope-kv-write followed by grouped-query-attention: the cache rows as
+    rope-kv-write stores them (values exact, rotated keys within the rope
+    tolerance), the output within the attention tolerance. Long contexts take several staging passes per CTA (3000
+    tokens over 8 CTAs); a position at or past the cache end writes nothing
+    and attends the whole cache with the query rotated at the position."""
+    qh, kvh, hs, rot = shape["qh"], shape["kvh"], shape["hs"], shape["rot"]
+    rng = np.random.default_rng(pos + 3 * hs + T)
+    qkv = rng.standard_normal(qh * hs + 2 * kvh * hs).astype(np.float32)
+    freq = oracle.rope_frequencies(10000.0, rot)
+    kc0 = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    vc0 = rng.standard_normal(T * kvh * hs).astype(np.float32)
+    bkc, bvc, out = dev.put(kc0), dev.put(vc0), dev.zeros(qh * hs, fill=-9)
+    N.call("si_rope_grouped_query_attention", p(dev.put(qkv)), p(dev.put([pos], np.int32)), p(dev.put(freq)), p(bkc),
+           p(bvc), p(out), qh, kvh, hs, rot, T, 1.1902381, S(ctx))
+    q_ref, kc_ref, vc_ref = oracle.rope_kv_write(qkv, pos, freq, kc0, vc0, qh * hs, kvh, hs, rot, T, 1.1902381)
+    if pos >= T:  # the query rotated at pos, from a cache that holds the position
+        ext = np.zeros((pos + 1) * kvh * hs, np.float32)
+        q_ref = oracle.rope_kv_write(qkv, pos, freq, ext, ext, qh * hs, kvh, hs, rot, pos + 1, 1.1902381)[0]
+    np.testing.assert_allclose(dev.get(bkc), kc_ref, rtol=1e-5, atol=2e-6)  # GPU cosf / sinf vs the host's
+    np.testing.assert_array_equal(dev.get(bvc), vc_ref)
+    ref = oracle.grouped_query_attention(q_ref, kc_ref, vc_ref, pos, qh, kvh, hs, T)
+    np.testing.assert_allclose(dev.get(out), ref, rtol=2e-5, atol=2e-6)
+
+
 @pytest.mark.parametrize("pos", [0, 5, 31, -1])
 def test_unfused_attention_matches_oracle(ctx, dev, pos):
     qh, kvh, hs, T = 6, 2, 32, 32
