@@ -582,32 +582,36 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 // ---- decode attention with the key/value rows staged in shared memory -------
 // One stream. The same cluster of kAttnCluster CTAs per key/value head and the
 // same contiguous token ranges as gqa_decode_kernel, but the CTA's cache rows
-// are copied into shared memory (cp.async) before the dependency wait, and
-// after it the work is laid out so that no step waits on a chain of shuffles:
-//   scores   one thread per (query head, token): a 4-way split dot product
-//            over the staged key row (rows padded by 4 floats, so the float4
-//            loads of consecutive tokens fall in different banks);
+// are copied into shared memory (cp.async, one warp per row) before the
+// dependency wait, and after it every warp works on its own tokens:
+//   scores   warp w takes blocks of 32 / MAXG tokens; lane j holds channel
+//            quads j (and j + 32 when head_size > 128) of the group's queries
+//            in registers and forms the 32 partial dot products (token x
+//            query head) of the block, then one reduce-scatter over the lanes
+//            (31 shuffles) leaves lane L with the sum of product L;
 //   softmax  one warp per query head: running max, rescale, exp, denominator;
-//   values   warp w takes tokens w, w + 16, ...; lane j holds channel quads
-//            j and j + 32 of every query head; warp partials summed in order.
+//   values   warp w takes tokens w, w + 16, ...; lane j holds channel quads j
+//            (and j + 32) of every query head; warp partials summed in warp
+//            order.
 // The CTA partials (weighted values, max, denominator) go into rank 0's shared
-// memory; one cluster-barrier phase later rank 0 merges them in rank order.
-// Tokens past the staging capacity are taken in further passes (online
-// softmax across passes).
-constexpr int kStThreads = 512, kStWarps = kStThreads / 32, kStMaxG = 8, kStSmemLimit = 227 * 1024;
+// memory; one cluster-barrier phase later rank 0 forms the per-(CTA, head)
+// factors exp(m_r - M) once and merges in rank order. Tokens past the staging
+// capacity are taken in further passes (online softmax across passes).
+constexpr int kStThreads = 512, kStWarps = kStThreads / 32, kStMaxG = 8;
+constexpr int kStSmemLimit = 227 * 1024;
 
 struct StLayout {
     int ks, vs, hb, qs, fr, ss, st, cs, sl, slot, total;  // float offsets; total floats
 };
 // The shared-memory carve-up for G query heads per key/value head, head size
-// hs, cap staged tokens and a rope table of `rotary` floats. Every region
-// starts on a 16-byte boundary.
+// hs (a multiple of 4), cap staged tokens and a rope table of `rotary`
+// floats. Every region starts on a 16-byte boundary.
 __host__ __device__ inline StLayout st_layout(int G, int hs, int cap, int rotary) {
     StLayout L{};
     const int capp = (cap + 31) & ~31;
     int o = 0;
-    L.ks = o;  // staged keys [cap][hs + 4]; at the end the warp partials [warps][G][hs]
-    o += cap * (hs + 4) > kStWarps * G * hs ? cap * (hs + 4) : kStWarps * G * hs;
+    L.ks = o;  // staged keys [cap][hs]; at the end the warp partials [warps][G][hs]
+    o += cap * hs > kStWarps * G * hs ? cap * hs : kStWarps * G * hs;
     L.vs = o;  // staged values [cap][hs]
     o += cap * hs;
     L.hb = o;  // the token's raw q heads, k head, v head
@@ -616,8 +620,8 @@ __host__ __device__ inline StLayout st_layout(int G, int hs, int cap, int rotary
     o += G * hs;
     L.fr = o;  // the token's key (after rope) and value [2][hs]
     o += 2 * hs;
-    L.ss = o;  // scores, then probabilities [G][capp]
-    o += G * capp;
+    L.ss = o;  // scores, then probabilities [G][capp]; at the end the merge factors [8][8]
+    o += G * capp > 64 ? G * capp : 64;
     L.st = o;  // running max [8], denominator [8], rescale [8]
     o += 32;
     L.cs = o;  // rope cos / sin
@@ -648,11 +652,13 @@ struct StagedAttn {
     float scale;
 };
 
-template <int MAXG, bool ROPE>
+// NQ: float4 channel quads per lane in the value pass (head_size <= 32 * 4 NQ).
+template <int MAXG, int NQ, bool ROPE>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThreads, 1)
     gqa_decode_staged_kernel(const StagedAttn a, const RopeFuse rf) {
     extern __shared__ __align__(16) float sm[];
-    const int G = a.group, hs = a.head_size, hs4 = hs >> 2, kst = hs + 4, cap = a.cap, capp = (cap + 31) & ~31;
+    const int G = a.group, hs = a.head_size, hs4 = hs >> 2;
+    const int cap = a.cap, capp = (cap + 31) & ~31;
     const StLayout L = st_layout(G, hs, cap, ROPE ? rf.rotary : 0);
     float *Ks = sm + L.ks, *Vs = sm + L.vs, *hb = sm + L.hb, *qs = sm + L.qs, *fr = sm + L.fr, *Ss = sm + L.ss,
           *stat = sm + L.st, *cs = sm + L.cs, *slots = sm + L.sl;
@@ -675,6 +681,22 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
     const int64_t stride = int64_t(a.kv_heads) * hs;
     const float *kbase = a.key_cache + int64_t(kvh) * hs, *vbase = a.value_cache + int64_t(kvh) * hs;
+    // rows c0 .. c0 + n - 1 of the CTA's range into Ks / Vs, one warp per row
+    // (the fresh row is written from registers instead)
+    auto stage = [&](int64_t c0, int n) {
+        for (int r = warp; r < n; r += kStWarps) {
+            const int64_t t = c0 + r;
+            if (t == fresh) continue;
+            const float *ksrc = kbase + t * stride, *vsrc = vbase + t * stride;
+            for (int c = lane; c < hs4; c += 32) {
+                cp_async16(Ks + r * hs + 4 * c, ksrc + 4 * c, true);
+                cp_async16(Vs + r * hs + 4 * c, vsrc + 4 * c, true);
+            }
+        }
+        cp_async_commit();
+    };
+    const int n0 = t1 - t0 < int64_t(cap) ? int(t1 - t0) : cap;  // <= 0: no tokens for this CTA
+    if (n0 > 0) stage(t0, n0);
     if (tid < 8) {
         stat[tid] = -INFINITY;
         stat[8 + tid] = 0.0f;
@@ -688,24 +710,6 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             cs[half + ri] = __fmul_rn(sinf(angle), rf.rope_scale);
         }
     }
-    // rows c0 .. c0 + n - 1 of the CTA's range into Ks / Vs (the fresh row is
-    // written from registers instead)
-    auto stage = [&](int64_t c0, int n) {
-        const int rowq = n * hs4;
-        for (int i = tid; i < 2 * rowq; i += kStThreads) {
-            const bool isv = i >= rowq;
-            const int j = isv ? i - rowq : i;
-            const int r = j / hs4, c = j - r * hs4;
-            const int64_t t = c0 + r;
-            if (t == fresh) continue;
-            const float *src = (isv ? vbase : kbase) + t * stride + 4 * c;
-            float *dst = isv ? Vs + r * hs + 4 * c : Ks + r * kst + 4 * c;
-            cp_async16(dst, src, true);
-        }
-        cp_async_commit();
-    };
-    const int n0 = t1 - t0 < int64_t(cap) ? int(t1 - t0) : cap;  // <= 0: no tokens for this CTA
-    if (n0 > 0) stage(t0, n0);
     pdl_wait();
     const bool mine = fresh >= t0 && fresh < t1;
     {
@@ -739,7 +743,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             fr[d] = kf;
             fr[hs + d] = vf;
             if (fresh < t0 + n0) {
-                Ks[int(fresh - t0) * kst + d] = kf;
+                Ks[int(fresh - t0) * hs + d] = kf;
                 Vs[int(fresh - t0) * hs + d] = vf;
             }
             if constexpr (ROPE) {  // rope-kv-write's stores (nothing for a position outside the cache)
@@ -748,9 +752,18 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             }
         }
     }
-    float4 acc[MAXG][2];
+    __syncthreads();  // qs
+    // the group's queries in registers: lane j holds channel quads j + 32 i
+    float4 qr[MAXG][NQ], acc[MAXG][NQ];
 #pragma unroll
-    for (int g = 0; g < MAXG; ++g) acc[g][0] = acc[g][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int g = 0; g < MAXG; ++g)
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+            const int c = lane + 32 * j;
+            qr[g][j] = (g < G && c < hs4) ? reinterpret_cast<const float4 *>(qs + g * hs)[c]
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            acc[g][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
     for (int64_t c0 = t0; c0 < t1; c0 += cap) {
         const int n = t1 - c0 < int64_t(cap) ? int(t1 - c0) : cap;
         if (c0 != t0) {
@@ -758,27 +771,54 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             stage(c0, n);
             if (fresh >= c0 && fresh < c0 + n)
                 for (int d = tid; d < hs; d += kStThreads) {
-                    Ks[int(fresh - c0) * kst + d] = fr[d];
+                    Ks[int(fresh - c0) * hs + d] = fr[d];
                     Vs[int(fresh - c0) * hs + d] = fr[hs + d];
                 }
         }
         cp_async_wait<0>();
         __syncthreads();
-        for (int i = tid; i < G * capp; i += kStThreads) {
-            const int g = i / capp, t = i - g * capp;
-            if (t >= n) continue;
-            const float4 *kr = reinterpret_cast<const float4 *>(Ks + t * kst);
-            const float4 *qr = reinterpret_cast<const float4 *>(qs + g * hs);
-            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-#pragma unroll 4
-            for (int c = 0; c < hs4; ++c) {
-                const float4 k4 = kr[c], q4 = qr[c];
-                s0 = __fadd_rn(s0, __fmul_rn(q4.x, k4.x));
-                s1 = __fadd_rn(s1, __fmul_rn(q4.y, k4.y));
-                s2 = __fadd_rn(s2, __fmul_rn(q4.z, k4.z));
-                s3 = __fadd_rn(s3, __fmul_rn(q4.w, k4.w));
+        // scores: blocks of TPW tokens per warp, 32 products per block
+        constexpr int TPW = 32 / MAXG;
+        for (int tb = warp * TPW; tb < n; tb += kStWarps * TPW) {
+            float v[32];  // product g * TPW + u
+#pragma unroll
+            for (int u = 0; u < TPW; ++u) {
+                const int t = tb + u < n ? tb + u : n - 1;  // past the end: a repeated row, result unused
+                float4 k4[NQ];
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) {
+                    const int c = lane + 32 * j;
+                    k4[j] = c < hs4 ? reinterpret_cast<const float4 *>(Ks + t * hs)[c]
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int g = 0; g < MAXG; ++g) {
+                    float sc = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < NQ; ++j) {
+                        sc = __fmaf_rn(qr[g][j].x, k4[j].x, sc);
+                        sc = __fmaf_rn(qr[g][j].y, k4[j].y, sc);
+                        sc = __fmaf_rn(qr[g][j].z, k4[j].z, sc);
+                        sc = __fmaf_rn(qr[g][j].w, k4[j].w, sc);
+                    }
+                    v[g * TPW + u] = sc;
+                }
             }
-            Ss[g * capp + t] = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), a.scale);
+            // reduce-scatter over the lanes: after the level of offset o, a
+            // lane keeps the half of the products selected by its bit o
+            // (summed with the partner's); lane L ends with product L
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const bool up = (lane & o) != 0;
+#pragma unroll
+                for (int k = 0; k < o; ++k) {
+                    const float send = up ? v[k] : v[k + o];
+                    const float keep = up ? v[k + o] : v[k];
+                    v[k] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+                }
+            }
+            const int g = lane / TPW, t = tb + lane % TPW;
+            if (g < G && t < n) Ss[g * capp + t] = __fmul_rn(v[0], a.scale);
         }
         __syncthreads();
         if (warp < G) {
@@ -803,35 +843,39 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int g = 0; g < MAXG; ++g) {
-            if (g >= G) break;
-            const float corr = stat[16 + g];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                acc[g][j].x = __fmul_rn(acc[g][j].x, corr);
-                acc[g][j].y = __fmul_rn(acc[g][j].y, corr);
-                acc[g][j].z = __fmul_rn(acc[g][j].z, corr);
-                acc[g][j].w = __fmul_rn(acc[g][j].w, corr);
-            }
-        }
-        for (int t = warp; t < n; t += kStWarps) {
-            float4 v4[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int c = lane + 32 * j;
-                v4[j] = c < hs4 ? reinterpret_cast<const float4 *>(Vs + t * hs)[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            }
+        {
 #pragma unroll
             for (int g = 0; g < MAXG; ++g) {
                 if (g >= G) break;
-                const float p = Ss[g * capp + t];
+                const float corr = stat[16 + g];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    acc[g][j].x = __fadd_rn(acc[g][j].x, __fmul_rn(p, v4[j].x));
-                    acc[g][j].y = __fadd_rn(acc[g][j].y, __fmul_rn(p, v4[j].y));
-                    acc[g][j].z = __fadd_rn(acc[g][j].z, __fmul_rn(p, v4[j].z));
-                    acc[g][j].w = __fadd_rn(acc[g][j].w, __fmul_rn(p, v4[j].w));
+                for (int j = 0; j < NQ; ++j) {
+                    acc[g][j].x = __fmul_rn(acc[g][j].x, corr);
+                    acc[g][j].y = __fmul_rn(acc[g][j].y, corr);
+                    acc[g][j].z = __fmul_rn(acc[g][j].z, corr);
+                    acc[g][j].w = __fmul_rn(acc[g][j].w, corr);
+                }
+            }
+#pragma unroll 2
+            for (int t = warp; t < n; t += kStWarps) {
+                float4 v4[NQ];
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) {
+                    const int c = lane + 32 * j;
+                    v4[j] = c < hs4 ? reinterpret_cast<const float4 *>(Vs + t * hs)[c]
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int g = 0; g < MAXG; ++g) {
+                    if (g >= G) break;
+                    const float p = Ss[g * capp + t];
+#pragma unroll
+                    for (int j = 0; j < NQ; ++j) {
+                        acc[g][j].x = __fmaf_rn(p, v4[j].x, acc[g][j].x);
+                        acc[g][j].y = __fmaf_rn(p, v4[j].y, acc[g][j].y);
+                        acc[g][j].z = __fmaf_rn(p, v4[j].z, acc[g][j].z);
+                        acc[g][j].w = __fmaf_rn(p, v4[j].w, acc[g][j].w);
+                    }
                 }
             }
         }
@@ -839,13 +883,15 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     cp_async_wait<0>();  // a CTA without tokens staged nothing; one with tokens has waited already
     __syncthreads();     // every pass done with Ks: it takes the warp partials now
     float *red = Ks;
+    {
 #pragma unroll
-    for (int g = 0; g < MAXG; ++g) {
-        if (g >= G) break;
+        for (int g = 0; g < MAXG; ++g) {
+            if (g >= G) break;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int c = lane + 32 * j;
-            if (c < hs4) reinterpret_cast<float4 *>(red + (warp * G + g) * hs)[c] = acc[g][j];
+            for (int j = 0; j < NQ; ++j) {
+                const int c = lane + 32 * j;
+                if (c < hs4) reinterpret_cast<float4 *>(red + (warp * G + g) * hs)[c] = acc[g][j];
+            }
         }
     }
     __syncthreads();
@@ -853,6 +899,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     const uint32_t slot0 = dsmem_addr(slots + int(rank) * L.slot, 0);
     for (int i = tid; i < G * hs; i += kStThreads) {
         float A = 0.0f;
+#pragma unroll
         for (int w = 0; w < kStWarps; ++w) A = __fadd_rn(A, red[w * G * hs + i]);
         dsmem_st_f32(slot0 + 4u * uint32_t(i), A);
     }
@@ -865,21 +912,25 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     asm volatile("barrier.cluster.arrive.release;" ::: "memory");
     if (rank != 0) return;
     asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-    for (int i = tid; i < G * hs; i += kStThreads) {
-        const int g = i / hs;
+    float *fac = Ss;  // [rank][8]: exp(m_r - M) for each query head (0 for a CTA without tokens)
+    if (tid < kAttnCluster * G) {
+        const int r = tid / G, g = tid - r * G;
         float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, slots[r * L.slot + G * hs + g]);
+        for (int r2 = 0; r2 < kAttnCluster; ++r2) M = fmaxf(M, slots[r2 * L.slot + G * hs + g]);
+        const float mr = slots[r * L.slot + G * hs + g];
+        fac[r * 8 + g] = mr == -INFINITY ? 0.0f : expf(__fsub_rn(mr, M));
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hs; i += kStThreads) {
+        const int g = i / hs;
         float A = 0.0f, Lsum = 0.0f;
-        if (M != -INFINITY)
 #pragma unroll
-            for (int r = 0; r < kAttnCluster; ++r) {
-                const float mr = slots[r * L.slot + G * hs + g];
-                if (mr == -INFINITY) continue;
-                const float f = expf(__fsub_rn(mr, M));
-                A = __fadd_rn(A, __fmul_rn(slots[r * L.slot + i], f));
-                Lsum = __fadd_rn(Lsum, __fmul_rn(slots[r * L.slot + G * hs + 8 + g], f));
-            }
+        for (int r = 0; r < kAttnCluster; ++r) {
+            const float f = fac[r * 8 + g];
+            A = __fadd_rn(A, __fmul_rn(slots[r * L.slot + i], f));
+            Lsum = __fadd_rn(Lsum, __fmul_rn(slots[r * L.slot + G * hs + 8 + g], f));
+        }
         a.out[int64_t(kvh) * G * hs + i] = __fdiv_rn(A, Lsum);
     }
 }
@@ -1401,6 +1452,7 @@ namespace {
 // memory hold them), or 0 when the shape needs the register-tile kernel.
 int staged_cap(int group, int head_size, int64_t context, int rotary) {
     if (group < 1 || group > kStMaxG || head_size < 4 || head_size > 256 || head_size % 4 != 0) return 0;
+    if (group > 4 && head_size > 128) return 0;  // 8 x 2 channel quads of queries and sums: beyond the registers
     int cap = int(std::min<int64_t>((context + kAttnCluster - 1) / kAttnCluster, 1024));
     while (cap > 0 && size_t(st_layout(group, head_size, cap, rotary).total) * sizeof(float) > size_t(kStSmemLimit))
         cap -= cap > 64 ? 16 : 1;
@@ -1409,7 +1461,9 @@ int staged_cap(int group, int head_size, int64_t context, int rotary) {
 
 template <bool ROPE>
 si_status launch_staged(const StagedAttn &a, const RopeFuse &rf, void *stream) {
-    auto kernel = a.group <= 4 ? gqa_decode_staged_kernel<4, ROPE> : gqa_decode_staged_kernel<kStMaxG, ROPE>;
+    auto kernel = a.head_size > 128 ? gqa_decode_staged_kernel<4, 2, ROPE>
+                  : a.group <= 4      ? gqa_decode_staged_kernel<4, 1, ROPE>
+                                      : gqa_decode_staged_kernel<kStMaxG, 1, ROPE>;
     const int smem = st_layout(a.group, a.head_size, a.cap, ROPE ? rf.rotary : 0).total * int(sizeof(float));
     if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), smem))
         return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
