@@ -303,6 +303,69 @@ __device__ __forceinline__ float inv_rms_parts_warp(const MmaParams &p, int64_t 
     return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, float(k)), p.eps)));
 }
 
+// The same 1 / rms (mode 1: of x; mode 3: of x + parts[0] + ... in rank
+// order, stored to h_out when given) formed by every thread of the CTA: the
+// epilogue of a K-split launch, where all warps are free, so the loads go out
+// in one batch instead of one warp's serial batches. Per thread the float4
+// groups tid, tid + T, .. (T threads); warp trees, then the warp sums added
+// in warp order by every thread (`red`: one float per warp of shared memory;
+// the caller has synchronised the CTA before its first use).
+__device__ float inv_rms_block(const MmaParams &p, int64_t k, float *red, float *h_out) {
+    constexpr int kJ = 4;  // float4 groups per thread per pass
+    const int nthr = int(blockDim.x), tid = int(threadIdx.x), lane = tid & 31, nw = nthr >> 5;
+    float s = 0.0f;
+    const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 && k % 4 == 0 &&
+                     (p.in_mode != 3 || p.nparts == 0 || ((reinterpret_cast<uintptr_t>(p.parts) & 15u) == 0 &&
+                                                          p.part_stride % 4 == 0));
+    if (vec) {
+        for (int64_t i0 = int64_t(tid) * 4; i0 < k; i0 += int64_t(nthr) * 4 * kJ) {
+            float4 v[kJ];
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) {
+                const int64_t i = i0 + int64_t(j) * nthr * 4;
+                v[j] = i < k ? __ldg(reinterpret_cast<const float4 *>(p.x + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (p.in_mode == 3)
+                for (int r = 0; r < p.nparts; ++r) {
+                    float4 q[kJ];
+#pragma unroll
+                    for (int j = 0; j < kJ; ++j) {
+                        const int64_t i = i0 + int64_t(j) * nthr * 4;
+                        q[j] = i < k ? __ldg(reinterpret_cast<const float4 *>(p.parts + r * p.part_stride + i))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int j = 0; j < kJ; ++j)
+                        v[j] = make_float4(__fadd_rn(v[j].x, q[j].x), __fadd_rn(v[j].y, q[j].y),
+                                           __fadd_rn(v[j].z, q[j].z), __fadd_rn(v[j].w, q[j].w));
+                }
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) {
+                const int64_t i = i0 + int64_t(j) * nthr * 4;
+                if (i < k) {
+                    if (h_out) *reinterpret_cast<float4 *>(h_out + i) = v[j];
+                    s = sq4(s, v[j]);
+                }
+            }
+        }
+    } else {
+        for (int64_t i = tid; i < k; i += nthr) {
+            float v = p.x[i];
+            if (p.in_mode == 3)
+                for (int r = 0; r < p.nparts; ++r) v = __fadd_rn(v, p.parts[r * p.part_stride + i]);
+            if (h_out) h_out[i] = v;
+            s = __fadd_rn(s, __fmul_rn(v, v));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    if (lane == 0) red[tid >> 5] = s;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < nw; ++w) t = __fadd_rn(t, red[w]);
+    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, float(k)), p.eps)));
+}
+
 // Every thread of every CTA of the cluster (hardware barrier).
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
@@ -522,11 +585,12 @@ __global__ void __launch_bounds__((MAXW + 2) * 32, 1) gemv_mma_q4k_kernel(const 
     if (CS > 1) {
         pdl_wait();          // y may still be read by the previous kernel
         if (warp == C + 1) consumer_wait(p, lane);
-        const float row_scale =
-            warp != C + 1 ? 1.0f
-            : p.in_mode == 1 ? inv_rms_warp(p.x, int64_t(p.nsb) * 256, p.eps, lane)
-            : p.in_mode == 3 ? inv_rms_parts_warp(p, int64_t(p.nsb) * 256, lane, blockIdx.x == 0 ? p.h_out : nullptr)
-                             : 1.0f;
+        float row_scale = 1.0f;
+        if (p.in_mode == 1 || p.in_mode == 3) {
+            __syncthreads();  // every warp is past its tile loop (the partial buffers are free) and the wait
+            row_scale = inv_rms_block(p, int64_t(p.nsb) * 256, part,
+                                      p.in_mode == 3 && blockIdx.x == 0 ? p.h_out : nullptr);
+        }
         const int local_tiles = first_tile < p.num_tiles ? (p.num_tiles - 1 - first_tile) / tile_step + 1 : 0;
         // residuals of this lane's first rows, loaded before the cluster barrier
         constexpr int kResAhead = 4;
