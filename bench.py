@@ -958,11 +958,54 @@ def run_case(case: list[str]) -> None:
       --case gemm Q4_K 200064 3072 512  (core.matrix-multiply, 512 rows)
       --case decode mini 64 2           (Phi-4-mini decoder: 64 prompt steps, then 2 steps; one graph per step)
       --case prefill mini 512           (Phi-4-mini decoder: one batched prefill of 512 tokens)
+      --case streams 14b 1024 2 32      (multi-stream session: 32 streams, each a 1024-token prompt, then 2 steps)
+      --case attention mini 520 1024    (fused rope-kv-write + decode attention at position 520, context 1024)
     """
     import numpy as np
 
     from sharpinference_b200 import native, phi4
     kind = case[0]
+    if kind == "streams":
+        cfg = dict(phi4.PHI4_MINI if case[1] == "mini" else phi4.PHI4_14B)
+        prompt_tokens, steps, streams = int(case[2]), int(case[3]), int(case[4])
+        cfg["context"] = prompt_tokens + steps + 1
+        shapes = phi4.linear_shapes(cfg)
+        wtype = cfg["weight_type"]
+        with native.Decoder(cfg, 0, streams=streams) as dec:
+            for i, name in enumerate(native.decoder_slot_names(cfg["layers"])):
+                if name in shapes:
+                    rows, cols = shapes[name]
+                    ptr, _ = dec.slot(name)
+                    native.synth_weight_rows_device(wtype, 11 * 1_000_003 + i, 0, rows, cols, 0.02, ptr, dec.stream)
+            first = [dec.prefill_stream(b, phi4.random_prompt(11 + b, prompt_tokens, cfg["vocab"]))
+                     for b in range(streams)]
+            toks = dec.generate_streams(first, [prompt_tokens] * streams, steps)
+            print(f"streams {case[1]} x{streams} prompt={prompt_tokens} steps={steps}: stream 0 {toks[:, 0].tolist()} "
+                  f"device_error={native.device_error_take(0)}")
+        return
+    if kind == "attention":
+        heads = {"mini": (24, 8, 128, 96), "14b": (40, 10, 128, 128)}[case[1]]
+        qh, kvh, hs, rot = heads
+        pos, context = int(case[2]), int(case[3])
+        rng = np.random.default_rng(5)
+        qkv = rng.standard_normal((qh + 2 * kvh) * hs).astype(np.float32)
+        cache = (0.1 * rng.standard_normal(context * kvh * hs)).astype(np.float32)
+        freq = (1.0 / 10000.0 ** (np.arange(rot // 2) * 2.0 / rot)).astype(np.float32)
+        with native.Context(0) as ctx:
+            B = [ctx.buffer(a.nbytes) for a in (qkv, cache, cache, freq)]
+            for b, a in zip(B, (qkv, cache, cache, freq)):
+                b.upload(a)
+            P, O = ctx.buffer(16), ctx.buffer(4 * qh * hs)
+            P.upload(np.array([pos], np.int32))
+            for _ in range(2):
+                native.call("si_rope_grouped_query_attention", B[0].device_pointer, P.device_pointer,
+                            B[3].device_pointer, B[1].device_pointer, B[2].device_pointer, O.device_pointer, qh, kvh,
+                            hs, rot, context, 1.1902381, ctx.stream)
+            ctx.synchronize()
+            y = O.readback().view(np.float32)
+            print(f"attention {case[1]} pos={pos} context={context}: finite={bool(np.all(np.isfinite(y)))} "
+                  f"device_error={native.device_error_take(0)}")
+        return
     if kind in ("decode", "prefill"):
         cfg = dict(phi4.PHI4_MINI if case[1] == "mini" else phi4.PHI4_14B)
         prompt_tokens = int(case[2])

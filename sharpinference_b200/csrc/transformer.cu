@@ -597,8 +597,12 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 // memory; one cluster-barrier phase later rank 0 forms the per-(CTA, head)
 // factors exp(m_r - M) once and merges in rank order. Tokens past the staging
 // capacity are taken in further passes (online softmax across passes).
-constexpr int kStThreads = 512, kStWarps = kStThreads / 32, kStMaxG = 8;
-constexpr int kStSmemLimit = 227 * 1024;
+// One stream: 512 threads and up to the 227 KB a CTA may hold (one CTA per
+// SM; the kernel is latency-bound). Several streams (thousands of CTAs, a
+// throughput problem): 256 threads and at most 113 KB, so two CTAs share an
+// SM and one streams its rows while the other computes.
+constexpr int kStThreadsOne = 512, kStThreadsMany = 256, kStMaxG = 8;
+constexpr int kStSmemOne = 227 * 1024, kStSmemMany = 113 * 1024;
 
 struct StLayout {
     int ks, vs, hb, qs, fr, ss, st, cs, sl, slot, total;  // float offsets; total floats
@@ -606,12 +610,12 @@ struct StLayout {
 // The shared-memory carve-up for G query heads per key/value head, head size
 // hs (a multiple of 4), cap staged tokens and a rope table of `rotary`
 // floats. Every region starts on a 16-byte boundary.
-__host__ __device__ inline StLayout st_layout(int G, int hs, int cap, int rotary) {
+__host__ __device__ inline StLayout st_layout(int G, int hs, int cap, int rotary, int nw) {
     StLayout L{};
     const int capp = (cap + 31) & ~31;
     int o = 0;
-    L.ks = o;  // staged keys [cap][hs]; at the end the warp partials [warps][G][hs]
-    o += cap * hs > kStWarps * G * hs ? cap * hs : kStWarps * G * hs;
+    L.ks = o;  // staged keys [cap][hs]; at the end the warp partials [nw][G][hs]
+    o += cap * hs > nw * G * hs ? cap * hs : nw * G * hs;
     L.vs = o;  // staged values [cap][hs]
     o += cap * hs;
     L.hb = o;  // the token's raw q heads, k head, v head
@@ -642,28 +646,32 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Several streams: cluster u serves key/value head u % kv_heads of stream
+// u / kv_heads, whose query / output rows are q_stride floats apart, caches
+// cache_stride floats apart and whose position is position[stream].
 struct StagedAttn {
     const float *query;  // without rope: the query vector
     const float *key_cache, *value_cache;
     const int32_t *position;
     float *out;
     int group, kv_heads, head_size, cap;
-    int64_t context;
+    int64_t context, q_stride, cache_stride;
     float scale;
 };
 
 // NQ: float4 channel quads per lane in the value pass (head_size <= 32 * 4 NQ).
-template <int MAXG, int NQ, bool ROPE>
-__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThreads, 1)
+template <int MAXG, int NQ, bool ROPE, int NT>
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT == kStThreadsOne ? 1 : 2)
     gqa_decode_staged_kernel(const StagedAttn a, const RopeFuse rf) {
+    constexpr int kStThreads = NT, kStWarps = NT / 32;
     extern __shared__ __align__(16) float sm[];
     const int G = a.group, hs = a.head_size, hs4 = hs >> 2;
     const int cap = a.cap, capp = (cap + 31) & ~31;
-    const StLayout L = st_layout(G, hs, cap, ROPE ? rf.rotary : 0);
+    const StLayout L = st_layout(G, hs, cap, ROPE ? rf.rotary : 0, kStWarps);
     float *Ks = sm + L.ks, *Vs = sm + L.vs, *hb = sm + L.hb, *qs = sm + L.qs, *fr = sm + L.fr, *Ss = sm + L.ss,
           *stat = sm + L.st, *cs = sm + L.cs, *slots = sm + L.sl;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kvh = blockIdx.x / kAttnCluster;
+    const int unit = blockIdx.x / kAttnCluster, kvh = unit % a.kv_heads, strm = unit / a.kv_heads;
     const uint32_t rank = cta_rank_in_cluster();
     // First cluster-barrier phase: arrived here, waited before the first
     // store into rank 0's shared memory (every CTA of the cluster has started).
@@ -673,14 +681,15 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     // earlier token (written by earlier steps). The row at the position is
     // this step's: from the qkv vector (ROPE) or from the preceding
     // rope-kv-write.
-    const int32_t pos = *a.position;
+    const int32_t pos = a.position[strm];
     int64_t active = pos;
     active = active < 0 ? 0 : (active > a.context - 1 ? a.context - 1 : active);
     const int64_t fresh = (pos >= 0 && pos < a.context) ? int64_t(pos) : -1;
     const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
     const int64_t stride = int64_t(a.kv_heads) * hs;
-    const float *kbase = a.key_cache + int64_t(kvh) * hs, *vbase = a.value_cache + int64_t(kvh) * hs;
+    const float *kbase = a.key_cache + strm * a.cache_stride + int64_t(kvh) * hs;
+    const float *vbase = a.value_cache + strm * a.cache_stride + int64_t(kvh) * hs;
     // rows c0 .. c0 + n - 1 of the CTA's range into Ks / Vs, one warp per row
     // (the fresh row is written from registers instead)
     auto stage = [&](int64_t c0, int n) {
@@ -714,7 +723,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
     const bool mine = fresh >= t0 && fresh < t1;
     {
         // the token's heads, one memory round trip
-        const float *qsrc = (ROPE ? rf.qkv : a.query) + int64_t(kvh) * G * hs;
+        const float *qsrc = (ROPE ? rf.qkv : a.query + strm * a.q_stride) + int64_t(kvh) * G * hs;
         float4 *hb4 = reinterpret_cast<float4 *>(hb);
         for (int i = tid; i < G * hs4; i += kStThreads) hb4[i] = *reinterpret_cast<const float4 *>(qsrc + 4 * i);
         if (mine && tid < 2 * hs4) {
@@ -931,7 +940,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kStThread
             A = __fadd_rn(A, __fmul_rn(slots[r * L.slot + i], f));
             Lsum = __fadd_rn(Lsum, __fmul_rn(slots[r * L.slot + G * hs + 8 + g], f));
         }
-        a.out[int64_t(kvh) * G * hs + i] = __fdiv_rn(A, Lsum);
+        a.out[strm * a.q_stride + int64_t(kvh) * G * hs + i] = __fdiv_rn(A, Lsum);
     }
 }
 
@@ -1447,28 +1456,33 @@ si_status launch_gqa(const float *query, const float *kc, const float *vc, const
 }  // namespace
 
 namespace {
-// Tokens per staging pass of gqa_decode_staged_kernel for this shape (the
-// most a CTA takes at the cache's last position, as far as 227 KB of shared
-// memory hold them), or 0 when the shape needs the register-tile kernel.
+// Tokens per staging pass of gqa_decode_staged_kernel<.., NT> for this
+// shape (the most a CTA takes at the cache's last position, as far as the
+// shared-memory limit of that thread count holds them), or 0 when the shape
+// needs the register-tile kernel.
+template <int NT>
 int staged_cap(int group, int head_size, int64_t context, int rotary) {
     if (group < 1 || group > kStMaxG || head_size < 4 || head_size > 256 || head_size % 4 != 0) return 0;
     if (group > 4 && head_size > 128) return 0;  // 8 x 2 channel quads of queries and sums: beyond the registers
+    const size_t limit = size_t(NT == kStThreadsOne ? kStSmemOne : kStSmemMany);
     int cap = int(std::min<int64_t>((context + kAttnCluster - 1) / kAttnCluster, 1024));
-    while (cap > 0 && size_t(st_layout(group, head_size, cap, rotary).total) * sizeof(float) > size_t(kStSmemLimit))
+    while (cap > 0 && size_t(st_layout(group, head_size, cap, rotary, NT / 32).total) * sizeof(float) > limit)
         cap -= cap > 64 ? 16 : 1;
     return cap;
 }
 
-template <bool ROPE>
-si_status launch_staged(const StagedAttn &a, const RopeFuse &rf, void *stream) {
-    auto kernel = a.head_size > 128 ? gqa_decode_staged_kernel<4, 2, ROPE>
-                  : a.group <= 4      ? gqa_decode_staged_kernel<4, 1, ROPE>
-                                      : gqa_decode_staged_kernel<kStMaxG, 1, ROPE>;
-    const int smem = st_layout(a.group, a.head_size, a.cap, ROPE ? rf.rotary : 0).total * int(sizeof(float));
+template <bool ROPE, int NT>
+si_status launch_staged(const StagedAttn &a, const RopeFuse &rf, int streams, void *stream) {
+    auto kernel = a.head_size > 128 ? gqa_decode_staged_kernel<4, 2, ROPE, NT>
+                  : a.group <= 4      ? gqa_decode_staged_kernel<4, 1, ROPE, NT>
+                                      : gqa_decode_staged_kernel<kStMaxG, 1, ROPE, NT>;
+    const int smem =
+        st_layout(a.group, a.head_size, a.cap, ROPE ? rf.rotary : 0, NT / 32).total * int(sizeof(float));
     if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), smem))
         return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
-    return launch("transformer.grouped-query-attention", kernel, dim3(unsigned(a.kv_heads * kAttnCluster)),
-                  dim3(kStThreads), size_t(smem), stream, a, rf);
+    return launch("transformer.grouped-query-attention", kernel,
+                  dim3(unsigned(int64_t(streams) * a.kv_heads * kAttnCluster)), dim3(NT), size_t(smem), stream, a,
+                  rf);
 }
 }  // namespace
 
@@ -1480,10 +1494,10 @@ si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, co
     const int npl = (head_size + 31) / 32;
     const int64_t qsize = int64_t(query_heads) * head_size, kvsize = int64_t(kv_heads) * head_size;
     const RopeFuse rf{qkv, freq, kc, vc, qsize, kvsize, rotary, rope_scale};
-    if (const int cap = staged_cap(group, head_size, context, rotary))
-        return launch_staged<true>(StagedAttn{nullptr, kc, vc, position, out, group, kv_heads, head_size, cap, context,
-                                              scale},
-                                   rf, stream);
+    if (const int cap = staged_cap<kStThreadsOne>(group, head_size, context, rotary))
+        return launch_staged<true, kStThreadsOne>(
+            StagedAttn{nullptr, kc, vc, position, out, group, kv_heads, head_size, cap, context, 0, 0, scale}, rf, 1,
+            stream);
 #define SI_GQA_R(NPL, MAXG, TILE)                                                                               \
     launch_gqa<NPL, MAXG, TILE, kAttnWarpsOne, true>(qkv, kc, vc, position, out, group, kv_heads, head_size,      \
                                                      context, scale, 1, qsize, 0, stream, rf)
@@ -1513,11 +1527,16 @@ si_status tr_attention_decode_streams(const float *query, const float *kc, const
     const float scale = 1.0f / sqrtf(float(head_size));
     const int npl = (head_size + 31) / 32;
     const int64_t q_stride = int64_t(query_heads) * head_size;
-    if (streams == 1)
-        if (const int cap = staged_cap(group, head_size, context, 0))
-            return launch_staged<false>(StagedAttn{query, kc, vc, position, out, group, kv_heads, head_size, cap,
-                                                   context, scale},
-                                        RopeFuse{}, stream);
+    if (streams == 1) {
+        if (const int cap = staged_cap<kStThreadsOne>(group, head_size, context, 0))
+            return launch_staged<false, kStThreadsOne>(
+                StagedAttn{query, kc, vc, position, out, group, kv_heads, head_size, cap, context, 0, 0, scale},
+                RopeFuse{}, 1, stream);
+    } else if (const int cap = staged_cap<kStThreadsMany>(group, head_size, context, 0)) {
+        return launch_staged<false, kStThreadsMany>(StagedAttn{query, kc, vc, position, out, group, kv_heads,
+                                                               head_size, cap, context, q_stride, cache_stride, scale},
+                                                    RopeFuse{}, streams, stream);
+    }
 #define SI_GQA(NPL, MAXG, TILE)                                                                                \
     (streams > 1 ? launch_gqa<NPL, MAXG, TILE, kAttnWarpsMany>(query, kc, vc, position, out, group, kv_heads,      \
                                                                head_size, context, scale, streams, q_stride,      \
