@@ -690,22 +690,23 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
     const int64_t stride = int64_t(a.kv_heads) * hs;
     const float *kbase = a.key_cache + strm * a.cache_stride + int64_t(kvh) * hs;
     const float *vbase = a.value_cache + strm * a.cache_stride + int64_t(kvh) * hs;
-    // rows c0 .. c0 + n - 1 of the CTA's range into Ks / Vs, one warp per row
-    // (the fresh row is written from registers instead)
-    auto stage = [&](int64_t c0, int n) {
+    // rows c0 .. c0 + n - 1 of the CTA's range of one cache into dst, one
+    // warp per row, as one copy group (the fresh row is written from
+    // registers instead)
+    auto stage = [&](float *dst, const float *base, int64_t c0, int n) {
         for (int r = warp; r < n; r += kStWarps) {
             const int64_t t = c0 + r;
             if (t == fresh) continue;
-            const float *ksrc = kbase + t * stride, *vsrc = vbase + t * stride;
-            for (int c = lane; c < hs4; c += 32) {
-                cp_async16(Ks + r * hs + 4 * c, ksrc + 4 * c, true);
-                cp_async16(Vs + r * hs + 4 * c, vsrc + 4 * c, true);
-            }
+            const float *src = base + t * stride;
+            for (int c = lane; c < hs4; c += 32) cp_async16(dst + r * hs + 4 * c, src + 4 * c, true);
         }
         cp_async_commit();
     };
     const int n0 = t1 - t0 < int64_t(cap) ? int(t1 - t0) : cap;  // <= 0: no tokens for this CTA
-    if (n0 > 0) stage(t0, n0);
+    if (n0 > 0) {
+        stage(Ks, kbase, t0, n0);
+        stage(Vs, vbase, t0, n0);
+    }
     if (tid < 8) {
         stat[tid] = -INFINITY;
         stat[8 + tid] = 0.0f;
@@ -773,18 +774,15 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
                                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             acc[g][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
+    // Passes of up to cap tokens. Copy groups in commit order: keys and
+    // values of pass 0, then per pass the next pass's keys (issued once the
+    // scores are done with Ks) and its values (once the value sums are done
+    // with Vs), so the next pass's rows stream in under this pass's work.
     for (int64_t c0 = t0; c0 < t1; c0 += cap) {
         const int n = t1 - c0 < int64_t(cap) ? int(t1 - c0) : cap;
-        if (c0 != t0) {
-            __syncthreads();  // the previous pass is done with Ks / Vs / Ss
-            stage(c0, n);
-            if (fresh >= c0 && fresh < c0 + n)
-                for (int d = tid; d < hs; d += kStThreads) {
-                    Ks[int(fresh - c0) * hs + d] = fr[d];
-                    Vs[int(fresh - c0) * hs + d] = fr[hs + d];
-                }
-        }
-        cp_async_wait<0>();
+        const int64_t c1 = c0 + cap;
+        const int n1 = c1 < t1 ? (t1 - c1 < int64_t(cap) ? int(t1 - c1) : cap) : 0;
+        cp_async_wait<1>();  // this pass's keys (its values may still be in flight)
         __syncthreads();
         // scores: blocks of TPW tokens per warp, 32 products per block
         constexpr int TPW = 32 / MAXG;
@@ -829,7 +827,12 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
             const int g = lane / TPW, t = tb + lane % TPW;
             if (g < G && t < n) Ss[g * capp + t] = __fmul_rn(v[0], a.scale);
         }
-        __syncthreads();
+        __syncthreads();  // Ks is free: the next pass's keys
+        if (n1 > 0) {
+            stage(Ks, kbase, c1, n1);
+            if (fresh >= c1 && fresh < c1 + n1)
+                for (int d = tid; d < hs; d += kStThreads) Ks[int(fresh - c1) * hs + d] = fr[d];
+        }
         if (warp < G) {
             const int g = warp;
             float mx = -INFINITY;
@@ -851,6 +854,10 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
                 stat[16 + g] = corr;
             }
         }
+        if (n1 > 0)
+            cp_async_wait<1>();  // this pass's values (the next pass's keys may still be in flight)
+        else
+            cp_async_wait<0>();
         __syncthreads();
         {
 #pragma unroll
@@ -887,6 +894,12 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
                     }
                 }
             }
+        }
+        if (n1 > 0) {
+            __syncthreads();  // Vs is free: the next pass's values
+            stage(Vs, vbase, c1, n1);
+            if (fresh >= c1 && fresh < c1 + n1)
+                for (int d = tid; d < hs; d += kStThreads) Vs[int(fresh - c1) * hs + d] = fr[hs + d];
         }
     }
     cp_async_wait<0>();  // a CTA without tokens staged nothing; one with tokens has waited already

@@ -40,6 +40,28 @@ def test_streams_decode_each_prompt_like_the_oracle(wtype):
     assert native.device_error_take(0) == 0
 
 
+def test_streams_long_prompts_take_several_staging_passes():
+    """Prompts long enough that the decode attention's CTAs (8 per stream and
+    key/value head, each a contiguous range of the stream's tokens) stage
+    their cache rows in more than one pass: in the multi-stream form a CTA
+    holds at most 113 KB of shared memory (two per SM), 96 rows of this
+    model, and the ranges here reach 150 rows. Streams of different lengths
+    take one or two passes side by side."""
+    cfg = dict(tiny_decoder_config(native.Q8_0), context=1280)
+    weights = tiny_decoder_weights(cfg, seed=51)
+    lengths, steps = [1100, 700, 1200], 4
+    prompts = _prompts(cfg, lengths, 51)
+    want = [oracle.Decoder(cfg, weights).generate(p, steps) for p in prompts]
+    with native.Decoder(cfg, streams=len(prompts)) as dec:
+        _load(dec, weights)
+        first = [dec.prefill_stream(b, p) for b, p in enumerate(prompts)]
+        assert first == [w[n - 1] for w, n in zip(want, lengths)]
+        out = dec.generate_streams(first, lengths, steps)
+        for b, (w, n) in enumerate(zip(want, lengths)):
+            assert list(out[:, b]) == w[n:n + steps], f"stream {b}"
+    assert native.device_error_take(0) == 0
+
+
 def test_streams_stepwise_prompt_equals_prefill():
     """Feeding the prompts through step_streams (all streams advancing
     together, shorter prompts padded by repeating their last token at the
