@@ -72,6 +72,11 @@ internal static unsafe partial class SharpInferCuda
         float ropeScale, nint stream);
     [LibraryImport(Lib)] public static partial Status si_grouped_query_attention(nint query, nint keyCache, nint valueCache,
         nint position, nint output, int queryHeads, int kvHeads, int headSize, long context, nint stream);
+    // transformer.rope-kv-write followed by transformer.grouped-query-attention in one launch
+    // (Phi4D3D12TextSession.cs:873-916 dispatches the two in turn).
+    [LibraryImport(Lib)] public static partial Status si_rope_grouped_query_attention(nint qkv, nint position,
+        nint frequencies, nint keyCache, nint valueCache, nint output, int queryHeads, int kvHeads, int headSize,
+        int rotarySize, long context, float ropeScale, nint stream);
     [LibraryImport(Lib)] public static partial Status si_argmax(nint input, long count, nint output, nint stream);
 
     // registry (InstructionCollection.cs:146-218)
