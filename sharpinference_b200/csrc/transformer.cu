@@ -602,6 +602,9 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 // throughput problem): 256 threads and at most 113 KB, so two CTAs share an
 // SM and one streams its rows while the other computes.
 constexpr int kStThreadsOne = 512, kStThreadsMany = 256, kStMaxG = 8;
+// CTAs per cluster, i.e. per stream and key/value head (contiguous token
+// ranges, partials merged in rank 0).
+constexpr int kStClusterOne = 8, kStClusterMany = 8;
 constexpr int kStSmemOne = 227 * 1024, kStSmemMany = 113 * 1024;
 
 struct StLayout {
@@ -660,8 +663,8 @@ struct StagedAttn {
 };
 
 // NQ: float4 channel quads per lane in the value pass (head_size <= 32 * 4 NQ).
-template <int MAXG, int NQ, bool ROPE, int NT>
-__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT == kStThreadsOne ? 1 : 2)
+template <int MAXG, int NQ, bool ROPE, int NT, int CL>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, NT == kStThreadsOne ? 1 : 2)
     gqa_decode_staged_kernel(const StagedAttn a, const RopeFuse rf) {
     constexpr int kStThreads = NT, kStWarps = NT / 32;
     extern __shared__ __align__(16) float sm[];
@@ -671,7 +674,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
     float *Ks = sm + L.ks, *Vs = sm + L.vs, *hb = sm + L.hb, *qs = sm + L.qs, *fr = sm + L.fr, *Ss = sm + L.ss,
           *stat = sm + L.st, *cs = sm + L.cs, *slots = sm + L.sl;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int unit = blockIdx.x / kAttnCluster, kvh = unit % a.kv_heads, strm = unit / a.kv_heads;
+    const int unit = blockIdx.x / CL, kvh = unit % a.kv_heads, strm = unit / a.kv_heads;
     const uint32_t rank = cta_rank_in_cluster();
     // First cluster-barrier phase: arrived here, waited before the first
     // store into rank 0's shared memory (every CTA of the cluster has started).
@@ -685,7 +688,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
     int64_t active = pos;
     active = active < 0 ? 0 : (active > a.context - 1 ? a.context - 1 : active);
     const int64_t fresh = (pos >= 0 && pos < a.context) ? int64_t(pos) : -1;
-    const int64_t T = active + 1, per = (T + kAttnCluster - 1) / kAttnCluster;
+    const int64_t T = active + 1, per = (T + CL - 1) / CL;
     const int64_t t0 = int64_t(rank) * per, t1 = t0 + per < T ? t0 + per : T;
     const int64_t stride = int64_t(a.kv_heads) * hs;
     const float *kbase = a.key_cache + strm * a.cache_stride + int64_t(kvh) * hs;
@@ -935,11 +938,11 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
     if (rank != 0) return;
     asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
     float *fac = Ss;  // [rank][8]: exp(m_r - M) for each query head (0 for a CTA without tokens)
-    if (tid < kAttnCluster * G) {
+    if (tid < CL * G) {
         const int r = tid / G, g = tid - r * G;
         float M = -INFINITY;
 #pragma unroll
-        for (int r2 = 0; r2 < kAttnCluster; ++r2) M = fmaxf(M, slots[r2 * L.slot + G * hs + g]);
+        for (int r2 = 0; r2 < CL; ++r2) M = fmaxf(M, slots[r2 * L.slot + G * hs + g]);
         const float mr = slots[r * L.slot + G * hs + g];
         fac[r * 8 + g] = mr == -INFINITY ? 0.0f : expf(__fsub_rn(mr, M));
     }
@@ -948,7 +951,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(NT, NT ==
         const int g = i / hs;
         float A = 0.0f, Lsum = 0.0f;
 #pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) {
+        for (int r = 0; r < CL; ++r) {
             const float f = fac[r * 8 + g];
             A = __fadd_rn(A, __fmul_rn(slots[r * L.slot + i], f));
             Lsum = __fadd_rn(Lsum, __fmul_rn(slots[r * L.slot + G * hs + 8 + g], f));
@@ -1473,28 +1476,28 @@ namespace {
 // shape (the most a CTA takes at the cache's last position, as far as the
 // shared-memory limit of that thread count holds them), or 0 when the shape
 // needs the register-tile kernel.
-template <int NT>
+template <int NT, int CL>
 int staged_cap(int group, int head_size, int64_t context, int rotary) {
     if (group < 1 || group > kStMaxG || head_size < 4 || head_size > 256 || head_size % 4 != 0) return 0;
     if (group > 4 && head_size > 128) return 0;  // 8 x 2 channel quads of queries and sums: beyond the registers
     const size_t limit = size_t(NT == kStThreadsOne ? kStSmemOne : kStSmemMany);
-    int cap = int(std::min<int64_t>((context + kAttnCluster - 1) / kAttnCluster, 1024));
+    int cap = int(std::min<int64_t>((context + CL - 1) / CL, 1024));
     while (cap > 0 && size_t(st_layout(group, head_size, cap, rotary, NT / 32).total) * sizeof(float) > limit)
         cap -= cap > 64 ? 16 : 1;
     return cap;
 }
 
-template <bool ROPE, int NT>
+template <bool ROPE, int NT, int CL>
 si_status launch_staged(const StagedAttn &a, const RopeFuse &rf, int streams, void *stream) {
-    auto kernel = a.head_size > 128 ? gqa_decode_staged_kernel<4, 2, ROPE, NT>
-                  : a.group <= 4      ? gqa_decode_staged_kernel<4, 1, ROPE, NT>
-                                      : gqa_decode_staged_kernel<kStMaxG, 1, ROPE, NT>;
+    auto kernel = a.head_size > 128 ? gqa_decode_staged_kernel<4, 2, ROPE, NT, CL>
+                  : a.group <= 4      ? gqa_decode_staged_kernel<4, 1, ROPE, NT, CL>
+                                      : gqa_decode_staged_kernel<kStMaxG, 1, ROPE, NT, CL>;
     const int smem =
         st_layout(a.group, a.head_size, a.cap, ROPE ? rf.rotary : 0, NT / 32).total * int(sizeof(float));
     if (const int ae = opt_in_smem(reinterpret_cast<const void *>(kernel), smem))
         return fail(SI_ERR_CUDA, "attention shared-memory opt-in failed: %s", cudaGetErrorString(cudaError_t(ae)));
     return launch("transformer.grouped-query-attention", kernel,
-                  dim3(unsigned(int64_t(streams) * a.kv_heads * kAttnCluster)), dim3(NT), size_t(smem), stream, a,
+                  dim3(unsigned(int64_t(streams) * a.kv_heads * CL)), dim3(NT), size_t(smem), stream, a,
                   rf);
 }
 }  // namespace
@@ -1507,8 +1510,8 @@ si_status tr_attention_decode_rope(const float *qkv, const int32_t *position, co
     const int npl = (head_size + 31) / 32;
     const int64_t qsize = int64_t(query_heads) * head_size, kvsize = int64_t(kv_heads) * head_size;
     const RopeFuse rf{qkv, freq, kc, vc, qsize, kvsize, rotary, rope_scale};
-    if (const int cap = staged_cap<kStThreadsOne>(group, head_size, context, rotary))
-        return launch_staged<true, kStThreadsOne>(
+    if (const int cap = staged_cap<kStThreadsOne, kStClusterOne>(group, head_size, context, rotary))
+        return launch_staged<true, kStThreadsOne, kStClusterOne>(
             StagedAttn{nullptr, kc, vc, position, out, group, kv_heads, head_size, cap, context, 0, 0, scale}, rf, 1,
             stream);
 #define SI_GQA_R(NPL, MAXG, TILE)                                                                               \
@@ -1541,12 +1544,12 @@ si_status tr_attention_decode_streams(const float *query, const float *kc, const
     const int npl = (head_size + 31) / 32;
     const int64_t q_stride = int64_t(query_heads) * head_size;
     if (streams == 1) {
-        if (const int cap = staged_cap<kStThreadsOne>(group, head_size, context, 0))
-            return launch_staged<false, kStThreadsOne>(
+        if (const int cap = staged_cap<kStThreadsOne, kStClusterOne>(group, head_size, context, 0))
+            return launch_staged<false, kStThreadsOne, kStClusterOne>(
                 StagedAttn{query, kc, vc, position, out, group, kv_heads, head_size, cap, context, 0, 0, scale},
                 RopeFuse{}, 1, stream);
-    } else if (const int cap = staged_cap<kStThreadsMany>(group, head_size, context, 0)) {
-        return launch_staged<false, kStThreadsMany>(StagedAttn{query, kc, vc, position, out, group, kv_heads,
+    } else if (const int cap = staged_cap<kStThreadsMany, kStClusterMany>(group, head_size, context, 0)) {
+        return launch_staged<false, kStThreadsMany, kStClusterMany>(StagedAttn{query, kc, vc, position, out, group, kv_heads,
                                                                head_size, cap, context, q_stride, cache_stride, scale},
                                                     RopeFuse{}, streams, stream);
     }
