@@ -603,8 +603,11 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnWarp
 // SM and one streams its rows while the other computes.
 constexpr int kStThreadsOne = 512, kStThreadsMany = 256, kStMaxG = 8;
 // CTAs per cluster, i.e. per stream and key/value head (contiguous token
-// ranges, partials merged in rank 0).
-constexpr int kStClusterOne = 8, kStClusterMany = 8;
+// ranges, partials merged in rank 0): 8 for one stream (short chains); 4 for
+// several, so each CTA's fixed phases (prologue, query heads, cluster merge)
+// are paid half as often (Phi-4-14B, 32 streams at ~1100 tokens: 130 vs
+// 141 us per layer).
+constexpr int kStClusterOne = 8, kStClusterMany = 4;
 constexpr int kStSmemOne = 227 * 1024, kStSmemMany = 113 * 1024;
 
 struct StLayout {
